@@ -1,0 +1,107 @@
+"""Pin the CPU oracle against outputs of the reference's own code.
+
+The fixtures under tests/golden were produced by tests/golden/make_golden.py,
+which runs the reference's `paper` Triton kernels (TRITON_INTERPRET=1) and
+ChannelPruner.update_rotatek (ROTATEK_SOLVER=eigh).  Nothing here needs a GPU.
+"""
+import numpy as np
+import pytest
+
+from oracle import decode as odec
+from oracle import rotation as orot
+from oracle.bf16 import round_bf16, truncate_bf16
+
+# The reference kernels compute in fp32 and store the output in q's dtype.
+# fp32: the reference itself sits ~1e-5 from the float64 closed form at logits
+# of magnitude ~50, so the bar is 1e-5 absolute plus 1e-5 relative.
+# bf16: 2e-3 absolute plus 2^-8 relative -- the output is itself rounded to
+# bf16 (half an ulp is 2^-9 relative), and small fixtures with peaked softmax
+# produce outputs up to ~2.5 where that rounding alone exceeds 2e-3.
+TOL = {"float32": (1e-5, 1e-5), "bfloat16": (2e-3, 2.0 ** -8)}
+
+
+def assert_matches_reference(oracle_out, ref_out, dtype):
+    """fp32: within TOL.  bf16: the fixtures come from Triton's interpreter, which
+    truncates fp32 -> bf16 on store; the oracle truncated the same way must give
+    the same bits (>= 99 %, the rest one ulp away from a rounding boundary)."""
+    if dtype == "float32":
+        atol, rtol = TOL[dtype]
+        np.testing.assert_allclose(oracle_out, ref_out, atol=atol, rtol=rtol)
+        return
+    t = truncate_bf16(oracle_out)
+    same = np.mean(t == ref_out)
+    assert same >= 0.99, same
+    np.testing.assert_allclose(t, ref_out, atol=0, rtol=2.0 ** -7)
+
+
+def test_bf16_rounding_matches_torch():
+    import torch
+    x = np.random.default_rng(0).standard_normal(10000).astype(np.float32) * 37.0
+    x[:4] = [1.00390625, 1.01171875, -3.0e38, 0.0]      # ties and extremes
+    want = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    np.testing.assert_array_equal(round_bf16(x), want)
+
+
+@pytest.mark.parametrize("case", ["cfg1_fp32", "small_bf16"])
+def test_decode_oracle_matches_reference_kernel(golden, case):
+    g = golden(case)
+    p, v = g["prompt_len"], g["vision_len"]
+    keys, values = g["keys"], g["values"]
+    k_full = np.concatenate([keys[:, :, :p], keys[:, :, p + v:]], axis=2)
+    v_full = np.concatenate([values[:, :, :p], values[:, :, p + v:]], axis=2)
+    mask = np.ones(k_full.shape[:1] + k_full.shape[2:3], dtype=np.uint8)
+    out = odec.rotatek_decode(g["q_decode"], g["R_partial"], g["delta_mu"], k_full, v_full, mask,
+                              g["kept"], values[:, :, p:p + v], g["num_kv_groups"])
+    assert_matches_reference(out, g["out_rotatek"], g["dtype"])
+    dense = odec.full_channel_decode(g["q_decode"], keys, values, g["num_kv_groups"])
+    assert_matches_reference(dense, g["out_dense"], g["dtype"])
+
+
+@pytest.mark.parametrize("case", ["dec_mask_nobias_fp32", "dec_empty_visual_fp32",
+                                  "dec_empty_full_fp32", "dec_g7_bf16"])
+def test_decode_edge_cases(golden, case):
+    g = golden(case)
+    out = odec.rotatek_decode(g["q_full"], g["R_partial"], g.get("delta_mu"), g["k_full"],
+                              g["v_full"], g["mask_full"], g["k_sparse"], g["v_sparse"],
+                              g["num_kv_groups"])
+    assert_matches_reference(out, g["out_rotatek"], g["dtype"])
+
+
+@pytest.mark.parametrize("case", ["dense_g1_fp32", "dense_g4_bf16"])
+def test_dense_oracle(golden, case):
+    g = golden(case)
+    out = odec.full_channel_decode(g["q"], g["k"], g["v"], g["num_kv_groups"])
+    assert_matches_reference(out, g["out_dense"], g["dtype"])
+
+
+@pytest.mark.parametrize("case,inputs", [("cfg1_fp32", "cfg1_fp32"),
+                                         ("cfg1_fp32_plain", "cfg1_fp32"),
+                                         ("small_bf16", "small_bf16")])
+def test_rotation_oracle_matches_update_rotatek(golden, case, inputs):
+    g, src = golden(case), golden(inputs)
+    p, v = g["prompt_len"], g["vision_len"]
+    keys = src["keys"]
+    _, vision, _ = orot.split_spans(keys, p, g["text_len"])
+    assert vision.shape[2] == v
+    keep = orot.keep_count(keys.shape[-1], g["ratio"])
+    res = orot.build_rotation(vision, src["queries_window"], keep, g["num_kv_groups"],
+                              query_aware=bool(g["query_aware"]), storage=g["dtype"])
+    np.testing.assert_array_equal(res.keep_mask, g["keep_mask"])
+    # the subspace is what decode depends on: compare projectors (sign/rotation invariant)
+    dist = orot.projector_distance(res.R_partial, g["R_partial"])
+    bound = 1e-4 if g["dtype"] == "float32" else 3e-2
+    assert dist.max() < bound, dist
+    # eigenvalues are separated here, so columns match up to sign
+    cos = np.abs((res.R_partial.astype(np.float64) * g["R_partial"]).sum(axis=-2))
+    assert cos.min() > (1 - 1e-4 if g["dtype"] == "float32" else 0.95), cos.min()
+    tol = 2e-4 if g["dtype"] == "float32" else 0.1
+    np.testing.assert_allclose(res.delta_mu, g["delta_mu"], atol=tol)
+    scale = np.abs(g["kept"]).max()
+    np.testing.assert_allclose(res.kept, g["kept"] * np.sign(cos_signs(res.R_partial, g["R_partial"])),
+                               atol=tol * scale)
+
+
+def cos_signs(a, b):
+    """Per-column sign aligning b's eigenvectors with a's: [B, H, 1, k]."""
+    s = np.sign((np.asarray(a, np.float64) * np.asarray(b, np.float64)).sum(axis=-2))
+    return s[:, :, None, :]
