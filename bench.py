@@ -1,0 +1,353 @@
+#!/usr/bin/env python
+"""Decode-step benchmark of the RotateK hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the headline metric): one attention layer's
+single-token decode at the Qwen2.5-VL-7B attention shape -- bf16, B=32,
+28 query / 4 KV heads (G=7), head_dim 128, D_keep=32 (channel_ratio 0.75),
+64 prompt + 15 360 visual + 576 text tokens.  A step is one call of
+``rotatek_b200.kernels.rotatek_decode`` over that batch (one kernel launch).
+Inputs are seeded synthetic tensors (low-rank-plus-noise Keys rotated into a
+top-32 basis, N(0,1) Values and queries); their 672.6 MB exceed the 126 MB
+L2, so no flush is needed between steps.
+
+With --gpus N (launched under torchrun) every rank runs its own batch of 32
+(batch-sharded replicas, weak scaling, no data-path collective); the timed
+region is bracketed by barriers and the max over ranks is reported.
+
+`value` is the whole-job time per batch-32 decode step in microseconds
+(timed region / (steps * ranks)), lower is better.
+
+--impl reference times the reference's own math on the host CPU: the eager
+PyTorch restatement of rotatek/kernels/fused_decode.py (the reference has no
+CPU decode of its own; its kernels are Triton-only), on a batch sample scaled
+to the full batch.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+METRIC = "fused decode-attn us/step & HBM GB/s %peak, bs32 16k ctx, 25% K channels kept"
+UNIT = "us/step"
+CFG = dict(batch=32, q_heads=28, kv_heads=4, head_dim=128, keep=32, prompt=64, vision=15360,
+           text=576)
+WORKLOAD = ("config2: Qwen2.5-VL-7B attention decode, bf16, B=32, H_q=28, H_kv=4 (G=7), "
+            "D=128, D_keep=32, S = 64 prompt + 15360 visual + 576 text")
+DATA = "synthetic: seeded low-rank+noise Keys rotated to a top-32 basis; N(0,1) Values/queries"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def algorithmic_bytes(d) -> int:
+    """Every input read once + output written once (mask excluded: all ones)."""
+    return d.nbytes()
+
+
+def load_peak_hbm():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic_per_launch():
+    """dram bytes per launch of the decode kernel from the committed ncu summary."""
+    path = os.path.join(REPO, "profiles", "decode_tc_config2.txt")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch"):
+                return int(float(line.split("=")[1].split()[0]))
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Polls NVML (what nvidia-smi reads) for SM clock and clock-event reasons
+    while running; reads only, changes nothing."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x1: "gpu_idle", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, index: int, period_s: float = 0.002):
+        self.index, self.period = index, period_s
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.nvml = None
+
+    def _run(self):
+        nv = self.nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                for bit, name in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def make_inputs(device, dtype=torch.bfloat16, seed=0, batch=None):
+    from rotatek_b200 import synthetic as syn
+    b = CFG["batch"] if batch is None else batch
+    return syn.make_decode(b, CFG["q_heads"], CFG["kv_heads"], CFG["vision"],
+                           CFG["prompt"] + CFG["text"], head_dim=CFG["head_dim"],
+                           keep=CFG["keep"], seed=seed, device=device, dtype=dtype)
+
+
+def cpu_baseline_sample(target_s: float = 12.0):
+    """The reference's math, eager PyTorch on the host CPU (all threads), on a
+    batch sample; returns (us per full batch-32 step, sample description, threads)."""
+    from oracle.eager_torch import rotatek_decode_eager
+    threads = torch.get_num_threads()
+    b = 1
+    d = make_inputs("cpu", batch=b, seed=1)
+    kw = d.as_kwargs()
+    rotatek_decode_eager(**kw)                       # warm-up
+    t0 = time.perf_counter()
+    rotatek_decode_eager(**kw)
+    one = time.perf_counter() - t0
+    reps = max(1, int(target_s / max(one, 1e-3)))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        rotatek_decode_eager(**kw)
+    per = (time.perf_counter() - t0) / reps
+    us_full = per * 1e6 * CFG["batch"] / b
+    sample = (f"batch {b} of {CFG['batch']} (other dims full), {reps} reps, eager torch fp32 "
+              f"restatement of fused_decode.py, scaled x{CFG['batch'] // b} to the batch-32 step")
+    return us_full, sample, threads
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    from oracle.eager_torch import rotatek_decode_eager
+    threads = torch.get_num_threads()
+    b = 1
+    d = make_inputs("cpu", batch=b, seed=1)
+    kw = d.as_kwargs()
+    for _ in range(args.warmup):
+        rotatek_decode_eager(**kw)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        rotatek_decode_eager(**kw)
+        times.append(time.perf_counter() - t0)
+    per_full_us = statistics.mean(times) * 1e6 * CFG["batch"] / b
+    sample = (f"batch {b} of {CFG['batch']} per step (other dims full), eager torch fp32 "
+              f"restatement of fused_decode.py, scaled x{CFG['batch'] // b}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": per_full_us, "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per_full_us / 1e3, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": DATA,
+        "config": {"workload": WORKLOAD, "global_batch": CFG["batch"], "seq_len": 16000,
+                   "parallelism": "host CPU, rank 0 only"},
+        "cpu_baseline": {"value": per_full_us, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": per_full_us, "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        pg = dist
+    from rotatek_b200 import _lib
+    from rotatek_b200.kernels import rotatek_decode
+
+    d = make_inputs(dev, seed=1000 + rank, batch=args.batch)
+    kw = d.as_kwargs()
+    nbytes = algorithmic_bytes(d)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        rotatek_decode(**kw)
+    torch.cuda.synchronize()
+
+    # ---- device-timed region: inputs resident in HBM
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        events[0].record(stream)
+        for i in range(args.steps):
+            rotatek_decode(**kw)
+            events[i + 1].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    per_step_ms = [events[i].elapsed_time(events[i + 1]) for i in range(args.steps)]
+    total_ms = events[0].elapsed_time(events[-1])
+    if pg is not None:
+        t = torch.tensor([total_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        total_ms = float(t.item())
+    status = _lib.read_status(dev)
+    if args.kernel_only:
+        if rank == 0:
+            print(json.dumps({"kernel_only": True, "batch": args.batch or CFG["batch"],
+                              "us_per_step": total_ms * 1e3 / args.steps,
+                              "device_status": status}), flush=True)
+        if pg is not None:
+            pg.destroy_process_group()
+        return 0
+
+    # ---- end-to-end through the public API with host buffers
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    host = {k: (v.cpu().pin_memory() if torch.is_tensor(v) else v) for k, v in kw.items()}
+    dev_in = {k: (torch.empty_like(v) if torch.is_tensor(v) else v) for k, v in kw.items()}
+    h2d = sum(v.numel() * v.element_size() for v in host.values() if torch.is_tensor(v))
+    out_host = torch.empty((CFG["batch"], 1, CFG["q_heads"], CFG["head_dim"]),
+                           dtype=torch.bfloat16).pin_memory()
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        for k, v in host.items():
+            if torch.is_tensor(v):
+                dev_in[k].copy_(v, non_blocking=True)
+        out, _, _ = rotatek_decode(**dev_in)
+        out_host.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if pg is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    barrier()
+
+    if rank == 0:
+        peak, peak_kind = load_peak_hbm()
+        avg_launch_s = statistics.mean(per_step_ms) / 1e3
+        achieved = nbytes / avg_launch_s / 1e9
+        us_per_step = total_ms * 1e3 / (args.steps * world)
+        line = {
+            "metric": METRIC, "value": us_per_step, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": total_ms / args.steps, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": DATA,
+            "config": {"workload": WORKLOAD, "global_batch": CFG["batch"] * world,
+                       "seq_len": CFG["prompt"] + CFG["vision"] + CFG["text"],
+                       "parallelism": f"batch-sharded replicas x{world} (no collective)",
+                       "l2": "inputs 672.6 MB per step > 126 MB L2; no flush"},
+            "hbm_gbs": achieved, "hbm_frac": achieved / peak,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": nbytes,
+                         "traffic": ncu_traffic_per_launch()},
+            "e2e": {"value": e2e_ms * 1e3 / (e2e_steps * world), "unit": UNIT,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps},
+            "gpu_launches": args.steps,
+            "clocks": sampler.summary(),
+            "device_status": status,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            us_cpu, sample, threads = cpu_baseline_sample()
+            line["cpu_baseline"] = {"value": us_cpu, "unit": UNIT, "cores": threads,
+                                    "kind": "port", "sample": sample}
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the batch (profiling cases only; the bench line uses 32)")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="decode launches only: no e2e, no CPU baseline, no JSON bench line")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,119 @@
+/*
+ * rotatek_b200 -- C ABI of the B200 (sm_100a) RotateK hot path.
+ *
+ * Every entry point takes plain device pointers wrapped in rtk_tensor
+ * descriptors (shape + element strides), a CUDA stream as `void*`
+ * (NULL = legacy default stream) and, where the kernels need scratch, a
+ * caller-owned device workspace.  Nothing here allocates device memory; no
+ * entry point synchronises the stream except rtk_read_status.
+ *
+ * Return value: RTK_OK (0) or an rtk_status code; rtk_last_error() then holds
+ * a message for the calling thread.  Shape errors use the reference's
+ * messages, so a host wrapper can raise them as ValueError unchanged.
+ *
+ * The reference (beomseokg/rotatek) is Python + Triton; each function names
+ * the Python entry point it replaces.
+ */
+#ifndef ROTATEK_B200_H
+#define ROTATEK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RTK_ABI_VERSION 1
+
+typedef enum rtk_dtype {
+  RTK_F32 = 0,
+  RTK_BF16 = 1,
+  RTK_F16 = 2,
+  RTK_U8 = 3
+} rtk_dtype;
+
+typedef enum rtk_status {
+  RTK_OK = 0,
+  RTK_ERR_INVALID = 1,      /* bad shape / dtype / argument (reference: ValueError) */
+  RTK_ERR_UNSUPPORTED = 2,  /* valid, but no kernel covers it                       */
+  RTK_ERR_WORKSPACE = 3,    /* workspace missing or smaller than *_workspace_size() */
+  RTK_ERR_CUDA = 4          /* a CUDA runtime / driver call failed                  */
+} rtk_status;
+
+/* Device-status bits a kernel may set in the workspace's status word. */
+#define RTK_DEVICE_TIMEOUT 1u /* a bounded wait gave up; outputs of that call are invalid */
+
+typedef struct rtk_tensor {
+  void *data;          /* device pointer; NULL only where a parameter says "nullable" */
+  int32_t dtype;       /* rtk_dtype */
+  int32_t ndim;        /* 1..4 */
+  int64_t shape[4];
+  int64_t stride[4];   /* in elements */
+} rtk_tensor;
+
+/* ABI version (RTK_ABI_VERSION of the built library). */
+int rtk_abi_version(void);
+
+/* Message of the last failed call made by this thread ("" if none). */
+const char *rtk_last_error(void);
+
+/* ------------------------------------------------------------------------
+ * Decode attention
+ * ------------------------------------------------------------------------ */
+
+/* Bytes of workspace rtk_rotatek_decode needs for these shapes on `device`.
+ * The workspace must be zero-filled once before its first use; every call
+ * leaves it ready for the next (its ticket counters return to zero).  Calls
+ * that share a workspace must be ordered on the GPU (same stream, or events):
+ * overlapping calls on one workspace race.                                   */
+size_t rtk_rotatek_decode_workspace_size(int32_t dtype, int64_t batch, int64_t q_heads,
+                                         int64_t kv_heads, int64_t head_dim,
+                                         int64_t head_dim_keep, int64_t seq_full,
+                                         int64_t seq_sparse, int32_t device);
+
+/* Fused RotateK decode for one query token.
+ * Replaces rotatek.kernels.rotatek_decode -- `paper` family
+ * rotatek/kernels/fused_decode.py:303-420 (and the `gqa` twin
+ * rotatek/kernels/gqa_decode.py:280-321).
+ *   q_full     [B, H_q, D]              f32 | bf16 | f16
+ *   R_partial  [B, H_kv, D, D_keep]     same dtype as q_full
+ *   delta_mu   [B, H_kv, D]             nullable (no mean-correction bias)
+ *   k_full     [B, H_kv, S_f, D]        prompt + text Keys, full width
+ *   v_full     [B, H_kv, S_f, D]
+ *   mask_full  [B, S_f] u8              nullable (= all ones); 0 masks a token
+ *   k_sparse   [B, H_kv, S_v, D_keep]   rotated + truncated visual Keys
+ *   v_sparse   [B, H_kv, S_v, D]        visual Values
+ *   out        [B, H_q, D] or [B, 1, H_q, D], dtype of q_full
+ * out = softmax([q.k_f * s ; (q.R.k_s + q.delta_mu) * s]) . [v_f ; v_s] / (l + 1e-6),
+ * s = 1/sqrt(D), H_q = H_kv * num_kv_groups.                                 */
+int rtk_rotatek_decode(const rtk_tensor *q_full, const rtk_tensor *R_partial,
+                       const rtk_tensor *delta_mu, const rtk_tensor *k_full,
+                       const rtk_tensor *v_full, const rtk_tensor *mask_full,
+                       const rtk_tensor *k_sparse, const rtk_tensor *v_sparse,
+                       int64_t num_kv_groups, const rtk_tensor *out, void *workspace,
+                       size_t workspace_bytes, void *stream);
+
+/* Bytes of workspace rtk_full_channel_decode needs (same rules as above). */
+size_t rtk_full_channel_decode_workspace_size(int32_t dtype, int64_t batch, int64_t q_heads,
+                                              int64_t kv_heads, int64_t head_dim,
+                                              int64_t seq, int32_t device);
+
+/* Full-channel split-K flash-decode for one query token.
+ * Replaces rotatek.kernels.full_channel_decode --
+ * rotatek/kernels/full_channel_flash_decoding.py:162-229 (`gqa` twin
+ * rotatek/kernels/gqa_decode.py:254-277).
+ *   q [B, H_q, D], k / v [B, H_kv, S, D], out [B, H_q, D] or [B, 1, H_q, D]. */
+int rtk_full_channel_decode(const rtk_tensor *q, const rtk_tensor *k, const rtk_tensor *v,
+                            int64_t num_kv_groups, const rtk_tensor *out, void *workspace,
+                            size_t workspace_bytes, void *stream);
+
+/* Copy the workspace's device-status word to *status (RTK_DEVICE_TIMEOUT bits)
+ * and clear it.  Synchronises `stream`.                                       */
+int rtk_read_status(void *workspace, void *stream, uint32_t *status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ROTATEK_B200_H */

@@ -32,44 +32,52 @@ def _f64(x) -> Optional[np.ndarray]:
 
 
 def _softmax_merge(logits: np.ndarray, values: np.ndarray) -> np.ndarray:
-    """logits [B, H, S] (may hold -inf), values [B, H, S, D] -> [B, H, D]."""
+    """logits [G, S] (may hold -inf), values [S, D] -> [G, D]."""
     if logits.shape[-1] == 0:
-        return np.zeros(values.shape[:2] + values.shape[-1:], dtype=np.float64)
+        return np.zeros((logits.shape[0], values.shape[-1]), dtype=np.float64)
     m = np.maximum(np.max(logits, axis=-1, keepdims=True), -1e30)
     p = np.exp(logits - m)
     l = p.sum(axis=-1, keepdims=True)
-    acc = np.einsum("bhs,bhsd->bhd", p, values)
-    return acc / (l + 1e-6)
+    return (p @ values) / (l + 1e-6)
 
 
 def rotatek_decode(q_full, R_partial, delta_mu, k_full, v_full, mask_full, k_sparse,
                    v_sparse, num_kv_groups: int) -> np.ndarray:
-    """Float64 reference of ``rotatek_decode_fused_triton``; returns [B, 1, H_q, D]."""
+    """Float64 reference of ``rotatek_decode_fused_triton``; returns [B, 1, H_q, D].
+
+    Works one (batch, KV head) at a time, so full-size decode steps fit in memory."""
     q = _f64(q_full)
-    R = _f64(R_partial)
-    dm = _f64(delta_mu)
-    kf, vf = _f64(k_full), _f64(v_full)
-    ks, vs = _f64(k_sparse), _f64(v_sparse)
-    mask = _f64(mask_full)
     bsz, heads, head_dim = q.shape
-    kv_of = np.arange(heads) // num_kv_groups
+    hkv = heads // num_kv_groups
+    g = num_kv_groups
     scale = 1.0 / math.sqrt(head_dim)
-
-    q_rot = np.einsum("bhd,bhdk->bhk", q, R[:, kv_of])
-    bias = np.einsum("bhd,bhd->bh", q, dm[:, kv_of]) if dm is not None else np.zeros((bsz, heads))
-    logit_v = np.einsum("bhk,bhsk->bhs", q_rot, ks[:, kv_of]) * scale + (bias * scale)[..., None]
-    logit_f = np.einsum("bhd,bhsd->bhs", q, kf[:, kv_of]) * scale
-    logit_f = np.where(mask[:, None, :] != 0, logit_f, -np.inf)
-
-    logits = np.concatenate([logit_f, logit_v], axis=-1)
-    values = np.concatenate([vf[:, kv_of], vs[:, kv_of]], axis=-2)
-    return _softmax_merge(logits, values)[:, None]
+    mask = None if mask_full is None else _f64(mask_full)
+    out = np.zeros((bsz, 1, heads, head_dim), dtype=np.float64)
+    for b in range(bsz):
+        for h in range(hkv):
+            qg = q[b, h * g:(h + 1) * g]                                  # [G, D]
+            R = _f64(R_partial[b, h])
+            q_rot = qg @ R
+            bias = qg @ _f64(delta_mu[b, h]) if delta_mu is not None else np.zeros(g)
+            logit_v = (q_rot @ _f64(k_sparse[b, h]).T) * scale + (bias * scale)[:, None]
+            logit_f = (qg @ _f64(k_full[b, h]).T) * scale
+            if mask is not None:
+                logit_f = np.where(mask[b][None, :] != 0, logit_f, -np.inf)
+            logits = np.concatenate([logit_f, logit_v], axis=-1)
+            values = np.concatenate([_f64(v_full[b, h]), _f64(v_sparse[b, h])], axis=0)
+            out[b, 0, h * g:(h + 1) * g] = _softmax_merge(logits, values)
+    return out
 
 
 def full_channel_decode(q, k, v, num_kv_groups: int = 1) -> np.ndarray:
     """Float64 reference of ``full_channel_decode_triton``; returns [B, 1, H_q, D]."""
-    q, k, v = _f64(q), _f64(k), _f64(v)
-    heads, head_dim = q.shape[1], q.shape[2]
-    kv_of = np.arange(heads) // num_kv_groups
-    logits = np.einsum("bhd,bhsd->bhs", q, k[:, kv_of]) / math.sqrt(head_dim)
-    return _softmax_merge(logits, v[:, kv_of])[:, None]
+    q = _f64(q)
+    bsz, heads, head_dim = q.shape
+    g = num_kv_groups
+    out = np.zeros((bsz, 1, heads, head_dim), dtype=np.float64)
+    for b in range(bsz):
+        for h in range(heads // g):
+            qg = q[b, h * g:(h + 1) * g]
+            logits = (qg @ _f64(k[b, h]).T) / math.sqrt(head_dim)
+            out[b, 0, h * g:(h + 1) * g] = _softmax_merge(logits, _f64(v[b, h]))
+    return out

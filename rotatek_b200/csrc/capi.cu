@@ -1,0 +1,448 @@
+// extern "C" entry points of librotatek_b200.so (declared in include/rotatek_b200.h).
+//
+// Host-side work per call: validate shapes and dtypes (messages follow the
+// reference's ValueErrors, rotatek/kernels/fused_decode.py:323-338 and
+// full_channel_flash_decoding.py:173-178), choose the kernel, encode the TMA
+// tensor maps, carve the caller's workspace, launch on the caller's stream.
+// Nothing allocates device memory and nothing synchronises the stream.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/rotatek_b200.h"
+#include "decode.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+  return fail(RTK_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+constexpr size_t kAlign = 256;
+constexpr int kBlockTokens = 64;
+
+size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+int sm_count(int device) {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  if (device < 0 || device >= 64) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[device] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+
+int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// ------------------------------------------------------------------ shapes
+struct View4 {  // a tensor seen as [B, H, S, D] with element strides
+  const void *data;
+  int64_t n[4], s[4];
+};
+
+bool as4(const rtk_tensor *t, View4 &v) {
+  if (t == nullptr || t->ndim != 4) return false;
+  v.data = t->data;
+  for (int i = 0; i < 4; ++i) {
+    v.n[i] = t->shape[i];
+    v.s[i] = t->stride[i];
+  }
+  return true;
+}
+
+// out may be [B, H_q, D] or [B, 1, H_q, D] (the reference returns the latter).
+bool out_view(const rtk_tensor *o, int64_t B, int64_t Hq, int64_t D, int64_t s[3]) {
+  if (o == nullptr || o->data == nullptr) return false;
+  if (o->ndim == 3 && o->shape[0] == B && o->shape[1] == Hq && o->shape[2] == D) {
+    s[0] = o->stride[0]; s[1] = o->stride[1]; s[2] = o->stride[2];
+    return true;
+  }
+  if (o->ndim == 4 && o->shape[0] == B && o->shape[1] == 1 && o->shape[2] == Hq && o->shape[3] == D) {
+    s[0] = o->stride[0]; s[1] = o->stride[2]; s[2] = o->stride[3];
+    return true;
+  }
+  return false;
+}
+
+// ------------------------------------------------------------------ TMA maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// [B, H, S, inner] 16-bit tensor -> 4-D map with a {box_inner, 64, 1, 1} box.
+// Returns false when TMA cannot describe the layout (the caller then uses the
+// generic kernel).  Size-1 dimensions get a canonical stride.
+bool encode_map(CUtensorMap *map, const View4 &v, CUtensorMapDataType dt, int box_inner,
+                CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  if (v.s[3] != 1) return false;
+  if (reinterpret_cast<uintptr_t>(v.data) % 16 != 0) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)v.n[3], (cuuint64_t)v.n[2], (cuuint64_t)v.n[1],
+                        (cuuint64_t)v.n[0]};
+  cuuint64_t strides[3];
+  int64_t natural = v.n[3] * 2;
+  for (int i = 0; i < 3; ++i) {
+    const int dim = 2 - i;  // S, H, B
+    int64_t sb = v.s[dim] * 2;
+    if (v.n[dim] == 1) sb = (natural + 15) / 16 * 16;
+    if (sb <= 0 || sb % 16 != 0) return false;
+    strides[i] = (cuuint64_t)sb;
+    natural = sb * v.n[dim];
+  }
+  for (int i = 0; i < 4; ++i)
+    if (dims[i] == 0 || dims[i] > (1ull << 31)) return false;
+  cuuint32_t box[4] = {(cuuint32_t)box_inner, (cuuint32_t)kBlockTokens, 1, 1};
+  cuuint32_t estride[4] = {1, 1, 1, 1};
+  return fn(map, dt, 4, const_cast<void *>(v.data), dims, strides, box, estride,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+CUtensorMapSwizzle swizzle_for_row_bytes(int bytes) {
+  if (bytes == 32) return CU_TENSOR_MAP_SWIZZLE_32B;
+  if (bytes == 64) return CU_TENSOR_MAP_SWIZZLE_64B;
+  return CU_TENSOR_MAP_SWIZZLE_128B;
+}
+
+// ------------------------------------------------------------------ workspace
+struct WorkspacePlan {
+  size_t ticket_off, partial_off, bytes;
+};
+
+WorkspacePlan plan_workspace(int64_t tickets, int64_t slots, int64_t slot_floats) {
+  WorkspacePlan w;
+  w.ticket_off = kAlign;  // [0, 256): device status word
+  w.partial_off = w.ticket_off + align_up((size_t)tickets * sizeof(int));
+  w.bytes = w.partial_off + align_up((size_t)slots * slot_floats * sizeof(float));
+  return w;
+}
+
+struct TcShape {
+  int heads_tile, head_chunks;
+  int64_t units, blocks_full, blocks_sparse, blocks_per_unit, total;
+  int grid;
+  int slot_floats;
+};
+
+TcShape tc_shape(int64_t B, int64_t Hkv, int64_t G, int64_t Sf, int64_t Sv, int device) {
+  TcShape t;
+  t.heads_tile = G <= 8 ? 8 : 16;
+  t.head_chunks = (int)cdiv(G, t.heads_tile);
+  t.units = B * Hkv * t.head_chunks;
+  t.blocks_full = cdiv(Sf, kBlockTokens);
+  t.blocks_sparse = cdiv(Sv, kBlockTokens);
+  t.blocks_per_unit = t.blocks_full + t.blocks_sparse;
+  t.total = t.units * t.blocks_per_unit;
+  t.grid = (int)std::max<int64_t>(1, std::min<int64_t>(t.total, sm_count(device)));
+  t.slot_floats = 32 + 16 * 128;
+  return t;
+}
+
+struct SimtShape {
+  int splits, tokens_per_split, slot_floats;
+  int64_t units;
+};
+
+SimtShape simt_shape(int64_t B, int64_t Hq, int64_t D, int64_t seq, int device) {
+  SimtShape s;
+  s.units = B * Hq;
+  const int64_t want = cdiv(4 * (int64_t)sm_count(device), std::max<int64_t>(1, s.units));
+  const int64_t max_splits = std::max<int64_t>(1, std::min<int64_t>(256, cdiv(seq, kBlockTokens)));
+  s.splits = (int)std::max<int64_t>(1, std::min(want, max_splits));
+  s.tokens_per_split = (int)std::max<int64_t>(1, cdiv(seq, s.splits));
+  s.slot_floats = (int)(4 + (D + 3) / 4 * 4);
+  return s;
+}
+
+size_t decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t Sf,
+                              int64_t Sv, int device) {
+  const int64_t G = Hkv > 0 ? Hq / Hkv : 1;
+  const TcShape t = tc_shape(B, Hkv, std::max<int64_t>(G, 1), Sf, Sv, device);
+  const size_t tc = plan_workspace(t.units, t.units + t.grid, t.slot_floats).bytes;
+  const SimtShape s = simt_shape(B, Hq, D, Sf + Sv, device);
+  const size_t simt = plan_workspace(s.units, s.units * s.splits, s.slot_floats).bytes;
+  return std::max(tc, simt);
+}
+
+bool is_half_type(int dt) { return dt == RTK_BF16 || dt == RTK_F16; }
+
+// ------------------------------------------------------------------ decode core
+struct DecodeArgs {
+  const rtk_tensor *q, *R, *dm, *kf, *vf, *mask, *ks, *vs, *out;
+  int64_t groups;
+  bool dense;  // full_channel_decode: no visual span, no mask
+};
+
+int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cudaStream_t stream) {
+  View4 kf{}, vf{}, ks{}, vs{}, R{};
+  as4(a.kf, kf);
+  as4(a.vf, vf);
+  const int64_t B = a.q->shape[0], Hq = a.q->shape[1], D = a.q->shape[2];
+  const int64_t Hkv = kf.n[1];
+  const int64_t G = a.groups;
+  const int64_t Sf = kf.n[2];
+  int64_t Sv = 0, DK = 0;
+  if (!a.dense) {
+    as4(a.ks, ks);
+    as4(a.vs, vs);
+    as4(a.R, R);
+    Sv = ks.n[2];
+    DK = R.n[3];
+  }
+  int64_t os[3];
+  out_view(a.out, B, Hq, D, os);
+  const int dt = a.q->dtype;
+  const int device = current_device();
+
+  if (workspace == nullptr)
+    return fail(RTK_ERR_WORKSPACE, "workspace is NULL (size it with *_workspace_size)");
+  const size_t need = decode_workspace_bytes(B, Hq, Hkv, D, Sf, Sv, device);
+  if (workspace_bytes < need)
+    return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, need);
+  unsigned char *ws = static_cast<unsigned char *>(workspace);
+  unsigned int *status = reinterpret_cast<unsigned int *>(ws);
+  const double scale_log2 = 1.4426950408889634 / std::sqrt((double)D);
+
+  // ---------------- tensor-core path
+  bool tc = is_half_type(dt) && D == 128 && (Sf + Sv) > 0 && a.q->stride[2] == 1 &&
+            os[2] == 1 && (a.dense || ((DK == 16 || DK == 32 || DK == 64) && R.s[3] == 1 &&
+                                       (a.dm == nullptr || a.dm->stride[2] == 1)));
+  rtk::DecodeTensorMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  if (tc) {
+    const CUtensorMapDataType et =
+        dt == RTK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if (Sf > 0)
+      tc = encode_map(&maps.kf, kf, et, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
+           encode_map(&maps.vf, vf, et, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (tc && Sv > 0)
+      tc = encode_map(&maps.ks, ks, et, (int)DK, swizzle_for_row_bytes((int)DK * 2)) &&
+           encode_map(&maps.vs, vs, et, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  if (tc) {
+    const TcShape t = tc_shape(B, Hkv, G, Sf, Sv, device);
+    const WorkspacePlan w = plan_workspace(t.units, t.units + t.grid, t.slot_floats);
+    rtk::DecodeParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.batch = (int)B; p.q_heads = (int)Hq; p.kv_heads = (int)Hkv; p.groups = (int)G;
+    p.head_dim_keep = (int)DK;
+    p.seq_full = (int)Sf; p.seq_sparse = (int)Sv;
+    p.head_chunks = t.head_chunks;
+    p.blocks_full = (int)t.blocks_full; p.blocks_sparse = (int)t.blocks_sparse;
+    p.blocks_per_unit = (int)t.blocks_per_unit;
+    p.total_blocks = t.total;
+    p.scale_log2 = (float)scale_log2;
+    p.q = a.q->data; p.q_sb = a.q->stride[0]; p.q_sh = a.q->stride[1];
+    if (!a.dense) {
+      p.R = R.data; p.R_sb = R.s[0]; p.R_sh = R.s[1]; p.R_sd = R.s[2];
+      if (a.dm != nullptr) { p.dm = a.dm->data; p.dm_sb = a.dm->stride[0]; p.dm_sh = a.dm->stride[1]; }
+      if (a.mask != nullptr) { p.mask = static_cast<const uint8_t *>(a.mask->data); p.mask_sb = a.mask->stride[0]; p.mask_ss = a.mask->stride[1]; }
+    }
+    p.out = a.out->data; p.o_sb = os[0]; p.o_sh = os[1];
+    p.partials = reinterpret_cast<float *>(ws + w.partial_off);
+    p.slot_floats = t.slot_floats;
+    p.tickets = reinterpret_cast<int *>(ws + w.ticket_off);
+    p.status = status;
+    const cudaError_t e = rtk::launch_decode_tc(dt == RTK_BF16, maps, p, t.heads_tile,
+                                                a.dense ? 32 : (int)DK, t.grid, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "rotatek decode (tensor-core kernel) launch");
+    return RTK_OK;
+  }
+
+  // ---------------- generic path
+  if (D > 256) return fail(RTK_ERR_UNSUPPORTED, "head_dim %lld > 256 is not supported", (long long)D);
+  const SimtShape s = simt_shape(B, Hq, D, Sf + Sv, device);
+  const WorkspacePlan w = plan_workspace(s.units, s.units * s.splits, s.slot_floats);
+  rtk::SimtParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.dtype = dt;
+  p.batch = (int)B; p.q_heads = (int)Hq; p.kv_heads = (int)Hkv; p.groups = (int)G;
+  p.head_dim = (int)D; p.head_dim_keep = (int)DK;
+  p.seq_full = (int)Sf; p.seq_sparse = (int)Sv;
+  p.splits = s.splits; p.tokens_per_split = s.tokens_per_split;
+  p.scale_log2 = (float)scale_log2;
+  p.q = a.q->data;
+  for (int i = 0; i < 3; ++i) p.q_s[i] = a.q->stride[i];
+  p.kf = kf.data; p.vf = vf.data;
+  for (int i = 0; i < 4; ++i) { p.kf_s[i] = kf.s[i]; p.vf_s[i] = vf.s[i]; }
+  if (!a.dense) {
+    p.R = R.data;
+    for (int i = 0; i < 4; ++i) { p.R_s[i] = R.s[i]; p.ks_s[i] = ks.s[i]; p.vs_s[i] = vs.s[i]; }
+    p.ks = ks.data; p.vs = vs.data;
+    if (a.dm != nullptr) { p.dm = a.dm->data; for (int i = 0; i < 3; ++i) p.dm_s[i] = a.dm->stride[i]; }
+    if (a.mask != nullptr) { p.mask = static_cast<const uint8_t *>(a.mask->data); p.mask_s[0] = a.mask->stride[0]; p.mask_s[1] = a.mask->stride[1]; }
+  }
+  p.out = a.out->data;
+  for (int i = 0; i < 3; ++i) p.o_s[i] = os[i];
+  p.partials = reinterpret_cast<float *>(ws + w.partial_off);
+  p.slot_floats = s.slot_floats;
+  p.tickets = reinterpret_cast<int *>(ws + w.ticket_off);
+  p.status = status;
+  const cudaError_t e = rtk::launch_decode_simt(p, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "rotatek decode (generic kernel) launch");
+  return RTK_OK;
+}
+
+bool same_dims(const rtk_tensor *t, int ndim, std::initializer_list<int64_t> want) {
+  if (t == nullptr || t->ndim != ndim) return false;
+  int i = 0;
+  for (int64_t w : want) {
+    if (w >= 0 && t->shape[i] != w) return false;
+    ++i;
+  }
+  return true;
+}
+
+bool dtype_ok(int dt) { return dt == RTK_F32 || dt == RTK_BF16 || dt == RTK_F16; }
+
+}  // namespace
+
+extern "C" {
+
+int rtk_abi_version(void) { return RTK_ABI_VERSION; }
+
+const char *rtk_last_error(void) { return g_last_error.c_str(); }
+
+size_t rtk_rotatek_decode_workspace_size(int32_t dtype, int64_t batch, int64_t q_heads,
+                                         int64_t kv_heads, int64_t head_dim,
+                                         int64_t head_dim_keep, int64_t seq_full,
+                                         int64_t seq_sparse, int32_t device) {
+  (void)dtype;
+  (void)head_dim_keep;
+  return decode_workspace_bytes(batch, q_heads, kv_heads, head_dim, seq_full, seq_sparse, device);
+}
+
+size_t rtk_full_channel_decode_workspace_size(int32_t dtype, int64_t batch, int64_t q_heads,
+                                              int64_t kv_heads, int64_t head_dim, int64_t seq,
+                                              int32_t device) {
+  (void)dtype;
+  return decode_workspace_bytes(batch, q_heads, kv_heads, head_dim, seq, 0, device);
+}
+
+int rtk_rotatek_decode(const rtk_tensor *q_full, const rtk_tensor *R_partial,
+                       const rtk_tensor *delta_mu, const rtk_tensor *k_full,
+                       const rtk_tensor *v_full, const rtk_tensor *mask_full,
+                       const rtk_tensor *k_sparse, const rtk_tensor *v_sparse,
+                       int64_t num_kv_groups, const rtk_tensor *out, void *workspace,
+                       size_t workspace_bytes, void *stream) {
+  g_last_error.clear();
+  if (q_full == nullptr || q_full->ndim != 3) return fail(RTK_ERR_INVALID, "q_full must be [B, H_q, D]");
+  if (R_partial == nullptr || R_partial->ndim != 4)
+    return fail(RTK_ERR_INVALID, "R_partial must be [B, H_kv, D, D_keep]");
+  if (mask_full != nullptr && mask_full->dtype != RTK_U8) return fail(RTK_ERR_INVALID, "mask_full must be uint8");
+  const int64_t B = q_full->shape[0], Hq = q_full->shape[1], D = q_full->shape[2];
+  const int64_t Hkv = R_partial->shape[1], DK = R_partial->shape[3];
+  if (num_kv_groups <= 0 || Hq / num_kv_groups != Hkv)
+    return fail(RTK_ERR_INVALID, "R_partial H_kv=%lld but H_q=%lld, num_kv_groups=%lld",
+                (long long)Hkv, (long long)Hq, (long long)num_kv_groups);
+  if (Hq != Hkv * num_kv_groups)
+    return fail(RTK_ERR_INVALID, "H_q=%lld is not H_kv=%lld * num_kv_groups=%lld", (long long)Hq,
+                (long long)Hkv, (long long)num_kv_groups);
+  if (!dtype_ok(q_full->dtype)) return fail(RTK_ERR_INVALID, "q_full dtype must be float32, bfloat16 or float16");
+  if (!same_dims(R_partial, 4, {B, Hkv, D, -1}) || DK < 1 || DK > D)
+    return fail(RTK_ERR_INVALID, "R_partial must be [B, H_kv, D, D_keep]");
+  if (delta_mu != nullptr && !same_dims(delta_mu, 3, {B, Hkv, D}))
+    return fail(RTK_ERR_INVALID, "delta_mu must be [B, H_kv, D]");
+  if (!same_dims(k_full, 4, {B, Hkv, -1, D})) return fail(RTK_ERR_INVALID, "k_full must be [B, H_kv, S_full, D]");
+  const int64_t Sf = k_full->shape[2];
+  if (!same_dims(v_full, 4, {B, Hkv, Sf, D})) return fail(RTK_ERR_INVALID, "v_full must be [B, H_kv, S_full, D]");
+  if (mask_full != nullptr && !same_dims(mask_full, 2, {B, Sf})) return fail(RTK_ERR_INVALID, "mask_full must be [B, S_full]");
+  if (!same_dims(k_sparse, 4, {B, Hkv, -1, DK})) return fail(RTK_ERR_INVALID, "k_sparse must be [B, H_kv, S_sparse, D_keep]");
+  const int64_t Sv = k_sparse->shape[2];
+  if (!same_dims(v_sparse, 4, {B, Hkv, Sv, D})) return fail(RTK_ERR_INVALID, "v_sparse must be [B, H_kv, S_sparse, D]");
+  for (const rtk_tensor *t : {R_partial, k_full, v_full, k_sparse, v_sparse, out})
+    if (t->dtype != q_full->dtype) return fail(RTK_ERR_INVALID, "all tensors but mask_full must share q_full's dtype");
+  if (delta_mu != nullptr && delta_mu->dtype != q_full->dtype)
+    return fail(RTK_ERR_INVALID, "all tensors but mask_full must share q_full's dtype");
+  int64_t os[3];
+  if (!out_view(out, B, Hq, D, os)) return fail(RTK_ERR_INVALID, "out must be [B, H_q, D] or [B, 1, H_q, D]");
+  if (B * Hq == 0 || D == 0) return RTK_OK;
+  DecodeArgs a{q_full, R_partial, delta_mu, k_full, v_full, mask_full, k_sparse, v_sparse, out, num_kv_groups, false};
+  return run_decode(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int rtk_full_channel_decode(const rtk_tensor *q, const rtk_tensor *k, const rtk_tensor *v,
+                            int64_t num_kv_groups, const rtk_tensor *out, void *workspace,
+                            size_t workspace_bytes, void *stream) {
+  g_last_error.clear();
+  if (q == nullptr || q->ndim != 3) return fail(RTK_ERR_INVALID, "q must be [B, H_q, D]");
+  const int64_t B = q->shape[0], Hq = q->shape[1], D = q->shape[2];
+  if (k == nullptr || v == nullptr || k->ndim != 4 || v->ndim != 4)
+    return fail(RTK_ERR_INVALID, "k/v must be [B, H_kv, S, D]");
+  if (k->shape[3] != D || v->shape[3] != D) return fail(RTK_ERR_INVALID, "k/v head_dim must match q's");
+  const int64_t Hkv = k->shape[1], S = k->shape[2];
+  if (!same_dims(k, 4, {B, Hkv, S, D}) || !same_dims(v, 4, {B, Hkv, S, D}))
+    return fail(RTK_ERR_INVALID, "k/v must be [B, H_kv, S, D]");
+  if (num_kv_groups <= 0 || Hq != Hkv * num_kv_groups)
+    return fail(RTK_ERR_INVALID, "H_q=%lld is not H_kv=%lld * num_kv_groups=%lld", (long long)Hq,
+                (long long)Hkv, (long long)num_kv_groups);
+  if (!dtype_ok(q->dtype) || k->dtype != q->dtype || v->dtype != q->dtype)
+    return fail(RTK_ERR_INVALID, "q, k, v and out must share one dtype (float32, bfloat16 or float16)");
+  int64_t os[3];
+  if (!out_view(out, B, Hq, D, os) || out->dtype != q->dtype)
+    return fail(RTK_ERR_INVALID, "out must be [B, H_q, D] or [B, 1, H_q, D] in q's dtype");
+  if (B * Hq == 0 || D == 0) return RTK_OK;
+  DecodeArgs a{q, nullptr, nullptr, k, v, nullptr, nullptr, nullptr, out, num_kv_groups, true};
+  return run_decode(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int rtk_read_status(void *workspace, void *stream, uint32_t *status) {
+  g_last_error.clear();
+  if (workspace == nullptr || status == nullptr) return fail(RTK_ERR_INVALID, "workspace and status must be non-NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t host = 0;
+  cudaError_t e = cudaMemcpyAsync(&host, workspace, sizeof(host), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(workspace, 0, sizeof(host), s);
+  if (e != cudaSuccess) return cuda_fail(e, "rtk_read_status");
+  *status = host;
+  return RTK_OK;
+}
+
+}  // extern "C"

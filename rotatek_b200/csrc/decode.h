@@ -1,0 +1,61 @@
+// Parameters shared by the decode kernels and their host-side launchers.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rtk {
+
+// Tensor-core path (decode_tc.cu).  All strides in elements; the head_dim
+// stride of every tensor is 1 and the D_keep stride of R is 1.
+struct DecodeParams {
+  int batch, q_heads, kv_heads, groups;   // groups = H_q / H_kv
+  int head_dim_keep;
+  int seq_full, seq_sparse;
+  int head_chunks;                        // ceil(groups / heads_tile)
+  int blocks_full, blocks_sparse, blocks_per_unit;
+  long long total_blocks;                 // units * blocks_per_unit
+  float scale_log2;                       // log2(e) / sqrt(head_dim)
+  const void *q;  long long q_sb, q_sh;
+  const void *R;  long long R_sb, R_sh, R_sd;
+  const void *dm; long long dm_sb, dm_sh;                // nullable
+  const uint8_t *mask; long long mask_sb, mask_ss;       // nullable
+  void *out; long long o_sb, o_sh;
+  float *partials; int slot_floats;       // (units + grid) slots
+  int *tickets;                           // one per unit, zero between calls
+  unsigned int *status;                   // RTK_DEVICE_TIMEOUT bits
+};
+
+struct DecodeTensorMaps {
+  CUtensorMap kf, vf, ks, vs;             // [D|Dk, S, H_kv, B] views, 64-token boxes
+};
+
+// heads_tile: 8 or 16 query heads per unit; dk: 16, 32 or 64.
+cudaError_t launch_decode_tc(int dtype_is_bf16, const DecodeTensorMaps &maps,
+                             const DecodeParams &p, int heads_tile, int dk, int grid,
+                             cudaStream_t stream);
+
+// Generic path (decode_simt.cu): any dtype, any strides, head_dim <= 256.
+struct SimtParams {
+  int dtype;                              // rtk_dtype of q / K / V / out
+  int batch, q_heads, kv_heads, groups, head_dim, head_dim_keep;
+  int seq_full, seq_sparse, splits, tokens_per_split;
+  float scale_log2;
+  const void *q;  long long q_s[3];
+  const void *R;  long long R_s[4];
+  const void *dm; long long dm_s[3];      // nullable
+  const uint8_t *mask; long long mask_s[2];  // nullable
+  const void *kf; long long kf_s[4];
+  const void *vf; long long vf_s[4];
+  const void *ks; long long ks_s[4];
+  const void *vs; long long vs_s[4];
+  void *out; long long o_s[3];
+  float *partials; int slot_floats;       // (B * H_q * splits) slots
+  int *tickets;                           // one per (b, query head)
+  unsigned int *status;
+};
+
+cudaError_t launch_decode_simt(const SimtParams &p, cudaStream_t stream);
+
+}  // namespace rtk

@@ -1,0 +1,123 @@
+"""Decode entry points with the reference's signatures.
+
+Mirrors ``rotatek.kernels`` (rotatek/kernels/__init__.py:15-26): the model
+adapters call ``rotatek_decode`` (RotateK) and ``full_channel_decode``
+(Full / ThinK / SparK) by keyword and get the same return conventions and
+ValueErrors.  There is one backend -- the sm_100a kernels of
+librotatek_b200.so -- so ``ROTATEK_KERNEL`` is kept only as an exported name
+(it reports "b200"); setting it to the reference's 'paper' or 'gqa' selects
+the same kernels.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from rotatek_b200 import _lib
+
+ROTATEK_KERNEL = "b200"
+
+_ws_size_cache = {}
+
+
+def _stream(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    return _lib._DTYPES.get(t.dtype, -1)
+
+
+def rotatek_decode(
+    q_full: torch.Tensor,                # [B, H_q, D]
+    R_partial: torch.Tensor,             # [B, H_kv, D, D_keep]
+    delta_mu: Optional[torch.Tensor],    # [B, H_kv, D] or None
+    k_full: torch.Tensor,                # [B, H_kv, S_full, D]
+    v_full: torch.Tensor,                # [B, H_kv, S_full, D]
+    mask_full: Optional[torch.Tensor],   # [B, S_full] uint8
+    k_sparse: torch.Tensor,              # [B, H_kv, S_sparse, D_keep]
+    v_sparse: torch.Tensor,              # [B, H_kv, S_sparse, D]
+    num_kv_groups: int,
+) -> Tuple[torch.Tensor, None, None]:
+    """RotateK decode of one query token; returns (out [B, 1, H_q, D], None, None).
+
+    Same contract as ``rotatek_decode_fused_triton``
+    (rotatek/kernels/fused_decode.py:303-420): visual logits use the rotated
+    query q.R and the q.delta_mu bias, prompt/text logits the full query, both
+    spans share one softmax, tokens with mask_full == 0 are skipped, and the
+    output is acc / (l + 1e-6) in q's dtype.  Unlike the reference the output
+    is a fresh tensor, never an alias of a cached buffer.  Inputs may be strided
+    views (e.g. the adapters' ``value_states[:, :, s_p:s_p + s_v]``); nothing is
+    copied.
+    """
+    if q_full.dim() != 3:
+        raise ValueError("q_full must be [B, H_q, D]")
+    if R_partial.dim() != 4:
+        raise ValueError("R_partial must be [B, H_kv, D, D_keep]")
+    if mask_full is not None and mask_full.dtype != torch.uint8:
+        raise ValueError("mask_full must be uint8")
+    bsz, heads, head_dim = q_full.shape
+    h_kv = R_partial.shape[1]
+    if num_kv_groups <= 0 or heads // num_kv_groups != h_kv:
+        raise ValueError(
+            f"R_partial H_kv={h_kv} but H_q={heads}, num_kv_groups={num_kv_groups}")
+    if heads != h_kv * num_kv_groups:
+        # the reference's floor-division check lets this through and then reads
+        # past the last KV head (fused_decode.py:124, 335)
+        raise ValueError(f"H_q={heads} is not H_kv={h_kv} * num_kv_groups={num_kv_groups}")
+    _lib.require_cuda(q_full, R_partial, delta_mu, k_full, v_full, mask_full, k_sparse, v_sparse)
+    lib = _lib.load()
+    dev = q_full.device
+    key = ("rk", _dtype_code(q_full), bsz, heads, h_kv, head_dim, R_partial.shape[-1],
+           k_full.shape[-2], k_sparse.shape[-2], dev.index)
+    need = _ws_size_cache.get(key)
+    if need is None:
+        need = lib.rtk_rotatek_decode_workspace_size(*key[1:-1], dev.index)
+        _ws_size_cache[key] = need
+    ws = _lib.workspace(dev, need)
+    out = torch.empty((bsz, 1, heads, head_dim), dtype=q_full.dtype, device=dev)
+    D = _lib.describe
+    _lib.check(lib.rtk_rotatek_decode(
+        D(q_full), D(R_partial), D(delta_mu), D(k_full), D(v_full), D(mask_full), D(k_sparse),
+        D(v_sparse), num_kv_groups, D(out), ctypes.c_void_p(ws.data_ptr()), ws.numel(),
+        _stream(dev)))
+    return out, None, None
+
+
+def full_channel_decode(
+    q: torch.Tensor,                   # [B, H_q, D]
+    k: torch.Tensor,                   # [B, H_kv, S, D]
+    v: torch.Tensor,                   # [B, H_kv, S, D]
+    num_kv_groups: int = 1,
+) -> torch.Tensor:
+    """Full-channel split-K decode of one query token; returns [B, 1, H_q, D].
+
+    Same contract as ``full_channel_decode_triton``
+    (rotatek/kernels/full_channel_flash_decoding.py:162-229) without its
+    ``.contiguous()`` copies: strided k / v are read in place.
+    """
+    if q.dim() != 3:
+        raise ValueError("q must be [B, H_q, D]")
+    bsz, heads, head_dim = q.shape
+    if k.shape[-1] != head_dim or v.shape[-1] != head_dim:
+        raise ValueError("k/v head_dim must match q's")
+    _lib.require_cuda(q, k, v)
+    lib = _lib.load()
+    dev = q.device
+    key = ("fc", _dtype_code(q), bsz, heads, k.shape[1], head_dim, k.shape[-2], dev.index)
+    need = _ws_size_cache.get(key)
+    if need is None:
+        need = lib.rtk_full_channel_decode_workspace_size(*key[1:-1], dev.index)
+        _ws_size_cache[key] = need
+    ws = _lib.workspace(dev, need)
+    out = torch.empty((bsz, 1, heads, head_dim), dtype=q.dtype, device=dev)
+    D = _lib.describe
+    _lib.check(lib.rtk_full_channel_decode(
+        D(q), D(k), D(v), num_kv_groups, D(out), ctypes.c_void_p(ws.data_ptr()), ws.numel(),
+        _stream(dev)))
+    return out
+
+
+__all__ = ["ROTATEK_KERNEL", "rotatek_decode", "full_channel_decode"]

@@ -1,0 +1,101 @@
+"""The C-ABI library without a GPU: it loads, exports every function the
+header declares, and rejects bad arguments with the reference's messages
+before touching the device."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from rotatek_b200 import _lib
+from rotatek_b200.kernels import full_channel_decode, rotatek_decode
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                      "rotatek_b200.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(_lib.LIB_PATH):
+        from rotatek_b200.csrc import build
+        build.build()
+    return _lib.load()
+
+
+def header_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(rtk_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_symbols_exported(lib):
+    names = header_functions()
+    assert "rtk_rotatek_decode" in names and "rtk_full_channel_decode" in names
+    for name in names:
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_abi_version(lib):
+    assert lib.rtk_abi_version() == 1
+
+
+def _fake(shape, dtype=1, data=0x1000):
+    d = _lib.RtkTensor()
+    d.data = data
+    d.dtype = dtype
+    d.ndim = len(shape)
+    stride = 1
+    for i in reversed(range(len(shape))):
+        d.shape[i] = shape[i]
+        d.stride[i] = stride
+        stride *= shape[i]
+    return ctypes.byref(d)
+
+
+def test_c_validation_messages(lib):
+    q, R, dm = _fake((2, 8, 128)), _fake((2, 2, 128, 32)), _fake((2, 2, 128))
+    kf, vf, mask = _fake((2, 2, 10, 128)), _fake((2, 2, 10, 128)), _fake((2, 10), dtype=3)
+    ks, vs, out = _fake((2, 2, 50, 32)), _fake((2, 2, 50, 128)), _fake((2, 1, 8, 128))
+
+    def call(**kw):
+        a = dict(q=q, R=R, dm=dm, kf=kf, vf=vf, mask=mask, ks=ks, vs=vs, g=4, out=out)
+        a.update(kw)
+        code = lib.rtk_rotatek_decode(a["q"], a["R"], a["dm"], a["kf"], a["vf"], a["mask"],
+                                      a["ks"], a["vs"], a["g"], a["out"], None, 0, None)
+        return code, lib.rtk_last_error().decode()
+
+    assert call(q=_fake((8, 128))) == (1, "q_full must be [B, H_q, D]")
+    assert call(R=_fake((2, 128, 32))) == (1, "R_partial must be [B, H_kv, D, D_keep]")
+    assert call(mask=_fake((2, 10), dtype=1)) == (1, "mask_full must be uint8")
+    assert call(g=2) == (1, "R_partial H_kv=2 but H_q=8, num_kv_groups=2")
+    assert call(vs=_fake((2, 2, 49, 128)))[1] == "v_sparse must be [B, H_kv, S_sparse, D]"
+    assert call(out=_fake((2, 8, 64)))[1] == "out must be [B, H_q, D] or [B, 1, H_q, D]"
+    code, msg = call()                      # valid shapes, but no workspace
+    assert code == _lib.RTK_ERR_WORKSPACE or code == _lib.RTK_ERR_CUDA, (code, msg)
+    code = lib.rtk_full_channel_decode(_fake((2, 8, 128)), _fake((2, 2, 10, 64)),
+                                       _fake((2, 2, 10, 128)), 4, out, None, 0, None)
+    assert (code, lib.rtk_last_error().decode()) == (1, "k/v head_dim must match q's")
+
+
+def test_python_errors_match_reference_and_no_cpu_fallback():
+    q = torch.zeros(2, 8, 128)
+    R = torch.zeros(2, 2, 128, 32)
+    kf = torch.zeros(2, 2, 10, 128)
+    mask = torch.ones(2, 10, dtype=torch.uint8)
+    ks, vs = torch.zeros(2, 2, 50, 32), torch.zeros(2, 2, 50, 128)
+    kw = dict(q_full=q, R_partial=R, delta_mu=None, k_full=kf, v_full=kf, mask_full=mask,
+              k_sparse=ks, v_sparse=vs, num_kv_groups=4)
+    with pytest.raises(ValueError, match=r"q_full must be \[B, H_q, D\]"):
+        rotatek_decode(**{**kw, "q_full": q[0]})
+    with pytest.raises(ValueError, match="mask_full must be uint8"):
+        rotatek_decode(**{**kw, "mask_full": mask.float()})
+    with pytest.raises(ValueError, match="R_partial H_kv=2 but H_q=8, num_kv_groups=2"):
+        rotatek_decode(**{**kw, "num_kv_groups": 2})
+    with pytest.raises(ValueError, match=r"H_q=8 is not H_kv=2 \* num_kv_groups=3"):
+        rotatek_decode(**{**kw, "num_kv_groups": 3})
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        rotatek_decode(**kw)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        full_channel_decode(q, kf, kf, 4)

@@ -1,0 +1,225 @@
+"""Decode parity on the GPU: rotatek_b200.kernels vs the float64 oracle.
+
+Tolerances (written out per dtype):
+  fp32  1e-5 absolute + 1e-5 relative  (the reference itself sits ~1e-5 from
+        the float64 closed form at logits of magnitude ~50)
+  bf16  2e-3 absolute + 2^-8 relative  (the output is stored in bf16: half an
+        ulp is 2^-9 relative, so outputs above 0.5 need the relative term)
+  fp16  1e-3 absolute + 2^-10 relative
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import decode as odec
+from rotatek_b200 import _lib, synthetic as syn
+from rotatek_b200.kernels import full_channel_decode, rotatek_decode
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: (1e-5, 1e-5), torch.bfloat16: (2e-3, 2.0 ** -8),
+       torch.float16: (1e-3, 2.0 ** -10)}
+DEV = "cuda"
+
+
+def _t(x, dtype):
+    return torch.as_tensor(np.asarray(x, dtype=np.float32)).to(DEV).to(dtype)
+
+
+def check(out, want, dtype):
+    atol, rtol = TOL[dtype]
+    got = out.float().cpu().numpy()
+    err = np.abs(got - want)
+    bound = atol + rtol * np.abs(want)
+    assert np.all(err <= bound), f"max err {err.max():.3e} (worst excess {(err - bound).max():.3e})"
+
+
+def assert_status_clean():
+    assert _lib.read_status() == 0
+
+
+@pytest.mark.parametrize("case", ["cfg1_fp32", "small_bf16"])
+def test_golden_prefill_cases(golden, case):
+    g = golden(case)
+    dtype = {"float32": torch.float32, "bfloat16": torch.bfloat16}[g["dtype"]]
+    p, v = g["prompt_len"], g["vision_len"]
+    keys, values = _t(g["keys"], dtype), _t(g["values"], dtype)
+    k_full = torch.cat([keys[:, :, :p], keys[:, :, p + v:]], dim=2)
+    v_full = torch.cat([values[:, :, :p], values[:, :, p + v:]], dim=2)
+    mask = torch.ones(k_full.shape[0], k_full.shape[2], dtype=torch.uint8, device=DEV)
+    args = dict(q_full=_t(g["q_decode"], dtype), R_partial=_t(g["R_partial"], dtype),
+                delta_mu=_t(g["delta_mu"], dtype), k_full=k_full, v_full=v_full, mask_full=mask,
+                k_sparse=_t(g["kept"], dtype), v_sparse=values[:, :, p:p + v],
+                num_kv_groups=g["num_kv_groups"])
+    out, a, b = rotatek_decode(**args)
+    assert a is None and b is None and out.shape == (keys.shape[0], 1, args["q_full"].shape[1], 128)
+    want = odec.rotatek_decode(**{k: (x.cpu() if torch.is_tensor(x) else x) for k, x in args.items()})
+    check(out, want, dtype)
+    dense = full_channel_decode(args["q_full"], keys, values, num_kv_groups=g["num_kv_groups"])
+    check(dense, odec.full_channel_decode(args["q_full"].cpu(), keys.cpu(), values.cpu(),
+                                          g["num_kv_groups"]), dtype)
+    assert_status_clean()
+
+
+@pytest.mark.parametrize("case", ["dec_mask_nobias_fp32", "dec_empty_visual_fp32",
+                                  "dec_empty_full_fp32", "dec_g7_bf16"])
+def test_golden_decode_edge_cases(golden, case):
+    g = golden(case)
+    dtype = {"float32": torch.float32, "bfloat16": torch.bfloat16}[g["dtype"]]
+    args = dict(q_full=_t(g["q_full"], dtype), R_partial=_t(g["R_partial"], dtype),
+                delta_mu=_t(g["delta_mu"], dtype) if g["has_bias"] else None,
+                k_full=_t(g["k_full"], dtype), v_full=_t(g["v_full"], dtype),
+                mask_full=torch.as_tensor(g["mask_full"]).to(DEV),
+                k_sparse=_t(g["k_sparse"], dtype), v_sparse=_t(g["v_sparse"], dtype),
+                num_kv_groups=g["num_kv_groups"])
+    out, _, _ = rotatek_decode(**args)
+    want = odec.rotatek_decode(**{k: (x.cpu() if torch.is_tensor(x) else x) for k, x in args.items()})
+    check(out, want, dtype)
+    assert_status_clean()
+
+
+def make(dtype, B, Hq, Hkv, Sv, Sf, keep=32, seed=0, bias=True):
+    return syn.make_decode(B, Hq, Hkv, Sv, Sf, keep=keep, seed=seed, device=DEV, dtype=dtype,
+                           with_bias=bias)
+
+
+def run_and_check(d, dtype, mask=None):
+    kw = d.as_kwargs()
+    if mask is not None:
+        kw["mask_full"] = mask
+    out, _, _ = rotatek_decode(**kw)
+    want = odec.rotatek_decode(**{k: (x.cpu() if torch.is_tensor(x) else x) for k, x in kw.items()})
+    check(out, want, dtype)
+    return out
+
+
+# (dtype, B, H_q, H_kv, S_v, S_f, keep): tensor-core path shapes (bf16/fp16, D=128,
+# keep in {16,32,64}) across group sizes 1..20, ragged spans, and generic-path shapes
+SHAPES = [
+    (torch.bfloat16, 2, 28, 4, 1000, 100, 32),     # G=7, the headline group
+    (torch.bfloat16, 1, 8, 8, 777, 13, 32),        # G=1 (MHA)
+    (torch.bfloat16, 3, 8, 2, 4096, 640, 16),      # G=4, keep 16
+    (torch.bfloat16, 2, 16, 2, 130, 65, 64),       # G=8, keep 64
+    (torch.bfloat16, 1, 12, 1, 300, 40, 32),       # G=12 -> 16-head tile
+    (torch.bfloat16, 1, 40, 2, 200, 70, 32),       # G=20 -> two head chunks
+    (torch.float16, 2, 28, 4, 1500, 200, 32),      # fp16
+    (torch.bfloat16, 1, 4, 2, 1, 1, 32),           # one token per span
+    (torch.bfloat16, 2, 8, 2, 64, 64, 32),         # exact block multiples
+    (torch.bfloat16, 1, 8, 2, 300, 50, 48),        # keep 48 -> generic kernel
+    (torch.float32, 2, 8, 2, 576, 96, 32),         # fp32 -> generic kernel
+]
+
+
+@pytest.mark.parametrize("dtype,B,Hq,Hkv,Sv,Sf,keep", SHAPES)
+def test_decode_shapes(dtype, B, Hq, Hkv, Sv, Sf, keep):
+    d = make(dtype, B, Hq, Hkv, Sv, Sf, keep=keep, seed=B * 100 + Hq)
+    run_and_check(d, dtype)
+    assert_status_clean()
+
+
+def test_decode_mask_and_no_bias():
+    d = make(torch.bfloat16, 2, 28, 4, 700, 333, seed=5, bias=False)
+    g = torch.Generator(device=DEV).manual_seed(3)
+    mask = (torch.rand(2, 333, generator=g, device=DEV) < 0.4).to(torch.uint8)
+    run_and_check(d, torch.bfloat16, mask=mask)
+    mask.zero_()                                   # every prompt/text token masked
+    run_and_check(d, torch.bfloat16, mask=mask)
+
+
+def test_decode_empty_spans():
+    for sv, sf in [(0, 50), (90, 0), (0, 0)]:
+        d = make(torch.bfloat16, 2, 8, 2, sv, sf, seed=sv + sf)
+        out = run_and_check(d, torch.bfloat16)
+        if sv == 0 and sf == 0:
+            assert torch.count_nonzero(out) == 0
+
+
+def test_decode_strided_views():
+    """The adapters pass v_sparse as a slice of the whole V cache and cat'ed k/v_full."""
+    B, Hq, Hkv, Sp, Sv, St = 2, 28, 4, 64, 1200, 100
+    dtype = torch.bfloat16
+    d = make(dtype, B, Hq, Hkv, Sv, Sp + St, seed=9)
+    v_cache = syn.normal((B, Hkv, Sp + Sv + St, 128), 11, DEV, dtype)
+    kw = d.as_kwargs()
+    kw["v_sparse"] = v_cache[:, :, Sp:Sp + Sv]
+    kw["v_full"] = torch.cat([v_cache[:, :, :Sp], v_cache[:, :, Sp + Sv:]], dim=2)
+    assert not kw["v_sparse"].is_contiguous()
+    out, _, _ = rotatek_decode(**kw)
+    want = odec.rotatek_decode(**{k: (x.cpu() if torch.is_tensor(x) else x) for k, x in kw.items()})
+    check(out, want, dtype)
+    # head-major Keys stored [B, S, H, D] and viewed as [B, H, S, D]
+    ks = d.k_sparse.transpose(1, 2).contiguous().transpose(1, 2)
+    kw["k_sparse"] = ks
+    out2, _, _ = rotatek_decode(**kw)
+    check(out2, want, dtype)
+
+
+def test_decode_config2_full_size():
+    """BASELINE config 2 at full size: B=32, 28/4 heads, 64+15360+576, keep 32, bf16."""
+    d = make(torch.bfloat16, 32, 28, 4, 15360, 640, seed=2024)
+    out, _, _ = rotatek_decode(**d.as_kwargs())
+    want = odec.rotatek_decode(**{k: (x.cpu() if torch.is_tensor(x) else x)
+                                  for k, x in d.as_kwargs().items()})
+    got = out.float().cpu().numpy()
+    assert np.abs(got - want).max() <= 2e-3          # the north-star bar, max-abs
+    check(out, want, torch.bfloat16)
+    assert_status_clean()
+
+
+def test_repeat_calls_identical():
+    """Ticket counters return to zero: a second call gives the same bits."""
+    d = make(torch.bfloat16, 4, 28, 4, 3000, 200, seed=17)
+    a, _, _ = rotatek_decode(**d.as_kwargs())
+    b, _, _ = rotatek_decode(**d.as_kwargs())
+    torch.testing.assert_close(a, b, rtol=0, atol=0)
+
+
+def test_full_channel_decode_shapes():
+    for dtype, B, Hq, Hkv, S in [(torch.bfloat16, 2, 28, 4, 16000), (torch.bfloat16, 1, 8, 8, 99),
+                                 (torch.float16, 3, 32, 8, 1000), (torch.float32, 1, 4, 2, 500)]:
+        q = syn.normal((B, Hq, 128), 1, DEV, dtype)
+        k = syn.lowrank_keys(B, Hkv, S, seed=2, device=DEV, dtype=dtype)
+        v = syn.normal((B, Hkv, S, 128), 3, DEV, dtype)
+        out = full_channel_decode(q, k, v, num_kv_groups=Hq // Hkv)
+        check(out, odec.full_channel_decode(q.cpu(), k.cpu(), v.cpu(), Hq // Hkv), dtype)
+
+
+def test_cuda_graph_capture_and_replay():
+    """graph_bench.py:27-44 captures the decode call; the replayed graph must match eager."""
+    d = make(torch.bfloat16, 4, 28, 4, 2000, 100, seed=21)
+    kw = d.as_kwargs()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            eager, _, _ = rotatek_decode(**kw)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        captured, _, _ = rotatek_decode(**kw)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(captured, eager, rtol=0, atol=0)
+
+
+def test_reference_value_errors():
+    d = make(torch.bfloat16, 1, 8, 2, 64, 8, seed=1)
+    kw = d.as_kwargs()
+    with pytest.raises(ValueError, match=r"q_full must be \[B, H_q, D\]"):
+        rotatek_decode(**{**kw, "q_full": kw["q_full"][0]})
+    with pytest.raises(ValueError, match="R_partial must be"):
+        rotatek_decode(**{**kw, "R_partial": kw["R_partial"][0]})
+    with pytest.raises(ValueError, match="mask_full must be uint8"):
+        rotatek_decode(**{**kw, "mask_full": kw["mask_full"].bool()})
+    with pytest.raises(ValueError, match="R_partial H_kv=2 but H_q=8, num_kv_groups=2"):
+        rotatek_decode(**{**kw, "num_kv_groups": 2})
+    with pytest.raises(ValueError, match="k_sparse must be"):
+        rotatek_decode(**{**kw, "k_sparse": kw["k_sparse"][:, :1]})
+    with pytest.raises(ValueError, match=r"q must be \[B, H_q, D\]"):
+        full_channel_decode(kw["q_full"][0], kw["k_full"], kw["v_full"], 4)
+    with pytest.raises(ValueError, match="head_dim must match"):
+        full_channel_decode(kw["q_full"], kw["k_full"][..., :64], kw["v_full"], 4)
