@@ -38,7 +38,9 @@ int cuda_fail(cudaError_t e, const char *what) {
 }
 
 constexpr size_t kAlign = 256;
-constexpr int kBlockTokens = 64;
+constexpr int kBlockTokens = 64;      // generic-kernel split granularity
+constexpr int kVisBlockTokens = 64;   // tensor-core kernel: visual block
+constexpr int kFullBlockTokens = 32;  // tensor-core kernel: prompt/text block
 
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
@@ -114,11 +116,11 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// [B, H, S, inner] 16-bit tensor -> 4-D map with a {box_inner, 64, 1, 1} box.
+// [B, H, S, inner] 16-bit tensor -> 4-D map with a {box_inner, box_rows, 1, 1} box.
 // Returns false when TMA cannot describe the layout (the caller then uses the
 // generic kernel).  Size-1 dimensions get a canonical stride.
 bool encode_map(CUtensorMap *map, const View4 &v, CUtensorMapDataType dt, int box_inner,
-                CUtensorMapSwizzle sw) {
+                int box_rows, CUtensorMapSwizzle sw) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return false;
   if (v.s[3] != 1) return false;
@@ -137,7 +139,7 @@ bool encode_map(CUtensorMap *map, const View4 &v, CUtensorMapDataType dt, int bo
   }
   for (int i = 0; i < 4; ++i)
     if (dims[i] == 0 || dims[i] > (1ull << 31)) return false;
-  cuuint32_t box[4] = {(cuuint32_t)box_inner, (cuuint32_t)kBlockTokens, 1, 1};
+  cuuint32_t box[4] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estride[4] = {1, 1, 1, 1};
   return fn(map, dt, 4, const_cast<void *>(v.data), dims, strides, box, estride,
             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -168,6 +170,7 @@ struct TcShape {
   int64_t units, blocks_full, blocks_sparse, blocks_per_unit, total;
   int grid;
   int slot_floats;
+  int64_t slots;  // one per (unit + cta, consumer warp); <= 5 consumer warps per CTA
 };
 
 TcShape tc_shape(int64_t B, int64_t Hkv, int64_t G, int64_t Sf, int64_t Sv, int device) {
@@ -175,12 +178,13 @@ TcShape tc_shape(int64_t B, int64_t Hkv, int64_t G, int64_t Sf, int64_t Sv, int 
   t.heads_tile = G <= 8 ? 8 : 16;
   t.head_chunks = (int)cdiv(G, t.heads_tile);
   t.units = B * Hkv * t.head_chunks;
-  t.blocks_full = cdiv(Sf, kBlockTokens);
-  t.blocks_sparse = cdiv(Sv, kBlockTokens);
+  t.blocks_full = cdiv(Sf, kFullBlockTokens);
+  t.blocks_sparse = cdiv(Sv, kVisBlockTokens);
   t.blocks_per_unit = t.blocks_full + t.blocks_sparse;
   t.total = t.units * t.blocks_per_unit;
   t.grid = (int)std::max<int64_t>(1, std::min<int64_t>(t.total, sm_count(device)));
   t.slot_floats = 32 + 16 * 128;
+  t.slots = (t.units + t.grid) * 5;
   return t;
 }
 
@@ -204,7 +208,7 @@ size_t decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int
                               int64_t Sv, int device) {
   const int64_t G = Hkv > 0 ? Hq / Hkv : 1;
   const TcShape t = tc_shape(B, Hkv, std::max<int64_t>(G, 1), Sf, Sv, device);
-  const size_t tc = plan_workspace(t.units, t.units + t.grid, t.slot_floats).bytes;
+  const size_t tc = plan_workspace(t.units, t.slots, t.slot_floats).bytes;
   const SimtShape s = simt_shape(B, Hq, D, Sf + Sv, device);
   const size_t simt = plan_workspace(s.units, s.units * s.splits, s.slot_floats).bytes;
   return std::max(tc, simt);
@@ -259,15 +263,15 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
     const CUtensorMapDataType et =
         dt == RTK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     if (Sf > 0)
-      tc = encode_map(&maps.kf, kf, et, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
-           encode_map(&maps.vf, vf, et, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+      tc = encode_map(&maps.kf, kf, et, 64, kFullBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B) &&
+           encode_map(&maps.vf, vf, et, 64, kFullBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B);
     if (tc && Sv > 0)
-      tc = encode_map(&maps.ks, ks, et, (int)DK, swizzle_for_row_bytes((int)DK * 2)) &&
-           encode_map(&maps.vs, vs, et, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+      tc = encode_map(&maps.ks, ks, et, (int)DK, kVisBlockTokens, swizzle_for_row_bytes((int)DK * 2)) &&
+           encode_map(&maps.vs, vs, et, 64, kVisBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B);
   }
   if (tc) {
     const TcShape t = tc_shape(B, Hkv, G, Sf, Sv, device);
-    const WorkspacePlan w = plan_workspace(t.units, t.units + t.grid, t.slot_floats);
+    const WorkspacePlan w = plan_workspace(t.units, t.slots, t.slot_floats);
     rtk::DecodeParams p;
     std::memset(&p, 0, sizeof(p));
     p.batch = (int)B; p.q_heads = (int)Hq; p.kv_heads = (int)Hkv; p.groups = (int)G;

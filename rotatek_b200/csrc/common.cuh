@@ -68,12 +68,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
                                                   volatile int *abort, unsigned int *status) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
+  // the clock is read only after many unsuccessful polls, so ordinary waits
+  // never pay for it; the limit counts from that first reading
+  unsigned long long t0 = 0;
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0) {
+    if ((it & 1023u) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      const unsigned long long now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
         *abort = 1;
         atomicOr(status, 1u);
         return false;
@@ -97,6 +102,20 @@ __device__ __forceinline__ void tma_load_4d(void *smem_dst, const CUtensorMap *m
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
       "r"(smem_u32(bar))
       : "memory");
+}
+
+// 16-byte global -> shared copy that bypasses registers (both addresses 16-B aligned).
+__device__ __forceinline__ void cp_async_16(void *smem_dst, const void *gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+__device__ __forceinline__ void prefetch_l2(const void *ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
 }
 
 // ---------------------------------------------------------------- sync

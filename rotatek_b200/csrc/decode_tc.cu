@@ -10,58 +10,74 @@
 //   unit   = (batch, KV head, head chunk of <= 8*NT query heads); every query
 //            head of a GQA group shares each K/V tile, so K/V bytes are read
 //            once per group, not once per query head.
-//   block  = 64 tokens of one unit: first the ceil(S_f/64) full-width blocks,
-//            then the ceil(S_v/64) visual blocks.
+//   block  = 32 prompt/text tokens or 64 visual tokens of one unit: first the
+//            ceil(S_f/32) full-width blocks, then the ceil(S_v/64) visual ones.
 //   The U * blocks_per_unit blocks are cut into `grid` equal contiguous ranges,
-//   one per CTA (one CTA per SM).  A CTA walks its range as segments (maximal
-//   runs inside one unit); a segment that covers a whole unit writes the
-//   output directly, otherwise it writes a partial (m, l, acc) to slot
-//   unit + cta of the workspace and takes a ticket; the last CTA of a unit
-//   merges that unit's partials and writes the output.  No CTA ever waits on
-//   another.
+//   one per CTA (one CTA per SM).  Inside a CTA, block i goes to consumer warp
+//   i % W and ring stage i % S (S a multiple of W: every stage belongs to one
+//   warp, so its parity waits are exact).
 //
-// Inside a CTA: warp 4*NGROUP is the producer -- it streams each block's K and
-// V tiles with 4-D TMA tensor copies (128B/64B/32B swizzle) into an NSTAGE
-// ring.  Consumer warps come in NGROUP groups of 4; group g takes the blocks
-// i = g (mod NGROUP) and each of its warps owns 16 of the 64 tokens.  Scores
-// are S^T[16 tokens x 8 heads] = K[16 x d] . Q^T on mma.m16n8k16 (bf16 in,
-// fp32 accumulate); the rotated query q~ = q.R is built in fp32 once per
-// segment and fed to the tensor cores as a bf16 hi/lo pair, so visual scores
-// keep ~16 mantissa bits of q~.  Probabilities go to bf16 (fp16) through
-// movmatrix and accumulate O^T[128 d x 8 heads] += V^T . P^T in fp32 registers.
+// Warps: one producer, W consumers, no CTA-wide barrier after the prologue.
+//   producer  streams each block's K and V tiles with 4-D TMA tensor copies
+//             (128B/64B/32B swizzle, no multicast) into a ring of ~20 KB stages
+//             sized to fill shared memory (10 stages = 200 KB in flight per SM
+//             at D_keep <= 32); at every unit change its lanes also copy the
+//             unit's query rows, R, delta_mu and mask row into a double-buffered
+//             header.
+//   consumer  builds its own query fragments from the header -- q~^T = R^T q^T
+//             on the tensor cores, split into a 16-bit hi + lo pair -- then for
+//             each of its blocks
+//               S^T[tokens x 8 heads] = K[tokens x d] . Q^T      (mma.m16n8k16)
+//               O^T[128 d x 8 heads] += V^T . P^T               (fp32 registers)
+//             with P split hi + lo and moved into B fragments by movmatrix, and
+//             the running-max rescale only when a max grows.  At the end of a
+//             unit it stores its partial (m, l, acc) to its own workspace slot
+//             and takes a ticket; the warp that completes the unit's count
+//             merges all of the unit's partials in slot order (deterministic)
+//             and writes the output.  No warp waits on another warp's merge.
 #include "common.cuh"
 #include "decode.h"
 
 namespace rtk {
 namespace {
 
-constexpr int kBlockTokens = 64;
+constexpr int kVisTokens = 64;           // tokens per visual block
+constexpr int kFullTokens = 32;          // tokens per prompt/text block
 constexpr int kHeadDim = 128;
-constexpr int kStages = 5;
-constexpr int kStageBytes = 32768;        // K region 16 KB + V region 16 KB
-constexpr int kKRegion = 16384;
-constexpr int kWarpsPerGroup = 4;
-constexpr float kNegBig = -1e30f;         // running-max floor (fused_decode.py:151)
+constexpr int kFullBoxBytes = kFullTokens * 128;  // one {64 d x 32 tokens} box
+constexpr int kVisBoxBytes = kVisTokens * 128;    // one {64 d x 64 tokens} box
+constexpr int kSmemBudget = 232448;      // 227 KB opt-in per CTA
+constexpr float kNegBig = -1e30f;        // running-max floor (fused_decode.py:151)
 
-template <int NT, int NGROUP>
-struct SmemLayout {
+template <int NT, int DK>
+struct Cfg {
   static constexpr int kHeads = 8 * NT;
-  static constexpr int kConsumerWarps = kWarpsPerGroup * NGROUP;
-  static constexpr int kAccStride = kHeadDim + 4;  // padding keeps red.shared conflict-free
-  static constexpr int kStagesOff = 0;
-  static constexpr int kQOff = kStages * kStageBytes;                        // fp32 [H][128]
-  static constexpr int kQRotOff = kQOff + kHeads * kHeadDim * 4;             // fp32 [H][64]
-  static constexpr int kBiasOff = kQRotOff + kHeads * 64 * 4;                // fp32 [H]
-  static constexpr int kAccOff = kBiasOff + kHeads * 4;                      // fp32 [H][132]
-  static constexpr int kMwOff = kAccOff + kHeads * kAccStride * 4;           // fp32 [W][H]
-  static constexpr int kLwOff = kMwOff + kConsumerWarps * kHeads * 4;        // fp32 [W][H]
-  static constexpr int kBarOff = (kLwOff + kConsumerWarps * kHeads * 4 + 15) & ~15;
-  static constexpr int kFlagOff = kBarOff + 2 * kStages * 8;
-  static constexpr int kBytes = kFlagOff + 16;
-};
-
-struct Seg {
-  int unit, b, kvh, hc, head0, nheads;
+  static constexpr int kWarps = (NT == 1 && DK <= 32) ? 5 : 4;   // consumer warps
+  static constexpr int kThreads = (kWarps + 1) * 32;             // + producer warp
+  static_assert(kWarps <= 5, "the host sizes the workspace for at most 5 partial slots per CTA");
+  static constexpr int kKsBytes = kVisTokens * DK * 2;           // visual Keys of a block
+  static constexpr int kStageBytes = (kKsBytes + 2 * kVisBoxBytes + 1023) / 1024 * 1024;
+  static_assert(kStageBytes >= 4 * kFullBoxBytes, "a stage must hold a prompt/text block");
+  // per-unit header: q rows [H][128], R [128][DK], delta_mu [128] (16-bit), mask bytes
+  static constexpr int kHdrQ = 0;
+  static constexpr int kHdrR = kHdrQ + kHeads * kHeadDim * 2;
+  static constexpr int kHdrDm = kHdrR + kHeadDim * DK * 2;
+  static constexpr int kHdrMask = kHdrDm + kHeadDim * 2;
+  static constexpr int kHdrMaskBytes = 1024;  // prompt/text masks up to this length live here
+  static constexpr int kHdrBytes = (kHdrMask + kHdrMaskBytes + 127) / 128 * 128;
+  static constexpr int kHdrBufs = DK == 64 ? 1 : 2;
+  static constexpr int kMaxStages = 16;
+  // barriers: full[16], empty[16], hdr_full[2], hdr_empty[2]; then flags
+  static constexpr int kBarOff = 0;
+  static constexpr int kFlagOff = kBarOff + (2 * kMaxStages + 4) * 8;
+  static constexpr int kHdrOff = 1024;
+  static constexpr int kRingOff = (kHdrOff + kHdrBufs * kHdrBytes + 1023) / 1024 * 1024;
+  // as many stages as fit, rounded down to a multiple of the consumer warps so
+  // that every stage belongs to exactly one warp (its parity waits are exact)
+  static constexpr int kStages0 = (kSmemBudget - 1024 - kRingOff) / kStageBytes;
+  static constexpr int kStages = (kStages0 < kMaxStages ? kStages0 : kMaxStages) / kWarps * kWarps;
+  static_assert(kStages >= kWarps, "ring too small");
+  static constexpr int kBytes = kRingOff + kStages * kStageBytes;
 };
 
 __device__ __forceinline__ long long cta_of_block(long long blk, long long total, int grid) {
@@ -69,29 +85,187 @@ __device__ __forceinline__ long long cta_of_block(long long blk, long long total
   return ((blk + 1) * grid - 1) / total;
 }
 
-template <typename T, int NT, int DK, int NGROUP>
-__global__ void __launch_bounds__((kWarpsPerGroup * NGROUP + 1) * 32, 1)
+// Online softmax over MT 16-token tiles of scores already in log2 units,
+// then O^T += V^T . P^T with P split hi + lo.  `valid[mt][r]` masks row g8 + 8r
+// of tile mt.  V tile: rows = tokens, two 64-d boxes `vbox` bytes apart.
+template <typename T, int NT, int MT>
+__device__ __forceinline__ void softmax_pv(float (&s)[MT][NT][4], const bool (&valid)[MT][2],
+                                           float (&m_run)[NT][2], float (&l_run)[NT][2],
+                                           float (&o)[8][NT][4], uint32_t vbase, uint32_t vbox,
+                                           int lane) {
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      if (!valid[mt][0]) s[mt][nt][0] = s[mt][nt][1] = -INFINITY;
+      if (!valid[mt][1]) s[mt][nt][2] = s[mt][nt][3] = -INFINITY;
+    }
+  }
+  bool grow = false;
+  float mnew[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      float mx = fmaxf(s[0][nt][c], s[0][nt][c + 2]);
+#pragma unroll
+      for (int mt = 1; mt < MT; ++mt) mx = fmaxf(mx, fmaxf(s[mt][nt][c], s[mt][nt][c + 2]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      mnew[nt][c] = fmaxf(m_run[nt][c], mx);
+      grow |= mnew[nt][c] > m_run[nt][c];
+    }
+  }
+  if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const float a0 = fast_exp2(m_run[nt][0] - mnew[nt][0]);
+      const float a1 = fast_exp2(m_run[nt][1] - mnew[nt][1]);
+      l_run[nt][0] *= a0;
+      l_run[nt][1] *= a1;
+#pragma unroll
+      for (int d = 0; d < 8; ++d) {
+        o[d][nt][0] *= a0;
+        o[d][nt][1] *= a1;
+        o[d][nt][2] *= a0;
+        o[d][nt][3] *= a1;
+      }
+      m_run[nt][0] = mnew[nt][0];
+      m_run[nt][1] = mnew[nt][1];
+    }
+  }
+  // probabilities -> hi/lo B fragments (k = token, n = head) per 16-token tile
+  uint32_t pb[MT][NT][2], pl[MT][NT][2];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const float p0 = fast_exp2(s[mt][nt][0] - m_run[nt][0]);
+      const float p1 = fast_exp2(s[mt][nt][1] - m_run[nt][1]);
+      const float p2 = fast_exp2(s[mt][nt][2] - m_run[nt][0]);
+      const float p3 = fast_exp2(s[mt][nt][3] - m_run[nt][1]);
+      l_run[nt][0] += p0 + p2;
+      l_run[nt][1] += p1 + p3;
+      float r0, r1, r2, r3;
+      const uint32_t h01 = pack2<T>(p0, p1), h23 = pack2<T>(p2, p3);
+      unpack2<T>(h01, r0, r1);
+      unpack2<T>(h23, r2, r3);
+      pb[mt][nt][0] = movmatrix_trans(h01);
+      pb[mt][nt][1] = movmatrix_trans(h23);
+      pl[mt][nt][0] = movmatrix_trans(pack2<T>(p0 - r0, p1 - r1));
+      pl[mt][nt][1] = movmatrix_trans(pack2<T>(p2 - r2, p3 - r3));
+    }
+  }
+  // O^T[d, head] += V^T[d, tok] . P^T[tok, head]   (ldmatrix.trans of V rows)
+  const int vrow = (lane & 7) + ((lane >> 4) & 1) * 8;
+  const int vcol = ((lane >> 3) & 1) * 8;
+#pragma unroll
+  for (int d = 0; d < 8; ++d) {
+    const uint32_t box = vbase + (d >= 4 ? vbox : 0u);
+#pragma unroll
+    for (int kk = 0; kk < MT; ++kk) {
+      uint32_t a[4];
+      ldmatrix_x4_trans(box + swizzled_offset<128>(kk * 16 + vrow, (d & 3) * 16 + vcol), a[0], a[1],
+                        a[2], a[3]);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        mma_16816<T>(o[d][nt], a, pb[kk][nt][0], pb[kk][nt][1]);
+        mma_16816<T>(o[d][nt], a, pl[kk][nt][0], pl[kk][nt][1]);
+      }
+    }
+  }
+}
+
+// Copy one unit's small operands into a header buffer (producer warp, all
+// lanes): the unit's query rows, R[b, kvh], delta_mu[b, kvh] and mask row.
+// Aligned rows go by cp.async (16 B, global -> shared, all issued before one
+// wait); the rest is staged through registers with every load issued first.
+template <typename T, int NT, int DK>
+__device__ __forceinline__ void load_header(unsigned char *hdr, const DecodeParams &p, int b,
+                                            int kvh, int head0, int nheads, int lane) {
+  using C = Cfg<NT, DK>;
+  constexpr int kHeads = C::kHeads;
+  constexpr int kRowChunks = kHeadDim / 8;  // 16-byte chunks of a 128-wide row
+  unsigned char *hq = hdr + C::kHdrQ;
+  unsigned char *hr = hdr + C::kHdrR;
+  T *hd = reinterpret_cast<T *>(hdr + C::kHdrDm);
+  uint8_t *hm = hdr + C::kHdrMask;
+  const T *q = reinterpret_cast<const T *>(p.q) + (long long)b * p.q_sb;
+  const bool q_vec = (p.q_sh * (long long)sizeof(T)) % 16 == 0 &&
+                     (reinterpret_cast<uintptr_t>(q + (long long)head0 * p.q_sh) & 15) == 0;
+  // query rows (zero rows pad the head tile)
+#pragma unroll
+  for (int e = lane; e < kHeads * kRowChunks; e += 32) {
+    const int h = e / kRowChunks, c = e % kRowChunks;
+    unsigned char *dst = hq + e * 16;
+    const T *src = q + (long long)(head0 + h) * p.q_sh + c * 8;
+    if (h >= nheads) {
+      *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
+    } else if (q_vec) {
+      cp_async_16(dst, src);
+    } else {
+      T tmp[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) tmp[k] = src[k];
+      *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<uint4 *>(tmp);
+    }
+  }
+  if (p.R != nullptr) {
+    const T *Rb = reinterpret_cast<const T *>(p.R) + (long long)b * p.R_sb + (long long)kvh * p.R_sh;
+    if (p.R_sd == DK && (reinterpret_cast<uintptr_t>(Rb) & 15) == 0) {
+#pragma unroll
+      for (int e = lane; e < kHeadDim * DK / 8; e += 32) cp_async_16(hr + e * 16, Rb + e * 8);
+    } else {
+      T *hrt = reinterpret_cast<T *>(hr);
+      for (int e = lane; e < kHeadDim * DK; e += 32) hrt[e] = Rb[(long long)(e / DK) * p.R_sd + e % DK];
+    }
+  }
+  {
+    T dv[kHeadDim / 32];
+#pragma unroll
+    for (int k = 0; k < kHeadDim / 32; ++k)
+      dv[k] = p.dm != nullptr ? reinterpret_cast<const T *>(p.dm)[(long long)b * p.dm_sb +
+                                                                  (long long)kvh * p.dm_sh + lane + 32 * k]
+                              : from_f32<T>(0.f);
+#pragma unroll
+    for (int k = 0; k < kHeadDim / 32; ++k) hd[lane + 32 * k] = dv[k];
+  }
+  if (p.mask != nullptr && p.seq_full <= C::kHdrMaskBytes) {
+    const uint8_t *mrow = p.mask + (long long)b * p.mask_sb;
+    uint8_t mv[C::kHdrMaskBytes / 32];
+#pragma unroll
+    for (int k = 0; k < C::kHdrMaskBytes / 32; ++k) {
+      const int t = lane + 32 * k;
+      mv[k] = t < p.seq_full ? mrow[(long long)t * p.mask_ss] : 0;
+    }
+#pragma unroll
+    for (int k = 0; k < C::kHdrMaskBytes / 32; ++k) hm[lane + 32 * k] = mv[k];
+  }
+  cp_async_wait_all();
+}
+
+template <typename T, int NT, int DK>
+__global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
     rotatek_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_kf,
                              const __grid_constant__ CUtensorMap tm_vf,
                              const __grid_constant__ CUtensorMap tm_ks,
                              const __grid_constant__ CUtensorMap tm_vs, const DecodeParams p) {
-  using L = SmemLayout<NT, NGROUP>;
-  constexpr int kHeads = L::kHeads;
-  constexpr int kConsumers = L::kConsumerWarps * 32;
+  using C = Cfg<NT, DK>;
+  constexpr int kHeads = C::kHeads;
+  constexpr int kStages = C::kStages;
+  constexpr int kWarps = C::kWarps;
+  constexpr int kNB = C::kHdrBufs;
   constexpr int kKsRowBytes = DK * 2;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float *q_s = reinterpret_cast<float *>(smem + L::kQOff);
-  float *qrot_s = reinterpret_cast<float *>(smem + L::kQRotOff);
-  float *bias_s = reinterpret_cast<float *>(smem + L::kBiasOff);
-  float *acc_s = reinterpret_cast<float *>(smem + L::kAccOff);
-  float *mw_s = reinterpret_cast<float *>(smem + L::kMwOff);
-  float *lw_s = reinterpret_cast<float *>(smem + L::kLwOff);
-  uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + L::kBarOff);
-  uint64_t *empty_bar = full_bar + kStages;
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::kFlagOff);
-  volatile int *last_flag = abort_flag + 1;
+  uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + C::kBarOff);
+  uint64_t *empty_bar = full_bar + C::kMaxStages;
+  uint64_t *hdr_full = empty_bar + C::kMaxStages;
+  uint64_t *hdr_empty = hdr_full + 2;
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kFlagOff);
+  unsigned char *ring = smem + C::kRingOff;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -99,58 +273,82 @@ __global__ void __launch_bounds__((kWarpsPerGroup * NGROUP + 1) * 32, 1)
   const long long lo = (long long)blockIdx.x * total / gridDim.x;
   const long long hi = (long long)(blockIdx.x + 1) * total / gridDim.x;
   const int nblk = static_cast<int>(hi - lo);
+  const int bpu = p.blocks_per_unit;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kWarpsPerGroup);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < kNB; ++b) {
+      mbar_init(&hdr_full[b], 1);
+      mbar_init(&hdr_empty[b], kWarps);
     }
     *abort_flag = 0;
-    *last_flag = 0;
     fence_barrier_init();
   }
   __syncthreads();
 
   // ======================================================== producer warp
-  if (warp == L::kConsumerWarps) {
+  if (warp == kWarps) {
     if (lane == 0) {
       if (p.blocks_full > 0) { tma_prefetch_desc(&tm_kf); tma_prefetch_desc(&tm_vf); }
       if (p.blocks_sparse > 0) { tma_prefetch_desc(&tm_ks); tma_prefetch_desc(&tm_vs); }
-      int issued = 0;
-      for (int i = 0; i < nblk; ++i) {
-        const int stage = i % kStages;
-        const uint32_t parity = ((i / kStages) & 1) ^ 1;
-        if (!mbar_wait_bounded(&empty_bar[stage], parity, abort_flag, p.status)) break;
-        const long long g = lo + i;
-        const int unit = static_cast<int>(g / p.blocks_per_unit);
-        const int j = static_cast<int>(g - (long long)unit * p.blocks_per_unit);
-        const int bk = unit / (p.kv_heads * p.head_chunks);
-        const int kvh = (unit / p.head_chunks) % p.kv_heads;
-        unsigned char *st = smem + stage * kStageBytes;
-        if (j < p.blocks_full) {
-          const int tok = j * kBlockTokens;
-          mbar_arrive_expect_tx(&full_bar[stage], 4 * 8192);
-          tma_load_4d(st, &tm_kf, 0, tok, kvh, bk, &full_bar[stage]);
-          tma_load_4d(st + 8192, &tm_kf, 64, tok, kvh, bk, &full_bar[stage]);
-          tma_load_4d(st + kKRegion, &tm_vf, 0, tok, kvh, bk, &full_bar[stage]);
-          tma_load_4d(st + kKRegion + 8192, &tm_vf, 64, tok, kvh, bk, &full_bar[stage]);
-        } else {
-          const int tok = (j - p.blocks_full) * kBlockTokens;
-          mbar_arrive_expect_tx(&full_bar[stage], kBlockTokens * DK * 2 + 2 * 8192);
-          tma_load_4d(st, &tm_ks, 0, tok, kvh, bk, &full_bar[stage]);
-          tma_load_4d(st + kKRegion, &tm_vs, 0, tok, kvh, bk, &full_bar[stage]);
-          tma_load_4d(st + kKRegion + 8192, &tm_vs, 64, tok, kvh, bk, &full_bar[stage]);
-        }
-        ++issued;
+    }
+    int unit = static_cast<int>(lo / bpu);
+    int j = static_cast<int>(lo - (long long)unit * bpu);
+    int seg = -1, bk = 0, kvh = 0, issued = 0;
+    for (int i = 0; i < nblk; ++i) {
+      if (i == 0 || j == 0) {
+        // a new unit: its header goes into buffer seg % kNB once the consumers
+        // are done with the unit that used the buffer before
+        ++seg;
+        const int buf = seg % kNB;
+        const int hc = unit % p.head_chunks;
+        kvh = (unit / p.head_chunks) % p.kv_heads;
+        bk = unit / (p.kv_heads * p.head_chunks);
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait_bounded(&hdr_empty[buf], ((seg / kNB) & 1) ^ 1, abort_flag, p.status);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (ok)
+          load_header<T, NT, DK>(smem + C::kHdrOff + buf * C::kHdrBytes, p, bk, kvh,
+                                 kvh * p.groups + hc * kHeads, min(kHeads, p.groups - hc * kHeads), lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&hdr_full[buf]);
       }
-      if (*abort_flag) {
-        // leave no copy in flight: wait (bounded) for the stages still loading
-        const int first = issued > kStages ? issued - kStages : 0;
-        for (int i = first; i < issued; ++i) {
-          const unsigned long long t0 = globaltimer_ns();
-          while (!mbar_try_wait(&full_bar[i % kStages], (i / kStages) & 1)) {
-            if (globaltimer_ns() - t0 > kWaitLimitNs / 4) break;
+      if (lane == 0) {
+        const int stage = i % kStages;
+        if (mbar_wait_bounded(&empty_bar[stage], ((i / kStages) & 1) ^ 1, abort_flag, p.status)) {
+          unsigned char *st = ring + stage * C::kStageBytes;
+          if (j < p.blocks_full) {
+            const int tok = j * kFullTokens;
+            mbar_arrive_expect_tx(&full_bar[stage], 4 * kFullBoxBytes);
+            tma_load_4d(st, &tm_kf, 0, tok, kvh, bk, &full_bar[stage]);
+            tma_load_4d(st + kFullBoxBytes, &tm_kf, 64, tok, kvh, bk, &full_bar[stage]);
+            tma_load_4d(st + 2 * kFullBoxBytes, &tm_vf, 0, tok, kvh, bk, &full_bar[stage]);
+            tma_load_4d(st + 3 * kFullBoxBytes, &tm_vf, 64, tok, kvh, bk, &full_bar[stage]);
+          } else {
+            const int tok = (j - p.blocks_full) * kVisTokens;
+            mbar_arrive_expect_tx(&full_bar[stage], C::kKsBytes + 2 * kVisBoxBytes);
+            tma_load_4d(st, &tm_ks, 0, tok, kvh, bk, &full_bar[stage]);
+            tma_load_4d(st + C::kKsBytes, &tm_vs, 0, tok, kvh, bk, &full_bar[stage]);
+            tma_load_4d(st + C::kKsBytes + kVisBoxBytes, &tm_vs, 64, tok, kvh, bk, &full_bar[stage]);
           }
+          ++issued;
+        }
+      }
+      if (++j == bpu) {
+        j = 0;
+        ++unit;
+      }
+    }
+    if (lane == 0 && *abort_flag) {
+      // leave no copy in flight: wait (bounded) for the stages still loading
+      const int first = issued > kStages ? issued - kStages : 0;
+      for (int i = first; i < issued; ++i) {
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full_bar[i % kStages], (i / kStages) & 1)) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs / 4) break;
         }
       }
     }
@@ -158,84 +356,102 @@ __global__ void __launch_bounds__((kWarpsPerGroup * NGROUP + 1) * 32, 1)
   }
 
   // ======================================================== consumer warps
-  const int cw = warp;                         // consumer warp 0 .. 4*NGROUP-1
-  const int group = cw / kWarpsPerGroup;
-  const int wig = cw % kWarpsPerGroup;         // warp in group: owns tokens [16*wig, +16)
-  const int g8 = lane >> 2;                    // fragment row
-  const int t4 = lane & 3;                     // fragment column pair
-  const int ctid = threadIdx.x;                // 0 .. kConsumers-1
+  const int cw = warp;                // consumer warp: owns blocks i = cw (mod kWarps)
+  const int g8 = lane >> 2;           // fragment row
+  const int t4 = lane & 3;            // fragment column pair
+  const int arow = (lane & 7) + ((lane >> 3) & 1) * 8;   // A-operand (ldmatrix) row
+  const int acol = (lane >> 4) * 8;                      // A-operand column offset
 
   int it = 0;
+  int seg = -1;
+  int unit = static_cast<int>(lo / bpu);
   while (it < nblk) {
-    Seg sg;
-    sg.unit = static_cast<int>((lo + it) / p.blocks_per_unit);
-    const long long unit_end = (long long)(sg.unit + 1) * p.blocks_per_unit;
+    ++seg;
+    const int buf = seg % kNB;
+    const long long unit_end = (long long)(unit + 1) * bpu;
     const int seg_end = static_cast<int>((hi < unit_end ? hi : unit_end) - lo);
-    sg.hc = sg.unit % p.head_chunks;
-    sg.kvh = (sg.unit / p.head_chunks) % p.kv_heads;
-    sg.b = sg.unit / (p.kv_heads * p.head_chunks);
-    sg.head0 = sg.kvh * p.groups + sg.hc * kHeads;
-    sg.nheads = min(kHeads, p.groups - sg.hc * kHeads);
+    const int j0 = static_cast<int>(lo + it - (long long)unit * bpu);  // first block of the unit here
+    const int hc = unit % p.head_chunks;
+    const int bk = unit / (p.kv_heads * p.head_chunks);
+    const int kvh = (unit / p.head_chunks) % p.kv_heads;
+    const int head0 = kvh * p.groups + hc * kHeads;
+    const int nheads = min(kHeads, p.groups - hc * kHeads);
 
-    // ---- segment set-up: q tile, q~ = q R, bias = q . delta_mu, zero the accumulator
-    named_barrier_sync(1, kConsumers);
-    {
-      const T *qb = reinterpret_cast<const T *>(p.q) + (long long)sg.b * p.q_sb;
-      for (int e = ctid; e < kHeads * kHeadDim; e += kConsumers) {
-        const int h = e / kHeadDim, d = e % kHeadDim;
-        q_s[e] = h < sg.nheads ? to_f32(qb[(long long)(sg.head0 + h) * p.q_sh + d]) : 0.f;
-      }
-      for (int e = ctid; e < kHeads * L::kAccStride; e += kConsumers) acc_s[e] = 0.f;
-    }
-    named_barrier_sync(1, kConsumers);
-    {
-      const T *Rb = reinterpret_cast<const T *>(p.R) + (long long)sg.b * p.R_sb +
-                    (long long)sg.kvh * p.R_sh;
-      for (int e = ctid; e < kHeads * DK; e += kConsumers) {
-        const int h = e / DK, jj = e % DK;
-        const float *qh = q_s + h * kHeadDim;
-        float acc = 0.f;
-        if (p.R != nullptr) {  // NULL for the dense (full-channel) decode
-#pragma unroll 8
-          for (int d = 0; d < kHeadDim; ++d) acc = fmaf(qh[d], to_f32(Rb[(long long)d * p.R_sd + jj]), acc);
-        }
-        qrot_s[h * 64 + jj] = acc;
-      }
-      if (ctid < kHeads) {
-        float acc = 0.f;
-        if (p.dm != nullptr) {
-          const T *db = reinterpret_cast<const T *>(p.dm) + (long long)sg.b * p.dm_sb +
-                        (long long)sg.kvh * p.dm_sh;
-          const float *qh = q_s + ctid * kHeadDim;
-          for (int d = 0; d < kHeadDim; ++d) acc = fmaf(qh[d], to_f32(db[d]), acc);
-        }
-        bias_s[ctid] = acc;
-      }
-    }
-    named_barrier_sync(1, kConsumers);
-
-    // ---- per-warp fragments of the queries (B operands: k = channel, n = head)
-    uint32_t qhi[DK / 16][NT][2], qlo[DK / 16][NT][2];
-    float bias2[NT][2];
+    // ---- unit header -> this warp's query fragments (no CTA-wide barrier)
+    mbar_wait_bounded(&hdr_full[buf], (seg / kNB) & 1, abort_flag, p.status);
+    const unsigned char *hdr = smem + C::kHdrOff + buf * C::kHdrBytes;
+    const uint32_t hq = smem_u32(hdr + C::kHdrQ);
+    const uint32_t hr = smem_u32(hdr + C::kHdrR);
+    const T *hdm = reinterpret_cast<const T *>(hdr + C::kHdrDm);
+    const uint8_t *hmask = hdr + C::kHdrMask;
+    // full-width query B fragments (k = d, n = head): ldmatrix of the query rows
+    uint32_t qf[kHeadDim / 16][NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const int h = nt * 8 + g8;
 #pragma unroll
-      for (int ks = 0; ks < DK / 16; ++ks) {
+      for (int ks = 0; ks < kHeadDim / 16; ks += 2) {
+        const int row = nt * 8 + (lane & 7);
+        const int col = (ks + (lane >> 4)) * 16 + ((lane >> 3) & 1) * 8;
+        ldmatrix_x4(hq + row * (kHeadDim * 2) + col * 2, qf[ks][nt][0], qf[ks][nt][1],
+                    qf[ks + 1][nt][0], qf[ks + 1][nt][1]);
+      }
+    }
+    // q~^T[ch, head] = R^T . q^T on the tensor cores (fp32 accumulate), then the
+    // fp32 result -> 16-bit hi + lo B fragments (k = channel, n = head)
+    uint32_t qhi[DK / 16][NT][2], qlo[DK / 16][NT][2];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int c = ks * 16 + half * 8 + 2 * t4;
-          const float v0 = qrot_s[h * 64 + c], v1 = qrot_s[h * 64 + c + 1];
-          const uint32_t hpk = pack2<T>(v0, v1);
-          float h0, h1;
-          unpack2<T>(hpk, h0, h1);
-          qhi[ks][nt][half] = hpk;
-          qlo[ks][nt][half] = pack2<T>(v0 - h0, v1 - h1);
+    for (int mt = 0; mt < DK / 16; ++mt) {
+      float c[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) c[nt][0] = c[nt][1] = c[nt][2] = c[nt][3] = 0.f;
+      if (p.R != nullptr) {
+#pragma unroll
+        for (int ks = 0; ks < kHeadDim / 16; ++ks) {
+          uint32_t a[4];
+          const int d = ks * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
+          const int ch = mt * 16 + ((lane >> 3) & 1) * 8;
+          ldmatrix_x4_trans(hr + d * kKsRowBytes + ch * 2, a[0], a[1], a[2], a[3]);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) mma_16816<T>(c[nt], a, qf[ks][nt][0], qf[ks][nt][1]);
         }
       }
-      bias2[nt][0] = bias_s[nt * 8 + 2 * t4];
-      bias2[nt][1] = bias_s[nt * 8 + 2 * t4 + 1];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const float v0 = c[nt][2 * half], v1 = c[nt][2 * half + 1];
+          const uint32_t h = pack2<T>(v0, v1);
+          float h0, h1;
+          unpack2<T>(h, h0, h1);
+          qhi[mt][nt][half] = movmatrix_trans(h);
+          qlo[mt][nt][half] = movmatrix_trans(pack2<T>(v0 - h0, v1 - h1));
+        }
+      }
     }
+    // bias = q . delta_mu per head: lane sums 4 channels, butterfly over the warp
+    float bias2[NT][2];
+    {
+      float dmv[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) dmv[k] = to_f32(hdm[lane * 4 + k]);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        bias2[nt][0] = bias2[nt][1] = 0.f;
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          const T *qrow = reinterpret_cast<const T *>(hdr + C::kHdrQ) + (nt * 8 + h) * kHeadDim + lane * 4;
+          float part = 0.f;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) part = fmaf(to_f32(qrow[k]), dmv[k], part);
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+          if (h == 2 * t4) bias2[nt][0] = part;
+          if (h == 2 * t4 + 1) bias2[nt][1] = part;
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&hdr_empty[buf]);
 
     float o[8][NT][4];
     float m_run[NT][2], l_run[NT][2];
@@ -244,115 +460,100 @@ __global__ void __launch_bounds__((kWarpsPerGroup * NGROUP + 1) * 32, 1)
       m_run[nt][0] = m_run[nt][1] = kNegBig;
       l_run[nt][0] = l_run[nt][1] = 0.f;
 #pragma unroll
-      for (int mt = 0; mt < 8; ++mt) o[mt][nt][0] = o[mt][nt][1] = o[mt][nt][2] = o[mt][nt][3] = 0.f;
+      for (int d = 0; d < 8; ++d) o[d][nt][0] = o[d][nt][1] = o[d][nt][2] = o[d][nt][3] = 0.f;
     }
 
-    // ---- stream this segment's blocks
-    for (int i = it; i < seg_end; ++i) {
-      if ((i % NGROUP) != group) continue;
+    // ---- this warp's blocks of the segment
+    const int first = it + ((cw - it) % kWarps + kWarps) % kWarps;
+    for (int i = first; i < seg_end; i += kWarps) {
       const int stage = i % kStages;
       const bool ready = mbar_wait_bounded(&full_bar[stage], (i / kStages) & 1, abort_flag, p.status);
-      const int j = static_cast<int>(lo + i - (long long)sg.unit * p.blocks_per_unit);
-      const bool is_full = j < p.blocks_full;
-      const int tok0 = (is_full ? j : j - p.blocks_full) * kBlockTokens + wig * 16;
-      const int seq = is_full ? p.seq_full : p.seq_sparse;
-      const uint32_t kbase = smem_u32(smem + stage * kStageBytes);
-      const uint32_t vbase = kbase + kKRegion;
-      const int r0 = wig * 16;                    // first box row of this warp
-
+      const int j = j0 + (i - it);
+      const uint32_t sbase = smem_u32(ring + stage * C::kStageBytes);
       if (ready) {
-        float s[NT][4];
+        if (j < p.blocks_full) {
+          // ---- prompt/text block: 32 tokens at full width, q . k
+          const int tok0 = j * kFullTokens;
+          float s[2][NT][4];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-        // A-operand row/col for this lane (non-transposed ldmatrix.x4)
-        const int arow = r0 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int acol = (lane >> 4) * 8;
-        if (is_full) {
+          for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) s[mt][nt][0] = s[mt][nt][1] = s[mt][nt][2] = s[mt][nt][3] = 0.f;
 #pragma unroll
           for (int ks = 0; ks < kHeadDim / 16; ++ks) {
-            uint32_t a[4];
-            const uint32_t box = kbase + (ks >= 4 ? 8192u : 0u);
-            ldmatrix_x4(box + swizzled_offset<128>(arow, (ks & 3) * 16 + acol), a[0], a[1], a[2], a[3]);
+            const uint32_t box = sbase + (ks >= 4 ? (uint32_t)kFullBoxBytes : 0u);
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              const float *qh = q_s + (nt * 8 + g8) * kHeadDim + ks * 16 + 2 * t4;
-              const uint32_t b0 = pack2<T>(qh[0], qh[1]);
-              const uint32_t b1 = pack2<T>(qh[8], qh[9]);
-              mma_16816<T>(s[nt], a, b0, b1);
+            for (int mt = 0; mt < 2; ++mt) {
+              uint32_t a[4];
+              ldmatrix_x4(box + swizzled_offset<128>(mt * 16 + arow, (ks & 3) * 16 + acol), a[0],
+                          a[1], a[2], a[3]);
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) mma_16816<T>(s[mt][nt], a, qf[ks][nt][0], qf[ks][nt][1]);
             }
           }
+          bool valid[2][2];
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+              const int tok = tok0 + mt * 16 + g8 + 8 * r;
+              bool v = tok < p.seq_full;
+              if (v && p.mask != nullptr)
+                v = (p.seq_full <= C::kHdrMaskBytes ? hmask[tok]
+                                                    : p.mask[(long long)bk * p.mask_sb +
+                                                             (long long)tok * p.mask_ss]) != 0;
+              valid[mt][r] = v;
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) s[mt][nt][e] *= p.scale_log2;
+          }
+          softmax_pv<T, NT, 2>(s, valid, m_run, l_run, o, sbase + 2 * kFullBoxBytes,
+                               kFullBoxBytes, lane);
         } else {
+          // ---- visual block: 64 tokens, rotated-truncated Keys, (q~ . k~ + bias)
+          const int tok0 = (j - p.blocks_full) * kVisTokens;
+          float s[4][NT][4];
+#pragma unroll
+          for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) s[mt][nt][0] = s[mt][nt][1] = s[mt][nt][2] = s[mt][nt][3] = 0.f;
 #pragma unroll
           for (int ks = 0; ks < DK / 16; ++ks) {
-            uint32_t a[4];
-            ldmatrix_x4(kbase + swizzled_offset<kKsRowBytes>(arow, ks * 16 + acol), a[0], a[1], a[2], a[3]);
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              mma_16816<T>(s[nt], a, qhi[ks][nt][0], qhi[ks][nt][1]);
-              mma_16816<T>(s[nt], a, qlo[ks][nt][0], qlo[ks][nt][1]);
+            for (int mt = 0; mt < 4; ++mt) {
+              uint32_t a[4];
+              ldmatrix_x4(sbase + swizzled_offset<kKsRowBytes>(mt * 16 + arow, ks * 16 + acol), a[0],
+                          a[1], a[2], a[3]);
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) {
+                mma_16816<T>(s[mt][nt], a, qhi[ks][nt][0], qhi[ks][nt][1]);
+                mma_16816<T>(s[mt][nt], a, qlo[ks][nt][0], qlo[ks][nt][1]);
+              }
             }
           }
-        }
-        // ---- scale, bias, masks -> online softmax (rows g8 / g8+8 = tokens, cols = heads)
-        const int tokA = tok0 + g8, tokB = tok0 + g8 + 8;
-        bool validA = tokA < seq, validB = tokB < seq;
-        if (is_full && p.mask != nullptr) {
-          const uint8_t *mrow = p.mask + (long long)sg.b * p.mask_sb;
-          if (validA) validA = mrow[(long long)tokA * p.mask_ss] != 0;
-          if (validB) validB = mrow[(long long)tokB * p.mask_ss] != 0;
-        }
-        uint32_t pb[NT][2];
+          bool valid[4][2];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          float sc[4];
+          for (int mt = 0; mt < 4; ++mt) {
+            valid[mt][0] = tok0 + mt * 16 + g8 < p.seq_sparse;
+            valid[mt][1] = tok0 + mt * 16 + g8 + 8 < p.seq_sparse;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float bias = is_full ? 0.f : bias2[nt][e & 1];
-            sc[e] = (s[nt][e] + bias) * p.scale_log2;
+            for (int nt = 0; nt < NT; ++nt) {
+              s[mt][nt][0] = (s[mt][nt][0] + bias2[nt][0]) * p.scale_log2;
+              s[mt][nt][1] = (s[mt][nt][1] + bias2[nt][1]) * p.scale_log2;
+              s[mt][nt][2] = (s[mt][nt][2] + bias2[nt][0]) * p.scale_log2;
+              s[mt][nt][3] = (s[mt][nt][3] + bias2[nt][1]) * p.scale_log2;
+            }
           }
-          if (!validA) sc[0] = sc[1] = -INFINITY;
-          if (!validB) sc[2] = sc[3] = -INFINITY;
-          float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
-#pragma unroll
-          for (int off = 4; off < 32; off <<= 1) {
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-          }
-          const float mn0 = fmaxf(m_run[nt][0], mx0), mn1 = fmaxf(m_run[nt][1], mx1);
-          const float al0 = fast_exp2(m_run[nt][0] - mn0), al1 = fast_exp2(m_run[nt][1] - mn1);
-          m_run[nt][0] = mn0;
-          m_run[nt][1] = mn1;
-          const float p0 = fast_exp2(sc[0] - mn0), p1 = fast_exp2(sc[1] - mn1);
-          const float p2 = fast_exp2(sc[2] - mn0), p3 = fast_exp2(sc[3] - mn1);
-          l_run[nt][0] = l_run[nt][0] * al0 + (p0 + p2);
-          l_run[nt][1] = l_run[nt][1] * al1 + (p1 + p3);
-#pragma unroll
-          for (int mt = 0; mt < 8; ++mt) {
-            o[mt][nt][0] *= al0;
-            o[mt][nt][1] *= al1;
-            o[mt][nt][2] *= al0;
-            o[mt][nt][3] *= al1;
-          }
-          pb[nt][0] = movmatrix_trans(pack2<T>(p0, p1));
-          pb[nt][1] = movmatrix_trans(pack2<T>(p2, p3));
-        }
-        // ---- O^T[d, head] += V^T[d, tok] . P^T[tok, head]
-        const int vrow = r0 + (lane & 7) + ((lane >> 4) & 1) * 8;
-        const int vcol = ((lane >> 3) & 1) * 8;
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          uint32_t a[4];
-          const uint32_t box = vbase + (mt >= 4 ? 8192u : 0u);
-          ldmatrix_x4_trans(box + swizzled_offset<128>(vrow, (mt & 3) * 16 + vcol), a[0], a[1], a[2], a[3]);
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) mma_16816<T>(o[mt][nt], a, pb[nt][0], pb[nt][1]);
+          softmax_pv<T, NT, 4>(s, valid, m_run, l_run, o, sbase + C::kKsBytes, kVisBoxBytes, lane);
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[stage]);
     }
 
-    // ---- segment end: merge the consumer warps (red.shared into acc_s)
+    // ---- segment end: this warp's partial (m, l, acc) -> its workspace slot
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -363,129 +564,135 @@ __global__ void __launch_bounds__((kWarpsPerGroup * NGROUP + 1) * 32, 1)
         l += __shfl_xor_sync(0xffffffffu, l, 16);
         l_run[nt][c] = l;
       }
-      if (g8 == 0) {
-        mw_s[cw * kHeads + nt * 8 + 2 * t4] = m_run[nt][0];
-        mw_s[cw * kHeads + nt * 8 + 2 * t4 + 1] = m_run[nt][1];
-        lw_s[cw * kHeads + nt * 8 + 2 * t4] = l_run[nt][0];
-        lw_s[cw * kHeads + nt * 8 + 2 * t4 + 1] = l_run[nt][1];
-      }
     }
-    named_barrier_sync(1, kConsumers);
+    const long long ublk0 = (long long)unit * bpu;
+    const int c_first = static_cast<int>(cta_of_block(ublk0, total, gridDim.x));
+    const int c_last = static_cast<int>(cta_of_block(ublk0 + bpu - 1, total, gridDim.x));
+    float *slot = p.partials + ((long long)(unit + blockIdx.x) * kWarps + cw) * p.slot_floats;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int h = nt * 8 + 2 * t4 + c;
-        float mx = kNegBig;
-        for (int w = 0; w < L::kConsumerWarps; ++w) mx = fmaxf(mx, mw_s[w * kHeads + h]);
-        const float sc = fast_exp2(m_run[nt][c] - mx);
+        if (g8 == 0) {
+          slot[h] = m_run[nt][c];
+          slot[16 + h] = l_run[nt][c];
+        }
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          const int d0 = mt * 16 + g8;
-          atomicAdd(&acc_s[h * L::kAccStride + d0], o[mt][nt][c] * sc);
-          atomicAdd(&acc_s[h * L::kAccStride + d0 + 8], o[mt][nt][2 + c] * sc);
+        for (int d = 0; d < 8; ++d) {
+          slot[32 + h * kHeadDim + d * 16 + g8] = o[d][nt][c];
+          slot[32 + h * kHeadDim + d * 16 + g8 + 8] = o[d][nt][2 + c];
         }
       }
     }
-    named_barrier_sync(1, kConsumers);
-
-    // per-head merged (m, l) of this CTA's segment, recomputed by every thread that needs it
-    auto seg_ml = [&](int h, float &m_out, float &l_out) {
-      float mx = kNegBig;
-      for (int w = 0; w < L::kConsumerWarps; ++w) mx = fmaxf(mx, mw_s[w * kHeads + h]);
-      float l = 0.f;
-      for (int w = 0; w < L::kConsumerWarps; ++w)
-        l += lw_s[w * kHeads + h] * fast_exp2(mw_s[w * kHeads + h] - mx);
-      m_out = mx;
-      l_out = l;
-    };
-
-    const long long ublk0 = (long long)sg.unit * p.blocks_per_unit;
-    const int c_first = static_cast<int>(cta_of_block(ublk0, total, gridDim.x));
-    const int c_last = static_cast<int>(cta_of_block(ublk0 + p.blocks_per_unit - 1, total, gridDim.x));
-    T *outb = reinterpret_cast<T *>(p.out) + (long long)sg.b * p.o_sb;
-
-    if (c_first == c_last) {
-      // the whole unit lives in this CTA: normalise and store
-      for (int e = ctid; e < kHeads * kHeadDim; e += kConsumers) {
-        const int h = e / kHeadDim, d = e % kHeadDim;
-        if (h >= sg.nheads) continue;
-        float m, l;
-        seg_ml(h, m, l);
-        outb[(long long)(sg.head0 + h) * p.o_sh + d] = from_f32<T>(acc_s[h * L::kAccStride + d] / (l + 1e-6f));
-      }
-    } else {
-      float *slot = p.partials + (long long)(sg.unit + blockIdx.x) * p.slot_floats;
-      for (int e = ctid; e < kHeads * kHeadDim; e += kConsumers) {
-        const int h = e / kHeadDim, d = e % kHeadDim;
-        slot[32 + e] = acc_s[h * L::kAccStride + d];
-      }
-      if (ctid < kHeads) {
-        float m, l;
-        seg_ml(ctid, m, l);
-        slot[ctid] = m;
-        slot[16 + ctid] = l;
-      }
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+      const int count = kWarps * (c_last - c_first + 1);
+      const int prev = atomicAdd(&p.tickets[unit], 1);
+      last = prev == count - 1;
+      if (last) p.tickets[unit] = 0;  // ready for the next call
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      // every partial of the unit is in place: merge them in slot order.
+      // Pass 1: lane k holds slot k0 + k; per-head max and normaliser by shuffles.
       __threadfence();
-      named_barrier_sync(1, kConsumers);
-      if (ctid == 0) {
-        const int count = c_last - c_first + 1;
-        const int prev = atomicAdd(&p.tickets[sg.unit], 1);
-        const int last = prev == count - 1;
-        if (last) p.tickets[sg.unit] = 0;  // ready for the next call
-        *last_flag = last;
+      const float *s0 = p.partials + (long long)(unit + c_first) * kWarps * p.slot_floats;
+      const int nslots = kWarps * (c_last - c_first + 1);
+      float mx[kHeads];
+#pragma unroll
+      for (int h = 0; h < kHeads; ++h) mx[h] = kNegBig;
+      for (int k0 = 0; k0 < nslots; k0 += 32) {
+        const bool on = k0 + lane < nslots;
+        const float *sl = s0 + (long long)(k0 + lane) * p.slot_floats;
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h) {
+          float v = on ? __ldcg(sl + h) : kNegBig;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+          mx[h] = fmaxf(mx[h], v);
+        }
       }
-      named_barrier_sync(1, kConsumers);
-      if (*last_flag) {
-        __threadfence();
-        for (int e = ctid; e < kHeads * kHeadDim; e += kConsumers) {
-          const int h = e / kHeadDim, d = e % kHeadDim;
-          if (h >= sg.nheads) continue;
-          float mx = kNegBig;
-          for (int c = c_first; c <= c_last; ++c) {
-            const float *sl = p.partials + (long long)(sg.unit + c) * p.slot_floats;
-            mx = fmaxf(mx, __ldcg(sl + h));
+      // Pass 2: weights w[k][h] = 2^(m_k - max) (lane k), then acc over slots;
+      // lane owns channels 4*lane .. 4*lane+3 of every head.
+      float lsum[kHeads];
+      float4 acc[kHeads];
+#pragma unroll
+      for (int h = 0; h < kHeads; ++h) {
+        lsum[h] = 0.f;
+        acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      for (int k0 = 0; k0 < nslots; k0 += 32) {
+        const bool on = k0 + lane < nslots;
+        const float *sl = s0 + (long long)(k0 + lane) * p.slot_floats;
+        float w[kHeads];
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h) {
+          w[h] = on ? fast_exp2(__ldcg(sl + h) - mx[h]) : 0.f;
+          float lw = on ? __ldcg(sl + 16 + h) * w[h] : 0.f;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
+          lsum[h] += lw;
+        }
+        const int nk = min(32, nslots - k0);
+        for (int k = 0; k < nk; ++k) {
+          const float4 *ok = reinterpret_cast<const float4 *>(s0 + (long long)(k0 + k) * p.slot_floats + 32) + lane;
+          float4 v[kHeads];
+#pragma unroll
+          for (int h = 0; h < kHeads; ++h) v[h] = __ldcg(ok + h * (kHeadDim / 4));
+#pragma unroll
+          for (int h = 0; h < kHeads; ++h) {
+            const float wk = __shfl_sync(0xffffffffu, w[h], k);
+            acc[h].x += v[h].x * wk;
+            acc[h].y += v[h].y * wk;
+            acc[h].z += v[h].z * wk;
+            acc[h].w += v[h].w * wk;
           }
-          float l = 0.f, a = 0.f;
-          for (int c = c_first; c <= c_last; ++c) {
-            const float *sl = p.partials + (long long)(sg.unit + c) * p.slot_floats;
-            const float w = fast_exp2(__ldcg(sl + h) - mx);
-            l += __ldcg(sl + 16 + h) * w;
-            a += __ldcg(sl + 32 + e) * w;
-          }
-          outb[(long long)(sg.head0 + h) * p.o_sh + d] = from_f32<T>(a / (l + 1e-6f));
+        }
+      }
+      T *outb = reinterpret_cast<T *>(p.out) + (long long)bk * p.o_sb;
+#pragma unroll
+      for (int h = 0; h < kHeads; ++h) {
+        if (h < nheads) {
+          const float inv = 1.f / (lsum[h] + 1e-6f);
+          T *orow = outb + (long long)(head0 + h) * p.o_sh + lane * 4;
+          orow[0] = from_f32<T>(acc[h].x * inv);
+          orow[1] = from_f32<T>(acc[h].y * inv);
+          orow[2] = from_f32<T>(acc[h].z * inv);
+          orow[3] = from_f32<T>(acc[h].w * inv);
         }
       }
     }
     it = seg_end;
+    ++unit;
   }
 }
 
-template <typename T, int NT, int DK, int NGROUP>
+template <typename T, int NT, int DK>
 cudaError_t launch_tc(const DecodeTensorMaps &maps, const DecodeParams &p, int grid,
                       cudaStream_t stream) {
-  using L = SmemLayout<NT, NGROUP>;
-  const int smem = L::kBytes + 1024;
-  auto kern = rotatek_decode_tc_kernel<T, NT, DK, NGROUP>;
+  using C = Cfg<NT, DK>;
+  const int smem = C::kBytes + 1024;
+  auto kern = rotatek_decode_tc_kernel<T, NT, DK>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (err != cudaSuccess) return err;
-  kern<<<grid, (kWarpsPerGroup * NGROUP + 1) * 32, smem, stream>>>(maps.kf, maps.vf, maps.ks,
-                                                                    maps.vs, p);
+  kern<<<grid, C::kThreads, smem, stream>>>(maps.kf, maps.vf, maps.ks, maps.vs, p);
   return cudaGetLastError();
 }
 
 template <typename T>
 cudaError_t dispatch_nt_dk(const DecodeTensorMaps &maps, const DecodeParams &p, int nt, int dk,
                            int grid, cudaStream_t stream) {
-  constexpr int NG = 2;
   if (nt == 1) {
-    if (dk == 16) return launch_tc<T, 1, 16, NG>(maps, p, grid, stream);
-    if (dk == 32) return launch_tc<T, 1, 32, NG>(maps, p, grid, stream);
-    if (dk == 64) return launch_tc<T, 1, 64, NG>(maps, p, grid, stream);
+    if (dk == 16) return launch_tc<T, 1, 16>(maps, p, grid, stream);
+    if (dk == 32) return launch_tc<T, 1, 32>(maps, p, grid, stream);
+    if (dk == 64) return launch_tc<T, 1, 64>(maps, p, grid, stream);
   } else {
-    if (dk == 16) return launch_tc<T, 2, 16, NG>(maps, p, grid, stream);
-    if (dk == 32) return launch_tc<T, 2, 32, NG>(maps, p, grid, stream);
-    if (dk == 64) return launch_tc<T, 2, 64, NG>(maps, p, grid, stream);
+    if (dk == 16) return launch_tc<T, 2, 16>(maps, p, grid, stream);
+    if (dk == 32) return launch_tc<T, 2, 32>(maps, p, grid, stream);
+    if (dk == 64) return launch_tc<T, 2, 64>(maps, p, grid, stream);
   }
   return cudaErrorInvalidValue;
 }
