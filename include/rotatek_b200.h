@@ -63,14 +63,20 @@ const char *rtk_last_error(void);
  * ------------------------------------------------------------------------ */
 
 /* Bytes of workspace rtk_rotatek_decode needs for these shapes on `device`.
- * The workspace must be zero-filled once before its first use; every call
- * leaves it ready for the next (its ticket counters return to zero).  Calls
- * that share a workspace must be ordered on the GPU (same stream, or events):
- * overlapping calls on one workspace race.                                   */
+ * The first rtk_decode_workspace_counter_bytes(batch, q_heads) bytes of a
+ * workspace hold counters that must read zero before a call; every call
+ * leaves them zero and overwrites the bytes after them.  A workspace zeroed
+ * once therefore serves any number of calls whose batch * q_heads does not
+ * grow.  Calls that share a workspace must be ordered on the GPU (same
+ * stream, or events): overlapping calls on one workspace race.              */
 size_t rtk_rotatek_decode_workspace_size(int32_t dtype, int64_t batch, int64_t q_heads,
                                          int64_t kv_heads, int64_t head_dim,
                                          int64_t head_dim_keep, int64_t seq_full,
                                          int64_t seq_sparse, int32_t device);
+
+/* Leading bytes of a decode workspace that must be zero before a call
+ * (status word + one counter per unit; depends on batch * q_heads only).    */
+size_t rtk_decode_workspace_counter_bytes(int64_t batch, int64_t q_heads);
 
 /* Fused RotateK decode for one query token.
  * Replaces rotatek.kernels.rotatek_decode -- `paper` family

@@ -35,6 +35,7 @@ SIGNATURES = {
     "rtk_abi_version": (ctypes.c_int, []),
     "rtk_last_error": (ctypes.c_char_p, []),
     "rtk_rotatek_decode_workspace_size": (ctypes.c_size_t, [ctypes.c_int32] + [ctypes.c_int64] * 7 + [ctypes.c_int32]),
+    "rtk_decode_workspace_counter_bytes": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64]),
     "rtk_rotatek_decode": (ctypes.c_int, [_P] * 8 + [ctypes.c_int64, _P, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "rtk_full_channel_decode_workspace_size": (ctypes.c_size_t, [ctypes.c_int32] + [ctypes.c_int64] * 5 + [ctypes.c_int32]),
     "rtk_full_channel_decode": (ctypes.c_int, [_P] * 3 + [ctypes.c_int64, _P, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
@@ -99,16 +100,20 @@ def require_cuda(*tensors):
 
 # ------------------------------------------------------------------ workspace
 _ws_lock = threading.Lock()
-_workspaces = {}
+_workspaces = {}     # device index -> uint8 buffer
+_zero_prefix = {}    # device index -> leading bytes known to read zero
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """A zero-initialised scratch buffer of at least `nbytes` for `device`.
+def workspace(device: torch.device, nbytes: int, counter_bytes: int) -> torch.Tensor:
+    """Scratch of at least `nbytes` for `device` whose first `counter_bytes`
+    read zero, as the decode kernels require before a call.
 
     One buffer per device, grown on demand and shared by every call on that
-    device (the kernels leave it zeroed).  Calls are ordered on the current
-    stream; callers that launch on several streams at once must synchronise
-    them, as for the reference's shape-keyed scratch cache
+    device.  The kernels leave the counter bytes zero and dirty what follows,
+    so the buffer is re-zeroed only when a call needs a longer zero prefix than
+    the last one left (a larger batch * q_heads).  Calls are ordered on the
+    current stream; callers that launch on several streams at once must
+    synchronise them, as for the reference's shape-keyed scratch cache
     (rotatek/kernels/fused_decode.py:47-70)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     with _ws_lock:
@@ -117,6 +122,10 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
             size = max(nbytes, 1 << 20)
             buf = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
             _workspaces[idx] = buf
+            _zero_prefix[idx] = size
+        if _zero_prefix[idx] < counter_bytes:
+            buf[:counter_bytes].zero_()
+        _zero_prefix[idx] = counter_bytes     # what follows is scratch after the call
         return buf
 
 

@@ -153,14 +153,27 @@ CUtensorMapSwizzle swizzle_for_row_bytes(int bytes) {
 }
 
 // ------------------------------------------------------------------ workspace
+// Layout of a decode workspace (every offset a multiple of 256 bytes):
+//   [0, 256)                   device-status word
+//   [256, counter_end)         one ticket counter per unit; units <= B * H_q for
+//                              every kernel, so counter_end depends on B * H_q only
+//   [counter_end, bytes)       split partials (scratch, overwritten by each call)
+// The counters must read zero before a call and every call leaves them zero,
+// so for a fixed B * H_q the workspace needs zeroing once, whatever the
+// sequence lengths; a call with a larger B * H_q needs the larger counter
+// region zeroed first (rtk_decode_workspace_counter_bytes).
 struct WorkspacePlan {
   size_t ticket_off, partial_off, bytes;
 };
 
-WorkspacePlan plan_workspace(int64_t tickets, int64_t slots, int64_t slot_floats) {
+size_t counter_end(int64_t batch, int64_t q_heads) {
+  return kAlign + align_up((size_t)(batch * q_heads) * sizeof(int));
+}
+
+WorkspacePlan plan_workspace(int64_t batch, int64_t q_heads, int64_t slots, int64_t slot_floats) {
   WorkspacePlan w;
-  w.ticket_off = kAlign;  // [0, 256): device status word
-  w.partial_off = w.ticket_off + align_up((size_t)tickets * sizeof(int));
+  w.ticket_off = kAlign;
+  w.partial_off = counter_end(batch, q_heads);
   w.bytes = w.partial_off + align_up((size_t)slots * slot_floats * sizeof(float));
   return w;
 }
@@ -208,13 +221,14 @@ size_t decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int
                               int64_t Sv, int device) {
   const int64_t G = Hkv > 0 ? Hq / Hkv : 1;
   const TcShape t = tc_shape(B, Hkv, std::max<int64_t>(G, 1), Sf, Sv, device);
-  const size_t tc = plan_workspace(t.units, t.slots, t.slot_floats).bytes;
+  const size_t tc = plan_workspace(B, Hq, t.slots, t.slot_floats).bytes;
   const SimtShape s = simt_shape(B, Hq, D, Sf + Sv, device);
-  const size_t simt = plan_workspace(s.units, s.units * s.splits, s.slot_floats).bytes;
+  const size_t simt = plan_workspace(B, Hq, s.units * s.splits, s.slot_floats).bytes;
   return std::max(tc, simt);
 }
 
 bool is_half_type(int dt) { return dt == RTK_BF16 || dt == RTK_F16; }
+
 
 // ------------------------------------------------------------------ decode core
 struct DecodeArgs {
@@ -271,7 +285,7 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
   }
   if (tc) {
     const TcShape t = tc_shape(B, Hkv, G, Sf, Sv, device);
-    const WorkspacePlan w = plan_workspace(t.units, t.slots, t.slot_floats);
+    const WorkspacePlan w = plan_workspace(B, Hq, t.slots, t.slot_floats);
     rtk::DecodeParams p;
     std::memset(&p, 0, sizeof(p));
     p.batch = (int)B; p.q_heads = (int)Hq; p.kv_heads = (int)Hkv; p.groups = (int)G;
@@ -302,7 +316,7 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
   // ---------------- generic path
   if (D > 256) return fail(RTK_ERR_UNSUPPORTED, "head_dim %lld > 256 is not supported", (long long)D);
   const SimtShape s = simt_shape(B, Hq, D, Sf + Sv, device);
-  const WorkspacePlan w = plan_workspace(s.units, s.units * s.splits, s.slot_floats);
+  const WorkspacePlan w = plan_workspace(B, Hq, s.units * s.splits, s.slot_floats);
   rtk::SimtParams p;
   std::memset(&p, 0, sizeof(p));
   p.dtype = dt;
@@ -360,6 +374,10 @@ size_t rtk_rotatek_decode_workspace_size(int32_t dtype, int64_t batch, int64_t q
   (void)dtype;
   (void)head_dim_keep;
   return decode_workspace_bytes(batch, q_heads, kv_heads, head_dim, seq_full, seq_sparse, device);
+}
+
+size_t rtk_decode_workspace_counter_bytes(int64_t batch, int64_t q_heads) {
+  return counter_end(batch, q_heads);
 }
 
 size_t rtk_full_channel_decode_workspace_size(int32_t dtype, int64_t batch, int64_t q_heads,

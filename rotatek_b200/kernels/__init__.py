@@ -74,9 +74,10 @@ def rotatek_decode(
            k_full.shape[-2], k_sparse.shape[-2], dev.index)
     need = _ws_size_cache.get(key)
     if need is None:
-        need = lib.rtk_rotatek_decode_workspace_size(*key[1:-1], dev.index)
+        need = (lib.rtk_rotatek_decode_workspace_size(*key[1:-1], dev.index),
+                lib.rtk_decode_workspace_counter_bytes(bsz, heads))
         _ws_size_cache[key] = need
-    ws = _lib.workspace(dev, need)
+    ws = _lib.workspace(dev, *need)
     out = torch.empty((bsz, 1, heads, head_dim), dtype=q_full.dtype, device=dev)
     D = _lib.describe
     _lib.check(lib.rtk_rotatek_decode(
@@ -109,9 +110,10 @@ def full_channel_decode(
     key = ("fc", _dtype_code(q), bsz, heads, k.shape[1], head_dim, k.shape[-2], dev.index)
     need = _ws_size_cache.get(key)
     if need is None:
-        need = lib.rtk_full_channel_decode_workspace_size(*key[1:-1], dev.index)
+        need = (lib.rtk_full_channel_decode_workspace_size(*key[1:-1], dev.index),
+                lib.rtk_decode_workspace_counter_bytes(bsz, heads))
         _ws_size_cache[key] = need
-    ws = _lib.workspace(dev, need)
+    ws = _lib.workspace(dev, *need)
     out = torch.empty((bsz, 1, heads, head_dim), dtype=q.dtype, device=dev)
     D = _lib.describe
     _lib.check(lib.rtk_full_channel_decode(

@@ -182,6 +182,18 @@ def test_decode_config2_full_size():
     assert_status_clean()
 
 
+def test_workspace_reuse_across_shapes():
+    """One workspace serves calls whose unit counts grow and shrink: a larger
+    B * H_q call must not read an earlier call's partials as ticket counters."""
+    seq = [(torch.bfloat16, 2, 8, 2, 300, 40), (torch.float32, 1, 4, 2, 200, 30),
+           (torch.bfloat16, 8, 28, 4, 2000, 100), (torch.bfloat16, 1, 8, 8, 900, 10),
+           (torch.bfloat16, 16, 28, 4, 3000, 200), (torch.float32, 4, 16, 4, 100, 20),
+           (torch.bfloat16, 16, 28, 4, 3000, 200)]
+    for n, (dtype, B, Hq, Hkv, Sv, Sf) in enumerate(seq):
+        run_and_check(make(dtype, B, Hq, Hkv, Sv, Sf, seed=300 + n), dtype)
+    assert_status_clean()
+
+
 def test_repeat_calls_identical():
     """Ticket counters return to zero: a second call gives the same bits."""
     d = make(torch.bfloat16, 4, 28, 4, 3000, 200, seed=17)
