@@ -100,6 +100,25 @@ int rtk_rotatek_decode(const rtk_tensor *q_full, const rtk_tensor *R_partial,
                        int64_t num_kv_groups, const rtk_tensor *out, void *workspace,
                        size_t workspace_bytes, void *stream);
 
+/* rtk_rotatek_decode without a workspace argument: it allocates nothing.
+ * No counterpart in the reference (whose Python launcher allocates its own
+ * scratch).  For callers that cannot give this library device memory -- a
+ * runtime whose pool owns all of HBM and forbids outside cudaMalloc, a
+ * foreign-language binding that only forwards tensor pointers, a step that
+ * must not enter cudaMalloc because it can synchronise the device.
+ * Its scratch is one fixed 16 MiB device array that every GPU loading the
+ * library holds until the process exits; shapes needing more
+ * (rtk_rotatek_decode_workspace_size) fail with RTK_ERR_WORKSPACE.  The first
+ * call on a device resolves the array's address (cudaGetSymbolAddress): make
+ * it before any stream capture.  All calls on a device share the array; each
+ * clears its counters first, and calls that overlap on the GPU race.
+ * Arguments, outputs and errors are those of rtk_rotatek_decode.             */
+int rtk_rotatek_decode_static(const rtk_tensor *q_full, const rtk_tensor *R_partial,
+                              const rtk_tensor *delta_mu, const rtk_tensor *k_full,
+                              const rtk_tensor *v_full, const rtk_tensor *mask_full,
+                              const rtk_tensor *k_sparse, const rtk_tensor *v_sparse,
+                              int64_t num_kv_groups, const rtk_tensor *out, void *stream);
+
 /* Bytes of workspace rtk_full_channel_decode needs (same rules as above). */
 size_t rtk_full_channel_decode_workspace_size(int32_t dtype, int64_t batch, int64_t q_heads,
                                               int64_t kv_heads, int64_t head_dim,

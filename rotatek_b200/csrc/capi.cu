@@ -229,6 +229,18 @@ size_t decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int
 
 bool is_half_type(int dt) { return dt == RTK_BF16 || dt == RTK_F16; }
 
+}  // namespace
+
+namespace rtk {
+// Bytes at the start of a decode workspace that must read zero before a call:
+// the device-status word and one ticket counter per unit (at most B * H_q).
+size_t decode_counter_bytes(int64_t batch, int64_t q_heads) { return counter_end(batch, q_heads); }
+
+// Record `msg` as this thread's rtk_last_error() and return `code`.
+int report_error(int code, const char *msg) { return fail(code, "%s", msg); }
+}  // namespace rtk
+
+namespace {
 
 // ------------------------------------------------------------------ decode core
 struct DecodeArgs {

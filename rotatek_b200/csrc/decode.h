@@ -58,4 +58,11 @@ struct SimtParams {
 
 cudaError_t launch_decode_simt(const SimtParams &p, cudaStream_t stream);
 
+// Leading bytes of a decode workspace that must be zero before a call (the
+// status word and the ticket counters); the rest is scratch the kernels overwrite.
+size_t decode_counter_bytes(int64_t batch, int64_t q_heads);
+
+// Set the calling thread's rtk_last_error() message; returns `code`.
+int report_error(int code, const char *msg);
+
 }  // namespace rtk
