@@ -133,6 +133,49 @@ int rtk_full_channel_decode(const rtk_tensor *q, const rtk_tensor *k, const rtk_
                             int64_t num_kv_groups, const rtk_tensor *out, void *workspace,
                             size_t workspace_bytes, void *stream);
 
+/* ------------------------------------------------------------------------
+ * Prefill rotation builder (head_dim 128)
+ * ------------------------------------------------------------------------ */
+
+/* cov_out[b,h] = sum_s k k^T (fp32, uncentred) and ksum_out[b,h] = sum_s k
+ * over the S tokens of keys [B, H, S, 128] (f32 | bf16 | f16).  The raw sums
+ * behind the covariance einsum of
+ * integrations/lmms_eval/models/model_utils/kv_pruning_utils.py:112-115;
+ * bf16 / fp16 keys run on the tcgen05 tensor cores.
+ *   cov_out [B, H, 128, 128] f32 contiguous, ksum_out [B, H, 128] f32 contiguous. */
+int rtk_key_covariance(const rtk_tensor *keys, const rtk_tensor *cov_out, const rtk_tensor *ksum_out,
+                       void *stream);
+
+/* Top-k eigenvectors of symmetric matrices, descending eigenvalue, each
+ * column's largest-magnitude component positive (batched 128 x 128 Jacobi).
+ * Replaces rotatek.rotation.power_iteration_gpu (rotatek/rotation.py:68-91),
+ * which returns an unconverged basis of approximately the same subspace.
+ *   cov [N, 128, 128] f32 contiguous, vecs_out [N, 128, k] f32,
+ *   vals_out [N, 128] f32 contiguous (all eigenvalues, descending), nullable. */
+int rtk_eigh_topk(const rtk_tensor *cov, int64_t k, const rtk_tensor *vecs_out,
+                  const rtk_tensor *vals_out, void *stream);
+
+/* Bytes of workspace rtk_build_rotation needs (no zeroing required). */
+size_t rtk_build_rotation_workspace_size(int64_t batch, int64_t kv_heads, int64_t head_dim);
+
+/* The RotateK prefill build for one layer: replaces the body of
+ * ChannelPruner.update_rotatek with the exact-eigh solver
+ * (kv_pruning_utils.py:105-160): centred covariance of the visual Keys,
+ * query weighting (when queries_recent is given), eigendecomposition, top-keep
+ * rotation R, mean correction delta_mu = mu - (mu R) R^T, rotated-truncated
+ * Keys kept = K_vis . R.  The keep mask (first `keep` channels) is implied.
+ *   keys_vision     [B, H_kv, S_v, 128]                 f32 | bf16 | f16
+ *   queries_recent  [B, H_kv * num_kv_groups, W, 128]   nullable (no weighting)
+ *   kept_out        [B, H_kv, S_v, keep]                keys' dtype
+ *   R_out           [B, H_kv, 128, keep]                keys' dtype
+ *   delta_mu_out    [B, H_kv, 128]                      keys' dtype, nullable
+ *   eigvals_out     [B, H_kv, 128] f32 contiguous       nullable (descending)   */
+int rtk_build_rotation(const rtk_tensor *keys_vision, const rtk_tensor *queries_recent,
+                       int64_t num_kv_groups, int64_t keep, const rtk_tensor *kept_out,
+                       const rtk_tensor *R_out, const rtk_tensor *delta_mu_out,
+                       const rtk_tensor *eigvals_out, void *workspace, size_t workspace_bytes,
+                       void *stream);
+
 /* Copy the workspace's device-status word to *status (RTK_DEVICE_TIMEOUT bits)
  * and clear it.  Synchronises `stream`.                                       */
 int rtk_read_status(void *workspace, void *stream, uint32_t *status);

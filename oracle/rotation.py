@@ -73,13 +73,20 @@ def weight_covariance(cov: np.ndarray, q_norm: np.ndarray) -> np.ndarray:
     return cov + ridge[..., None, None] * np.eye(d)
 
 
-def covariance(vision: np.ndarray, storage: str):
-    """kv_pruning_utils.py:112-115 -- (mu [B,H,D], symmetric C [B,H,D,D])."""
+def covariance(vision: np.ndarray, storage: str, round_cov: bool = True):
+    """kv_pruning_utils.py:112-115 -- (mu [B,H,D], symmetric C [B,H,D,D]).
+
+    With ``round_cov`` False the centred Keys and the covariance stay in
+    float64 (only the mean is rounded to ``storage`` before centring) -- the
+    arithmetic of a build that accumulates the covariance in fp32."""
     k = np.asarray(vision, dtype=np.float64)
     mu = np.asarray(round_to(k.mean(axis=-2), "float32"), dtype=np.float64)
-    kc = np.asarray(round_to(k - round_to(mu, storage)[..., None, :], storage), dtype=np.float64)
+    kc = k - np.asarray(round_to(mu, storage), dtype=np.float64)[..., None, :]
+    if round_cov:
+        kc = np.asarray(round_to(kc, storage), dtype=np.float64)
     cov = np.einsum("bhsd,bhse->bhde", kc, kc)
-    cov = np.asarray(round_to(cov, storage), dtype=np.float64)
+    if round_cov:
+        cov = np.asarray(round_to(cov, storage), dtype=np.float64)
     cov = 0.5 * (cov + np.swapaxes(cov, -1, -2))
     return mu, cov
 
@@ -96,11 +103,13 @@ class RotationResult:
 
 
 def build_rotation(keys_vision, queries: Optional[np.ndarray], keep: int, num_kv_groups: int,
-                   query_aware: bool = True, storage: str = "float32") -> RotationResult:
-    """The rotation build for one layer from the visual Keys [B, H_kv, S_v, D]."""
+                   query_aware: bool = True, storage: str = "float32",
+                   round_cov: bool = True) -> RotationResult:
+    """The rotation build for one layer from the visual Keys [B, H_kv, S_v, D]
+    (``round_cov``: see ``covariance``)."""
     kv = np.asarray(keys_vision, dtype=np.float64)
     bsz, hkv, _, d = kv.shape
-    mu, cov = covariance(kv, storage)
+    mu, cov = covariance(kv, storage, round_cov)
     if query_aware:
         cov = weight_covariance(cov, query_weights(queries, hkv, storage))
     cov32 = np.asarray(round_to(cov, "float32"), dtype=np.float64)

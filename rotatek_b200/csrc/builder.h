@@ -1,0 +1,64 @@
+// Parameters of the prefill rotation-builder kernels (covariance, Jacobi
+// eigensolver + top-k + delta_mu, rotation of the visual Keys).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rtk {
+
+constexpr int kBuildDim = 128;  // head_dim the builder kernels are written for
+
+// Covariance pass: per matrix m = (b, h), S_m = sum_s k k^T (fp32) and the
+// channel sums sum_s k (fp32), written to `cov` [nmat][128][128] / `ksum` [nmat][128].
+struct CovParams {
+  int dtype;                    // rtk_dtype of the Keys
+  int batch, heads, seq;        // matrices = batch * heads
+  const void *keys; long long k_s[4];   // [B, H, S, 128] element strides (generic kernel)
+  float *cov;                   // [nmat][128][128]
+  float *ksum;                  // [nmat][128]
+  int splits;                   // token splits per matrix (cluster size on the tensor-core path)
+};
+
+cudaError_t launch_cov_tc(int dtype_is_bf16, const CUtensorMap &keys_map, const CovParams &p,
+                          cudaStream_t stream);
+cudaError_t launch_cov_simt(const CovParams &p, cudaStream_t stream);
+
+// Eigensolver: per matrix, the covariance (centred if ksum is given), optionally
+// weighted by the query norms, diagonalised by cyclic Jacobi; the top `keep`
+// eigenvectors (descending eigenvalue) go out as R, plus delta_mu.
+struct JacobiParams {
+  int nmat, heads;              // matrix m = b * heads + h
+  const float *cov;             // [nmat][128][128]
+  const float *ksum;            // [nmat][128] or NULL: `cov` is already the matrix to solve
+  int count;                    // tokens behind cov / ksum
+  int center_dtype;             // dtype the reference rounds the mean to before centring
+  // query weighting (kv_pruning_utils.py:117-140); q == NULL disables it
+  const void *q; int q_dtype; long long q_s[4];  // [B, H_q, W, 128]
+  int window, groups;
+  // outputs
+  int keep;
+  void *R; int R_dtype; long long R_s[4];        // [B, H, 128, keep]
+  void *dm; long long dm_s[3];                    // [B, H, 128] (R's dtype), nullable
+  float *evals;                                   // [nmat][128] descending, nullable
+  int *sweeps;                                    // [nmat] sweeps used, nullable
+  int max_sweeps;
+  float tol;                                      // stop when off(A) <= tol * ||diag(A)||
+};
+
+cudaError_t launch_jacobi(const JacobiParams &p, cudaStream_t stream);
+
+// Rotation: kept = K_vis . R (uncentred), stored in the Keys' dtype.
+struct RotateParams {
+  int dtype;
+  int batch, heads, seq, keep;
+  const void *keys; long long k_s[4];             // [B, H, S, 128]
+  const void *R; long long R_s[4];                // [B, H, 128, keep]
+  void *out; long long o_s[4];                    // [B, H, S, keep]
+};
+
+cudaError_t launch_rotate_tc(int dtype_is_bf16, const RotateParams &p, cudaStream_t stream);
+cudaError_t launch_rotate_simt(const RotateParams &p, cudaStream_t stream);
+
+}  // namespace rtk

@@ -17,6 +17,7 @@
 #include <string>
 
 #include "../../include/rotatek_b200.h"
+#include "builder.h"
 #include "decode.h"
 
 namespace {
@@ -464,6 +465,197 @@ int rtk_full_channel_decode(const rtk_tensor *q, const rtk_tensor *k, const rtk_
   if (B * Hq == 0 || D == 0) return RTK_OK;
   DecodeArgs a{q, nullptr, nullptr, k, v, nullptr, nullptr, nullptr, out, num_kv_groups, true};
   return run_decode(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------------------------------ rotation builder
+}  // extern "C"
+
+namespace {
+// sum_s k k^T and sum_s k for every (b, h) of a [B, H, S, 128] Key view:
+// tensor-core kernel for bf16 / fp16 layouts TMA can describe, else the
+// CUDA-core kernel.
+cudaError_t launch_covariance(const View4 &kv, int dt, float *cov, float *ksum, int device,
+                              cudaStream_t st) {
+  const int64_t B = kv.n[0], H = kv.n[1], S = kv.n[2];
+  rtk::CovParams cp;
+  std::memset(&cp, 0, sizeof(cp));
+  cp.dtype = dt;
+  cp.batch = (int)B; cp.heads = (int)H; cp.seq = (int)S;
+  cp.keys = kv.data;
+  for (int i = 0; i < 4; ++i) cp.k_s[i] = kv.s[i];
+  cp.cov = cov; cp.ksum = ksum;
+  bool tc = is_half_type(dt) && S > 0;
+  CUtensorMap kmap;
+  if (tc)
+    tc = encode_map(&kmap, kv, dt == RTK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                    64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (tc) {
+    const int64_t tiles = cdiv(S, 64);
+    int z = 8;
+    while (z > 1 && (B * H * z > 2 * (int64_t)sm_count(device) || z > tiles)) z >>= 1;
+    cp.splits = z;
+    return rtk::launch_cov_tc(dt == RTK_BF16, kmap, cp, st);
+  }
+  cp.splits = 1;
+  return rtk::launch_cov_simt(cp, st);
+}
+}  // namespace
+
+extern "C" {
+
+int rtk_key_covariance(const rtk_tensor *keys, const rtk_tensor *cov_out, const rtk_tensor *ksum_out,
+                       void *stream) {
+  g_last_error.clear();
+  View4 kv;
+  if (!as4(keys, kv) || !dtype_ok(keys->dtype)) return fail(RTK_ERR_INVALID, "keys must be a [B, H, S, 128] float tensor");
+  if (kv.n[3] != 128) return fail(RTK_ERR_UNSUPPORTED, "head_dim must be 128 (got %lld)", (long long)kv.n[3]);
+  const int64_t B = kv.n[0], H = kv.n[1];
+  if (!same_dims(cov_out, 4, {B, H, 128, 128}) || cov_out->dtype != RTK_F32 || cov_out->stride[3] != 1 ||
+      cov_out->stride[2] != 128 || cov_out->stride[1] != 128 * 128 || cov_out->stride[0] != H * 128 * 128)
+    return fail(RTK_ERR_INVALID, "cov_out must be a contiguous float32 [B, H, 128, 128]");
+  if (!same_dims(ksum_out, 3, {B, H, 128}) || ksum_out->dtype != RTK_F32 || ksum_out->stride[2] != 1 ||
+      ksum_out->stride[1] != 128 || ksum_out->stride[0] != H * 128)
+    return fail(RTK_ERR_INVALID, "ksum_out must be a contiguous float32 [B, H, 128]");
+  if (B * H == 0) return RTK_OK;
+  const cudaError_t e = launch_covariance(kv, keys->dtype, static_cast<float *>(cov_out->data),
+                                          static_cast<float *>(ksum_out->data), current_device(),
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "key covariance launch");
+  return RTK_OK;
+}
+
+size_t rtk_build_rotation_workspace_size(int64_t batch, int64_t kv_heads, int64_t head_dim) {
+  const int64_t n = batch * kv_heads;
+  return align_up((size_t)n * head_dim * head_dim * sizeof(float)) +
+         align_up((size_t)n * head_dim * sizeof(float)) + align_up((size_t)n * sizeof(int));
+}
+
+int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_t num_kv_groups,
+                       int64_t keep, const rtk_tensor *kept_out, const rtk_tensor *R_out,
+                       const rtk_tensor *delta_mu_out, const rtk_tensor *eigvals_out,
+                       void *workspace, size_t workspace_bytes, void *stream) {
+  g_last_error.clear();
+  View4 kv;
+  if (!as4(keys, kv)) return fail(RTK_ERR_INVALID, "keys_vision must be [B, H_kv, S_v, D]");
+  const int64_t B = kv.n[0], H = kv.n[1], S = kv.n[2], D = kv.n[3];
+  if (!dtype_ok(keys->dtype)) return fail(RTK_ERR_INVALID, "keys_vision dtype must be float32, bfloat16 or float16");
+  if (D != 128) return fail(RTK_ERR_UNSUPPORTED, "the rotation builder supports head_dim 128 (got %lld)", (long long)D);
+  if (keep < 1 || keep > D) return fail(RTK_ERR_INVALID, "keep must be in [1, head_dim] (got %lld)", (long long)keep);
+  if (queries != nullptr) {
+    if (queries->ndim != 4 || queries->shape[0] != B || queries->shape[3] != D ||
+        num_kv_groups <= 0 || queries->shape[1] != H * num_kv_groups)
+      return fail(RTK_ERR_INVALID, "queries_recent must be [B, H_kv * num_kv_groups, W, D]");
+    if (!dtype_ok(queries->dtype)) return fail(RTK_ERR_INVALID, "queries_recent dtype must be float32, bfloat16 or float16");
+  }
+  if (!same_dims(kept_out, 4, {B, H, S, keep}) || kept_out->dtype != keys->dtype)
+    return fail(RTK_ERR_INVALID, "kept_out must be [B, H_kv, S_v, keep] in the Keys' dtype");
+  if (!same_dims(R_out, 4, {B, H, D, keep}) || R_out->dtype != keys->dtype)
+    return fail(RTK_ERR_INVALID, "R_out must be [B, H_kv, D, keep] in the Keys' dtype");
+  if (delta_mu_out != nullptr && (!same_dims(delta_mu_out, 3, {B, H, D}) || delta_mu_out->dtype != keys->dtype))
+    return fail(RTK_ERR_INVALID, "delta_mu_out must be [B, H_kv, D] in the Keys' dtype");
+  if (eigvals_out != nullptr && (!same_dims(eigvals_out, 3, {B, H, D}) || eigvals_out->dtype != RTK_F32 ||
+                                 eigvals_out->stride[2] != 1 || eigvals_out->stride[1] != D ||
+                                 eigvals_out->stride[0] != H * D))
+    return fail(RTK_ERR_INVALID, "eigvals_out must be a contiguous float32 [B, H_kv, D]");
+  if (B * H == 0) return RTK_OK;
+  const size_t need = rtk_build_rotation_workspace_size(B, H, D);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, need);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  unsigned char *ws = static_cast<unsigned char *>(workspace);
+  float *cov = reinterpret_cast<float *>(ws);
+  float *ksum = reinterpret_cast<float *>(ws + align_up((size_t)B * H * D * D * sizeof(float)));
+  int *sweeps = reinterpret_cast<int *>(reinterpret_cast<unsigned char *>(ksum) +
+                                        align_up((size_t)B * H * D * sizeof(float)));
+  const int device = current_device();
+  const int dt = keys->dtype;
+  // ---- covariance + channel sums
+  cudaError_t e = launch_covariance(kv, dt, cov, ksum, device, st);
+  if (e != cudaSuccess) return cuda_fail(e, "rotation builder (covariance) launch");
+
+  // ---- centring, query weighting, Jacobi, top-k R and delta_mu
+  rtk::JacobiParams jp;
+  std::memset(&jp, 0, sizeof(jp));
+  jp.nmat = (int)(B * H); jp.heads = (int)H;
+  jp.cov = cov; jp.ksum = ksum; jp.count = (int)std::max<int64_t>(S, 1);
+  jp.center_dtype = dt;
+  if (queries != nullptr) {
+    jp.q = queries->data; jp.q_dtype = queries->dtype;
+    for (int i = 0; i < 4; ++i) jp.q_s[i] = queries->stride[i];
+    jp.window = (int)queries->shape[2];
+    jp.groups = (int)num_kv_groups;
+  }
+  jp.keep = (int)keep;
+  jp.R = R_out->data; jp.R_dtype = dt;
+  for (int i = 0; i < 4; ++i) jp.R_s[i] = R_out->stride[i];
+  if (delta_mu_out != nullptr) {
+    jp.dm = delta_mu_out->data;
+    for (int i = 0; i < 3; ++i) jp.dm_s[i] = delta_mu_out->stride[i];
+  }
+  jp.evals = eigvals_out ? static_cast<float *>(eigvals_out->data) : nullptr;
+  jp.sweeps = sweeps;
+  jp.max_sweeps = 15;
+  jp.tol = 1e-7f;
+  e = rtk::launch_jacobi(jp, st);
+  if (e != cudaSuccess) return cuda_fail(e, "rotation builder (eigensolver) launch");
+
+  // ---- kept = K_vis . R
+  rtk::RotateParams rp;
+  std::memset(&rp, 0, sizeof(rp));
+  rp.dtype = dt;
+  rp.batch = (int)B; rp.heads = (int)H; rp.seq = (int)S; rp.keep = (int)keep;
+  rp.keys = kv.data;
+  for (int i = 0; i < 4; ++i) {
+    rp.k_s[i] = kv.s[i];
+    rp.R_s[i] = R_out->stride[i];
+    rp.o_s[i] = kept_out->stride[i];
+  }
+  rp.R = R_out->data;
+  rp.out = kept_out->data;
+  if (S > 0) {
+    const bool rtc = is_half_type(dt) && keep % 16 == 0 && kv.s[3] == 1 && (kv.s[2] * 2) % 16 == 0 &&
+                     (kv.s[1] * 2) % 16 == 0 && (kv.s[0] * 2) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(kv.data) % 16 == 0 && kept_out->stride[3] == 1 &&
+                     (kept_out->stride[2] * 2) % 16 == 0 && (kept_out->stride[1] * 2) % 16 == 0 &&
+                     (kept_out->stride[0] * 2) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(kept_out->data) % 16 == 0;
+    e = rtc ? rtk::launch_rotate_tc(dt == RTK_BF16, rp, st) : rtk::launch_rotate_simt(rp, st);
+    if (e != cudaSuccess) return cuda_fail(e, "rotation builder (rotate) launch");
+  }
+  return RTK_OK;
+}
+
+int rtk_eigh_topk(const rtk_tensor *cov, int64_t k, const rtk_tensor *vecs_out,
+                  const rtk_tensor *vals_out, void *stream) {
+  g_last_error.clear();
+  if (cov == nullptr || cov->ndim != 3 || cov->dtype != RTK_F32)
+    return fail(RTK_ERR_INVALID, "cov must be a float32 [N, D, D]");
+  const int64_t N = cov->shape[0], D = cov->shape[1];
+  if (cov->shape[2] != D) return fail(RTK_ERR_INVALID, "cov must be a float32 [N, D, D]");
+  if (D != 128) return fail(RTK_ERR_UNSUPPORTED, "the eigensolver supports D = 128 (got %lld)", (long long)D);
+  if (cov->stride[2] != 1 || cov->stride[1] != D || cov->stride[0] != D * D)
+    return fail(RTK_ERR_INVALID, "cov must be contiguous");
+  if (k < 1 || k > D) return fail(RTK_ERR_INVALID, "k must be in [1, D] (got %lld)", (long long)k);
+  if (!same_dims(vecs_out, 3, {N, D, k}) || vecs_out->dtype != RTK_F32)
+    return fail(RTK_ERR_INVALID, "vecs_out must be a float32 [N, D, k]");
+  if (vals_out != nullptr && (!same_dims(vals_out, 2, {N, D}) || vals_out->dtype != RTK_F32 ||
+                              vals_out->stride[1] != 1 || vals_out->stride[0] != D))
+    return fail(RTK_ERR_INVALID, "vals_out must be a contiguous float32 [N, D]");
+  if (N == 0) return RTK_OK;
+  rtk::JacobiParams jp;
+  std::memset(&jp, 0, sizeof(jp));
+  jp.nmat = (int)N; jp.heads = 1;
+  jp.cov = static_cast<const float *>(cov->data);
+  jp.count = 1;
+  jp.keep = (int)k;
+  jp.R = vecs_out->data; jp.R_dtype = RTK_F32;
+  jp.R_s[0] = vecs_out->stride[0]; jp.R_s[1] = 0; jp.R_s[2] = vecs_out->stride[1]; jp.R_s[3] = vecs_out->stride[2];
+  jp.evals = vals_out ? static_cast<float *>(vals_out->data) : nullptr;
+  jp.max_sweeps = 15;
+  jp.tol = 1e-7f;
+  const cudaError_t e = rtk::launch_jacobi(jp, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "eigensolver launch");
+  return RTK_OK;
 }
 
 int rtk_read_status(void *workspace, void *stream, uint32_t *status) {

@@ -1,0 +1,345 @@
+// Batched 128x128 symmetric eigensolver (cyclic Jacobi in shared memory) with
+// the RotateK prologue and epilogue fused around it:
+//
+//   prologue  C = S_kk - mu^ s^T - s mu^^T + n mu^ mu^^T     (centring,
+//             kv_pruning_utils.py:112-115, with the reference's mean rounded to
+//             the Keys' dtype), then the query weighting of kv_pruning_utils.py:
+//             117-140: per channel q_norm = ||group-mean(q)||_2 over the query
+//             window, floored at 1e-3 * lower median; C *= q_norm q_norm^T;
+//             C += max(1e-4 * mean|diag C|, 1e-6) I
+//   solve     cyclic Jacobi, parallel ordering: round r = 1..127 pairs every
+//             index i with i XOR r (each round is a perfect matching, and the
+//             127 rounds meet every pair once); a sweep is 127 rounds; stop when
+//             off(A) <= tol * ||diag A|| or after max_sweeps sweeps
+//   epilogue  eigenvalues descending; the top `keep` eigenvectors (largest
+//             component made positive) rounded to the output dtype are R
+//             (kv_pruning_utils.py:142-150 takes eigh's columns in descending
+//             order); delta_mu = mu - (mu R) R^T with that rounded R in fp32
+//             (kv_pruning_utils.py:153-156).
+//
+// One CTA of 512 threads per matrix.  A (fp32, row stride 129) and V^T (fp32,
+// row stride 132) live in shared memory (133 KB).  Per round: 64 threads
+// compute the rotations (symmetric Schur 2x2, Golub & Van Loan 8.4.2); then
+// every thread updates whole 2x2 blocks of A for block pairs (a <= b), writing
+// both the block and its mirror (A' = J^T A J, one load and one store per
+// element), and rotates row pairs of V^T with float4 accesses (V' = V J).
+#include "builder.h"
+#include "common.cuh"
+
+namespace rtk {
+namespace {
+
+constexpr int kN = 128;
+constexpr int kPairs = kN / 2;
+constexpr int kThreads = 512;
+constexpr int kAS = kN + 1;            // A row stride: bank = (row + col) mod 32
+constexpr int kVS = kN + 4;            // V^T row stride (float4-aligned rows)
+constexpr int kBlocks = kPairs * (kPairs + 1) / 2;  // 2x2 blocks with a <= b
+
+struct JSmem {
+  float A[kN * kAS];
+  float VT[kN * kVS];
+  float c[kPairs], s[kPairs], t[kPairs];
+  int pidx[kPairs];
+  unsigned int blk[kBlocks];           // (a | b << 8) for a <= b
+  float vec[kN];                       // mean, then query norms, then eigenvalues
+  float vec2[kN];
+  int rank[kN];
+  float red[2][kThreads / 32];
+  int flag;
+};
+
+__device__ __forceinline__ float load_any(const void *p, int dtype, long long i) {
+  if (dtype == 1) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i]);
+  if (dtype == 2) return __half2float(reinterpret_cast<const __half *>(p)[i]);
+  return reinterpret_cast<const float *>(p)[i];
+}
+
+__device__ __forceinline__ void store_any(void *p, int dtype, long long i, float v) {
+  if (dtype == 1) reinterpret_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
+  else if (dtype == 2) reinterpret_cast<__half *>(p)[i] = __float2half_rn(v);
+  else reinterpret_cast<float *>(p)[i] = v;
+}
+
+__device__ __forceinline__ float round_to(float v, int dtype) {
+  if (dtype == 1) return __bfloat162float(__float2bfloat16_rn(v));
+  if (dtype == 2) return __half2float(__float2half_rn(v));
+  return v;
+}
+
+__device__ __forceinline__ float block_sum(float v, float *red, int tid) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  __syncthreads();
+  if ((tid & 31) == 0) red[tid >> 5] = v;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kThreads / 32; ++w) tot += red[w];
+  return tot;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) jacobi_kernel(const JacobiParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  JSmem &sm = *reinterpret_cast<JSmem *>(smem_raw);
+  const int tid = threadIdx.x;
+  const int m = blockIdx.x;
+  const int b = m / p.heads, h = m % p.heads;
+  float *A = sm.A;
+  float *VT = sm.VT;
+
+  // ---------------------------------------------------------------- prologue
+  for (int i = tid; i < kBlocks; i += kThreads) {
+    int bb = static_cast<int>((sqrtf(8.f * i + 1.f) - 1.f) * 0.5f);
+    while (bb * (bb + 1) / 2 > i) --bb;
+    while ((bb + 1) * (bb + 2) / 2 <= i) ++bb;
+    const int aa = i - bb * (bb + 1) / 2;
+    sm.blk[i] = static_cast<unsigned>(aa) | (static_cast<unsigned>(bb) << 8);
+  }
+  const float *C0 = p.cov + (long long)m * kN * kN;
+  if (tid < kN) {
+    float mu = 0.f;
+    if (p.ksum != nullptr) mu = p.ksum[(long long)m * kN + tid] / static_cast<float>(p.count);
+    sm.vec[tid] = mu;                                  // fp32 mean
+    sm.vec2[tid] = round_to(mu, p.center_dtype);       // the mean the reference centres with
+  }
+  __syncthreads();
+  for (int e = tid; e < kN * kN; e += kThreads) {
+    const int i = e / kN, j = e % kN;
+    float v = C0[e];
+    if (p.ksum != nullptr) {
+      const float si = p.ksum[(long long)m * kN + i], sj = p.ksum[(long long)m * kN + j];
+      const float mi = sm.vec2[i], mj = sm.vec2[j];
+      v = v - mi * sj - si * mj + static_cast<float>(p.count) * mi * mj;
+    }
+    A[i * kAS + j] = v;
+  }
+  __syncthreads();
+  for (int e = tid; e < kN * kN; e += kThreads) {  // symmetrise: (C + C^T) / 2
+    const int i = e / kN, j = e % kN;
+    if (i < j) {
+      const float v = 0.5f * (A[i * kAS + j] + A[j * kAS + i]);
+      A[i * kAS + j] = v;
+      A[j * kAS + i] = v;
+    }
+  }
+  __syncthreads();
+  if (p.q != nullptr) {
+    // q_norm[d] = || mean_g q[b, h*G + g, w, d] ||_2 over the window (mean rounded
+    // to the query dtype when G > 1, as torch's bf16 mean does)
+    if (tid < kN) {
+      float acc = 0.f;
+      const float inv_g = 1.f / static_cast<float>(p.groups);
+      for (int w = 0; w < p.window; ++w) {
+        float v;
+        if (p.groups > 1) {
+          float sgrp = 0.f;
+          for (int g = 0; g < p.groups; ++g)
+            sgrp += load_any(p.q, p.q_dtype,
+                             b * p.q_s[0] + (long long)(h * p.groups + g) * p.q_s[1] +
+                                 (long long)w * p.q_s[2] + tid * p.q_s[3]);
+          v = round_to(sgrp * inv_g, p.q_dtype);
+        } else {
+          v = load_any(p.q, p.q_dtype,
+                       b * p.q_s[0] + (long long)h * p.q_s[1] + (long long)w * p.q_s[2] + tid * p.q_s[3]);
+        }
+        acc = fmaf(v, v, acc);
+      }
+      sm.vec2[tid] = sqrtf(acc);
+    }
+    __syncthreads();
+    if (tid < kN) {  // lower median: the element of rank 63
+      const float x = sm.vec2[tid];
+      int r = 0;
+      for (int e = 0; e < kN; ++e) {
+        const float y = sm.vec2[e];
+        r += (y < x) || (y == x && e < tid);
+      }
+      sm.rank[tid] = r;
+      if (r == (kN - 1) / 2) sm.red[1][0] = x;
+    }
+    __syncthreads();
+    const float qfloor = 1e-3f * sm.red[1][0];
+    __syncthreads();
+    if (tid < kN) sm.vec2[tid] = fmaxf(sm.vec2[tid], qfloor);
+    __syncthreads();
+    for (int e = tid; e < kN * kN; e += kThreads) {
+      const int i = e / kN, j = e % kN;
+      A[i * kAS + j] *= sm.vec2[i] * sm.vec2[j];
+    }
+    __syncthreads();
+    float dsum = 0.f;
+    if (tid < kN) dsum = fabsf(A[tid * kAS + tid]);
+    const float ridge = fmaxf(1e-4f * block_sum(dsum, sm.red[0], tid) / kN, 1e-6f);
+    if (tid < kN) A[tid * kAS + tid] += ridge;
+  }
+  for (int e = tid; e < kN * kN; e += kThreads) {
+    const int i = e / kN, j = e % kN;
+    VT[i * kVS + j] = (i == j) ? 1.f : 0.f;
+  }
+  __syncthreads();
+
+  // ---------------------------------------------------------------- sweeps
+  int sweep = 0;
+  for (; sweep < p.max_sweeps; ++sweep) {
+    float off = 0.f, dia = 0.f;
+    for (int e = tid; e < kN * kN; e += kThreads) {
+      const int i = e / kN, j = e % kN;
+      const float v = A[i * kAS + j];
+      if (i == j) dia = fmaf(v, v, dia);
+      else off = fmaf(v, v, off);
+    }
+    off = block_sum(off, sm.red[0], tid);
+    dia = block_sum(dia, sm.red[1], tid);
+    if (off <= p.tol * p.tol * dia) break;
+
+    for (int r = 1; r < kN; ++r) {
+      const int hbit = 31 - __clz(r);
+      // ---- rotations of this round (pairs k: p = k with a 0 inserted at bit hbit)
+      if (tid < kPairs) {
+        const int k = tid;
+        const int pp = ((k >> hbit) << (hbit + 1)) | (k & ((1 << hbit) - 1));
+        const int qq = pp ^ r;
+        const float app = A[pp * kAS + pp], aqq = A[qq * kAS + qq], apq = A[pp * kAS + qq];
+        float c = 1.f, s = 0.f, t = 0.f;
+        if (apq != 0.f && fabsf(apq) > 1e-12f * (fabsf(app) + fabsf(aqq))) {
+          const float theta = (aqq - app) / (2.f * apq);
+          t = copysignf(1.f, theta) / (fabsf(theta) + sqrtf(fmaf(theta, theta, 1.f)));
+          c = 1.f / sqrtf(fmaf(t, t, 1.f));
+          s = t * c;
+        }
+        sm.c[k] = c;
+        sm.s[k] = s;
+        sm.t[k] = t;
+        sm.pidx[k] = pp;
+      }
+      __syncthreads();
+      // ---- A <- J^T A J, one 2x2 block pair per item
+      for (int i = tid; i < kBlocks; i += kThreads) {
+        const unsigned ab = sm.blk[i];
+        const int a = ab & 0xff, bb = ab >> 8;
+        const int pa = sm.pidx[a], qa = pa ^ r, pb = sm.pidx[bb], qb = pb ^ r;
+        const float ca = sm.c[a], sa = sm.s[a], cb = sm.c[bb], sb = sm.s[bb];
+        if (a == bb) {
+          const float app = A[pa * kAS + pa], aqq = A[qa * kAS + qa], apq = A[pa * kAS + qa];
+          const float t = sm.t[a];
+          A[pa * kAS + pa] = app - t * apq;
+          A[qa * kAS + qa] = aqq + t * apq;
+          A[pa * kAS + qa] = 0.f;
+          A[qa * kAS + pa] = 0.f;
+        } else {
+          const float x00 = A[pa * kAS + pb], x01 = A[pa * kAS + qb];
+          const float x10 = A[qa * kAS + pb], x11 = A[qa * kAS + qb];
+          // rows (J_a^T): p' = c p - s q, q' = s p + c q
+          const float y00 = ca * x00 - sa * x10, y01 = ca * x01 - sa * x11;
+          const float y10 = sa * x00 + ca * x10, y11 = sa * x01 + ca * x11;
+          // columns (J_b)
+          const float z00 = y00 * cb - y01 * sb, z01 = y00 * sb + y01 * cb;
+          const float z10 = y10 * cb - y11 * sb, z11 = y10 * sb + y11 * cb;
+          A[pa * kAS + pb] = z00;
+          A[pa * kAS + qb] = z01;
+          A[qa * kAS + pb] = z10;
+          A[qa * kAS + qb] = z11;
+          A[pb * kAS + pa] = z00;
+          A[qb * kAS + pa] = z01;
+          A[pb * kAS + qa] = z10;
+          A[qb * kAS + qa] = z11;
+        }
+      }
+      // ---- V <- V J: rows p, q of V^T; 8 threads per pair, 16 columns each
+      {
+        const int k = tid >> 3, part = tid & 7;
+        const int pp = sm.pidx[k], qq = pp ^ r;
+        const float c = sm.c[k], s = sm.s[k];
+        if (s != 0.f) {
+          float4 *vp = reinterpret_cast<float4 *>(VT + pp * kVS + part * 16);
+          float4 *vq = reinterpret_cast<float4 *>(VT + qq * kVS + part * 16);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float4 a4 = vp[u], b4 = vq[u];
+            vp[u] = make_float4(c * a4.x - s * b4.x, c * a4.y - s * b4.y, c * a4.z - s * b4.z,
+                                c * a4.w - s * b4.w);
+            vq[u] = make_float4(s * a4.x + c * b4.x, s * a4.y + c * b4.y, s * a4.z + c * b4.z,
+                                s * a4.w + c * b4.w);
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  if (tid == 0 && p.sweeps != nullptr) p.sweeps[m] = sweep;
+
+  // ---------------------------------------------------------------- epilogue
+  // eigenvalues and their descending rank
+  if (tid < kN) sm.vec2[tid] = A[tid * kAS + tid];
+  __syncthreads();
+  if (tid < kN) {
+    const float x = sm.vec2[tid];
+    int r = 0;
+    for (int e = 0; e < kN; ++e) {
+      const float y = sm.vec2[e];
+      r += (y > x) || (y == x && e < tid);
+    }
+    sm.rank[tid] = r;
+    if (p.evals != nullptr) p.evals[(long long)m * kN + r] = x;
+  }
+  __syncthreads();
+  // selected eigenvectors: column rank r < keep is V[:, i] = VT[i][:]; sign so
+  // that the largest-magnitude component is positive; round to the dtype
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int i = warp; i < kN; i += kThreads / 32) {
+    const int r = sm.rank[i];
+    if (r >= p.keep) continue;
+    float best = 0.f, nrm = 0.f;
+    for (int d = lane; d < kN; d += 32) {
+      const float v = VT[i * kVS + d];
+      nrm = fmaf(v, v, nrm);
+      if (fabsf(v) > fabsf(best)) best = v;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float o = __shfl_xor_sync(0xffffffffu, best, off);
+      if (fabsf(o) > fabsf(best) || (fabsf(o) == fabsf(best) && o > best)) best = o;
+      nrm += __shfl_xor_sync(0xffffffffu, nrm, off);
+    }
+    // unit length (rounding drift over ~10^3 rotations) and a fixed sign
+    const float scale = (best < 0.f ? -1.f : 1.f) / sqrtf(nrm);
+    for (int d = lane; d < kN; d += 32) {
+      const float v = round_to(scale * VT[i * kVS + d], p.R_dtype);
+      VT[i * kVS + d] = v;
+      store_any(p.R, p.R_dtype,
+                b * p.R_s[0] + (long long)h * p.R_s[1] + (long long)d * p.R_s[2] + (long long)r * p.R_s[3], v);
+    }
+  }
+  __syncthreads();
+  if (p.dm != nullptr) {
+    // proj[r] = mu . R[:, r]  (kept columns only), then delta_mu = mu - sum_r proj[r] R[:, r]
+    if (tid < kN) {
+      const int r = sm.rank[tid];
+      float pr = 0.f;
+      if (r < p.keep)
+        for (int d = 0; d < kN; ++d) pr = fmaf(sm.vec[d], VT[tid * kVS + d], pr);
+      sm.vec2[tid] = pr;
+    }
+    __syncthreads();
+    if (tid < kN) {
+      float acc = 0.f;
+      for (int i = 0; i < kN; ++i)
+        if (sm.rank[i] < p.keep) acc = fmaf(sm.vec2[i], VT[i * kVS + tid], acc);
+      store_any(p.dm, p.R_dtype, b * p.dm_s[0] + (long long)h * p.dm_s[1] + tid * p.dm_s[2],
+                sm.vec[tid] - acc);
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_jacobi(const JacobiParams &p, cudaStream_t stream) {
+  const int smem = static_cast<int>(sizeof(JSmem));
+  cudaError_t err = cudaFuncSetAttribute(jacobi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (err != cudaSuccess) return err;
+  jacobi_kernel<<<p.nmat, kThreads, smem, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace rtk

@@ -1,0 +1,133 @@
+"""RotateK rotation builder on B200 -- the counterpart of ``rotatek.rotation``
+plus the fused prefill build that ``ChannelPruner.update_rotatek`` performs.
+
+``power_iteration_gpu`` keeps the reference's signature (rotatek/rotation.py:
+68-91) and the ``_ROTATEK_QUERY_AWARE_ACTIVE`` flag (rotation.py:18), but
+returns the *converged* top-k eigenvectors (descending eigenvalue) from a
+batched 128x128 Jacobi eigensolver instead of five unconverged subspace
+iterations from a random start; ``num_iters`` and ``seed`` are accepted and
+unused.  The subspace is the one the iteration approaches, and decode depends
+only on that subspace (logits equal q . (P k + (I - P) mu), P = R R^T).
+
+``build_rotation`` runs the whole build of kv_pruning_utils.py:105-160 for one
+layer in three kernels: tcgen05 covariance of the visual Keys, Jacobi with the
+centring / query weighting / top-k / delta_mu fused in, and the rotation
+K_vis . R.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional, Tuple
+
+import torch
+
+from rotatek_b200 import _lib
+
+# Same switch as the reference (rotation.py:18, kv_pruning_utils.py:21).
+_ROTATEK_QUERY_AWARE_ACTIVE = bool(int(os.environ.get("ROTATEK_QUERY_AWARE", "1")))
+
+QUERY_WINDOW = 32  # kv_pruning_utils.py:23
+
+_build_ws = {}
+
+
+def _stream(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def power_iteration_gpu(cov: torch.Tensor, k: int, num_iters: int = 5, seed: int = 0) -> torch.Tensor:
+    """Top-k eigenvectors of ``cov`` ([..., D, D]) as columns, [..., D, k], in
+    descending eigenvalue order, each column's largest component positive.
+
+    Drop-in for rotatek.rotation.power_iteration_gpu; ``num_iters`` and ``seed``
+    are ignored (the result is converged, not an iterate)."""
+    del num_iters, seed
+    assert cov.is_cuda
+    d = cov.shape[-1]
+    lead = cov.shape[:-2]
+    mats = cov.reshape(-1, d, d).to(torch.float32).contiguous()
+    vecs = torch.empty(mats.shape[0], d, k, dtype=torch.float32, device=cov.device)
+    lib = _lib.load()
+    D = _lib.describe
+    _lib.check(lib.rtk_eigh_topk(D(mats), k, D(vecs), None, _stream(cov.device)))
+    return vecs.reshape(*lead, d, k).to(cov.dtype)
+
+
+def eigh_topk(cov: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(eigenvalues [..., D] descending, top-k eigenvectors [..., D, k]) of fp32 ``cov``."""
+    _lib.require_cuda(cov)
+    d = cov.shape[-1]
+    lead = cov.shape[:-2]
+    mats = cov.reshape(-1, d, d).to(torch.float32).contiguous()
+    vecs = torch.empty(mats.shape[0], d, k, dtype=torch.float32, device=cov.device)
+    vals = torch.empty(mats.shape[0], d, dtype=torch.float32, device=cov.device)
+    D = _lib.describe
+    _lib.check(_lib.load().rtk_eigh_topk(D(mats), k, D(vecs), D(vals), _stream(cov.device)))
+    return vals.reshape(*lead, d), vecs.reshape(*lead, d, k)
+
+
+def key_covariance(keys: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(sum_s k k^T [B, H, 128, 128] fp32, sum_s k [B, H, 128] fp32) of keys [B, H, S, 128]."""
+    if keys.dim() != 4:
+        raise ValueError("keys must be [B, H, S, D]")
+    _lib.require_cuda(keys)
+    b, h, _, d = keys.shape
+    cov = torch.empty(b, h, d, d, dtype=torch.float32, device=keys.device)
+    ksum = torch.empty(b, h, d, dtype=torch.float32, device=keys.device)
+    D = _lib.describe
+    _lib.check(_lib.load().rtk_key_covariance(D(keys), D(cov), D(ksum), _stream(keys.device)))
+    return cov, ksum
+
+
+def keep_count(head_dim: int, channel_ratio: float) -> int:
+    """Channels kept for a pruning ratio (kv_pruning_utils.py:108)."""
+    return head_dim - min(head_dim, max(0, int(head_dim * channel_ratio)))
+
+
+def build_rotation(keys_vision: torch.Tensor, queries_recent: Optional[torch.Tensor], keep: int,
+                   num_kv_groups: int, query_aware: Optional[bool] = None,
+                   return_eigvals: bool = False):
+    """The RotateK prefill build of one layer.
+
+    keys_vision     [B, H_kv, S_v, D]   visual-span Keys (any strides)
+    queries_recent  [B, H_q, W, D]      the last W (<= 32) queries, or None
+    keep            channels kept (``keep_count(D, channel_ratio)``)
+
+    Returns (kept [B, H_kv, S_v, keep], R_partial [B, H_kv, D, keep],
+    delta_mu [B, H_kv, D], keep_mask [B, H_kv, D] bool) -- the values
+    ``update_rotatek`` returns / stores (kv_pruning_utils.py:152-160), all but
+    the mask in the Keys' dtype; with ``return_eigvals`` also the eigenvalues
+    [B, H_kv, D] (fp32, descending) of the solved matrix."""
+    if keys_vision.dim() != 4:
+        raise ValueError("keys_vision must be [B, H_kv, S_v, D]")
+    if query_aware is None:
+        query_aware = _ROTATEK_QUERY_AWARE_ACTIVE
+    q = queries_recent if query_aware else None
+    _lib.require_cuda(keys_vision, q)
+    b, h, s, d = keys_vision.shape
+    dev = keys_vision.device
+    dt = keys_vision.dtype
+    kept = torch.empty(b, h, s, keep, dtype=dt, device=dev)
+    R = torch.empty(b, h, d, keep, dtype=dt, device=dev)
+    dm = torch.empty(b, h, d, dtype=dt, device=dev)
+    ev = torch.empty(b, h, d, dtype=torch.float32, device=dev) if return_eigvals else None
+    lib = _lib.load()
+    need = lib.rtk_build_rotation_workspace_size(b, h, d)
+    idx = dev.index
+    ws = _build_ws.get(idx)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        _build_ws[idx] = ws
+    D = _lib.describe
+    _lib.check(lib.rtk_build_rotation(D(keys_vision), D(q), num_kv_groups, keep, D(kept), D(R), D(dm),
+                                      D(ev), ctypes.c_void_p(ws.data_ptr()), ws.numel(), _stream(dev)))
+    mask = torch.zeros(b, h, d, dtype=torch.bool, device=dev)
+    mask[..., :keep] = True
+    if return_eigvals:
+        return kept, R, dm, mask, ev
+    return kept, R, dm, mask
+
+
+__all__ = ["_ROTATEK_QUERY_AWARE_ACTIVE", "power_iteration_gpu", "eigh_topk", "key_covariance",
+           "keep_count", "build_rotation"]

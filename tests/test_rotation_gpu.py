@@ -1,0 +1,158 @@
+"""Rotation-builder parity on the GPU.
+
+Oracles: float64 numpy (sum k k^T, LAPACK eigh) and the golden fixtures made
+by running the reference's ChannelPruner.update_rotatek (eigh solver).
+Eigenvectors are compared through projectors P = R R^T (sign- and
+rotation-invariant; decode depends only on P), columns additionally up to
+sign where eigenvalues are separated.
+
+Tolerances (in each test): covariance 1e-5 relative (Frobenius); eigenvalues
+2e-5 of the largest; fp32 subspaces 1e-4 in ||P - P_ref||_F.  bf16 builds:
+the reference rounds its centred Keys and its covariance to bf16
+(kv_pruning_utils.py:113-114), this build accumulates the covariance in fp32.
+So a bf16 build must (a) match the float64 oracle run without those two
+roundings (``round_cov=False``) to 1e-2, and (b) sit no further from the
+reference than that oracle does, plus 1e-2.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import rotation as orot
+from oracle.bf16 import round_bf16
+from rotatek_b200 import rotation as rot, synthetic as syn
+from rotatek_b200.pruner import ChannelPruner, update_rotatek
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def f64(t):
+    return t.detach().float().cpu().numpy().astype(np.float64)
+
+
+@pytest.mark.parametrize("dtype,B,H,S", [
+    (torch.bfloat16, 2, 4, 15360),   # 8 matrices -> 8-CTA clusters, 30 tiles per CTA
+    (torch.bfloat16, 1, 2, 1000),    # ragged last tile
+    (torch.bfloat16, 3, 1, 40),      # fewer tokens than one tile
+    (torch.float16, 2, 2, 777),
+    (torch.bfloat16, 40, 8, 256),    # 320 matrices -> no cluster
+    (torch.float32, 2, 2, 300),      # generic kernel
+])
+def test_key_covariance(dtype, B, H, S):
+    k = syn.lowrank_keys(B, H, S, seed=S + B, device=DEV, dtype=dtype)
+    cov, ksum = rot.key_covariance(k)
+    kk = f64(k)
+    want = np.einsum("bhsd,bhse->bhde", kk, kk)
+    err = np.sqrt(((f64(cov) - want) ** 2).sum(axis=(-1, -2)) / (want ** 2).sum(axis=(-1, -2)))
+    assert err.max() < 1e-5, err.max()
+    np.testing.assert_allclose(f64(ksum), kk.sum(axis=2), rtol=1e-5, atol=1e-3)
+
+
+def test_key_covariance_strided_view():
+    """The visual span is a slice of the full Keys [B, H, S_total, D]."""
+    full = syn.lowrank_keys(2, 4, 64 + 3000 + 100, seed=3, device=DEV, dtype=torch.bfloat16)
+    view = full[:, :, 64:3064]
+    cov, ksum = rot.key_covariance(view)
+    kk = f64(view)
+    want = np.einsum("bhsd,bhse->bhde", kk, kk)
+    assert np.abs(f64(cov) - want).max() <= 1e-5 * np.abs(want).max()
+    np.testing.assert_allclose(f64(ksum), kk.sum(axis=2), rtol=1e-5, atol=1e-3)
+
+
+def _spd(n_mat, seed, decay=0.9):
+    rng = np.random.default_rng(seed)
+    q, _ = np.linalg.qr(rng.standard_normal((n_mat, 128, 128)))
+    lam = decay ** np.arange(128) * rng.uniform(0.5, 2.0, (n_mat, 1))
+    return (q * lam[:, None, :]) @ np.swapaxes(q, -1, -2)
+
+
+@pytest.mark.parametrize("decay", [0.9, 0.97])
+def test_eigh_topk_matches_lapack(decay):
+    mats = _spd(64, seed=int(decay * 100), decay=decay)
+    vals, vecs = rot.eigh_topk(torch.tensor(mats, dtype=torch.float32, device=DEV), 32)
+    w, v = np.linalg.eigh(mats.astype(np.float32).astype(np.float64))
+    w, v = w[:, ::-1], v[:, :, ::-1]
+    np.testing.assert_allclose(f64(vals), w, atol=2e-5 * np.abs(w).max())
+    dist = orot.projector_distance(f64(vecs), v[:, :, :32])
+    assert dist.max() < 1e-4, dist.max()
+    cos = np.abs((f64(vecs) * v[:, :, :32]).sum(axis=1))
+    assert cos.min() > 1 - 1e-4
+    # largest component of every returned column is positive
+    g = f64(vecs)
+    idx = np.abs(g).argmax(axis=1)
+    assert (np.take_along_axis(g, idx[:, None, :], axis=1) > 0).all()
+
+
+def test_power_iteration_gpu_drop_in():
+    cov = torch.tensor(_spd(6, seed=5), dtype=torch.float32, device=DEV).reshape(2, 3, 128, 128)
+    r = rot.power_iteration_gpu(cov, k=32, num_iters=5, seed=0)
+    assert r.shape == (2, 3, 128, 32) and r.dtype == torch.float32
+    eye = torch.eye(32, device=DEV)
+    torch.testing.assert_close(r.transpose(-1, -2) @ r, eye.expand(2, 3, 32, 32), atol=5e-5, rtol=0)
+
+
+@pytest.mark.parametrize("case,inputs", [("cfg1_fp32", "cfg1_fp32"), ("cfg1_fp32_plain", "cfg1_fp32"),
+                                         ("small_bf16", "small_bf16")])
+def test_build_rotation_matches_reference(golden, case, inputs):
+    g, src = golden(case), golden(inputs)
+    dtype = {"float32": torch.float32, "bfloat16": torch.bfloat16}[g["dtype"]]
+    keys = torch.as_tensor(src["keys"]).to(DEV).to(dtype)
+    p, v = g["prompt_len"], g["vision_len"]
+    kv = keys[:, :, p:p + v]
+    qw = torch.as_tensor(src["queries_window"]).to(DEV).to(dtype)
+    keep = orot.keep_count(128, g["ratio"])
+    kept, R, dm, mask = rot.build_rotation(kv, qw, keep, g["num_kv_groups"],
+                                           query_aware=bool(g["query_aware"]))
+    fp32 = dtype == torch.float32
+    np.testing.assert_array_equal(mask.cpu().numpy(), g["keep_mask"])
+    dist = orot.projector_distance(f64(R), g["R_partial"])
+    if fp32:
+        assert dist.max() < 1e-4, dist
+    else:
+        exact = orot.build_rotation(src["keys"][:, :, p:p + v], src["queries_window"], keep,
+                                    g["num_kv_groups"], bool(g["query_aware"]), "bfloat16",
+                                    round_cov=False)
+        assert orot.projector_distance(f64(R), exact.R_partial).max() < 1e-2
+        own = orot.projector_distance(exact.R_partial, g["R_partial"])
+        assert np.all(dist <= own + 1e-2), (dist, own)
+    sgn = np.sign((f64(R) * g["R_partial"]).sum(axis=-2))[:, :, None, :]
+    np.testing.assert_allclose(f64(dm), g["delta_mu"], atol=2e-4 if fp32 else 0.1)
+    scale = np.abs(g["kept"]).max()
+    np.testing.assert_allclose(f64(kept), g["kept"] * sgn, atol=(2e-4 if fp32 else 0.1) * scale)
+
+
+def test_build_rotation_config4_layer():
+    """One layer of BASELINE config 4: B=8, 4 KV heads (G=7), S_v=15360, bf16, keep 32."""
+    B, H, G, S = 8, 4, 7, 15360
+    k = syn.lowrank_keys(B, H, S, seed=44, device=DEV, dtype=torch.bfloat16)
+    q = syn.normal((B, H * G, 32, 128), 45, DEV, torch.bfloat16)
+    kept, R, dm, mask, ev = rot.build_rotation(k, q, 32, G, query_aware=True, return_eigvals=True)
+    ref = orot.build_rotation(f64(k), f64(q), 32, G, query_aware=True, storage="bfloat16",
+                              round_cov=False)
+    dist = orot.projector_distance(f64(R), ref.R_partial)
+    assert dist.max() < 1e-2, dist.max()
+    # eigenvalues of the solved (weighted) matrix, relative to each matrix's largest.
+    # The query group-mean is rounded to bf16 (as the reference does); fp32 here and
+    # float64 in the oracle can land on neighbouring bf16 values (2^-9 apart), which
+    # moves a channel weight and the eigenvalues by up to ~1e-3.
+    err = np.abs(f64(ev)[..., :32] - ref.eigvals[..., :32]) / ref.eigvals[..., :1]
+    assert err.max() < 2e-3, err.max()
+    np.testing.assert_allclose(f64(dm), ref.delta_mu, atol=0.1)
+    # kept is exactly K . R (this build's R) rounded to bf16
+    want = np.asarray(round_bf16(np.einsum("bhsd,bhdk->bhsk", f64(k), f64(R))), dtype=np.float64)
+    err = np.abs(f64(kept) - want)
+    assert np.mean(err == 0) > 0.99 and err.max() <= 2.0 ** -7 * np.abs(want).max()
+    assert mask.sum().item() == B * H * 32
+
+
+def test_pruner_update_rotatek_contract():
+    B, Hq, Hkv, P, V, T = 1, 8, 2, 16, 300, 20
+    pre = syn.make_prefill(B, Hq, Hkv, P, V, T, seed=9, device=DEV, dtype=torch.bfloat16)
+    pr = ChannelPruner(ratio=0.75, prompt_seqlen=P, query_seqlen=T)
+    kept, kp, kt, mask, vals = pr.update_rotatek(pre.keys, pre.queries, pre.values, None, 4)
+    assert kept.shape == (B, Hkv, V, 32) and kp.shape == (B, Hkv, P, 128) and kt.shape == (B, Hkv, T, 128)
+    assert vals is pre.values and mask[..., :32].all() and not mask[..., 32:].any()
+    assert pr.current_rotatek_R_partial.shape == (B, Hkv, 128, 32)
+    assert pr.current_rotatek_delta_mu.shape == (B, Hkv, 128)
+    assert update_rotatek is ChannelPruner.update_rotatek
