@@ -595,7 +595,7 @@ int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_
   jp.evals = eigvals_out ? static_cast<float *>(eigvals_out->data) : nullptr;
   jp.sweeps = sweeps;
   jp.max_sweeps = 15;
-  jp.tol = 1e-7f;
+  jp.tol = 1e-6f;
   e = rtk::launch_jacobi(jp, st);
   if (e != cudaSuccess) return cuda_fail(e, "rotation builder (eigensolver) launch");
 
@@ -652,7 +652,7 @@ int rtk_eigh_topk(const rtk_tensor *cov, int64_t k, const rtk_tensor *vecs_out,
   jp.R_s[0] = vecs_out->stride[0]; jp.R_s[1] = 0; jp.R_s[2] = vecs_out->stride[1]; jp.R_s[3] = vecs_out->stride[2];
   jp.evals = vals_out ? static_cast<float *>(vals_out->data) : nullptr;
   jp.max_sweeps = 15;
-  jp.tol = 1e-7f;
+  jp.tol = 1e-6f;
   const cudaError_t e = rtk::launch_jacobi(jp, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "eigensolver launch");
   return RTK_OK;

@@ -17,12 +17,16 @@
 //             order); delta_mu = mu - (mu R) R^T with that rounded R in fp32
 //             (kv_pruning_utils.py:153-156).
 //
-// One CTA of 512 threads per matrix.  A (fp32, row stride 129) and V^T (fp32,
-// row stride 132) live in shared memory (133 KB).  Per round: 64 threads
-// compute the rotations (symmetric Schur 2x2, Golub & Van Loan 8.4.2); then
-// every thread updates whole 2x2 blocks of A for block pairs (a <= b), writing
-// both the block and its mirror (A' = J^T A J, one load and one store per
-// element), and rotates row pairs of V^T with float4 accesses (V' = V J).
+// One CTA of 512 threads per matrix.  A (fp32, row stride 129) lives in shared
+// memory and only its upper triangle is kept current: element (x, y) is read and
+// written at (min, max), whose bank (x + y) mod 32 is the same either way.  Per
+// round: 64 threads compute the rotations (symmetric Schur 2x2, Golub & Van Loan
+// 8.4.2) and apply them to their own 2x2 diagonal block; then every thread
+// updates its fixed set of off-diagonal 2x2 blocks (a < b) -- one load and one
+// store per element, all loads issued before the stores -- and its 32 entries of
+// V (V' = V J).  V stays in registers: warp w holds rows 8w..8w+7, lane l holds
+// columns l, l+32, l+64, l+96, so the round-r partner column j ^ r is one
+// __shfl_xor away (in register u ^ (r >> 5)).
 #include "builder.h"
 #include "common.cuh"
 
@@ -32,22 +36,115 @@ namespace {
 constexpr int kN = 128;
 constexpr int kPairs = kN / 2;
 constexpr int kThreads = 512;
-constexpr int kAS = kN + 1;            // A row stride: bank = (row + col) mod 32
-constexpr int kVS = kN + 4;            // V^T row stride (float4-aligned rows)
-constexpr int kBlocks = kPairs * (kPairs + 1) / 2;  // 2x2 blocks with a <= b
+constexpr int kAS = kN + 1;            // A row stride: bank of (x, y) = (x + y) mod 32
+constexpr int kVS = kN + 4;            // V^T row stride (epilogue)
+constexpr int kOffBlocks = kPairs * (kPairs - 1) / 2;             // 2x2 blocks with a < b
+constexpr int kItems = (kOffBlocks + kThreads - 1) / kThreads;    // blocks per thread
+constexpr int kRowsPerWarp = kN / (kThreads / 32);                // V rows per warp
 
 struct JSmem {
   float A[kN * kAS];
   float VT[kN * kVS];
-  float c[kPairs], s[kPairs], t[kPairs];
-  int pidx[kPairs];
-  unsigned int blk[kBlocks];           // (a | b << 8) for a <= b
+  float2 cs[kPairs];                   // (c, s) of this round's rotations
   float vec[kN];                       // mean, then query norms, then eigenvalues
   float vec2[kN];
   int rank[kN];
   float red[2][kThreads / 32];
   int flag;
 };
+
+// k with a 0 bit inserted at position h: the smaller index of pair k in a round
+// whose highest set bit is h.
+__device__ __forceinline__ int insert0(int k, int h) {
+  return ((k >> h) << (h + 1)) | (k & ((1 << h) - 1));
+}
+
+// Offset of A(x, y), x != y, in upper-triangle storage.
+__device__ __forceinline__ int upper(int x, int y) { return x < y ? x * kAS + y : y * kAS + x; }
+
+// Rounds r = 32 * RH + rl of one sweep (rl from 1 when RH == 0).  Round r
+// rotates every index pair (p, p ^ r), p with bit h = msb(r) clear.
+template <int RH>
+__device__ __forceinline__ void jacobi_rounds(float *A, float2 *cs, float (&v)[kRowsPerWarp][4],
+                                              const int (&blk)[kItems], int tid, int lane) {
+#pragma unroll 1
+  for (int rl = (RH == 0 ? 1 : 0); rl < 32; ++rl) {
+    const int r = RH * 32 + rl;
+    const int h = 31 - __clz(r);
+    // ---- rotations of this round; each thread also finishes its diagonal block
+    if (tid < kPairs) {
+      const int pp = insert0(tid, h), qq = pp ^ r;
+      const float app = A[pp * kAS + pp], aqq = A[qq * kAS + qq], apq = A[pp * kAS + qq];
+      float c = 1.f, s = 0.f, t = 0.f;
+      if (apq != 0.f && fabsf(apq) > 1e-12f * (fabsf(app) + fabsf(aqq))) {
+        const float theta = (aqq - app) / (2.f * apq);
+        t = copysignf(1.f, theta) / (fabsf(theta) + sqrtf(fmaf(theta, theta, 1.f)));
+        c = 1.f / sqrtf(fmaf(t, t, 1.f));
+        s = t * c;
+      }
+      cs[tid] = make_float2(c, s);
+      A[pp * kAS + pp] = app - t * apq;
+      A[qq * kAS + qq] = aqq + t * apq;
+      A[pp * kAS + qq] = 0.f;
+    }
+    __syncthreads();
+    // ---- A <- J^T A J on this thread's off-diagonal blocks (pa < pb < qb always)
+    {
+      int off[kItems][4];
+      float x[kItems][4];
+      float2 ja[kItems], jb[kItems];
+#pragma unroll
+      for (int u = 0; u < kItems; ++u) {
+        if (blk[u] < 0) continue;
+        const int a = blk[u] & 0xff, b = blk[u] >> 8;
+        const int pa = insert0(a, h), qa = pa ^ r, pb = insert0(b, h), qb = pb ^ r;
+        off[u][0] = pa * kAS + pb;
+        off[u][1] = pa * kAS + qb;
+        off[u][2] = upper(qa, pb);
+        off[u][3] = upper(qa, qb);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[u][e] = A[off[u][e]];
+        ja[u] = cs[a];
+        jb[u] = cs[b];
+      }
+#pragma unroll
+      for (int u = 0; u < kItems; ++u) {
+        if (blk[u] < 0) continue;
+        const float ca = ja[u].x, sa = ja[u].y, cb = jb[u].x, sb = jb[u].y;
+        // rows (J_a^T): p' = c p - s q, q' = s p + c q
+        const float y00 = ca * x[u][0] - sa * x[u][2], y01 = ca * x[u][1] - sa * x[u][3];
+        const float y10 = sa * x[u][0] + ca * x[u][2], y11 = sa * x[u][1] + ca * x[u][3];
+        // columns (J_b)
+        A[off[u][0]] = y00 * cb - y01 * sb;
+        A[off[u][1]] = y00 * sb + y01 * cb;
+        A[off[u][2]] = y10 * cb - y11 * sb;
+        A[off[u][3]] = y10 * sb + y11 * cb;
+      }
+    }
+    // ---- V <- V J on this thread's 8 x 4 entries
+    {
+      float cu[4], su[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = lane + 32 * u;
+        const bool qside = (j >> h) & 1;
+        const int pj = qside ? (j ^ r) : j;
+        const float2 t = cs[((pj >> (h + 1)) << h) | (pj & ((1 << h) - 1))];
+        cu[u] = t.x;
+        su[u] = qside ? t.y : -t.y;       // p' = c p - s q,  q' = c q + s p
+      }
+#pragma unroll
+      for (int i = 0; i < kRowsPerWarp; ++i) {
+        float part[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) part[u] = __shfl_xor_sync(0xffffffffu, v[i][u ^ RH], rl);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[i][u] = fmaf(su[u], part[u], cu[u] * v[i][u]);
+      }
+    }
+    __syncthreads();
+  }
+}
 
 __device__ __forceinline__ float load_any(const void *p, int dtype, long long i) {
   if (dtype == 1) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i]);
@@ -89,13 +186,6 @@ __global__ void __launch_bounds__(kThreads, 1) jacobi_kernel(const JacobiParams 
   float *VT = sm.VT;
 
   // ---------------------------------------------------------------- prologue
-  for (int i = tid; i < kBlocks; i += kThreads) {
-    int bb = static_cast<int>((sqrtf(8.f * i + 1.f) - 1.f) * 0.5f);
-    while (bb * (bb + 1) / 2 > i) --bb;
-    while ((bb + 1) * (bb + 2) / 2 <= i) ++bb;
-    const int aa = i - bb * (bb + 1) / 2;
-    sm.blk[i] = static_cast<unsigned>(aa) | (static_cast<unsigned>(bb) << 8);
-  }
   const float *C0 = p.cov + (long long)m * kN * kN;
   if (tid < kN) {
     float mu = 0.f;
@@ -173,100 +263,51 @@ __global__ void __launch_bounds__(kThreads, 1) jacobi_kernel(const JacobiParams 
     const float ridge = fmaxf(1e-4f * block_sum(dsum, sm.red[0], tid) / kN, 1e-6f);
     if (tid < kN) A[tid * kAS + tid] += ridge;
   }
-  for (int e = tid; e < kN * kN; e += kThreads) {
-    const int i = e / kN, j = e % kN;
-    VT[i * kVS + j] = (i == j) ? 1.f : 0.f;
-  }
   __syncthreads();
 
   // ---------------------------------------------------------------- sweeps
+  // This thread's off-diagonal blocks: items i = tid + 512 u of the strict upper
+  // triangle of the 64 x 64 block grid, folded so rows g and 62 - g share 64
+  // items (consecutive lanes take consecutive b: conflict-free banks).
+  int blk[kItems];
+#pragma unroll
+  for (int u = 0; u < kItems; ++u) {
+    const int i = tid + kThreads * u;
+    const int g = i >> 6, o = i & 63;
+    const int a = (o < 63 - g) ? g : 62 - g;
+    const int bb = (o < 63 - g) ? g + 1 + o : o;
+    blk[u] = (i < kOffBlocks) ? (a | (bb << 8)) : -1;
+  }
+  const int warp = tid >> 5, lane = tid & 31;
+  float v[kRowsPerWarp][4];
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i)
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[i][u] = (warp * kRowsPerWarp + i == lane + 32 * u) ? 1.f : 0.f;
+
   int sweep = 0;
   for (; sweep < p.max_sweeps; ++sweep) {
     float off = 0.f, dia = 0.f;
     for (int e = tid; e < kN * kN; e += kThreads) {
       const int i = e / kN, j = e % kN;
-      const float v = A[i * kAS + j];
-      if (i == j) dia = fmaf(v, v, dia);
-      else off = fmaf(v, v, off);
+      const float x = A[i * kAS + j];
+      if (i == j) dia = fmaf(x, x, dia);
+      else if (i < j) off = fmaf(x, x, off);
     }
-    off = block_sum(off, sm.red[0], tid);
+    off = 2.f * block_sum(off, sm.red[0], tid);
     dia = block_sum(dia, sm.red[1], tid);
     if (off <= p.tol * p.tol * dia) break;
-
-    for (int r = 1; r < kN; ++r) {
-      const int hbit = 31 - __clz(r);
-      // ---- rotations of this round (pairs k: p = k with a 0 inserted at bit hbit)
-      if (tid < kPairs) {
-        const int k = tid;
-        const int pp = ((k >> hbit) << (hbit + 1)) | (k & ((1 << hbit) - 1));
-        const int qq = pp ^ r;
-        const float app = A[pp * kAS + pp], aqq = A[qq * kAS + qq], apq = A[pp * kAS + qq];
-        float c = 1.f, s = 0.f, t = 0.f;
-        if (apq != 0.f && fabsf(apq) > 1e-12f * (fabsf(app) + fabsf(aqq))) {
-          const float theta = (aqq - app) / (2.f * apq);
-          t = copysignf(1.f, theta) / (fabsf(theta) + sqrtf(fmaf(theta, theta, 1.f)));
-          c = 1.f / sqrtf(fmaf(t, t, 1.f));
-          s = t * c;
-        }
-        sm.c[k] = c;
-        sm.s[k] = s;
-        sm.t[k] = t;
-        sm.pidx[k] = pp;
-      }
-      __syncthreads();
-      // ---- A <- J^T A J, one 2x2 block pair per item
-      for (int i = tid; i < kBlocks; i += kThreads) {
-        const unsigned ab = sm.blk[i];
-        const int a = ab & 0xff, bb = ab >> 8;
-        const int pa = sm.pidx[a], qa = pa ^ r, pb = sm.pidx[bb], qb = pb ^ r;
-        const float ca = sm.c[a], sa = sm.s[a], cb = sm.c[bb], sb = sm.s[bb];
-        if (a == bb) {
-          const float app = A[pa * kAS + pa], aqq = A[qa * kAS + qa], apq = A[pa * kAS + qa];
-          const float t = sm.t[a];
-          A[pa * kAS + pa] = app - t * apq;
-          A[qa * kAS + qa] = aqq + t * apq;
-          A[pa * kAS + qa] = 0.f;
-          A[qa * kAS + pa] = 0.f;
-        } else {
-          const float x00 = A[pa * kAS + pb], x01 = A[pa * kAS + qb];
-          const float x10 = A[qa * kAS + pb], x11 = A[qa * kAS + qb];
-          // rows (J_a^T): p' = c p - s q, q' = s p + c q
-          const float y00 = ca * x00 - sa * x10, y01 = ca * x01 - sa * x11;
-          const float y10 = sa * x00 + ca * x10, y11 = sa * x01 + ca * x11;
-          // columns (J_b)
-          const float z00 = y00 * cb - y01 * sb, z01 = y00 * sb + y01 * cb;
-          const float z10 = y10 * cb - y11 * sb, z11 = y10 * sb + y11 * cb;
-          A[pa * kAS + pb] = z00;
-          A[pa * kAS + qb] = z01;
-          A[qa * kAS + pb] = z10;
-          A[qa * kAS + qb] = z11;
-          A[pb * kAS + pa] = z00;
-          A[qb * kAS + pa] = z01;
-          A[pb * kAS + qa] = z10;
-          A[qb * kAS + qa] = z11;
-        }
-      }
-      // ---- V <- V J: rows p, q of V^T; 8 threads per pair, 16 columns each
-      {
-        const int k = tid >> 3, part = tid & 7;
-        const int pp = sm.pidx[k], qq = pp ^ r;
-        const float c = sm.c[k], s = sm.s[k];
-        if (s != 0.f) {
-          float4 *vp = reinterpret_cast<float4 *>(VT + pp * kVS + part * 16);
-          float4 *vq = reinterpret_cast<float4 *>(VT + qq * kVS + part * 16);
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float4 a4 = vp[u], b4 = vq[u];
-            vp[u] = make_float4(c * a4.x - s * b4.x, c * a4.y - s * b4.y, c * a4.z - s * b4.z,
-                                c * a4.w - s * b4.w);
-            vq[u] = make_float4(s * a4.x + c * b4.x, s * a4.y + c * b4.y, s * a4.z + c * b4.z,
-                                s * a4.w + c * b4.w);
-          }
-        }
-      }
-      __syncthreads();
-    }
+    jacobi_rounds<0>(A, sm.cs, v, blk, tid, lane);
+    jacobi_rounds<1>(A, sm.cs, v, blk, tid, lane);
+    jacobi_rounds<2>(A, sm.cs, v, blk, tid, lane);
+    jacobi_rounds<3>(A, sm.cs, v, blk, tid, lane);
   }
+  // eigenvector j (column j of V) -> row j of V^T
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i)
+#pragma unroll
+    for (int u = 0; u < 4; ++u) VT[(lane + 32 * u) * kVS + warp * kRowsPerWarp + i] = v[i][u];
+  __syncthreads();
   if (tid == 0 && p.sweeps != nullptr) p.sweeps[m] = sweep;
 
   // ---------------------------------------------------------------- epilogue
@@ -286,7 +327,6 @@ __global__ void __launch_bounds__(kThreads, 1) jacobi_kernel(const JacobiParams 
   __syncthreads();
   // selected eigenvectors: column rank r < keep is V[:, i] = VT[i][:]; sign so
   // that the largest-magnitude component is positive; round to the dtype
-  const int warp = tid >> 5, lane = tid & 31;
   for (int i = warp; i < kN; i += kThreads / 32) {
     const int r = sm.rank[i];
     if (r >= p.keep) continue;
