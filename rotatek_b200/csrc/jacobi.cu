@@ -62,88 +62,136 @@ __device__ __forceinline__ int insert0(int k, int h) {
 // Offset of A(x, y), x != y, in upper-triangle storage.
 __device__ __forceinline__ int upper(int x, int y) { return x < y ? x * kAS + y : y * kAS + x; }
 
-// Rounds r = 32 * RH + rl of one sweep (rl from 1 when RH == 0).  Round r
-// rotates every index pair (p, p ^ r), p with bit h = msb(r) clear.
-template <int RH>
-__device__ __forceinline__ void jacobi_rounds(float *A, float2 *cs, float (&v)[kRowsPerWarp][4],
-                                              const int (&blk)[kItems], int tid, int lane) {
-#pragma unroll 1
-  for (int rl = (RH == 0 ? 1 : 0); rl < 32; ++rl) {
-    const int r = RH * 32 + rl;
-    const int h = 31 - __clz(r);
-    // ---- rotations of this round; each thread also finishes its diagonal block
-    if (tid < kPairs) {
-      const int pp = insert0(tid, h), qq = pp ^ r;
-      const float app = A[pp * kAS + pp], aqq = A[qq * kAS + qq], apq = A[pp * kAS + qq];
-      float c = 1.f, s = 0.f, t = 0.f;
-      if (apq != 0.f && fabsf(apq) > 1e-12f * (fabsf(app) + fabsf(aqq))) {
-        const float theta = (aqq - app) / (2.f * apq);
-        t = copysignf(1.f, theta) / (fabsf(theta) + sqrtf(fmaf(theta, theta, 1.f)));
-        c = 1.f / sqrtf(fmaf(t, t, 1.f));
-        s = t * c;
-      }
-      cs[tid] = make_float2(c, s);
-      A[pp * kAS + pp] = app - t * apq;
-      A[qq * kAS + qq] = aqq + t * apq;
-      A[pp * kAS + qq] = 0.f;
-    }
-    __syncthreads();
-    // ---- A <- J^T A J on this thread's off-diagonal blocks (pa < pb < qb always)
-    {
-      int off[kItems][4];
-      float x[kItems][4];
-      float2 ja[kItems], jb[kItems];
+// Per-thread state of the sweep loop.
+struct Sweep {
+  float v[kRowsPerWarp][4];  // V rows 8w..8w+7, columns lane + 32 u
+  float cu[4], su[4];        // V coefficients of the previous round, per column
+  int blk[kItems];           // this thread's off-diagonal blocks a | b << 8 (-1: none)
+  int pab[kItems];           // their smaller indices pa | pb << 8 for the current h
+  int pp;                    // rotation threads: smaller index of pair `tid`
+};
+
+// Start of a run of rounds sharing h = msb(r): the smaller pair indices.
+__device__ __forceinline__ void segment(Sweep &w, int h, int tid) {
 #pragma unroll
-      for (int u = 0; u < kItems; ++u) {
-        if (blk[u] < 0) continue;
-        const int a = blk[u] & 0xff, b = blk[u] >> 8;
-        const int pa = insert0(a, h), qa = pa ^ r, pb = insert0(b, h), qb = pb ^ r;
-        off[u][0] = pa * kAS + pb;
-        off[u][1] = pa * kAS + qb;
-        off[u][2] = upper(qa, pb);
-        off[u][3] = upper(qa, qb);
+  for (int u = 0; u < kItems; ++u)
+    w.pab[u] = insert0(w.blk[u] & 0xff, h) | (insert0((w.blk[u] >> 8) & 0xff, h) << 8);
+  w.pp = insert0(tid & (kPairs - 1), h);
+}
+
+// V <- V J for the previous round (RHP = its r >> 5, rl = its r & 31), with the
+// coefficients loaded during that round.
+template <int RHP>
+__device__ __forceinline__ void v_apply(Sweep &w, int rl) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) x[u][e] = A[off[u][e]];
-        ja[u] = cs[a];
-        jb[u] = cs[b];
-      }
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    float part[4];
 #pragma unroll
-      for (int u = 0; u < kItems; ++u) {
-        if (blk[u] < 0) continue;
-        const float ca = ja[u].x, sa = ja[u].y, cb = jb[u].x, sb = jb[u].y;
-        // rows (J_a^T): p' = c p - s q, q' = s p + c q
-        const float y00 = ca * x[u][0] - sa * x[u][2], y01 = ca * x[u][1] - sa * x[u][3];
-        const float y10 = sa * x[u][0] + ca * x[u][2], y11 = sa * x[u][1] + ca * x[u][3];
-        // columns (J_b)
-        A[off[u][0]] = y00 * cb - y01 * sb;
-        A[off[u][1]] = y00 * sb + y01 * cb;
-        A[off[u][2]] = y10 * cb - y11 * sb;
-        A[off[u][3]] = y10 * sb + y11 * cb;
-      }
-    }
-    // ---- V <- V J on this thread's 8 x 4 entries
-    {
-      float cu[4], su[4];
+    for (int u = 0; u < 4; ++u) part[u] = __shfl_xor_sync(0xffffffffu, w.v[i][u ^ RHP], rl);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = lane + 32 * u;
-        const bool qside = (j >> h) & 1;
-        const int pj = qside ? (j ^ r) : j;
-        const float2 t = cs[((pj >> (h + 1)) << h) | (pj & ((1 << h) - 1))];
-        cu[u] = t.x;
-        su[u] = qside ? t.y : -t.y;       // p' = c p - s q,  q' = c q + s p
-      }
-#pragma unroll
-      for (int i = 0; i < kRowsPerWarp; ++i) {
-        float part[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) part[u] = __shfl_xor_sync(0xffffffffu, v[i][u ^ RH], rl);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) v[i][u] = fmaf(su[u], part[u], cu[u] * v[i][u]);
-      }
-    }
-    __syncthreads();
+    for (int u = 0; u < 4; ++u) w.v[i][u] = fmaf(w.su[u], part[u], w.cu[u] * w.v[i][u]);
   }
+}
+
+// One round r (h = msb(r)).  Rotation threads compute (c, s) and finish their
+// diagonal block while every warp applies the previous round (r - 1, or 127 of
+// the previous sweep when r = 1; RHP = its r >> 5) to V; then all threads update
+// their off-diagonal blocks of A and fetch this round's V coefficients.
+template <int RHP>
+__device__ __forceinline__ void round_step(float *A, float2 *cs, Sweep &w, int r, int h,
+                                           bool have_prev, int tid, int lane) {
+  if (tid < kPairs) {
+    const int pp = w.pp, qq = pp ^ r;
+    const float app = A[pp * kAS + pp], aqq = A[qq * kAS + qq], apq = A[pp * kAS + qq];
+    float c = 1.f, s = 0.f, t = 0.f;
+    if (apq != 0.f && fabsf(apq) > 1e-12f * (fabsf(app) + fabsf(aqq))) {
+      // t = sign(theta) / (|theta| + sqrt(theta^2 + 1)), theta = (aqq - app) / (2 apq);
+      // |t| <= 1.  c = 1 / sqrt(1 + t^2) from rsqrt plus one Newton step.
+      const float theta = __fdividef(aqq - app, 2.f * apq);
+      t = copysignf(__fdividef(1.f, fabsf(theta) + sqrtf(fmaf(theta, theta, 1.f))), theta);
+      const float x = fmaf(t, t, 1.f);
+      const float c0 = rsqrtf(x);
+      c = c0 * fmaf(-0.5f * x * c0, c0, 1.5f);
+      s = t * c;
+    }
+    cs[tid] = make_float2(c, s);
+    A[pp * kAS + pp] = app - t * apq;
+    A[qq * kAS + qq] = aqq + t * apq;
+    A[pp * kAS + qq] = 0.f;
+  }
+  if (have_prev) v_apply<RHP>(w, (r == 1 ? 127 : r - 1) & 31);
+  __syncthreads();
+  // ---- A <- J^T A J on this thread's off-diagonal blocks (pa < pb < qb always),
+  // two blocks at a time with their loads issued before their stores
+#pragma unroll
+  for (int u0 = 0; u0 < kItems; u0 += 2) {
+    int off[2][4];
+    float x[2][4];
+    float2 ja[2], jb[2];
+#pragma unroll
+    for (int d = 0; d < 2; ++d) {
+      const int u = u0 + d;
+      if (w.blk[u] < 0) continue;
+      const int pa = w.pab[u] & 0xff, pb = w.pab[u] >> 8, qa = pa ^ r, qb = pb ^ r;
+      off[d][0] = pa * kAS + pb;
+      off[d][1] = pa * kAS + qb;
+      off[d][2] = upper(qa, pb);
+      off[d][3] = upper(qa, qb);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[d][e] = A[off[d][e]];
+      ja[d] = cs[w.blk[u] & 0xff];
+      jb[d] = cs[w.blk[u] >> 8];
+    }
+#pragma unroll
+    for (int d = 0; d < 2; ++d) {
+      if (w.blk[u0 + d] < 0) continue;
+      const float ca = ja[d].x, sa = ja[d].y, cb = jb[d].x, sb = jb[d].y;
+      // rows (J_a^T): p' = c p - s q, q' = s p + c q
+      const float y00 = ca * x[d][0] - sa * x[d][2], y01 = ca * x[d][1] - sa * x[d][3];
+      const float y10 = sa * x[d][0] + ca * x[d][2], y11 = sa * x[d][1] + ca * x[d][3];
+      // columns (J_b)
+      A[off[d][0]] = y00 * cb - y01 * sb;
+      A[off[d][1]] = y00 * sb + y01 * cb;
+      A[off[d][2]] = y10 * cb - y11 * sb;
+      A[off[d][3]] = y10 * sb + y11 * cb;
+    }
+  }
+  // ---- this round's V coefficients for columns lane + 32 u (applied next round)
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int j = lane + 32 * u;
+    const bool qside = (j >> h) & 1;
+    const int pj = qside ? (j ^ r) : j;
+    const float2 t = cs[((pj >> (h + 1)) << h) | (pj & ((1 << h) - 1))];
+    w.cu[u] = t.x;
+    w.su[u] = qside ? t.y : -t.y;       // p' = c p - s q,  q' = c q + s p
+  }
+  __syncthreads();
+}
+
+// One sweep: rounds r = 1..127 in runs of equal h = msb(r).  Leaves round 127's
+// V update pending.
+__device__ __forceinline__ void sweep_rounds(float *A, float2 *cs, Sweep &w, bool have_prev, int tid,
+                                             int lane) {
+  segment(w, 0, tid);
+  round_step<3>(A, cs, w, 1, 0, have_prev, tid, lane);
+#pragma unroll 1
+  for (int h = 1; h < 5; ++h) {
+    segment(w, h, tid);
+#pragma unroll 1
+    for (int r = 1 << h; r < (2 << h); ++r) round_step<0>(A, cs, w, r, h, true, tid, lane);
+  }
+  segment(w, 5, tid);
+  round_step<0>(A, cs, w, 32, 5, true, tid, lane);
+#pragma unroll 1
+  for (int r = 33; r < 64; ++r) round_step<1>(A, cs, w, r, 5, true, tid, lane);
+  segment(w, 6, tid);
+  round_step<1>(A, cs, w, 64, 6, true, tid, lane);
+#pragma unroll 1
+  for (int r = 65; r < 96; ++r) round_step<2>(A, cs, w, r, 6, true, tid, lane);
+  round_step<2>(A, cs, w, 96, 6, true, tid, lane);
+#pragma unroll 1
+  for (int r = 97; r < 128; ++r) round_step<3>(A, cs, w, r, 6, true, tid, lane);
 }
 
 __device__ __forceinline__ float load_any(const void *p, int dtype, long long i) {
@@ -269,21 +317,20 @@ __global__ void __launch_bounds__(kThreads, 1) jacobi_kernel(const JacobiParams 
   // This thread's off-diagonal blocks: items i = tid + 512 u of the strict upper
   // triangle of the 64 x 64 block grid, folded so rows g and 62 - g share 64
   // items (consecutive lanes take consecutive b: conflict-free banks).
-  int blk[kItems];
+  Sweep w;
 #pragma unroll
   for (int u = 0; u < kItems; ++u) {
     const int i = tid + kThreads * u;
     const int g = i >> 6, o = i & 63;
     const int a = (o < 63 - g) ? g : 62 - g;
     const int bb = (o < 63 - g) ? g + 1 + o : o;
-    blk[u] = (i < kOffBlocks) ? (a | (bb << 8)) : -1;
+    w.blk[u] = (i < kOffBlocks) ? (a | (bb << 8)) : -1;
   }
   const int warp = tid >> 5, lane = tid & 31;
-  float v[kRowsPerWarp][4];
 #pragma unroll
   for (int i = 0; i < kRowsPerWarp; ++i)
 #pragma unroll
-    for (int u = 0; u < 4; ++u) v[i][u] = (warp * kRowsPerWarp + i == lane + 32 * u) ? 1.f : 0.f;
+    for (int u = 0; u < 4; ++u) w.v[i][u] = (warp * kRowsPerWarp + i == lane + 32 * u) ? 1.f : 0.f;
 
   int sweep = 0;
   for (; sweep < p.max_sweeps; ++sweep) {
@@ -297,16 +344,14 @@ __global__ void __launch_bounds__(kThreads, 1) jacobi_kernel(const JacobiParams 
     off = 2.f * block_sum(off, sm.red[0], tid);
     dia = block_sum(dia, sm.red[1], tid);
     if (off <= p.tol * p.tol * dia) break;
-    jacobi_rounds<0>(A, sm.cs, v, blk, tid, lane);
-    jacobi_rounds<1>(A, sm.cs, v, blk, tid, lane);
-    jacobi_rounds<2>(A, sm.cs, v, blk, tid, lane);
-    jacobi_rounds<3>(A, sm.cs, v, blk, tid, lane);
+    sweep_rounds(A, sm.cs, w, sweep > 0, tid, lane);
   }
+  if (sweep > 0) v_apply<3>(w, 31);   // round 127 of the last sweep
   // eigenvector j (column j of V) -> row j of V^T
 #pragma unroll
   for (int i = 0; i < kRowsPerWarp; ++i)
 #pragma unroll
-    for (int u = 0; u < 4; ++u) VT[(lane + 32 * u) * kVS + warp * kRowsPerWarp + i] = v[i][u];
+    for (int u = 0; u < 4; ++u) VT[(lane + 32 * u) * kVS + warp * kRowsPerWarp + i] = w.v[i][u];
   __syncthreads();
   if (tid == 0 && p.sweeps != nullptr) p.sweeps[m] = sweep;
 
