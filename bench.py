@@ -32,7 +32,6 @@ import math
 import os
 import statistics
 import sys
-import threading
 import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
@@ -77,60 +76,79 @@ def ncu_traffic_per_launch():
     return None
 
 
+_SAMPLER_CHILD = r"""
+import json, select, sys, time
+import pynvml as nv
+REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+           0x4: "sw_power_cap", 0x1: "gpu_idle", 0x80: "hw_power_brake_slowdown"}
+nv.nvmlInit()
+uuid, index = sys.argv[1], int(sys.argv[2])
+try:
+    h = nv.nvmlDeviceGetHandleByUUID(uuid)
+except Exception:
+    h = nv.nvmlDeviceGetHandleByIndex(index)
+out = {"max": nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM), "mhz": [], "reasons": []}
+print("ready", flush=True)
+seen = set()
+while True:
+    out["mhz"].append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+    mask = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+    seen.update(name for bit, name in REASONS.items() if mask & bit)
+    if select.select([sys.stdin], [], [], 0.001)[0]:
+        break
+out["reasons"] = sorted(seen)
+print(json.dumps(out), flush=True)
+"""
+
+
 class ClockSampler:
-    """Polls NVML (what nvidia-smi reads) for SM clock and clock-event reasons
-    while running; reads only, changes nothing."""
+    """SM clock and clock-event reasons of one GPU, polled through NVML (what
+    nvidia-smi reads) by a child process for as long as the context is open, so
+    that sampling neither waits for nor delays the launching thread.  Reads only;
+    changes no GPU setting."""
 
-    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
-               0x4: "sw_power_cap", 0x1: "gpu_idle", 0x80: "hw_power_brake_slowdown"}
-
-    def __init__(self, index: int, period_s: float = 0.002):
-        self.index, self.period = index, period_s
-        self.samples, self.reasons = [], set()
-        self.max_mhz = None
-        self._stop = threading.Event()
-        self._thread = None
-        self.ok = False
+    def __init__(self, device: int):
+        import subprocess
+        self.proc, self.result = None, None
         try:
-            import pynvml
-            pynvml.nvmlInit()
-            self.nvml = pynvml
-            self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
-            self.ok = True
+            props = torch.cuda.get_device_properties(device)
+            uuid = "GPU-" + str(props.uuid)
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_CHILD, uuid, str(device)],
+                                         stdin=subprocess.PIPE, stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            if self.proc.stdout.readline().strip() != "ready":
+                self._close()
         except Exception:
-            self.nvml = None
+            self._close()
 
-    def _run(self):
-        nv = self.nvml
-        while not self._stop.is_set():
+    def _close(self):
+        if self.proc is not None:
             try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
-                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
-                for bit, name in self.REASONS.items():
-                    if mask & bit:
-                        self.reasons.add(name)
+                self.proc.kill()
+                self.proc.wait(timeout=10)
             except Exception:
                 pass
-            time.sleep(self.period)
+        self.proc = None
 
     def __enter__(self):
-        if self.ok:
-            self._thread = threading.Thread(target=self._run, daemon=True)
-            self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self._thread is not None:
-            self._stop.set()
-            self._thread.join()
+        if self.proc is None:
+            return
+        try:
+            out, _ = self.proc.communicate("stop\n", timeout=30)
+            self.result = json.loads(out.strip().splitlines()[-1])
+        except Exception:
+            self._close()
 
     def summary(self):
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
-                    "samples": 0}
-        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+        r = self.result
+        if not r or not r["mhz"]:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(r["mhz"]), "sm_max_mhz": r["max"],
+                "sm_min_mhz": min(r["mhz"]),
+                "reasons": [x for x in r["reasons"] if x != "gpu_idle"], "samples": len(r["mhz"])}
 
 
 def dist_env():
@@ -293,6 +311,15 @@ def run_ours(args):
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         e2e_ms = float(t.item())
     barrier()
+    clocks = sampler.summary()
+    if pg is not None:
+        per_rank = [None] * world
+        pg.all_gather_object(per_rank, clocks)
+        mhz = [c["sm_mhz"] for c in per_rank if c["sm_mhz"] is not None]
+        clocks = {"sm_mhz": statistics.median(mhz) if mhz else None,
+                  "sm_max_mhz": per_rank[0]["sm_max_mhz"],
+                  "reasons": sorted({x for c in per_rank for x in c["reasons"]}),
+                  "samples": sum(c["samples"] for c in per_rank), "per_rank": per_rank}
 
     if rank == 0:
         peak, peak_kind = load_peak_hbm()
@@ -317,7 +344,7 @@ def run_ours(args):
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps},
             "gpu_launches": args.steps,
-            "clocks": sampler.summary(),
+            "clocks": clocks,
             "device_status": status,
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -334,7 +361,7 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=10)
