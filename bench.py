@@ -166,11 +166,22 @@ def make_inputs(device, dtype=torch.bfloat16, seed=0, batch=None):
                            keep=CFG["keep"], seed=seed, device=device, dtype=dtype)
 
 
+def use_all_host_threads() -> int:
+    """The CPU arms use every host thread this process may run on (torchrun sets
+    OMP_NUM_THREADS=1 for its ranks; only rank 0 does CPU work here)."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
 def cpu_baseline_sample(target_s: float = 12.0):
     """The reference's math, eager PyTorch on the host CPU (all threads), on a
     batch sample; returns (us per full batch-32 step, sample description, threads)."""
     from oracle.eager_torch import rotatek_decode_eager
-    threads = torch.get_num_threads()
+    threads = use_all_host_threads()
     b = 1
     d = make_inputs("cpu", batch=b, seed=1)
     kw = d.as_kwargs()
@@ -194,7 +205,7 @@ def run_reference(args):
     if rank != 0:
         return 0
     from oracle.eager_torch import rotatek_decode_eager
-    threads = torch.get_num_threads()
+    threads = use_all_host_threads()
     b = 1
     d = make_inputs("cpu", batch=b, seed=1)
     kw = d.as_kwargs()
