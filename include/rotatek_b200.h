@@ -146,16 +146,22 @@ int rtk_full_channel_decode(const rtk_tensor *q, const rtk_tensor *k, const rtk_
 int rtk_key_covariance(const rtk_tensor *keys, const rtk_tensor *cov_out, const rtk_tensor *ksum_out,
                        void *stream);
 
+/* Bytes of workspace rtk_eigh_topk needs for n matrices (no zeroing required):
+ * the solver's rotation log, about 0.93 MiB per matrix. */
+size_t rtk_eigh_topk_workspace_size(int64_t n);
+
 /* Top-k eigenvectors of symmetric matrices, descending eigenvalue, each
  * column's largest-magnitude component positive (batched 128 x 128 Jacobi).
  * Replaces rotatek.rotation.power_iteration_gpu (rotatek/rotation.py:68-91),
  * which returns an unconverged basis of approximately the same subspace.
  *   cov [N, 128, 128] f32 contiguous, vecs_out [N, 128, k] f32,
- *   vals_out [N, 128] f32 contiguous (all eigenvalues, descending), nullable. */
+ *   vals_out [N, 128] f32 contiguous (all eigenvalues, descending), nullable,
+ *   workspace of rtk_eigh_topk_workspace_size(N) bytes. */
 int rtk_eigh_topk(const rtk_tensor *cov, int64_t k, const rtk_tensor *vecs_out,
-                  const rtk_tensor *vals_out, void *stream);
+                  const rtk_tensor *vals_out, void *workspace, size_t workspace_bytes, void *stream);
 
-/* Bytes of workspace rtk_build_rotation needs (no zeroing required). */
+/* Bytes of workspace rtk_build_rotation needs (no zeroing required): the
+ * fp32 sums plus the eigensolver's rotation log, about 1 MiB per (b, h). */
 size_t rtk_build_rotation_workspace_size(int64_t batch, int64_t kv_heads, int64_t head_dim);
 
 /* The RotateK prefill build for one layer: replaces the body of

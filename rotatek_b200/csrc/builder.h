@@ -4,6 +4,7 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <stddef.h>
 #include <stdint.h>
 
 namespace rtk {
@@ -25,6 +26,11 @@ cudaError_t launch_cov_tc(int dtype_is_bf16, const CUtensorMap &keys_map, const 
                           cudaStream_t stream);
 cudaError_t launch_cov_simt(const CovParams &p, cudaStream_t stream);
 
+// Jacobi rotation log: the (c, s) of every rotation of every sweep, per matrix,
+// so that only the selected eigenvectors are ever formed.
+constexpr int kJacobiMaxSweeps = 15;
+constexpr size_t kJacobiLogBytes = sizeof(float2) * kJacobiMaxSweeps * (kBuildDim - 1) * (kBuildDim / 2);
+
 // Eigensolver: per matrix, the covariance (centred if ksum is given), optionally
 // weighted by the query norms, diagonalised by cyclic Jacobi; the top `keep`
 // eigenvectors (descending eigenvalue) go out as R, plus delta_mu.
@@ -43,6 +49,7 @@ struct JacobiParams {
   void *dm; long long dm_s[3];                    // [B, H, 128] (R's dtype), nullable
   float *evals;                                   // [nmat][128] descending, nullable
   int *sweeps;                                    // [nmat] sweeps used, nullable
+  float2 *rot_log;                                // [nmat][kJacobiLogBytes / 8] scratch
   int max_sweeps;
   float tol;                                      // stop when off(A) <= tol * ||diag(A)||
 };

@@ -527,7 +527,12 @@ int rtk_key_covariance(const rtk_tensor *keys, const rtk_tensor *cov_out, const 
 size_t rtk_build_rotation_workspace_size(int64_t batch, int64_t kv_heads, int64_t head_dim) {
   const int64_t n = batch * kv_heads;
   return align_up((size_t)n * head_dim * head_dim * sizeof(float)) +
-         align_up((size_t)n * head_dim * sizeof(float)) + align_up((size_t)n * sizeof(int));
+         align_up((size_t)n * head_dim * sizeof(float)) + align_up((size_t)n * sizeof(int)) +
+         rtk_eigh_topk_workspace_size(n);
+}
+
+size_t rtk_eigh_topk_workspace_size(int64_t n) {
+  return n > 0 ? align_up((size_t)n * rtk::kJacobiLogBytes) : 0;
 }
 
 int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_t num_kv_groups,
@@ -567,6 +572,8 @@ int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_
   float *ksum = reinterpret_cast<float *>(ws + align_up((size_t)B * H * D * D * sizeof(float)));
   int *sweeps = reinterpret_cast<int *>(reinterpret_cast<unsigned char *>(ksum) +
                                         align_up((size_t)B * H * D * sizeof(float)));
+  float2 *rot_log = reinterpret_cast<float2 *>(reinterpret_cast<unsigned char *>(sweeps) +
+                                               align_up((size_t)B * H * sizeof(int)));
   const int device = current_device();
   const int dt = keys->dtype;
   // ---- covariance + channel sums
@@ -594,7 +601,8 @@ int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_
   }
   jp.evals = eigvals_out ? static_cast<float *>(eigvals_out->data) : nullptr;
   jp.sweeps = sweeps;
-  jp.max_sweeps = 15;
+  jp.rot_log = rot_log;
+  jp.max_sweeps = rtk::kJacobiMaxSweeps;
   jp.tol = 1e-6f;
   e = rtk::launch_jacobi(jp, st);
   if (e != cudaSuccess) return cuda_fail(e, "rotation builder (eigensolver) launch");
@@ -626,7 +634,7 @@ int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_
 }
 
 int rtk_eigh_topk(const rtk_tensor *cov, int64_t k, const rtk_tensor *vecs_out,
-                  const rtk_tensor *vals_out, void *stream) {
+                  const rtk_tensor *vals_out, void *workspace, size_t workspace_bytes, void *stream) {
   g_last_error.clear();
   if (cov == nullptr || cov->ndim != 3 || cov->dtype != RTK_F32)
     return fail(RTK_ERR_INVALID, "cov must be a float32 [N, D, D]");
@@ -642,6 +650,9 @@ int rtk_eigh_topk(const rtk_tensor *cov, int64_t k, const rtk_tensor *vecs_out,
                               vals_out->stride[1] != 1 || vals_out->stride[0] != D))
     return fail(RTK_ERR_INVALID, "vals_out must be a contiguous float32 [N, D]");
   if (N == 0) return RTK_OK;
+  const size_t need = rtk_eigh_topk_workspace_size(N);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, need);
   rtk::JacobiParams jp;
   std::memset(&jp, 0, sizeof(jp));
   jp.nmat = (int)N; jp.heads = 1;
@@ -651,7 +662,8 @@ int rtk_eigh_topk(const rtk_tensor *cov, int64_t k, const rtk_tensor *vecs_out,
   jp.R = vecs_out->data; jp.R_dtype = RTK_F32;
   jp.R_s[0] = vecs_out->stride[0]; jp.R_s[1] = 0; jp.R_s[2] = vecs_out->stride[1]; jp.R_s[3] = vecs_out->stride[2];
   jp.evals = vals_out ? static_cast<float *>(vals_out->data) : nullptr;
-  jp.max_sweeps = 15;
+  jp.rot_log = static_cast<float2 *>(workspace);
+  jp.max_sweeps = rtk::kJacobiMaxSweeps;
   jp.tol = 1e-6f;
   const cudaError_t e = rtk::launch_jacobi(jp, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "eigensolver launch");

@@ -17,16 +17,22 @@
 //             order); delta_mu = mu - (mu R) R^T with that rounded R in fp32
 //             (kv_pruning_utils.py:153-156).
 //
-// One CTA of 512 threads per matrix.  A (fp32, row stride 129) lives in shared
-// memory and only its upper triangle is kept current: element (x, y) is read and
-// written at (min, max), whose bank (x + y) mod 32 is the same either way.  Per
-// round: 64 threads compute the rotations (symmetric Schur 2x2, Golub & Van Loan
-// 8.4.2) and apply them to their own 2x2 diagonal block; then every thread
+// One CTA of 512 threads per matrix, two CTAs per SM.  A (fp32, row stride
+// 129) lives in shared memory and only its upper triangle is kept current:
+// element (x, y) is read and written at (min, max), whose bank (x + y) mod 32 is
+// the same either way.  Per round: 64 threads compute the rotations (symmetric
+// Schur 2x2, Golub & Van Loan 8.4.2), apply them to their own 2x2 diagonal block
+// and append them to a per-matrix log in global memory; then every thread
 // updates its fixed set of off-diagonal 2x2 blocks (a < b) -- one load and one
-// store per element, all loads issued before the stores -- and its 32 entries of
-// V (V' = V J).  V stays in registers: warp w holds rows 8w..8w+7, lane l holds
-// columns l, l+32, l+64, l+96, so the round-r partner column j ^ r is one
-// __shfl_xor away (in register u ^ (r >> 5)).
+// store per element, loads issued before stores.
+//
+// The eigenvector matrix V = J_1 J_2 ... J_n is never formed.  Once the
+// eigenvalues are known, only the `keep` columns that are needed, V e_i for the
+// selected i, are computed by applying the logged rounds in reverse to those
+// unit vectors (X <- J_t X, t = n..1).  X (128 x keep) stays in registers: each
+// warp owns whole columns, lane l holds rows l, l+32, l+64, l+96, so the round-r
+// partner row j ^ r is one __shfl_xor away (in register u ^ (r >> 5)); the log is
+// streamed through shared memory with cp.async, 16 rounds per stage.
 #include "builder.h"
 #include "common.cuh"
 
@@ -35,22 +41,38 @@ namespace {
 
 constexpr int kN = 128;
 constexpr int kPairs = kN / 2;
+constexpr int kRounds = kN - 1;        // rounds per sweep
 constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
 constexpr int kAS = kN + 1;            // A row stride: bank of (x, y) = (x + y) mod 32
-constexpr int kVS = kN + 4;            // V^T row stride (epilogue)
+constexpr int kXS = kN;                // row stride of X^T (selected eigenvectors, one per row)
 constexpr int kOffBlocks = kPairs * (kPairs - 1) / 2;             // 2x2 blocks with a < b
 constexpr int kItems = (kOffBlocks + kThreads - 1) / kThreads;    // blocks per thread
-constexpr int kRowsPerWarp = kN / (kThreads / 32);                // V rows per warp
+constexpr int kChunk = 16;             // logged rounds per shared-memory stage
+static_assert(kJacobiLogBytes == sizeof(float2) * kJacobiMaxSweeps * kRounds * kPairs, "log size");
+
+// The matrix, then the staged log, then X^T: each is dead before the next.
+// (With keep > 64 the pass for columns 64.. writes X^T rows 64.. before the
+// pass for columns 0..63 stages again: staging must stay below row 64.)
+struct BackStage {
+  float2 raw[2][kChunk][kPairs];       // logged (c, s), double-buffered
+  float2 coef[kChunk][kN];             // per-row coefficients of the current chunk
+};
+union JWork {
+  float A[kN * kAS];
+  BackStage bt;
+  float XT[kN * kXS];
+};
+static_assert(sizeof(BackStage) <= sizeof(float) * 64 * kXS, "staging must stay below X^T row 64");
 
 struct JSmem {
-  float A[kN * kAS];
-  float VT[kN * kVS];
+  JWork w;
   float2 cs[kPairs];                   // (c, s) of this round's rotations
-  float vec[kN];                       // mean, then query norms, then eigenvalues
-  float vec2[kN];
-  int rank[kN];
-  float red[2][kThreads / 32];
-  int flag;
+  float vec[kN];                       // fp32 mean
+  float vec2[kN];                      // query norms, then eigenvalues, then mu . R[:, c]
+  int rank[kN];                        // descending rank of eigenvalue i
+  int sel[kN];                         // sel[c]: the eigenvalue of rank c
+  float red[2][kWarps];
 };
 
 // k with a 0 bit inserted at position h: the smaller index of pair k in a round
@@ -62,10 +84,16 @@ __device__ __forceinline__ int insert0(int k, int h) {
 // Offset of A(x, y), x != y, in upper-triangle storage.
 __device__ __forceinline__ int upper(int x, int y) { return x < y ? x * kAS + y : y * kAS + x; }
 
+// Pair index of row/column j in round r (h = msb(r)): j or j ^ r, whichever has
+// bit h clear, with bit h removed.  `qside` tells which of the two j is.
+__device__ __forceinline__ int pair_of(int j, int r, int h, bool &qside) {
+  qside = (j >> h) & 1;
+  const int pj = qside ? (j ^ r) : j;
+  return ((pj >> (h + 1)) << h) | (pj & ((1 << h) - 1));
+}
+
 // Per-thread state of the sweep loop.
 struct Sweep {
-  float v[kRowsPerWarp][4];  // V rows 8w..8w+7, columns lane + 32 u
-  float cu[4], su[4];        // V coefficients of the previous round, per column
   int blk[kItems];           // this thread's off-diagonal blocks a | b << 8 (-1: none)
   int pab[kItems];           // their smaller indices pa | pb << 8 for the current h
   int pp;                    // rotation threads: smaller index of pair `tid`
@@ -79,27 +107,10 @@ __device__ __forceinline__ void segment(Sweep &w, int h, int tid) {
   w.pp = insert0(tid & (kPairs - 1), h);
 }
 
-// V <- V J for the previous round (RHP = its r >> 5, rl = its r & 31), with the
-// coefficients loaded during that round.
-template <int RHP>
-__device__ __forceinline__ void v_apply(Sweep &w, int rl) {
-#pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i) {
-    float part[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) part[u] = __shfl_xor_sync(0xffffffffu, w.v[i][u ^ RHP], rl);
-#pragma unroll
-    for (int u = 0; u < 4; ++u) w.v[i][u] = fmaf(w.su[u], part[u], w.cu[u] * w.v[i][u]);
-  }
-}
-
-// One round r (h = msb(r)).  Rotation threads compute (c, s) and finish their
-// diagonal block while every warp applies the previous round (r - 1, or 127 of
-// the previous sweep when r = 1; RHP = its r >> 5) to V; then all threads update
-// their off-diagonal blocks of A and fetch this round's V coefficients.
-template <int RHP>
-__device__ __forceinline__ void round_step(float *A, float2 *cs, Sweep &w, int r, int h,
-                                           bool have_prev, int tid, int lane) {
+// One round r: rotation threads compute (c, s), log them to `log` [64] and
+// finish their diagonal block; then all threads update their off-diagonal blocks.
+__device__ __forceinline__ void round_step(float *A, float2 *cs, float2 *log, const Sweep &w, int r,
+                                           int tid) {
   if (tid < kPairs) {
     const int pp = w.pp, qq = pp ^ r;
     const float app = A[pp * kAS + pp], aqq = A[qq * kAS + qq], apq = A[pp * kAS + qq];
@@ -114,12 +125,13 @@ __device__ __forceinline__ void round_step(float *A, float2 *cs, Sweep &w, int r
       c = c0 * fmaf(-0.5f * x * c0, c0, 1.5f);
       s = t * c;
     }
-    cs[tid] = make_float2(c, s);
+    const float2 j = make_float2(c, s);
+    cs[tid] = j;
+    log[tid] = j;
     A[pp * kAS + pp] = app - t * apq;
     A[qq * kAS + qq] = aqq + t * apq;
     A[pp * kAS + qq] = 0.f;
   }
-  if (have_prev) v_apply<RHP>(w, (r == 1 ? 127 : r - 1) & 31);
   __syncthreads();
   // ---- A <- J^T A J on this thread's off-diagonal blocks (pa < pb < qb always),
   // two blocks at a time with their loads issued before their stores
@@ -156,42 +168,116 @@ __device__ __forceinline__ void round_step(float *A, float2 *cs, Sweep &w, int r
       A[off[d][3]] = y10 * sb + y11 * cb;
     }
   }
-  // ---- this round's V coefficients for columns lane + 32 u (applied next round)
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int j = lane + 32 * u;
-    const bool qside = (j >> h) & 1;
-    const int pj = qside ? (j ^ r) : j;
-    const float2 t = cs[((pj >> (h + 1)) << h) | (pj & ((1 << h) - 1))];
-    w.cu[u] = t.x;
-    w.su[u] = qside ? t.y : -t.y;       // p' = c p - s q,  q' = c q + s p
-  }
   __syncthreads();
 }
 
-// One sweep: rounds r = 1..127 in runs of equal h = msb(r).  Leaves round 127's
-// V update pending.
-__device__ __forceinline__ void sweep_rounds(float *A, float2 *cs, Sweep &w, bool have_prev, int tid,
-                                             int lane) {
-  segment(w, 0, tid);
-  round_step<3>(A, cs, w, 1, 0, have_prev, tid, lane);
+// One sweep (rounds 1..127 in runs of equal h = msb(r)); round r logs to
+// log[(r - 1) * 64 ...].
+__device__ __forceinline__ void sweep_rounds(float *A, float2 *cs, float2 *log, Sweep &w, int tid) {
 #pragma unroll 1
-  for (int h = 1; h < 5; ++h) {
+  for (int h = 0; h < 7; ++h) {
     segment(w, h, tid);
 #pragma unroll 1
-    for (int r = 1 << h; r < (2 << h); ++r) round_step<0>(A, cs, w, r, h, true, tid, lane);
+    for (int r = 1 << h; r < (2 << h); ++r) round_step(A, cs, log + (r - 1) * kPairs, w, r, tid);
   }
-  segment(w, 5, tid);
-  round_step<0>(A, cs, w, 32, 5, true, tid, lane);
+}
+
+// X <- J X for one round (RH = r >> 5, rl = r & 31): row j mixes with row j ^ r,
+// p-side j' = c j + s (j ^ r), q-side j' = c j - s (j ^ r) (J[p][q] = s).
+template <int RH, int CPW>
+__device__ __forceinline__ void back_round(float (&x)[4][CPW], const float (&cu)[4], const float (&su)[4],
+                                           int rl) {
+#pragma unroll
+  for (int t = 0; t < CPW; ++t) {
+    float part[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) part[u] = __shfl_xor_sync(0xffffffffu, x[u ^ RH][t], rl);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) x[u][t] = fmaf(su[u], part[u], cu[u] * x[u][t]);
+  }
+}
+
+// Columns c0 .. c0 + 16 CPW - 1 (those below keep) of X = J_1 ... J_n
+// [e_sel[0] ... e_sel[keep-1]] from the n logged rounds, written to X^T (row c =
+// selected eigenvector c, unnormalised).  CPW = columns per warp.  The log is
+// staged kChunk rounds at a time (cp.async, double-buffered) and expanded once
+// per CTA into per-row coefficients (c, +-s), so that the per-warp loop is
+// loads, shuffles and FMAs only.
+template <int CPW>
+__device__ __forceinline__ void back_transform(JSmem &sm, const float2 *log, int nrounds, int c0,
+                                               int keep, int tid) {
+  const int warp = tid >> 5, lane = tid & 31;
+  const int cw = c0 + warp * CPW;            // this warp's first column
+  const bool active = cw < keep;
+  float x[4][CPW];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int t = 0; t < CPW; ++t) {
+      const int c = cw + t;
+      x[u][t] = (c < keep && sm.sel[c] == lane + 32 * u) ? 1.f : 0.f;
+    }
+  // chunk ci: rounds [lo, hi), hi = nrounds - ci * kChunk, into raw[ci & 1]
+  const int nchunks = (nrounds + kChunk - 1) / kChunk;
+  auto issue = [&](int ci) {
+    const int hi = nrounds - ci * kChunk, lo = hi > kChunk ? hi - kChunk : 0;
+    const char *src = reinterpret_cast<const char *>(log + (long long)lo * kPairs);
+    char *dst = reinterpret_cast<char *>(&sm.w.bt.raw[ci & 1][0][0]);
+    const int n16 = (hi - lo) * kPairs * static_cast<int>(sizeof(float2)) / 16;
+    for (int e = tid; e < n16; e += kThreads) cp_async_16(dst + 16 * e, src + 16 * e);
+    cp_async_commit();
+  };
+  if (nchunks > 0) issue(0);
 #pragma unroll 1
-  for (int r = 33; r < 64; ++r) round_step<1>(A, cs, w, r, 5, true, tid, lane);
-  segment(w, 6, tid);
-  round_step<1>(A, cs, w, 64, 6, true, tid, lane);
+  for (int ci = 0; ci < nchunks; ++ci) {
+    if (ci + 1 < nchunks) {
+      issue(ci + 1);
+      cp_async_wait_group<1>();
+    } else {
+      cp_async_wait_group<0>();
+    }
+    __syncthreads();
+    const int hi = nrounds - ci * kChunk, lo = hi > kChunk ? hi - kChunk : 0;
+    // expand: coef[n - lo][j] = (c, s) of row j's pair, s negated on the q side
+    // (X <- J X: p' = c p + s q, q' = c q - s p)
+    for (int e = tid; e < (hi - lo) * kN; e += kThreads) {
+      const int nl = e / kN, j = e % kN;
+      const int r = (lo + nl) % kRounds + 1, h = 31 - __clz(r);
+      bool qside;
+      const float2 cs = sm.w.bt.raw[ci & 1][nl][pair_of(j, r, h, qside)];
+      sm.w.bt.coef[nl][j] = make_float2(cs.x, qside ? -cs.y : cs.y);
+    }
+    __syncthreads();
+    if (active) {
 #pragma unroll 1
-  for (int r = 65; r < 96; ++r) round_step<2>(A, cs, w, r, 6, true, tid, lane);
-  round_step<2>(A, cs, w, 96, 6, true, tid, lane);
-#pragma unroll 1
-  for (int r = 97; r < 128; ++r) round_step<3>(A, cs, w, r, 6, true, tid, lane);
+      for (int n = hi - 1; n >= lo; --n) {
+        const int r = n % kRounds + 1;
+        const float2 *cf = sm.w.bt.coef[n - lo];
+        float cu[4], su[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float2 j = cf[lane + 32 * u];
+          cu[u] = j.x;
+          su[u] = j.y;
+        }
+        switch (r >> 5) {
+          case 0: back_round<0, CPW>(x, cu, su, r & 31); break;
+          case 1: back_round<1, CPW>(x, cu, su, r & 31); break;
+          case 2: back_round<2, CPW>(x, cu, su, r & 31); break;
+          default: back_round<3, CPW>(x, cu, su, r & 31); break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (active) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int t = 0; t < CPW; ++t)
+        if (cw + t < keep) sm.w.XT[(cw + t) * kXS + lane + 32 * u] = x[u][t];
+  }
+  __syncthreads();
 }
 
 __device__ __forceinline__ float load_any(const void *p, int dtype, long long i) {
@@ -224,14 +310,13 @@ __device__ __forceinline__ float block_sum(float v, float *red, int tid) {
   return tot;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) jacobi_kernel(const JacobiParams p) {
+__global__ void __launch_bounds__(kThreads, 2) jacobi_kernel(const JacobiParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   JSmem &sm = *reinterpret_cast<JSmem *>(smem_raw);
   const int tid = threadIdx.x;
   const int m = blockIdx.x;
   const int b = m / p.heads, h = m % p.heads;
-  float *A = sm.A;
-  float *VT = sm.VT;
+  float *A = sm.w.A;
 
   // ---------------------------------------------------------------- prologue
   const float *C0 = p.cov + (long long)m * kN * kN;
@@ -316,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) jacobi_kernel(const JacobiParams 
   // ---------------------------------------------------------------- sweeps
   // This thread's off-diagonal blocks: items i = tid + 512 u of the strict upper
   // triangle of the 64 x 64 block grid, folded so rows g and 62 - g share 64
-  // items (consecutive lanes take consecutive b: conflict-free banks).
+  // items (consecutive lanes take consecutive b).
   Sweep w;
 #pragma unroll
   for (int u = 0; u < kItems; ++u) {
@@ -326,14 +411,10 @@ __global__ void __launch_bounds__(kThreads, 1) jacobi_kernel(const JacobiParams 
     const int bb = (o < 63 - g) ? g + 1 + o : o;
     w.blk[u] = (i < kOffBlocks) ? (a | (bb << 8)) : -1;
   }
-  const int warp = tid >> 5, lane = tid & 31;
-#pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i)
-#pragma unroll
-    for (int u = 0; u < 4; ++u) w.v[i][u] = (warp * kRowsPerWarp + i == lane + 32 * u) ? 1.f : 0.f;
-
+  float2 *log = p.rot_log + (long long)m * (kJacobiMaxSweeps * kRounds * kPairs);
+  const int max_sweeps = p.max_sweeps < kJacobiMaxSweeps ? p.max_sweeps : kJacobiMaxSweeps;
   int sweep = 0;
-  for (; sweep < p.max_sweeps; ++sweep) {
+  for (; sweep < max_sweeps; ++sweep) {
     float off = 0.f, dia = 0.f;
     for (int e = tid; e < kN * kN; e += kThreads) {
       const int i = e / kN, j = e % kN;
@@ -344,19 +425,12 @@ __global__ void __launch_bounds__(kThreads, 1) jacobi_kernel(const JacobiParams 
     off = 2.f * block_sum(off, sm.red[0], tid);
     dia = block_sum(dia, sm.red[1], tid);
     if (off <= p.tol * p.tol * dia) break;
-    sweep_rounds(A, sm.cs, w, sweep > 0, tid, lane);
+    sweep_rounds(A, sm.cs, log + (long long)sweep * kRounds * kPairs, w, tid);
   }
-  if (sweep > 0) v_apply<3>(w, 31);   // round 127 of the last sweep
-  // eigenvector j (column j of V) -> row j of V^T
-#pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i)
-#pragma unroll
-    for (int u = 0; u < 4; ++u) VT[(lane + 32 * u) * kVS + warp * kRowsPerWarp + i] = w.v[i][u];
-  __syncthreads();
   if (tid == 0 && p.sweeps != nullptr) p.sweeps[m] = sweep;
 
   // ---------------------------------------------------------------- epilogue
-  // eigenvalues and their descending rank
+  // eigenvalues, their descending ranks and the selected indices
   if (tid < kN) sm.vec2[tid] = A[tid * kAS + tid];
   __syncthreads();
   if (tid < kN) {
@@ -367,17 +441,32 @@ __global__ void __launch_bounds__(kThreads, 1) jacobi_kernel(const JacobiParams 
       r += (y > x) || (y == x && e < tid);
     }
     sm.rank[tid] = r;
+    sm.sel[r] = tid;
     if (p.evals != nullptr) p.evals[(long long)m * kN + r] = x;
   }
   __syncthreads();
-  // selected eigenvectors: column rank r < keep is V[:, i] = VT[i][:]; sign so
-  // that the largest-magnitude component is positive; round to the dtype
-  for (int i = warp; i < kN; i += kThreads / 32) {
-    const int r = sm.rank[i];
-    if (r >= p.keep) continue;
-    float best = 0.f, nrm = 0.f;
-    for (int d = lane; d < kN; d += 32) {
-      const float v = VT[i * kVS + d];
+  // the selected eigenvectors (A is dead from here on)
+  const int nrounds = sweep * kRounds;
+  if (p.keep <= kWarps) {
+    back_transform<1>(sm, log, nrounds, 0, p.keep, tid);
+  } else if (p.keep <= 2 * kWarps) {
+    back_transform<2>(sm, log, nrounds, 0, p.keep, tid);
+  } else {
+    // at most 64 columns per pass (8 per warp would not fit two CTAs' registers
+    // per SM); columns 64.. first, since their X^T rows lie above the staging
+    if (p.keep > 4 * kWarps) back_transform<4>(sm, log, nrounds, 4 * kWarps, p.keep, tid);
+    back_transform<4>(sm, log, nrounds, 0, p.keep, tid);
+  }
+  // unit length (rounding drift over ~10^3 rotations), largest component
+  // positive, rounded to the output dtype; then mu . R[:, c] with that R
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int c = warp; c < p.keep; c += kWarps) {
+    float *xr = sm.w.XT + c * kXS;
+    float vals[4], best = 0.f, nrm = 0.f;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float v = xr[lane + 32 * u];
+      vals[u] = v;
       nrm = fmaf(v, v, nrm);
       if (fabsf(v) > fabsf(best)) best = v;
     }
@@ -387,39 +476,34 @@ __global__ void __launch_bounds__(kThreads, 1) jacobi_kernel(const JacobiParams 
       if (fabsf(o) > fabsf(best) || (fabsf(o) == fabsf(best) && o > best)) best = o;
       nrm += __shfl_xor_sync(0xffffffffu, nrm, off);
     }
-    // unit length (rounding drift over ~10^3 rotations) and a fixed sign
     const float scale = (best < 0.f ? -1.f : 1.f) / sqrtf(nrm);
-    for (int d = lane; d < kN; d += 32) {
-      const float v = round_to(scale * VT[i * kVS + d], p.R_dtype);
-      VT[i * kVS + d] = v;
+    float pr = 0.f;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int d = lane + 32 * u;
+      const float v = round_to(scale * vals[u], p.R_dtype);
+      xr[d] = v;
       store_any(p.R, p.R_dtype,
-                b * p.R_s[0] + (long long)h * p.R_s[1] + (long long)d * p.R_s[2] + (long long)r * p.R_s[3], v);
+                b * p.R_s[0] + (long long)h * p.R_s[1] + (long long)d * p.R_s[2] + (long long)c * p.R_s[3], v);
+      pr = fmaf(sm.vec[d], v, pr);
     }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) pr += __shfl_xor_sync(0xffffffffu, pr, off);
+    if (lane == 0) sm.vec2[c] = pr;
   }
   __syncthreads();
-  if (p.dm != nullptr) {
-    // proj[r] = mu . R[:, r]  (kept columns only), then delta_mu = mu - sum_r proj[r] R[:, r]
-    if (tid < kN) {
-      const int r = sm.rank[tid];
-      float pr = 0.f;
-      if (r < p.keep)
-        for (int d = 0; d < kN; ++d) pr = fmaf(sm.vec[d], VT[tid * kVS + d], pr);
-      sm.vec2[tid] = pr;
-    }
-    __syncthreads();
-    if (tid < kN) {
-      float acc = 0.f;
-      for (int i = 0; i < kN; ++i)
-        if (sm.rank[i] < p.keep) acc = fmaf(sm.vec2[i], VT[i * kVS + tid], acc);
-      store_any(p.dm, p.R_dtype, b * p.dm_s[0] + (long long)h * p.dm_s[1] + tid * p.dm_s[2],
-                sm.vec[tid] - acc);
-    }
+  if (p.dm != nullptr && tid < kN) {
+    // delta_mu = mu - sum_c (mu . R[:, c]) R[:, c]
+    float acc = 0.f;
+    for (int c = 0; c < p.keep; ++c) acc = fmaf(sm.vec2[c], sm.w.XT[c * kXS + tid], acc);
+    store_any(p.dm, p.R_dtype, b * p.dm_s[0] + (long long)h * p.dm_s[1] + tid * p.dm_s[2], sm.vec[tid] - acc);
   }
 }
 
 }  // namespace
 
 cudaError_t launch_jacobi(const JacobiParams &p, cudaStream_t stream) {
+  if (p.rot_log == nullptr) return cudaErrorInvalidValue;
   const int smem = static_cast<int>(sizeof(JSmem));
   cudaError_t err = cudaFuncSetAttribute(jacobi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (err != cudaSuccess) return err;

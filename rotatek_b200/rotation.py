@@ -36,6 +36,25 @@ def _stream(device) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+def _workspace(device: torch.device, need: int) -> torch.Tensor:
+    """A per-device scratch buffer of at least ``need`` bytes, reused across calls
+    on the current stream (no zeroing required by the builder kernels)."""
+    idx = device.index
+    ws = _build_ws.get(idx)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
+        _build_ws[idx] = ws
+    return ws
+
+
+def _eigh(mats: torch.Tensor, k: int, vecs: torch.Tensor, vals: Optional[torch.Tensor]) -> None:
+    lib = _lib.load()
+    ws = _workspace(mats.device, lib.rtk_eigh_topk_workspace_size(mats.shape[0]))
+    D = _lib.describe
+    _lib.check(lib.rtk_eigh_topk(D(mats), k, D(vecs), D(vals), ctypes.c_void_p(ws.data_ptr()), ws.numel(),
+                                 _stream(mats.device)))
+
+
 def power_iteration_gpu(cov: torch.Tensor, k: int, num_iters: int = 5, seed: int = 0) -> torch.Tensor:
     """Top-k eigenvectors of ``cov`` ([..., D, D]) as columns, [..., D, k], in
     descending eigenvalue order, each column's largest component positive.
@@ -48,9 +67,7 @@ def power_iteration_gpu(cov: torch.Tensor, k: int, num_iters: int = 5, seed: int
     lead = cov.shape[:-2]
     mats = cov.reshape(-1, d, d).to(torch.float32).contiguous()
     vecs = torch.empty(mats.shape[0], d, k, dtype=torch.float32, device=cov.device)
-    lib = _lib.load()
-    D = _lib.describe
-    _lib.check(lib.rtk_eigh_topk(D(mats), k, D(vecs), None, _stream(cov.device)))
+    _eigh(mats, k, vecs, None)
     return vecs.reshape(*lead, d, k).to(cov.dtype)
 
 
@@ -62,8 +79,7 @@ def eigh_topk(cov: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
     mats = cov.reshape(-1, d, d).to(torch.float32).contiguous()
     vecs = torch.empty(mats.shape[0], d, k, dtype=torch.float32, device=cov.device)
     vals = torch.empty(mats.shape[0], d, dtype=torch.float32, device=cov.device)
-    D = _lib.describe
-    _lib.check(_lib.load().rtk_eigh_topk(D(mats), k, D(vecs), D(vals), _stream(cov.device)))
+    _eigh(mats, k, vecs, vals)
     return vals.reshape(*lead, d), vecs.reshape(*lead, d, k)
 
 
@@ -113,12 +129,7 @@ def build_rotation(keys_vision: torch.Tensor, queries_recent: Optional[torch.Ten
     dm = torch.empty(b, h, d, dtype=dt, device=dev)
     ev = torch.empty(b, h, d, dtype=torch.float32, device=dev) if return_eigvals else None
     lib = _lib.load()
-    need = lib.rtk_build_rotation_workspace_size(b, h, d)
-    idx = dev.index
-    ws = _build_ws.get(idx)
-    if ws is None or ws.numel() < need:
-        ws = torch.empty(need, dtype=torch.uint8, device=dev)
-        _build_ws[idx] = ws
+    ws = _workspace(dev, lib.rtk_build_rotation_workspace_size(b, h, d))
     D = _lib.describe
     _lib.check(lib.rtk_build_rotation(D(keys_vision), D(q), num_kv_groups, keep, D(kept), D(R), D(dm),
                                       D(ev), ctypes.c_void_p(ws.data_ptr()), ws.numel(), _stream(dev)))

@@ -84,6 +84,27 @@ def test_eigh_topk_matches_lapack(decay):
     assert (np.take_along_axis(g, idx[:, None, :], axis=1) > 0).all()
 
 
+@pytest.mark.parametrize("k", [1, 16, 33, 64, 65, 96, 128])
+def test_eigh_topk_every_width(k):
+    """Each eigenvector-width path (16, 32, 64 columns per pass; two passes above
+    64) on spectra spaced 1/128 apart, where fp32 pins every eigenvector."""
+    rng = np.random.default_rng(k)
+    q, _ = np.linalg.qr(rng.standard_normal((6, 128, 128)))
+    lam = np.linspace(2.0, 1.0, 128)[None, :] * rng.uniform(0.5, 2.0, (6, 1))
+    mats = (q * lam[:, None, :]) @ np.swapaxes(q, -1, -2)
+    vals, vecs = rot.eigh_topk(torch.tensor(mats, dtype=torch.float32, device=DEV), k)
+    w, v = np.linalg.eigh(mats.astype(np.float32).astype(np.float64))
+    w, v = w[:, ::-1], v[:, :, ::-1]
+    np.testing.assert_allclose(f64(vals), w, atol=2e-5 * np.abs(w).max())
+    g = f64(vecs)
+    cos = np.abs((g * v[:, :, :k]).sum(axis=1))
+    assert cos.min() > 1 - 1e-4, cos.min()
+    gram = np.swapaxes(g, -1, -2) @ g
+    assert np.abs(gram - np.eye(k)).max() < 5e-5
+    idx = np.abs(g).argmax(axis=1)
+    assert (np.take_along_axis(g, idx[:, None, :], axis=1) > 0).all()
+
+
 def test_power_iteration_gpu_drop_in():
     cov = torch.tensor(_spd(6, seed=5), dtype=torch.float32, device=DEV).reshape(2, 3, 128, 128)
     r = rot.power_iteration_gpu(cov, k=32, num_iters=5, seed=0)
@@ -107,19 +128,33 @@ def test_build_rotation_matches_reference(golden, case, inputs):
     fp32 = dtype == torch.float32
     np.testing.assert_array_equal(mask.cpu().numpy(), g["keep_mask"])
     dist = orot.projector_distance(f64(R), g["R_partial"])
+    exact = orot.build_rotation(src["keys"][:, :, p:p + v], src["queries_window"], keep,
+                                g["num_kv_groups"], bool(g["query_aware"]), g["dtype"],
+                                round_cov=fp32)
     if fp32:
         assert dist.max() < 1e-4, dist
     else:
-        exact = orot.build_rotation(src["keys"][:, :, p:p + v], src["queries_window"], keep,
-                                    g["num_kv_groups"], bool(g["query_aware"]), "bfloat16",
-                                    round_cov=False)
         assert orot.projector_distance(f64(R), exact.R_partial).max() < 1e-2
         own = orot.projector_distance(exact.R_partial, g["R_partial"])
         assert np.all(dist <= own + 1e-2), (dist, own)
-    sgn = np.sign((f64(R) * g["R_partial"]).sum(axis=-2))[:, :, None, :]
     np.testing.assert_allclose(f64(dm), g["delta_mu"], atol=2e-4 if fp32 else 0.1)
-    scale = np.abs(g["kept"]).max()
-    np.testing.assert_allclose(f64(kept), g["kept"] * sgn, atol=(2e-4 if fp32 else 0.1) * scale)
+    # kept = K_vis . R.  Decode depends on span(R) only, and inside the kept span
+    # eigenvectors of nearly equal eigenvalues are not determined (cfg1 has two
+    # kept eigenvalues 6e-5 apart; the reference's own fp32 columns are up to
+    # ~7e-4 rad from float64 there).  So: kept against the reference's kept
+    # re-expressed in this build's basis, kept_ref . (R_ref^T R) ...
+    tol = (2e-4 if fp32 else 0.1) * np.abs(g["kept"]).max()
+    align = np.swapaxes(g["R_partial"], -1, -2) @ f64(R)
+    np.testing.assert_allclose(f64(kept), g["kept"] @ align, atol=tol)
+    # ... and column by column (up to sign) where the eigenvalue is separated
+    # from its neighbours by more than 1e-2 of the largest.
+    ev = exact.eigvals[..., :keep + 1]
+    gap = np.abs(np.diff(ev, axis=-1)) / ev[..., :1]
+    sep = np.minimum(gap[..., :keep], np.concatenate([np.full_like(gap[..., :1], np.inf),
+                                                      gap[..., :keep - 1]], axis=-1)) > 1e-2
+    sgn = np.sign((f64(R) * g["R_partial"]).sum(axis=-2))[:, :, None, :]
+    diff = np.abs(f64(kept) - g["kept"] * sgn) * sep[:, :, None, :]
+    assert diff.max() <= tol, diff.max()
 
 
 def test_build_rotation_config4_layer():
