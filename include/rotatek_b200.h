@@ -146,8 +146,9 @@ int rtk_full_channel_decode(const rtk_tensor *q, const rtk_tensor *k, const rtk_
 int rtk_key_covariance(const rtk_tensor *keys, const rtk_tensor *cov_out, const rtk_tensor *ksum_out,
                        void *stream);
 
-/* Bytes of workspace rtk_eigh_topk needs for n matrices (no zeroing required):
- * the solver's rotation log, about 0.93 MiB per matrix. */
+/* Bytes of workspace rtk_eigh_topk needs for n matrices: a 256-byte head (as
+ * in the build workspace) and the solver's rotation log, about 0.93 MiB per
+ * matrix.  No zeroing required. */
 size_t rtk_eigh_topk_workspace_size(int64_t n);
 
 /* Top-k eigenvectors of symmetric matrices, descending eigenvalue, each
@@ -160,8 +161,10 @@ size_t rtk_eigh_topk_workspace_size(int64_t n);
 int rtk_eigh_topk(const rtk_tensor *cov, int64_t k, const rtk_tensor *vecs_out,
                   const rtk_tensor *vals_out, void *workspace, size_t workspace_bytes, void *stream);
 
-/* Bytes of workspace rtk_build_rotation needs (no zeroing required): the
- * fp32 sums plus the eigensolver's rotation log, about 1 MiB per (b, h). */
+/* Bytes of workspace rtk_build_rotation needs: a device-status word in the
+ * first 256 bytes (zero it once before first use; rtk_read_status reads and
+ * clears it, a bounded wait that gave up sets RTK_DEVICE_TIMEOUT), then the
+ * fp32 sums and the eigensolver's rotation log, about 1 MiB per (b, h). */
 size_t rtk_build_rotation_workspace_size(int64_t batch, int64_t kv_heads, int64_t head_dim);
 
 /* The RotateK prefill build for one layer: replaces the body of

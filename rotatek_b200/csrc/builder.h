@@ -63,8 +63,13 @@ struct RotateParams {
   const void *keys; long long k_s[4];             // [B, H, S, 128]
   const void *R; long long R_s[4];                // [B, H, 128, keep]
   void *out; long long o_s[4];                    // [B, H, S, keep]
+  unsigned int *status;                           // device status word (bounded-wait timeouts)
 };
 
+// keep in {16, 32, 48, 64}; keys_map: [B, H, S, 128] bf16/f16, box 64 x 64, 128B swizzle
+cudaError_t launch_rotate_tma(int dtype_is_bf16, const CUtensorMap &keys_map, const RotateParams &p,
+                              cudaStream_t stream);
+// keep in {16, 32, 48, 64, 96, 128}
 cudaError_t launch_rotate_tc(int dtype_is_bf16, const RotateParams &p, cudaStream_t stream);
 cudaError_t launch_rotate_simt(const RotateParams &p, cudaStream_t stream);
 

@@ -39,6 +39,7 @@ int cuda_fail(cudaError_t e, const char *what) {
 }
 
 constexpr size_t kAlign = 256;
+constexpr size_t kStatusBytes = 256;   // device-status word at the head of a workspace
 constexpr int kBlockTokens = 64;      // generic-kernel split granularity
 constexpr int kVisBlockTokens = 64;   // tensor-core kernel: visual block
 constexpr int kFullBlockTokens = 32;  // tensor-core kernel: prompt/text block
@@ -526,13 +527,15 @@ int rtk_key_covariance(const rtk_tensor *keys, const rtk_tensor *cov_out, const 
 
 size_t rtk_build_rotation_workspace_size(int64_t batch, int64_t kv_heads, int64_t head_dim) {
   const int64_t n = batch * kv_heads;
-  return align_up((size_t)n * head_dim * head_dim * sizeof(float)) +
+  return kStatusBytes + align_up((size_t)n * head_dim * head_dim * sizeof(float)) +
          align_up((size_t)n * head_dim * sizeof(float)) + align_up((size_t)n * sizeof(int)) +
-         rtk_eigh_topk_workspace_size(n);
+         align_up((size_t)n * rtk::kJacobiLogBytes);
 }
 
+// [0, 256) status word (unused by the solver, kept so that one buffer can
+// serve both entry points), then the rotation log
 size_t rtk_eigh_topk_workspace_size(int64_t n) {
-  return n > 0 ? align_up((size_t)n * rtk::kJacobiLogBytes) : 0;
+  return kStatusBytes + align_up((size_t)std::max<int64_t>(n, 0) * rtk::kJacobiLogBytes);
 }
 
 int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_t num_kv_groups,
@@ -568,8 +571,9 @@ int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_
     return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, need);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   unsigned char *ws = static_cast<unsigned char *>(workspace);
-  float *cov = reinterpret_cast<float *>(ws);
-  float *ksum = reinterpret_cast<float *>(ws + align_up((size_t)B * H * D * D * sizeof(float)));
+  unsigned int *status = reinterpret_cast<unsigned int *>(ws);
+  float *cov = reinterpret_cast<float *>(ws + kStatusBytes);
+  float *ksum = reinterpret_cast<float *>(ws + kStatusBytes + align_up((size_t)B * H * D * D * sizeof(float)));
   int *sweeps = reinterpret_cast<int *>(reinterpret_cast<unsigned char *>(ksum) +
                                         align_up((size_t)B * H * D * sizeof(float)));
   float2 *rot_log = reinterpret_cast<float2 *>(reinterpret_cast<unsigned char *>(sweeps) +
@@ -620,6 +624,7 @@ int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_
   }
   rp.R = R_out->data;
   rp.out = kept_out->data;
+  rp.status = status;
   if (S > 0) {
     const bool rtc = is_half_type(dt) && keep % 16 == 0 && kv.s[3] == 1 && (kv.s[2] * 2) % 16 == 0 &&
                      (kv.s[1] * 2) % 16 == 0 && (kv.s[0] * 2) % 16 == 0 &&
@@ -627,7 +632,13 @@ int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_
                      (kept_out->stride[2] * 2) % 16 == 0 && (kept_out->stride[1] * 2) % 16 == 0 &&
                      (kept_out->stride[0] * 2) % 16 == 0 &&
                      reinterpret_cast<uintptr_t>(kept_out->data) % 16 == 0;
-    e = rtc ? rtk::launch_rotate_tc(dt == RTK_BF16, rp, st) : rtk::launch_rotate_simt(rp, st);
+    CUtensorMap kmap;
+    const bool tma = rtc && keep <= 64 &&
+                     encode_map(&kmap, kv, dt == RTK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    e = tma ? rtk::launch_rotate_tma(dt == RTK_BF16, kmap, rp, st)
+            : rtc ? rtk::launch_rotate_tc(dt == RTK_BF16, rp, st) : rtk::launch_rotate_simt(rp, st);
     if (e != cudaSuccess) return cuda_fail(e, "rotation builder (rotate) launch");
   }
   return RTK_OK;
@@ -662,7 +673,7 @@ int rtk_eigh_topk(const rtk_tensor *cov, int64_t k, const rtk_tensor *vecs_out,
   jp.R = vecs_out->data; jp.R_dtype = RTK_F32;
   jp.R_s[0] = vecs_out->stride[0]; jp.R_s[1] = 0; jp.R_s[2] = vecs_out->stride[1]; jp.R_s[3] = vecs_out->stride[2];
   jp.evals = vals_out ? static_cast<float *>(vals_out->data) : nullptr;
-  jp.rot_log = static_cast<float2 *>(workspace);
+  jp.rot_log = reinterpret_cast<float2 *>(static_cast<unsigned char *>(workspace) + kStatusBytes);
   jp.max_sweeps = rtk::kJacobiMaxSweeps;
   jp.tol = 1e-6f;
   const cudaError_t e = rtk::launch_jacobi(jp, static_cast<cudaStream_t>(stream));

@@ -118,6 +118,168 @@ __global__ void __launch_bounds__(kRotThreads) rotate_tc_kernel(const RotatePara
   }
 }
 
+// ---------------------------------------------------------------- TMA kernel
+// keep <= 64.  One persistent CTA per SM takes a contiguous range of the
+// linear (matrix, 64-token tile) units; unit i of the range goes to warp i % 4.
+// Each warp owns kStages / 4 ring stages and refills a stage itself, by TMA
+// (two 64-channel x 64-token boxes, 128B swizzle), as soon as it has read the
+// tile in it, so up to kStages tiles (~190 KB) per SM are in flight.  R's MMA
+// B-fragments live in registers and are reloaded only when the matrix
+// changes.  A warp stages its rounded 64 x keep output tile in its own shared
+// buffer and writes it with 16-byte stores.
+template <int KEEP>
+struct RotCfg {
+  static constexpr int kWarps = 4;
+  static constexpr int kOutStride = KEEP + 8;                   // staged row, elements
+  static constexpr int kOutBytes = kTile * kOutStride * 2;      // per warp
+  static constexpr int kStages =
+      ((227 * 1024 - 2048 - kWarps * kOutBytes) / kTileBytes) / kWarps * kWarps;
+  static constexpr int kPerWarp = kStages / kWarps;
+  static constexpr int kSmem = kStages * kTileBytes + kWarps * kOutBytes + kStages * 8 + 1024;
+  static_assert(kStages >= kWarps, "at least one stage per warp");
+};
+
+__device__ __forceinline__ uint32_t ld_pair_bits(const uint16_t *p, int i0, int i1) {
+  return static_cast<uint32_t>(p[i0]) | (static_cast<uint32_t>(p[i1]) << 16);
+}
+
+template <typename T, int KEEP>
+__global__ void __launch_bounds__(128, 1)
+    rotate_tma_kernel(const __grid_constant__ CUtensorMap kmap, const RotateParams p) {
+  using C = RotCfg<KEEP>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char *ring = smem;
+  T *outs = reinterpret_cast<T *>(smem + C::kStages * kTileBytes);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::kStages * kTileBytes + C::kWarps * C::kOutBytes);
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long tiles = (p.seq + kTile - 1) / kTile;
+  const long long total = (long long)p.batch * p.heads * tiles;
+  const long long u0 = blockIdx.x * total / gridDim.x;
+  const int n = static_cast<int>((blockIdx.x + 1) * total / gridDim.x - u0);
+  if (tid < C::kStages) mbar_init(&full[tid], 1);
+  if (tid == 0) {
+    abort_flag = 0;
+    tma_prefetch_desc(&kmap);
+  }
+  fence_barrier_init();
+  __syncthreads();
+
+  // unit i -> warp i % 4, ring stage warp + 4 * ((i / 4) % kPerWarp), used for
+  // the ((i / 4) / kPerWarp)-th time
+  auto issue = [&](int i) {
+    const long long u = u0 + i, m = u / tiles;
+    const int t = static_cast<int>(u % tiles), b = static_cast<int>(m / p.heads), h = static_cast<int>(m % p.heads);
+    const int stage = warp + C::kWarps * ((i / C::kWarps) % C::kPerWarp);
+    unsigned char *dst = ring + stage * kTileBytes;
+    mbar_arrive_expect_tx(&full[stage], kTileBytes);
+    tma_load_4d(dst, &kmap, 0, t * kTile, h, b, &full[stage]);
+    tma_load_4d(dst + kBox, &kmap, 64, t * kTile, h, b, &full[stage]);
+  };
+  if (lane == 0)
+    for (int j = 0; j < C::kPerWarp; ++j)
+      if (warp + C::kWarps * j < n) issue(warp + C::kWarps * j);
+
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, acol = (lane >> 4) * 8;
+  T *ob = outs + warp * (C::kOutBytes / 2);
+  long long cur_m = -1;
+  uint32_t rf[8][KEEP / 8][2];
+  for (int i = warp; i < n; i += C::kWarps) {
+    const long long u = u0 + i, m = u / tiles;
+    const int t = static_cast<int>(u % tiles), b = static_cast<int>(m / p.heads), h = static_cast<int>(m % p.heads);
+    if (m != cur_m) {
+      // B fragment (k = channel, n = kept column): {R[16ks + 2t4 (+1)][8nn + g8]}, +8 rows
+      // (offsets within one matrix's R fit in 32 bits: 128 x keep elements)
+      const uint16_t *R = reinterpret_cast<const uint16_t *>(p.R) + (long long)b * p.R_s[0] +
+                          (long long)h * p.R_s[1] + (long long)(2 * t4) * p.R_s[2] + (long long)g8 * p.R_s[3];
+      const int rs2 = static_cast<int>(p.R_s[2]), rs3 = static_cast<int>(p.R_s[3]);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+#pragma unroll
+        for (int nn = 0; nn < KEEP / 8; ++nn) {
+          const int o = ks * 16 * rs2 + nn * 8 * rs3;
+          rf[ks][nn][0] = ld_pair_bits(R, o, o + rs2);
+          rf[ks][nn][1] = ld_pair_bits(R, o + 8 * rs2, o + 9 * rs2);
+          // keep the loads of one k-step in flight at a time (all 4 x keep at
+          // once would take as many registers)
+          if (nn == KEEP / 8 - 1) asm volatile("" ::: "memory");
+        }
+      cur_m = m;
+    }
+    const int stage = warp + C::kWarps * ((i / C::kWarps) % C::kPerWarp);
+    const uint32_t parity = static_cast<uint32_t>((i / C::kWarps) / C::kPerWarp) & 1u;
+    if (!mbar_wait_bounded(&full[stage], parity, &abort_flag, p.status)) break;
+    const uint32_t tile = smem_u32(ring + stage * kTileBytes);
+#pragma unroll 1
+    for (int mb = 0; mb < 4; ++mb) {
+      float acc[KEEP / 8][4];
+#pragma unroll
+      for (int nn = 0; nn < KEEP / 8; ++nn) acc[nn][0] = acc[nn][1] = acc[nn][2] = acc[nn][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t a[4];
+        ldmatrix_x4(tile + (ks >= 4 ? kBox : 0) + swizzled_offset<128>(mb * 16 + arow, (ks & 3) * 16 + acol),
+                    a[0], a[1], a[2], a[3]);
+#pragma unroll
+        for (int nn = 0; nn < KEEP / 8; ++nn) mma_16816<T>(acc[nn], a, rf[ks][nn][0], rf[ks][nn][1]);
+      }
+#pragma unroll
+      for (int nn = 0; nn < KEEP / 8; ++nn) {
+        const int ch = nn * 8 + 2 * t4;
+        *reinterpret_cast<uint32_t *>(ob + (mb * 16 + g8) * C::kOutStride + ch) = pack2<T>(acc[nn][0], acc[nn][1]);
+        *reinterpret_cast<uint32_t *>(ob + (mb * 16 + g8 + 8) * C::kOutStride + ch) = pack2<T>(acc[nn][2], acc[nn][3]);
+      }
+    }
+    __syncwarp();
+    // the tile has been read: refill the stage with this warp's unit kStages ahead
+    if (lane == 0 && i + C::kStages < n) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(i + C::kStages);
+    }
+    T *og = reinterpret_cast<T *>(p.out) + (long long)b * p.o_s[0] + (long long)h * p.o_s[1];
+    constexpr int kChunks = kTile * KEEP / 8;                   // 16-byte chunks of the tile
+#pragma unroll 4
+    for (int e = lane; e < kChunks; e += 32) {
+      const int row = e / (KEEP / 8), c = e % (KEEP / 8);
+      const int tok = t * kTile + row;
+      if (tok < p.seq)
+        *reinterpret_cast<uint4 *>(og + (long long)tok * p.o_s[2] + c * 8) =
+            *reinterpret_cast<const uint4 *>(ob + row * C::kOutStride + c * 8);
+    }
+    __syncwarp();
+  }
+}
+
+template <typename T, int KEEP>
+cudaError_t launch_rot_tma(const CUtensorMap &kmap, const RotateParams &p, cudaStream_t stream) {
+  using C = RotCfg<KEEP>;
+  const long long units = (long long)p.batch * p.heads * ((p.seq + kTile - 1) / kTile);
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = static_cast<int>(units < sms ? units : sms);
+  if (grid == 0) return cudaSuccess;
+  cudaError_t err = cudaFuncSetAttribute(rotate_tma_kernel<T, KEEP>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  if (err != cudaSuccess) return err;
+  rotate_tma_kernel<T, KEEP><<<grid, 128, C::kSmem, stream>>>(kmap, p);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t dispatch_rot_tma(const CUtensorMap &kmap, const RotateParams &p, cudaStream_t stream) {
+  switch (p.keep) {
+    case 16: return launch_rot_tma<T, 16>(kmap, p, stream);
+    case 32: return launch_rot_tma<T, 32>(kmap, p, stream);
+    case 48: return launch_rot_tma<T, 48>(kmap, p, stream);
+    case 64: return launch_rot_tma<T, 64>(kmap, p, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ float ldf(const void *p, long long i) {
   return to_f32(reinterpret_cast<const T *>(p)[i]);
@@ -221,6 +383,12 @@ cudaError_t dispatch_rot(const RotateParams &p, cudaStream_t stream) {
 
 cudaError_t launch_rotate_tc(int dtype_is_bf16, const RotateParams &p, cudaStream_t stream) {
   return dtype_is_bf16 ? dispatch_rot<__nv_bfloat16>(p, stream) : dispatch_rot<__half>(p, stream);
+}
+
+cudaError_t launch_rotate_tma(int dtype_is_bf16, const CUtensorMap &keys_map, const RotateParams &p,
+                              cudaStream_t stream) {
+  return dtype_is_bf16 ? dispatch_rot_tma<__nv_bfloat16>(keys_map, p, stream)
+                       : dispatch_rot_tma<__half>(keys_map, p, stream);
 }
 
 cudaError_t launch_rotate_simt(const RotateParams &p, cudaStream_t stream) {

@@ -38,13 +38,28 @@ def _stream(device) -> ctypes.c_void_p:
 
 def _workspace(device: torch.device, need: int) -> torch.Tensor:
     """A per-device scratch buffer of at least ``need`` bytes, reused across calls
-    on the current stream (no zeroing required by the builder kernels)."""
+    on the current stream.  Its first 256 bytes are the device-status word,
+    zeroed here once (the kernels only ever set bits in it)."""
     idx = device.index
     ws = _build_ws.get(idx)
     if ws is None or ws.numel() < need:
-        ws = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
+        ws = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+        ws[:256].zero_()
         _build_ws[idx] = ws
     return ws
+
+
+def read_build_status(device=None) -> int:
+    """Read and clear the device-status word of this device's builder workspace
+    (0: every bounded wait of the builder kernels completed)."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index)
+    ws = _build_ws.get(dev.index)
+    if ws is None:
+        return 0
+    lib = _lib.load()
+    st = ctypes.c_uint32(0)
+    _lib.check(lib.rtk_read_status(ctypes.c_void_p(ws.data_ptr()), _stream(dev), ctypes.byref(st)))
+    return st.value
 
 
 def _eigh(mats: torch.Tensor, k: int, vecs: torch.Tensor, vals: Optional[torch.Tensor]) -> None:
@@ -141,4 +156,4 @@ def build_rotation(keys_vision: torch.Tensor, queries_recent: Optional[torch.Ten
 
 
 __all__ = ["_ROTATEK_QUERY_AWARE_ACTIVE", "power_iteration_gpu", "eigh_topk", "key_covariance",
-           "keep_count", "build_rotation"]
+           "keep_count", "build_rotation", "read_build_status"]

@@ -179,6 +179,26 @@ def test_build_rotation_config4_layer():
     err = np.abs(f64(kept) - want)
     assert np.mean(err == 0) > 0.99 and err.max() <= 2.0 ** -7 * np.abs(want).max()
     assert mask.sum().item() == B * H * 32
+    assert rot.read_build_status() == 0
+
+
+@pytest.mark.parametrize("keep,S,dtype", [(16, 1000, torch.bfloat16), (32, 4099, torch.bfloat16),
+                                          (48, 777, torch.float16), (64, 130, torch.bfloat16),
+                                          (96, 1000, torch.bfloat16), (128, 64, torch.float16)])
+def test_build_rotation_kept_is_rotated_keys(keep, S, dtype):
+    """kept == K_vis . R rounded to the Keys' dtype, for every keep the
+    tensor-core rotations take, ragged tiles, on a strided visual-span view."""
+    full = syn.lowrank_keys(3, 2, 16 + S + 40, seed=keep + S, device=DEV, dtype=dtype)
+    k = full[:, :, 16:16 + S]
+    q = syn.normal((3, 6, 32, 128), keep, DEV, dtype)
+    kept, R, dm, mask = rot.build_rotation(k, q, keep, 3)
+    assert rot.read_build_status() == 0
+    rnd = round_bf16 if dtype == torch.bfloat16 else (lambda x: x.astype(np.float16).astype(np.float64))
+    want = np.asarray(rnd(np.einsum("bhsd,bhdk->bhsk", f64(k), f64(R))), dtype=np.float64)
+    err = np.abs(f64(kept) - want)
+    ulp = 2.0 ** (-7 if dtype == torch.bfloat16 else -10)
+    assert np.mean(err == 0) > 0.99 and err.max() <= ulp * np.abs(want).max(), (np.mean(err == 0), err.max())
+    assert kept.shape == (3, 2, S, keep) and int(mask.sum()) == 3 * 2 * keep
 
 
 def test_pruner_update_rotatek_contract():
