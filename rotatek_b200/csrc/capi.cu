@@ -633,7 +633,9 @@ int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_
                      (kept_out->stride[0] * 2) % 16 == 0 &&
                      reinterpret_cast<uintptr_t>(kept_out->data) % 16 == 0;
     CUtensorMap kmap;
-    const bool tma = rtc && keep <= 64 &&
+    const bool r_vec = R_out->stride[3] == 1 && R_out->stride[2] % 8 == 0 && R_out->stride[1] % 8 == 0 &&
+                       R_out->stride[0] % 8 == 0 && reinterpret_cast<uintptr_t>(R_out->data) % 16 == 0;
+    const bool tma = rtc && r_vec && keep <= 64 && B * H * cdiv(S, 64) < (1ll << 31) &&
                      encode_map(&kmap, kv, dt == RTK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                                 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);

@@ -125,23 +125,24 @@ __global__ void __launch_bounds__(kRotThreads) rotate_tc_kernel(const RotatePara
 // (two 64-channel x 64-token boxes, 128B swizzle), as soon as it has read the
 // tile in it, so up to kStages tiles (~190 KB) per SM are in flight.  R's MMA
 // B-fragments live in registers and are reloaded only when the matrix
-// changes.  A warp stages its rounded 64 x keep output tile in its own shared
-// buffer and writes it with 16-byte stores.
+// changes (R rows must be 16-byte aligned).  A warp stages its rounded 64 x
+// keep output tile in its own shared buffer and writes it with 16-byte stores.
 template <int KEEP>
 struct RotCfg {
   static constexpr int kWarps = 4;
   static constexpr int kOutStride = KEEP + 8;                   // staged row, elements
   static constexpr int kOutBytes = kTile * kOutStride * 2;      // per warp
-  static constexpr int kStages =
-      ((227 * 1024 - 2048 - kWarps * kOutBytes) / kTileBytes) / kWarps * kWarps;
+  // two 16 KB tiles per warp (128 KB per SM) keep HBM busy; deeper rings
+  // measured slower
+  static constexpr int kStages = 2 * kWarps;
   static constexpr int kPerWarp = kStages / kWarps;
-  static constexpr int kSmem = kStages * kTileBytes + kWarps * kOutBytes + kStages * 8 + 1024;
+  static constexpr int kRSlot = 128 * kOutStride * 2;            // one matrix's R, padded rows
+  static constexpr int kRSlots = 2;                              // preloaded at kernel start
+  static_assert(kStages * kTileBytes + kWarps * kOutBytes + kRSlots * kRSlot + 2048 <= 227 * 1024,
+                "shared memory");
+  static constexpr int kSmem = kStages * kTileBytes + kWarps * kOutBytes + kRSlots * kRSlot + kStages * 8 + 1024;
   static_assert(kStages >= kWarps, "at least one stage per warp");
 };
-
-__device__ __forceinline__ uint32_t ld_pair_bits(const uint16_t *p, int i0, int i1) {
-  return static_cast<uint32_t>(p[i0]) | (static_cast<uint32_t>(p[i1]) << 16);
-}
 
 template <typename T, int KEEP>
 __global__ void __launch_bounds__(128, 1)
@@ -152,14 +153,18 @@ __global__ void __launch_bounds__(128, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char *ring = smem;
   T *outs = reinterpret_cast<T *>(smem + C::kStages * kTileBytes);
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::kStages * kTileBytes + C::kWarps * C::kOutBytes);
+  T *rslot = reinterpret_cast<T *>(smem + C::kStages * kTileBytes + C::kWarps * C::kOutBytes);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::kStages * kTileBytes + C::kWarps * C::kOutBytes +
+                                                C::kRSlots * C::kRSlot);
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const long long tiles = (p.seq + kTile - 1) / kTile;
+  // units (< 2^31, checked by the launcher) are walked with (matrix, tile)
+  // cursors; no division on the per-tile path
+  const int tiles = (p.seq + kTile - 1) / kTile;
   const long long total = (long long)p.batch * p.heads * tiles;
-  const long long u0 = blockIdx.x * total / gridDim.x;
-  const int n = static_cast<int>((blockIdx.x + 1) * total / gridDim.x - u0);
+  const int u0 = static_cast<int>(blockIdx.x * total / gridDim.x);
+  const int n = static_cast<int>((blockIdx.x + 1) * total / gridDim.x) - u0;
   if (tid < C::kStages) mbar_init(&full[tid], 1);
   if (tid == 0) {
     abort_flag = 0;
@@ -169,77 +174,136 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
 
   // unit i -> warp i % 4, ring stage warp + 4 * ((i / 4) % kPerWarp), used for
-  // the ((i / 4) / kPerWarp)-th time
-  auto issue = [&](int i) {
-    const long long u = u0 + i, m = u / tiles;
-    const int t = static_cast<int>(u % tiles), b = static_cast<int>(m / p.heads), h = static_cast<int>(m % p.heads);
-    const int stage = warp + C::kWarps * ((i / C::kWarps) % C::kPerWarp);
+  // the ((i / 4) / kPerWarp)-th time.  A cursor is (unit i, matrix m, tile t).
+  struct Cursor {
+    int i, m, t;
+  };
+  auto advance = [&](Cursor &c, int step) {
+    c.i += step;
+    c.t += step;
+    while (c.t >= tiles) {
+      c.t -= tiles;
+      ++c.m;
+    }
+  };
+  auto issue = [&](const Cursor &c) {
+    const int b = c.m / p.heads, h = c.m - b * p.heads;
+    const int stage = warp + C::kWarps * ((c.i / C::kWarps) % C::kPerWarp);
     unsigned char *dst = ring + stage * kTileBytes;
     mbar_arrive_expect_tx(&full[stage], kTileBytes);
-    tma_load_4d(dst, &kmap, 0, t * kTile, h, b, &full[stage]);
-    tma_load_4d(dst + kBox, &kmap, 64, t * kTile, h, b, &full[stage]);
+    tma_load_4d(dst, &kmap, 0, c.t * kTile, h, b, &full[stage]);
+    tma_load_4d(dst + kBox, &kmap, 64, c.t * kTile, h, b, &full[stage]);
   };
-  if (lane == 0)
-    for (int j = 0; j < C::kPerWarp; ++j)
-      if (warp + C::kWarps * j < n) issue(warp + C::kWarps * j);
+  Cursor cc = {0, (u0 + warp) / tiles, (u0 + warp) % tiles};   // the unit being computed
+  cc.i = warp;
+  Cursor ic = cc;                                                // the next unit to load
+  for (int j = 0; j < C::kPerWarp && ic.i < n; ++j) {
+    if (lane == 0) issue(ic);
+    advance(ic, C::kWarps);
+  }
+  // R of the range's first kRSlots matrices -> shared memory (all threads,
+  // cp.async, while the first tiles are in flight); a range that reaches
+  // further loads the rest per warp when it gets there
+  const int m_first = n > 0 ? u0 / tiles : 0;
+  const int nslot = n > 0 ? min(C::kRSlots, (u0 + n - 1) / tiles - m_first + 1) : 0;
+  for (int e = tid; e < nslot * 128 * (KEEP / 8); e += blockDim.x) {
+    const int sl = e / (128 * (KEEP / 8)), rem = e % (128 * (KEEP / 8));
+    const int row = rem / (KEEP / 8), c = rem % (KEEP / 8);
+    const int mm = m_first + sl, bb = mm / p.heads, hh = mm - bb * p.heads;
+    cp_async_16(rslot + sl * (C::kRSlot / 2) + row * C::kOutStride + c * 8,
+                reinterpret_cast<const T *>(p.R) + (long long)bb * p.R_s[0] + (long long)hh * p.R_s[1] +
+                    (long long)row * p.R_s[2] + c * 8);
+  }
+  cp_async_wait_all();
+  __syncthreads();
 
   const int g8 = lane >> 2, t4 = lane & 3;
   const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, acol = (lane >> 4) * 8;
   T *ob = outs + warp * (C::kOutBytes / 2);
-  long long cur_m = -1;
+  int cur_m = -1, b = 0, h = 0;
   uint32_t rf[8][KEEP / 8][2];
-  for (int i = warp; i < n; i += C::kWarps) {
-    const long long u = u0 + i, m = u / tiles;
-    const int t = static_cast<int>(u % tiles), b = static_cast<int>(m / p.heads), h = static_cast<int>(m % p.heads);
+  for (; cc.i < n; advance(cc, C::kWarps)) {
+    const int i = cc.i, m = cc.m, t = cc.t;
     if (m != cur_m) {
-      // B fragment (k = channel, n = kept column): {R[16ks + 2t4 (+1)][8nn + g8]}, +8 rows
-      // (offsets within one matrix's R fit in 32 bits: 128 x keep elements)
-      const uint16_t *R = reinterpret_cast<const uint16_t *>(p.R) + (long long)b * p.R_s[0] +
-                          (long long)h * p.R_s[1] + (long long)(2 * t4) * p.R_s[2] + (long long)g8 * p.R_s[3];
-      const int rs2 = static_cast<int>(p.R_s[2]), rs3 = static_cast<int>(p.R_s[3]);
+      b = m / p.heads;
+      h = m - b * p.heads;
+      // R of the new matrix -> B fragments, through this warp's (idle) output
+      // buffer in two 64-row halves: 16-byte loads, then ldmatrix.trans
+      const T *R = reinterpret_cast<const T *>(p.R) + (long long)b * p.R_s[0] + (long long)h * p.R_s[1];
+      const int brow = (lane & 7) + ((lane >> 3) & 1) * 8, bcol = (lane >> 4) * 8;
+      const bool preloaded = m - m_first < nslot;
+      const T *src = rslot + (m - m_first) * (C::kRSlot / 2);
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks)
+      for (int half = 0; half < 2; ++half) {
+        const T *rows = src + 64 * half * C::kOutStride;
+        if (!preloaded) {
+          constexpr int kVec = 64 * KEEP / 8;               // 16-byte pieces per half
 #pragma unroll
-        for (int nn = 0; nn < KEEP / 8; ++nn) {
-          const int o = ks * 16 * rs2 + nn * 8 * rs3;
-          rf[ks][nn][0] = ld_pair_bits(R, o, o + rs2);
-          rf[ks][nn][1] = ld_pair_bits(R, o + 8 * rs2, o + 9 * rs2);
-          // keep the loads of one k-step in flight at a time (all 4 x keep at
-          // once would take as many registers)
-          if (nn == KEEP / 8 - 1) asm volatile("" ::: "memory");
+          for (int e = lane; e < kVec; e += 32) {
+            const int row = e / (KEEP / 8), c = e % (KEEP / 8);
+            *reinterpret_cast<uint4 *>(ob + row * C::kOutStride + c * 8) =
+                *reinterpret_cast<const uint4 *>(R + (long long)(64 * half + row) * p.R_s[2] + c * 8);
+          }
+          __syncwarp();
+          rows = ob;
         }
+#pragma unroll
+        for (int kq = 0; kq < 4; ++kq)
+#pragma unroll
+          for (int g = 0; g < KEEP / 16; ++g) {
+            uint32_t f[4];
+            ldmatrix_x4_trans(smem_u32(rows + (kq * 16 + brow) * C::kOutStride + g * 16 + bcol), f[0], f[1], f[2], f[3]);
+            rf[4 * half + kq][2 * g][0] = f[0];
+            rf[4 * half + kq][2 * g][1] = f[1];
+            rf[4 * half + kq][2 * g + 1][0] = f[2];
+            rf[4 * half + kq][2 * g + 1][1] = f[3];
+          }
+        __syncwarp();
+      }
       cur_m = m;
     }
     const int stage = warp + C::kWarps * ((i / C::kWarps) % C::kPerWarp);
     const uint32_t parity = static_cast<uint32_t>((i / C::kWarps) / C::kPerWarp) & 1u;
     if (!mbar_wait_bounded(&full[stage], parity, &abort_flag, p.status)) break;
     const uint32_t tile = smem_u32(ring + stage * kTileBytes);
+    // MBP m-blocks of 16 rows at once: each k-step issues MBP x keep/8
+    // independent MMAs (one warp per SM sub-partition has no other latency cover)
+    constexpr int MBP = KEEP <= 32 ? 4 : 2;
 #pragma unroll 1
-    for (int mb = 0; mb < 4; ++mb) {
-      float acc[KEEP / 8][4];
+    for (int mb0 = 0; mb0 < 4; mb0 += MBP) {
+      float acc[MBP][KEEP / 8][4];
 #pragma unroll
-      for (int nn = 0; nn < KEEP / 8; ++nn) acc[nn][0] = acc[nn][1] = acc[nn][2] = acc[nn][3] = 0.f;
+      for (int j = 0; j < MBP; ++j)
+#pragma unroll
+        for (int nn = 0; nn < KEEP / 8; ++nn) acc[j][nn][0] = acc[j][nn][1] = acc[j][nn][2] = acc[j][nn][3] = 0.f;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
-        uint32_t a[4];
-        ldmatrix_x4(tile + (ks >= 4 ? kBox : 0) + swizzled_offset<128>(mb * 16 + arow, (ks & 3) * 16 + acol),
-                    a[0], a[1], a[2], a[3]);
+        uint32_t a[MBP][4];
 #pragma unroll
-        for (int nn = 0; nn < KEEP / 8; ++nn) mma_16816<T>(acc[nn], a, rf[ks][nn][0], rf[ks][nn][1]);
+        for (int j = 0; j < MBP; ++j)
+          ldmatrix_x4(tile + (ks >= 4 ? kBox : 0) + swizzled_offset<128>((mb0 + j) * 16 + arow, (ks & 3) * 16 + acol),
+                      a[j][0], a[j][1], a[j][2], a[j][3]);
+#pragma unroll
+        for (int j = 0; j < MBP; ++j)
+#pragma unroll
+          for (int nn = 0; nn < KEEP / 8; ++nn) mma_16816<T>(acc[j][nn], a[j], rf[ks][nn][0], rf[ks][nn][1]);
       }
 #pragma unroll
-      for (int nn = 0; nn < KEEP / 8; ++nn) {
-        const int ch = nn * 8 + 2 * t4;
-        *reinterpret_cast<uint32_t *>(ob + (mb * 16 + g8) * C::kOutStride + ch) = pack2<T>(acc[nn][0], acc[nn][1]);
-        *reinterpret_cast<uint32_t *>(ob + (mb * 16 + g8 + 8) * C::kOutStride + ch) = pack2<T>(acc[nn][2], acc[nn][3]);
-      }
+      for (int j = 0; j < MBP; ++j)
+#pragma unroll
+        for (int nn = 0; nn < KEEP / 8; ++nn) {
+          const int ch = nn * 8 + 2 * t4, row = (mb0 + j) * 16 + g8;
+          *reinterpret_cast<uint32_t *>(ob + row * C::kOutStride + ch) = pack2<T>(acc[j][nn][0], acc[j][nn][1]);
+          *reinterpret_cast<uint32_t *>(ob + (row + 8) * C::kOutStride + ch) = pack2<T>(acc[j][nn][2], acc[j][nn][3]);
+        }
     }
     __syncwarp();
     // the tile has been read: refill the stage with this warp's unit kStages ahead
-    if (lane == 0 && i + C::kStages < n) {
+    if (lane == 0 && ic.i < n) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(i + C::kStages);
+      issue(ic);
     }
+    advance(ic, C::kWarps);
     T *og = reinterpret_cast<T *>(p.out) + (long long)b * p.o_s[0] + (long long)h * p.o_s[1];
     constexpr int kChunks = kTile * KEEP / 8;                   // 16-byte chunks of the tile
 #pragma unroll 4
@@ -260,6 +324,7 @@ cudaError_t launch_rot_tma(const CUtensorMap &kmap, const RotateParams &p, cudaS
   const long long units = (long long)p.batch * p.heads * ((p.seq + kTile - 1) / kTile);
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (units >= (1ll << 31)) return cudaErrorInvalidValue;
   const int grid = static_cast<int>(units < sms ? units : sms);
   if (grid == 0) return cudaSuccess;
   cudaError_t err = cudaFuncSetAttribute(rotate_tma_kernel<T, KEEP>,
