@@ -146,6 +146,15 @@ int rtk_full_channel_decode(const rtk_tensor *q, const rtk_tensor *k, const rtk_
 int rtk_key_covariance(const rtk_tensor *keys, const rtk_tensor *cov_out, const rtk_tensor *ksum_out,
                        void *stream);
 
+/* kept_out = keys . R in the Keys' dtype: the rotation pass of
+ * rtk_build_rotation on its own (kv_pruning_utils.py:152, K_vis . R on the
+ * uncentred Keys), for a caller that already holds R.
+ *   keys [B, H, S, 128] f32 | bf16 | f16 (any strides), R [B, H, 128, keep] and
+ *   kept_out [B, H, S, keep] in the same dtype; workspace >= 256 bytes whose
+ *   first word is the device-status word (see rtk_build_rotation_workspace_size). */
+int rtk_rotate_keys(const rtk_tensor *keys, const rtk_tensor *R, const rtk_tensor *kept_out, void *workspace,
+                    size_t workspace_bytes, void *stream);
+
 /* Bytes of workspace rtk_eigh_topk needs for n matrices: a 256-byte head (as
  * in the build workspace) and the solver's rotation log, about 0.93 MiB per
  * matrix.  No zeroing required. */

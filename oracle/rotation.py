@@ -10,7 +10,7 @@ Restates ``ChannelPruner.update_rotatek`` with the exact-eigh solver
   114-115  C = K_c^T K_c, output in K's dtype, then fp32; C = (C + C^T) / 2
   117-140  query weighting (window 32, GQA group mean in the query dtype, L2 over
            the window in fp32, floor at 1e-3 * lower median, C *= q q^T,
-           symmetrise, ridge 1e-4 * mean|diag| clamped to >= 1e-6)
+           symmetrise, ridge 1e-4 * max(mean|diag|, 1e-6))
   145-150  eigh, eigenvalues ascending -> flip -> first `keep` columns -> K's dtype
   152      kept = K_vis . R  (uncentered Keys)
   153-156  delta_mu = mu - (mu R) R^T with R = fp32(R in K's dtype) -> K's dtype
@@ -69,7 +69,7 @@ def weight_covariance(cov: np.ndarray, q_norm: np.ndarray) -> np.ndarray:
     d = cov.shape[-1]
     cov = cov * (q_norm[..., :, None] * q_norm[..., None, :])
     cov = 0.5 * (cov + np.swapaxes(cov, -1, -2))
-    ridge = np.maximum(1e-4 * np.abs(np.diagonal(cov, axis1=-2, axis2=-1)).mean(axis=-1), 1e-6)
+    ridge = 1e-4 * np.maximum(np.abs(np.diagonal(cov, axis1=-2, axis2=-1)).mean(axis=-1), 1e-6)
     return cov + ridge[..., None, None] * np.eye(d)
 
 

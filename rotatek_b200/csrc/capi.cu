@@ -500,6 +500,42 @@ cudaError_t launch_covariance(const View4 &kv, int dt, float *cov, float *ksum, 
   cp.splits = 1;
   return rtk::launch_cov_simt(cp, st);
 }
+
+// kept = K . R on the tensor cores where the layouts allow (TMA kernel for
+// keep <= 64, cp.async kernel for keep in {96, 128}), else the CUDA-core kernel.
+cudaError_t launch_rotation(const View4 &kv, int dt, int64_t keep, const rtk_tensor *R_out,
+                            const rtk_tensor *kept_out, unsigned int *status, cudaStream_t st) {
+  const int64_t B = kv.n[0], H = kv.n[1], S = kv.n[2];
+  if (S == 0) return cudaSuccess;
+  rtk::RotateParams rp;
+  std::memset(&rp, 0, sizeof(rp));
+  rp.dtype = dt;
+  rp.batch = (int)B; rp.heads = (int)H; rp.seq = (int)S; rp.keep = (int)keep;
+  rp.keys = kv.data;
+  for (int i = 0; i < 4; ++i) {
+    rp.k_s[i] = kv.s[i];
+    rp.R_s[i] = R_out->stride[i];
+    rp.o_s[i] = kept_out->stride[i];
+  }
+  rp.R = R_out->data;
+  rp.out = kept_out->data;
+  rp.status = status;
+  const bool rtc = is_half_type(dt) && keep % 16 == 0 && kv.s[3] == 1 && (kv.s[2] * 2) % 16 == 0 &&
+                   (kv.s[1] * 2) % 16 == 0 && (kv.s[0] * 2) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(kv.data) % 16 == 0 && kept_out->stride[3] == 1 &&
+                   (kept_out->stride[2] * 2) % 16 == 0 && (kept_out->stride[1] * 2) % 16 == 0 &&
+                   (kept_out->stride[0] * 2) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(kept_out->data) % 16 == 0;
+  const bool r_vec = R_out->stride[3] == 1 && R_out->stride[2] % 8 == 0 && R_out->stride[1] % 8 == 0 &&
+                     R_out->stride[0] % 8 == 0 && reinterpret_cast<uintptr_t>(R_out->data) % 16 == 0;
+  CUtensorMap kmap;
+  const bool tma = rtc && r_vec && keep <= 64 && B * H * cdiv(S, 64) < (1ll << 31) &&
+                   encode_map(&kmap, kv, dt == RTK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                              64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  return tma ? rtk::launch_rotate_tma(dt == RTK_BF16, kmap, rp, st)
+             : rtc ? rtk::launch_rotate_tc(dt == RTK_BF16, rp, st) : rtk::launch_rotate_simt(rp, st);
+}
 }  // namespace
 
 extern "C" {
@@ -612,37 +648,31 @@ int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_
   if (e != cudaSuccess) return cuda_fail(e, "rotation builder (eigensolver) launch");
 
   // ---- kept = K_vis . R
-  rtk::RotateParams rp;
-  std::memset(&rp, 0, sizeof(rp));
-  rp.dtype = dt;
-  rp.batch = (int)B; rp.heads = (int)H; rp.seq = (int)S; rp.keep = (int)keep;
-  rp.keys = kv.data;
-  for (int i = 0; i < 4; ++i) {
-    rp.k_s[i] = kv.s[i];
-    rp.R_s[i] = R_out->stride[i];
-    rp.o_s[i] = kept_out->stride[i];
-  }
-  rp.R = R_out->data;
-  rp.out = kept_out->data;
-  rp.status = status;
-  if (S > 0) {
-    const bool rtc = is_half_type(dt) && keep % 16 == 0 && kv.s[3] == 1 && (kv.s[2] * 2) % 16 == 0 &&
-                     (kv.s[1] * 2) % 16 == 0 && (kv.s[0] * 2) % 16 == 0 &&
-                     reinterpret_cast<uintptr_t>(kv.data) % 16 == 0 && kept_out->stride[3] == 1 &&
-                     (kept_out->stride[2] * 2) % 16 == 0 && (kept_out->stride[1] * 2) % 16 == 0 &&
-                     (kept_out->stride[0] * 2) % 16 == 0 &&
-                     reinterpret_cast<uintptr_t>(kept_out->data) % 16 == 0;
-    CUtensorMap kmap;
-    const bool r_vec = R_out->stride[3] == 1 && R_out->stride[2] % 8 == 0 && R_out->stride[1] % 8 == 0 &&
-                       R_out->stride[0] % 8 == 0 && reinterpret_cast<uintptr_t>(R_out->data) % 16 == 0;
-    const bool tma = rtc && r_vec && keep <= 64 && B * H * cdiv(S, 64) < (1ll << 31) &&
-                     encode_map(&kmap, kv, dt == RTK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                                64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-    e = tma ? rtk::launch_rotate_tma(dt == RTK_BF16, kmap, rp, st)
-            : rtc ? rtk::launch_rotate_tc(dt == RTK_BF16, rp, st) : rtk::launch_rotate_simt(rp, st);
-    if (e != cudaSuccess) return cuda_fail(e, "rotation builder (rotate) launch");
-  }
+  e = launch_rotation(kv, dt, keep, R_out, kept_out, status, st);
+  if (e != cudaSuccess) return cuda_fail(e, "rotation builder (rotate) launch");
+  return RTK_OK;
+}
+
+int rtk_rotate_keys(const rtk_tensor *keys, const rtk_tensor *R, const rtk_tensor *kept_out, void *workspace,
+                    size_t workspace_bytes, void *stream) {
+  g_last_error.clear();
+  View4 kv;
+  if (!as4(keys, kv) || !dtype_ok(keys->dtype)) return fail(RTK_ERR_INVALID, "keys must be a [B, H, S, 128] float tensor");
+  const int64_t B = kv.n[0], H = kv.n[1], S = kv.n[2], D = kv.n[3];
+  if (D != 128) return fail(RTK_ERR_UNSUPPORTED, "head_dim must be 128 (got %lld)", (long long)D);
+  if (R == nullptr || R->ndim != 4 || R->shape[0] != B || R->shape[1] != H || R->shape[2] != D ||
+      R->dtype != keys->dtype)
+    return fail(RTK_ERR_INVALID, "R must be [B, H, D, keep] in the Keys' dtype");
+  const int64_t keep = R->shape[3];
+  if (keep < 1 || keep > D) return fail(RTK_ERR_INVALID, "keep must be in [1, head_dim] (got %lld)", (long long)keep);
+  if (!same_dims(kept_out, 4, {B, H, S, keep}) || kept_out->dtype != keys->dtype)
+    return fail(RTK_ERR_INVALID, "kept_out must be [B, H, S, keep] in the Keys' dtype");
+  if (workspace == nullptr || workspace_bytes < kStatusBytes)
+    return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, kStatusBytes);
+  if (B * H == 0) return RTK_OK;
+  const cudaError_t e = launch_rotation(kv, keys->dtype, keep, R, kept_out, static_cast<unsigned int *>(workspace),
+                                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rotate launch");
   return RTK_OK;
 }
 

@@ -6,7 +6,7 @@
 //             the Keys' dtype), then the query weighting of kv_pruning_utils.py:
 //             117-140: per channel q_norm = ||group-mean(q)||_2 over the query
 //             window, floored at 1e-3 * lower median; C *= q_norm q_norm^T;
-//             C += max(1e-4 * mean|diag C|, 1e-6) I
+//             C += 1e-4 * max(mean|diag C|, 1e-6) I
 //   solve     cyclic Jacobi, parallel ordering: round r = 1..127 pairs every
 //             index i with i XOR r (each round is a perfect matching, and the
 //             127 rounds meet every pair once); a sweep is 127 rounds; stop when
@@ -393,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 2) jacobi_kernel(const JacobiParams 
     __syncthreads();
     float dsum = 0.f;
     if (tid < kN) dsum = fabsf(A[tid * kAS + tid]);
-    const float ridge = fmaxf(1e-4f * block_sum(dsum, sm.red[0], tid) / kN, 1e-6f);
+    const float ridge = 1e-4f * fmaxf(block_sum(dsum, sm.red[0], tid) / kN, 1e-6f);
     if (tid < kN) A[tid * kAS + tid] += ridge;
   }
   __syncthreads();

@@ -111,6 +111,22 @@ def key_covariance(keys: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     return cov, ksum
 
 
+def rotate_keys(keys: torch.Tensor, R: torch.Tensor) -> torch.Tensor:
+    """kept = keys . R ([B, H, S, 128] x [B, H, 128, keep] -> [B, H, S, keep], in
+    the Keys' dtype): the rotation pass of ``build_rotation`` on its own."""
+    if keys.dim() != 4 or R.dim() != 4:
+        raise ValueError("keys must be [B, H, S, D] and R [B, H, D, keep]")
+    _lib.require_cuda(keys, R)
+    b, h, s, _ = keys.shape
+    kept = torch.empty(b, h, s, R.shape[-1], dtype=keys.dtype, device=keys.device)
+    lib = _lib.load()
+    ws = _workspace(keys.device, 256)
+    D = _lib.describe
+    _lib.check(lib.rtk_rotate_keys(D(keys), D(R), D(kept), ctypes.c_void_p(ws.data_ptr()), ws.numel(),
+                                   _stream(keys.device)))
+    return kept
+
+
 def keep_count(head_dim: int, channel_ratio: float) -> int:
     """Channels kept for a pruning ratio (kv_pruning_utils.py:108)."""
     return head_dim - min(head_dim, max(0, int(head_dim * channel_ratio)))
@@ -156,4 +172,4 @@ def build_rotation(keys_vision: torch.Tensor, queries_recent: Optional[torch.Ten
 
 
 __all__ = ["_ROTATEK_QUERY_AWARE_ACTIVE", "power_iteration_gpu", "eigh_topk", "key_covariance",
-           "keep_count", "build_rotation", "read_build_status"]
+           "keep_count", "build_rotation", "rotate_keys", "read_build_status"]

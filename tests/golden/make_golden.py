@@ -80,6 +80,37 @@ def prefill_case(name, mods, torch, synth, *, batch, q_heads, kv_heads, prompt, 
     print(f"wrote {name}.npz")
 
 
+def solved_matrix_case(name, mods, torch, synth, *, batch, q_heads, kv_heads, prompt, vision, text,
+                       ratio, scale, seed):
+    """The exact matrix the reference hands to torch.linalg.eigh (captured by
+    wrapping that function around one update_rotatek call), for Keys scaled
+    down so far that mean|diag| < 1e-2, where the ridge's clamp is active."""
+    pre = synth.make_prefill(batch, q_heads, kv_heads, prompt, vision, text, seed=seed,
+                             dtype=torch.float32)
+    keys = pre.keys * scale
+    pruner = mods[True].ChannelPruner(ratio=ratio, prompt_seqlen=prompt, query_seqlen=text)
+    seen = []
+    real_eigh = torch.linalg.eigh
+
+    def capture(mat, *a, **k):
+        seen.append(mat.detach().clone())
+        return real_eigh(mat, *a, **k)
+
+    torch.linalg.eigh = capture
+    try:
+        pruner.update_rotatek(keys, pre.queries, pre.values, None, num_key_value_groups=q_heads // kv_heads)
+    finally:
+        torch.linalg.eigh = real_eigh
+    solved = seen[0]
+    diag_mean = solved.diagonal(dim1=-2, dim2=-1).abs().mean(dim=-1)
+    assert float(diag_mean.max()) < 1e-2, diag_mean
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), keys=_np(keys),
+                        queries_window=_np(pre.queries[:, :, -min(32, pre.queries.shape[2]):]),
+                        solved=_np(solved), prompt_len=prompt, vision_len=vision, text_len=text,
+                        num_kv_groups=q_heads // kv_heads, dtype="float32")
+    print(f"wrote {name}.npz")
+
+
 def decode_case(name, torch, synth, paper, *, batch, q_heads, kv_heads, vision, full, keep,
                 dtype, seed, with_bias=True, mask_density=1.0):
     d = synth.make_decode(batch, q_heads, kv_heads, vision, full, keep=keep, seed=seed,
@@ -115,6 +146,7 @@ def dense_case(name, torch, synth, dense, *, batch, q_heads, kv_heads, seq, dtyp
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
+    ap.add_argument("--only", default=None, help="write only the fixture of this name")
     args = ap.parse_args()
     os.environ["TRITON_INTERPRET"] = "1"
     sys.path.insert(0, args.reference)
@@ -126,35 +158,52 @@ def main():
 
     mods = {True: _load_pruner_module(args.reference, "eigh", True, "qa"),
             False: _load_pruner_module(args.reference, "eigh", False, "plain")}
+
+    def want(name):
+        return args.only is None or args.only == name
     bf16 = torch.bfloat16
     # fp32, B=2, 8/2 heads, 32 + 576 + 64, ratio 0.75
-    prefill_case("cfg1_fp32", mods, torch, synth, batch=2, q_heads=8, kv_heads=2, prompt=32,
-                 vision=576, text=64, ratio=0.75, dtype=torch.float32, seed=1,
-                 paper=paper, dense=dense)
+    if want("cfg1_fp32"):
+        prefill_case("cfg1_fp32", mods, torch, synth, batch=2, q_heads=8, kv_heads=2, prompt=32,
+                     vision=576, text=64, ratio=0.75, dtype=torch.float32, seed=1,
+                     paper=paper, dense=dense)
     # the same shape without query weighting (ROTATEK_QUERY_AWARE=0)
-    prefill_case("cfg1_fp32_plain", mods, torch, synth, batch=2, q_heads=8, kv_heads=2,
-                 prompt=32, vision=576, text=64, ratio=0.75, dtype=torch.float32, seed=1,
-                 query_aware=False, decode=False, store_inputs=False)
+    if want("cfg1_fp32_plain"):
+        prefill_case("cfg1_fp32_plain", mods, torch, synth, batch=2, q_heads=8, kv_heads=2,
+                     prompt=32, vision=576, text=64, ratio=0.75, dtype=torch.float32, seed=1,
+                     query_aware=False, decode=False, store_inputs=False)
     # bf16, ragged visual span (not a multiple of 64), GQA group 2
-    prefill_case("small_bf16", mods, torch, synth, batch=1, q_heads=4, kv_heads=2, prompt=8,
-                 vision=200, text=24, ratio=0.75, dtype=bf16, seed=2, paper=paper, dense=dense)
+    if want("small_bf16"):
+        prefill_case("small_bf16", mods, torch, synth, batch=1, q_heads=4, kv_heads=2, prompt=8,
+                     vision=200, text=24, ratio=0.75, dtype=bf16, seed=2, paper=paper, dense=dense)
     # decode edge cases (fp32): partial mask and no delta_mu, G=3, D_keep=16
-    decode_case("dec_mask_nobias_fp32", torch, synth, paper, batch=2, q_heads=6, kv_heads=2,
-                vision=70, full=45, keep=16, dtype=torch.float32, seed=3, with_bias=False,
-                mask_density=0.6)
+    if want("dec_mask_nobias_fp32"):
+        decode_case("dec_mask_nobias_fp32", torch, synth, paper, batch=2, q_heads=6, kv_heads=2,
+                    vision=70, full=45, keep=16, dtype=torch.float32, seed=3, with_bias=False,
+                    mask_density=0.6)
     # empty visual span; empty prompt/text span
-    decode_case("dec_empty_visual_fp32", torch, synth, paper, batch=1, q_heads=4, kv_heads=1,
-                vision=0, full=40, keep=32, dtype=torch.float32, seed=4)
-    decode_case("dec_empty_full_fp32", torch, synth, paper, batch=1, q_heads=2, kv_heads=2,
-                vision=100, full=0, keep=32, dtype=torch.float32, seed=5)
+    if want("dec_empty_visual_fp32"):
+        decode_case("dec_empty_visual_fp32", torch, synth, paper, batch=1, q_heads=4, kv_heads=1,
+                    vision=0, full=40, keep=32, dtype=torch.float32, seed=4)
+    if want("dec_empty_full_fp32"):
+        decode_case("dec_empty_full_fp32", torch, synth, paper, batch=1, q_heads=2, kv_heads=2,
+                    vision=100, full=0, keep=32, dtype=torch.float32, seed=5)
     # bf16 decode at G=7 (the headline group size) with a mostly-masked text span
-    decode_case("dec_g7_bf16", torch, synth, paper, batch=1, q_heads=7, kv_heads=1, vision=300,
-                full=90, keep=32, dtype=bf16, seed=6, mask_density=0.5)
+    if want("dec_g7_bf16"):
+        decode_case("dec_g7_bf16", torch, synth, paper, batch=1, q_heads=7, kv_heads=1, vision=300,
+                    full=90, keep=32, dtype=bf16, seed=6, mask_density=0.5)
     # dense decode, MHA (G=1) and G=4
-    dense_case("dense_g1_fp32", torch, synth, dense, batch=1, q_heads=2, kv_heads=2, seq=150,
-               dtype=torch.float32, seed=7)
-    dense_case("dense_g4_bf16", torch, synth, dense, batch=2, q_heads=8, kv_heads=2, seq=333,
-               dtype=bf16, seed=8)
+    if want("dense_g1_fp32"):
+        dense_case("dense_g1_fp32", torch, synth, dense, batch=1, q_heads=2, kv_heads=2, seq=150,
+                   dtype=torch.float32, seed=7)
+    if want("dense_g4_bf16"):
+        dense_case("dense_g4_bf16", torch, synth, dense, batch=2, q_heads=8, kv_heads=2, seq=333,
+                   dtype=bf16, seed=8)
+
+    # the matrix the reference solves, at a scale where the ridge's clamp matters
+    if want("tiny_solved_fp32"):
+        solved_matrix_case("tiny_solved_fp32", mods, torch, synth, batch=1, q_heads=4, kv_heads=2,
+                           prompt=8, vision=300, text=24, ratio=0.75, scale=1e-5, seed=12)
 
 
 if __name__ == "__main__":

@@ -105,3 +105,18 @@ def cos_signs(a, b):
     """Per-column sign aligning b's eigenvectors with a's: [B, H, 1, k]."""
     s = np.sign((np.asarray(a, np.float64) * np.asarray(b, np.float64)).sum(axis=-2))
     return s[:, :, None, :]
+
+
+def test_solved_matrix_matches_reference_at_tiny_scale(golden):
+    """The matrix the reference hands to eigh (captured from update_rotatek) for
+    Keys so small that mean|diag| < 1e-2: pins the centring, the query weighting
+    and the ridge 1e-4 * max(mean|diag|, 1e-6) (kv_pruning_utils.py:112-140)."""
+    g = golden("tiny_solved_fp32")
+    p, v = int(g["prompt_len"]), int(g["vision_len"])
+    vision = g["keys"][:, :, p:p + v]
+    hkv = vision.shape[1]
+    _, cov = orot.covariance(vision, "float32")
+    mat = orot.weight_covariance(cov, orot.query_weights(g["queries_window"], hkv, "float32"))
+    ref = g["solved"].astype(np.float64)
+    assert np.abs(np.diagonal(ref, axis1=-2, axis2=-1)).mean(axis=-1).max() < 1e-2
+    np.testing.assert_allclose(mat, ref, rtol=0, atol=2e-6 * np.abs(ref).max())

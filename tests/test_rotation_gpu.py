@@ -201,6 +201,34 @@ def test_build_rotation_kept_is_rotated_keys(keep, S, dtype):
     assert kept.shape == (3, 2, S, keep) and int(mask.sum()) == 3 * 2 * keep
 
 
+def test_build_rotation_tiny_scale_eigenvalues(golden):
+    """Eigenvalues of the solved matrix against those of the matrix the reference
+    solves (captured), at a scale where the ridge's clamp is active."""
+    g = golden("tiny_solved_fp32")
+    p, v = int(g["prompt_len"]), int(g["vision_len"])
+    keys = torch.as_tensor(g["keys"][:, :, p:p + v]).to(DEV)
+    q = torch.as_tensor(g["queries_window"]).to(DEV)
+    *_, ev = rot.build_rotation(keys, q, 32, int(g["num_kv_groups"]), query_aware=True, return_eigvals=True)
+    want = np.linalg.eigvalsh(g["solved"].astype(np.float64))[..., ::-1]
+    np.testing.assert_allclose(f64(ev), want, rtol=0, atol=2e-5 * np.abs(want).max())
+
+
+def test_rotate_keys_matches_build():
+    """rotate_keys is the build's rotation pass: identical kept for the build's R;
+    fp32 Keys take the generic kernel (fp32 sums, 1e-5 relative)."""
+    k = syn.lowrank_keys(2, 2, 1000, seed=21, device=DEV, dtype=torch.bfloat16)
+    q = syn.normal((2, 8, 32, 128), 22, DEV, torch.bfloat16)
+    kept, R, _, _ = rot.build_rotation(k, q, 32, 4)
+    assert torch.equal(rot.rotate_keys(k, R), kept)
+    k32 = syn.lowrank_keys(1, 2, 300, seed=23, device=DEV, dtype=torch.float32)
+    R32 = torch.linalg.qr(torch.randn(1, 2, 128, 40, device=DEV))[0]
+    want = np.einsum("bhsd,bhdk->bhsk", f64(k32), f64(R32))
+    np.testing.assert_allclose(f64(rot.rotate_keys(k32, R32)), want, rtol=1e-5, atol=1e-5 * np.abs(want).max())
+    assert rot.read_build_status() == 0
+    with pytest.raises(ValueError):
+        rot.rotate_keys(k[0], R)
+
+
 def test_pruner_update_rotatek_contract():
     B, Hq, Hkv, P, V, T = 1, 8, 2, 16, 300, 20
     pre = syn.make_prefill(B, Hq, Hkv, P, V, T, seed=9, device=DEV, dtype=torch.bfloat16)
