@@ -369,10 +369,221 @@ def run_ours(args):
     return 0
 
 
+# ---------------------------------------------------------------- config 4: the rotation build
+BUILD_METRIC = "config4 prefill rotation build us/step (28 layers x B=8 x 4 KV heads, S_v=15360, bf16)"
+CFG4 = dict(layers=28, batch=8, q_heads=28, kv_heads=4, head_dim=128, keep=32, vision=15360, window=32)
+BUILD_WORKLOAD = ("config4: Qwen2.5-VL-7B prefill rotation build for all 28 layers, bf16, B=8, "
+                  "H_kv=4 (G=7), D=128, keep 32, 15360 visual Keys per head (896 128x128 solves)")
+
+
+def build_inputs(device, seed=0, layers=None, batch=None):
+    from rotatek_b200 import synthetic as syn
+    nb = (CFG4["layers"] if layers is None else layers) * (CFG4["batch"] if batch is None else batch)
+    keys = syn.lowrank_keys(nb, CFG4["kv_heads"], CFG4["vision"], seed=seed, device=device,
+                            dtype=torch.bfloat16)
+    queries = syn.normal((nb, CFG4["q_heads"], CFG4["window"], CFG4["head_dim"]), seed + 1, device,
+                         torch.bfloat16)
+    return keys, queries
+
+
+def run_build(args):
+    """Config 4: one step builds all 28 layers' rotations in one batched call
+    (the 28 x 8 (layer, batch) problems stacked on the batch axis)."""
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        pg = dist
+    from rotatek_b200 import rotation as rot
+    G = CFG4["q_heads"] // CFG4["kv_heads"]
+    keep = CFG4["keep"]
+    keys, queries = build_inputs(dev, seed=100 + rank)
+    nmat = keys.shape[0] * keys.shape[1]
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return rot.build_rotation(keys, queries, keep, G)
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    def timed(fn, reps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+        ev[0].record(stream)
+        for i in range(reps):
+            fn()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+        return [ev[i].elapsed_time(ev[i + 1]) for i in range(reps)]
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        per_step = timed(step, args.steps)
+    barrier()
+    total_ms = sum(per_step)
+    if pg is not None:
+        t = torch.tensor([total_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        total_ms = float(t.item())
+    status = rot.read_build_status(dev)
+
+    # the build's kernels one at a time, on the same inputs (CUDA events)
+    kept, R, dm, _ = step()
+    cov_ms = statistics.mean(timed(lambda: rot.key_covariance(keys), 3))
+    rot_ms = statistics.mean(timed(lambda: rot.rotate_keys(keys, R), 3))
+    layer = lambda: rot.build_rotation(keys[:CFG4["batch"]], queries[:CFG4["batch"]], keep, G)  # noqa: E731
+    layer()
+    layer_ms = statistics.mean(timed(layer, 3))
+    step_ms = statistics.mean(per_step)
+    jac_ms = max(step_ms - cov_ms - rot_ms, 0.0)
+
+    # end to end through the public API: Keys and queries from pinned host memory,
+    # kept / R / delta_mu back to pinned host memory, every step
+    e2e_steps = max(1, min(args.steps, 2))
+    hk, hq = keys.cpu().pin_memory(), queries.cpu().pin_memory()
+    dk, dq = torch.empty_like(keys), torch.empty_like(queries)
+    ok, oR, od = (torch.empty(kept.shape, dtype=kept.dtype).pin_memory(),
+                  torch.empty(R.shape, dtype=R.dtype).pin_memory(),
+                  torch.empty(dm.shape, dtype=dm.dtype).pin_memory())
+
+    def e2e():
+        dk.copy_(hk, non_blocking=True)
+        dq.copy_(hq, non_blocking=True)
+        k2, r2, d2, _ = rot.build_rotation(dk, dq, keep, G)
+        ok.copy_(k2, non_blocking=True)
+        oR.copy_(r2, non_blocking=True)
+        od.copy_(d2, non_blocking=True)
+
+    e2e()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = sum(timed(e2e, e2e_steps))
+    if pg is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    clocks = sampler.summary()
+    if pg is not None:
+        per_rank = [None] * world
+        pg.all_gather_object(per_rank, clocks)
+        mhz = [c["sm_mhz"] for c in per_rank if c["sm_mhz"] is not None]
+        clocks = {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": per_rank[0]["sm_max_mhz"],
+                  "reasons": sorted({x for c in per_rank for x in c["reasons"]}),
+                  "samples": sum(c["samples"] for c in per_rank), "per_rank": per_rank}
+
+    if rank == 0:
+        peak, peak_kind = load_peak_hbm()
+        kbytes = keys.numel() * keys.element_size()
+        cov_bytes = kbytes + nmat * (128 * 128 + 128) * 4
+        rot_bytes = kbytes + kept.numel() * kept.element_size() + R.numel() * R.element_size()
+        us_per_step = total_ms * 1e3 / (args.steps * world)
+        h2d = (hk.numel() + hq.numel()) * 2
+        d2h = ok.numel() * 2 + oR.numel() * 2 + od.numel() * 2
+        line = {
+            "metric": BUILD_METRIC, "value": us_per_step, "unit": "us/step", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": total_ms / args.steps,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded low-rank+noise Keys (BASELINE generator), N(0,1) queries",
+            "config": {"workload": BUILD_WORKLOAD, "global_batch": CFG4["batch"] * world,
+                       "seq_len": CFG4["vision"], "parallelism": f"replicas x{world} (no collective)",
+                       "l2": f"Keys {kbytes / 1e9:.2f} GB per step > 126 MB L2; no flush"},
+            "phases_us": {"covariance": cov_ms * 1e3, "rotate": rot_ms * 1e3,
+                          "eigensolve_and_rest": jac_ms * 1e3,
+                          "eigensolve_us_per_128x128_solve": jac_ms * 1e3 / nmat,
+                          "one_layer_build": layer_ms * 1e3,
+                          "per_layer_sequential_28": layer_ms * 1e3 * CFG4["layers"]},
+            "roofline": {"bound": "fp32", "kernel": "jacobi_kernel (batched 128x128 Jacobi, CUDA cores)",
+                         "achieved": None, "peak": None, "unit": None, "frac": None, "traffic": None,
+                         "note": "no byte or tensor roofline applies; reported as time per solve"},
+            "hbm_kernels": {
+                "covariance": {"bound": "hbm", "achieved": cov_bytes / cov_ms / 1e6, "peak": peak,
+                               "unit": "GB/s", "frac": cov_bytes / cov_ms / 1e6 / peak,
+                               "algorithmic_bytes": cov_bytes, "peak_source": peak_kind},
+                "rotate": {"bound": "hbm", "achieved": rot_bytes / rot_ms / 1e6, "peak": peak,
+                           "unit": "GB/s", "frac": rot_bytes / rot_ms / 1e6 / peak,
+                           "algorithmic_bytes": rot_bytes, "peak_source": peak_kind}},
+            "e2e": {"value": e2e_ms * 1e3 / (e2e_steps * world), "unit": "us/step",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+            "gpu_launches": 3 * args.steps, "clocks": clocks, "device_status": status,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = build_cpu_baseline()
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def build_cpu_baseline(target_s: float = 12.0):
+    """The reference's update_rotatek (eigh solver) in eager torch on the host:
+    one layer at batch 1 (4 KV heads), scaled x8 x28 to the config-4 step."""
+    from oracle.eager_torch import update_rotatek_eager
+    threads = use_all_host_threads()
+    keys, queries = build_inputs("cpu", seed=7, layers=1, batch=1)
+    G = CFG4["q_heads"] // CFG4["kv_heads"]
+    update_rotatek_eager(keys, queries, CFG4["keep"], G)
+    t0 = time.perf_counter()
+    update_rotatek_eager(keys, queries, CFG4["keep"], G)
+    one = time.perf_counter() - t0
+    reps = max(1, int(target_s / max(one, 1e-3)))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        update_rotatek_eager(keys, queries, CFG4["keep"], G)
+    per = (time.perf_counter() - t0) / reps
+    scale = CFG4["layers"] * CFG4["batch"]
+    return {"value": per * 1e6 * scale, "unit": "us/step", "cores": threads, "kind": "port",
+            "sample": f"1 layer at batch 1 (4 KV heads, full S_v), {reps} reps, eager torch "
+                      f"update_rotatek (eigh), scaled x{scale}"}
+
+
+def run_build_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    from oracle.eager_torch import update_rotatek_eager
+    threads = use_all_host_threads()
+    keys, queries = build_inputs("cpu", seed=7, layers=1, batch=1)
+    G = CFG4["q_heads"] // CFG4["kv_heads"]
+    for _ in range(args.warmup):
+        update_rotatek_eager(keys, queries, CFG4["keep"], G)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        update_rotatek_eager(keys, queries, CFG4["keep"], G)
+        times.append(time.perf_counter() - t0)
+    scale = CFG4["layers"] * CFG4["batch"]
+    v = statistics.mean(times) * 1e6 * scale
+    line = {"impl": "reference", "metric": BUILD_METRIC, "value": v, "unit": "us/step", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": v / 1e3, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded low-rank+noise Keys, N(0,1) queries",
+            "config": {"workload": BUILD_WORKLOAD, "global_batch": CFG4["batch"], "seq_len": CFG4["vision"],
+                       "parallelism": "host CPU, rank 0 only"},
+            "cpu_baseline": {"value": v, "unit": "us/step", "cores": threads, "kind": "port",
+                             "sample": f"1 layer at batch 1 per step, eager torch update_rotatek (eigh), "
+                                       f"scaled x{scale}"},
+            "e2e": {"value": v, "unit": "us/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "gpu_launches": 0}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default 2000 decode steps, 20 build steps)")
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=10)
@@ -381,7 +592,13 @@ def main():
                     help="override the batch (profiling cases only; the bench line uses 32)")
     ap.add_argument("--kernel-only", action="store_true",
                     help="decode launches only: no e2e, no CPU baseline, no JSON bench line")
+    ap.add_argument("--workload", choices=["decode", "build"], default="decode",
+                    help="decode: BASELINE config 2 (the headline); build: config 4 rotation build")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 20 if args.workload == "build" else 2000
+    if args.workload == "build":
+        return run_build_reference(args) if args.impl == "reference" else run_build(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
