@@ -401,7 +401,7 @@ def run_build(args):
     from rotatek_b200 import rotation as rot
     G = CFG4["q_heads"] // CFG4["kv_heads"]
     keep = CFG4["keep"]
-    keys, queries = build_inputs(dev, seed=100 + rank)
+    keys, queries = build_inputs(dev, seed=100 + rank, layers=args.layers)
     nmat = keys.shape[0] * keys.shape[1]
     stream = torch.cuda.current_stream(dev)
 
@@ -494,7 +494,8 @@ def run_build(args):
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": total_ms / args.steps,
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded low-rank+noise Keys (BASELINE generator), N(0,1) queries",
-            "config": {"workload": BUILD_WORKLOAD, "global_batch": CFG4["batch"] * world,
+            "config": {"workload": BUILD_WORKLOAD, "layers": keys.shape[0] // CFG4["batch"],
+                       "global_batch": CFG4["batch"] * world,
                        "seq_len": CFG4["vision"], "parallelism": f"replicas x{world} (no collective)",
                        "l2": f"Keys {kbytes / 1e9:.2f} GB per step > 126 MB L2; no flush"},
             "phases_us": {"covariance": cov_ms * 1e3, "rotate": rot_ms * 1e3,
@@ -594,6 +595,8 @@ def main():
                     help="decode launches only: no e2e, no CPU baseline, no JSON bench line")
     ap.add_argument("--workload", choices=["decode", "build"], default="decode",
                     help="decode: BASELINE config 2 (the headline); build: config 4 rotation build")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="build workload: layers per step (profiling cases only; the bench line uses 28)")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 20 if args.workload == "build" else 2000
