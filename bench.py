@@ -580,6 +580,125 @@ def run_build_reference(args):
     return 0
 
 
+# ---------------------------------------------------------------- config 5: multi-GPU decode
+DEC72_METRIC = "config5 decode step us/step (80 layers, B=64, 64/8 heads, 32k ctx, 25% K channels kept)"
+CFG5 = dict(layers=80, batch=64, q_heads=64, kv_heads=8, head_dim=128, keep=32, prompt=64, vision=31744,
+            text=960)
+DEC72_WORKLOAD = ("config5: 72B-class GQA decode attention, bf16, 80 layers, B=64, H_q=64, H_kv=8 (G=8), "
+                  "D=128, D_keep=32, S = 64 prompt + 31744 visual + 960 text")
+
+
+def run_decode72b(args):
+    """Config 5: one step = the decode attention of all 80 layers for one new
+    token of the whole batch (strong scaling: the batch is fixed, ranks split
+    it).  One KV head per GPU at N = 8 (outputs all_gathered along heads each
+    layer, overlapped with the next layer), batch-sharded at N = 2 and 4."""
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        pg = dist
+    from rotatek_b200 import sharding, synthetic as syn
+    from rotatek_b200.kernels import rotatek_decode
+    G = CFG5["q_heads"] // CFG5["kv_heads"]
+    p = sharding.plan(rank, world, CFG5["batch"], CFG5["kv_heads"], G, mode=args.shard)
+    full_len = CFG5["prompt"] + CFG5["text"]
+    # A pool of resident layers, cycled over the 80 layer calls: 80 layers of
+    # this shard (55-437 GB) need not fit, and every layer's K/V exceed the L2,
+    # so each call still streams its full bytes from HBM.
+    pool = []
+    for j in range(args.pool):
+        d = syn.make_decode(p.local_batch, p.local_q_heads, p.local_kv_heads, CFG5["vision"], full_len,
+                            keep=CFG5["keep"], seed=500 + 10 * j + rank, device=dev, dtype=torch.bfloat16)
+        kw = d.as_kwargs()
+        kw.pop("q_full")
+        pool.append(kw)
+        layer_bytes = d.nbytes()
+    qs = [syn.normal((p.local_batch, p.local_q_heads, CFG5["head_dim"]), 900 + l, dev, torch.bfloat16)
+          for l in range(CFG5["layers"])]
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        works = []
+        for l in range(CFG5["layers"]):
+            out, _, _ = rotatek_decode(q_full=qs[l], **pool[l % len(pool)])
+            if p.needs_gather:
+                works.append(sharding.gather_output(p, out, async_op=True)[1])
+        for w in works:
+            w.wait()
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with sampler:
+        ev[0].record(stream)
+        for i in range(args.steps):
+            step()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    total_ms = sum(per)
+    mine = total_ms
+    if pg is not None:
+        t = torch.tensor([total_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        total_ms = float(t.item())
+    clocks = sampler.summary()
+    if pg is not None:
+        per_rank = [None] * world
+        pg.all_gather_object(per_rank, clocks)
+        mhz = [c["sm_mhz"] for c in per_rank if c["sm_mhz"] is not None]
+        clocks = {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": per_rank[0]["sm_max_mhz"],
+                  "reasons": sorted({x for c in per_rank for x in c["reasons"]}),
+                  "samples": sum(c["samples"] for c in per_rank), "per_rank": per_rank}
+    from rotatek_b200 import _lib
+    status = _lib.read_status(dev)
+    if rank == 0:
+        peak, peak_kind = load_peak_hbm()
+        step_us = total_ms * 1e3 / args.steps
+        rank_bytes = layer_bytes * CFG5["layers"]
+        achieved = rank_bytes / (mine * 1e-3 / args.steps) / 1e9
+        line = {
+            "metric": DEC72_METRIC, "value": step_us, "unit": "us/step", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": step_us / 1e3,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded low-rank+noise Keys rotated to a top-32 basis; N(0,1) Values/queries",
+            "config": {"workload": DEC72_WORKLOAD, "global_batch": CFG5["batch"],
+                       "seq_len": CFG5["prompt"] + CFG5["vision"] + CFG5["text"],
+                       "parallelism": (f"KV heads {p.h0}..{p.h1 - 1} of {CFG5['kv_heads']} per rank, all_gather "
+                                       f"of outputs per layer" if p.mode == "heads" else
+                                       f"batch-sharded x{world} (no collective)"),
+                       "layers_resident": len(pool),
+                       "l2": f"{layer_bytes / 1e9:.2f} GB per layer per rank > 126 MB L2; no flush"},
+            "tokens_per_s": CFG5["batch"] / (step_us * 1e-6),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": peak_kind,
+                         "algorithmic_bytes_per_rank_step": rank_bytes, "traffic": None,
+                         "note": "rank 0's bytes over rank 0's own step time"},
+            "gpu_launches": CFG5["layers"] * args.steps * (3 if p.needs_gather else 1),
+            "clocks": clocks, "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -593,13 +712,24 @@ def main():
                     help="override the batch (profiling cases only; the bench line uses 32)")
     ap.add_argument("--kernel-only", action="store_true",
                     help="decode launches only: no e2e, no CPU baseline, no JSON bench line")
-    ap.add_argument("--workload", choices=["decode", "build"], default="decode",
-                    help="decode: BASELINE config 2 (the headline); build: config 4 rotation build")
+    ap.add_argument("--workload", choices=["decode", "build", "decode72b"], default="decode",
+                    help="decode: BASELINE config 2 (the headline); build: config 4 rotation build; "
+                         "decode72b: config 5 multi-GPU decode")
+    ap.add_argument("--shard", choices=["auto", "heads", "batch"], default="auto",
+                    help="decode72b: KV-head or batch sharding (auto: heads when N = 8)")
+    ap.add_argument("--pool", type=int, default=4, help="decode72b: resident layers cycled over the 80")
     ap.add_argument("--layers", type=int, default=None,
                     help="build workload: layers per step (profiling cases only; the bench line uses 28)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 20 if args.workload == "build" else 2000
+        args.steps = {"build": 20, "decode72b": 10}.get(args.workload, 2000)
+    if args.workload == "decode72b":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "metric": DEC72_METRIC,
+                              "unavailable": "config 5 is measured for this build only; the reference "
+                                             "CPU arm covers configs 2 and 4"}), flush=True)
+            return 0
+        return run_decode72b(args)
     if args.workload == "build":
         return run_build_reference(args) if args.impl == "reference" else run_build(args)
     if args.impl == "reference":
