@@ -580,6 +580,80 @@ def run_build_reference(args):
     return 0
 
 
+# ---------------------------------------------------------------- config 2 with cache maintenance
+STEP_METRIC = "decode step incl. KV-cache append us/step, config 2 shape (bs32 16k ctx, 25% K channels kept)"
+
+
+def run_decode_step(args):
+    """One decode step of one layer as a model runs it: append the new token's
+    K/V to the cache, then the fused decode.  ``SpanKVCache`` appends in place and
+    hands the decode views; the reference's cache and adapter instead copy the
+    whole V cache (torch.cat, cache_utils.py:52-53) and build k_full / v_full /
+    mask with torch.cat and torch.ones (llama_visionzip.py:203-214) every step --
+    timed here as ``adapter_path`` with the same decode kernel."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    from rotatek_b200 import synthetic as syn
+    from rotatek_b200.cache import SpanKVCache
+    from rotatek_b200.kernels import rotatek_decode
+    G = CFG["q_heads"] // CFG["kv_heads"]
+    sp, st, sv = CFG["prompt"], CFG["text"], CFG["vision"]
+    d = make_inputs(dev, seed=3)
+    kw = d.as_kwargs()
+    b, h = CFG["batch"], CFG["kv_heads"]
+    # prefill-order tensors: V = [prompt | visual | text]
+    k_prompt, k_text = kw["k_full"][:, :, :sp].contiguous(), kw["k_full"][:, :, sp:].contiguous()
+    values = torch.cat([kw["v_full"][:, :, :sp], kw["v_sparse"], kw["v_full"][:, :, sp:]], dim=-2)
+    n_steps = max(args.warmup, 3) + args.steps
+    cache = SpanKVCache(max_new_tokens=n_steps)
+    cache.store_pruned(kw["k_sparse"], k_prompt, k_text, values, kw["R_partial"], kw["delta_mu"], 0)
+    new_k = syn.normal((n_steps, b, h, 1, 128), 41, dev, torch.bfloat16)
+    new_v = syn.normal((n_steps, b, h, 1, 128), 42, dev, torch.bfloat16)
+    qs = syn.normal((n_steps, b, CFG["q_heads"], 128), 43, dev, torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+
+    def cache_step(i):
+        cache.update(new_k[i], new_v[i], 0)
+        rotatek_decode(q_full=qs[i], num_kv_groups=G, **cache.decode_args(0))
+
+    state = {"k_text": k_text, "values": values}
+
+    def adapter_step(i):
+        state["k_text"] = torch.cat([state["k_text"], new_k[i]], dim=-2)
+        state["values"] = torch.cat([state["values"], new_v[i]], dim=-2)
+        vals = state["values"]
+        rotatek_decode(q_full=qs[i], R_partial=kw["R_partial"], delta_mu=kw["delta_mu"],
+                       k_full=torch.cat([k_prompt, state["k_text"]], dim=-2),
+                       v_full=torch.cat([vals[:, :, :sp], vals[:, :, sp + sv:]], dim=-2),
+                       mask_full=torch.ones(b, sp + state["k_text"].shape[2], device=dev, dtype=torch.uint8),
+                       k_sparse=kw["k_sparse"], v_sparse=vals[:, :, sp:sp + sv], num_kv_groups=G)
+
+    def timed(fn):
+        w = max(args.warmup, 3)
+        for i in range(w):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(w, w + args.steps):
+            fn(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / args.steps
+
+    sampler = ClockSampler(0)
+    with sampler:
+        ours = timed(cache_step)
+    adapter = timed(adapter_step)
+    line = {"metric": STEP_METRIC, "value": ours, "unit": "us/step", "n_gpus": 1, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "higher_is_better": False, "dtype": "bf16",
+            "data": DATA, "config": {"workload": WORKLOAD + "; one token appended per step"},
+            "adapter_path_us": adapter, "speedup_vs_adapter_path": adapter / ours,
+            "gpu_launches": 3 * args.steps, "clocks": sampler.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------- config 5: multi-GPU decode
 DEC72_METRIC = "config5 decode step us/step (80 layers, B=64, 64/8 heads, 32k ctx, 25% K channels kept)"
 CFG5 = dict(layers=80, batch=64, q_heads=64, kv_heads=8, head_dim=128, keep=32, prompt=64, vision=31744,
@@ -712,9 +786,9 @@ def main():
                     help="override the batch (profiling cases only; the bench line uses 32)")
     ap.add_argument("--kernel-only", action="store_true",
                     help="decode launches only: no e2e, no CPU baseline, no JSON bench line")
-    ap.add_argument("--workload", choices=["decode", "build", "decode72b"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "build", "decode72b", "decode_step"], default="decode",
                     help="decode: BASELINE config 2 (the headline); build: config 4 rotation build; "
-                         "decode72b: config 5 multi-GPU decode")
+                         "decode72b: config 5 multi-GPU decode; decode_step: config 2 with cache appends")
     ap.add_argument("--shard", choices=["auto", "heads", "batch"], default="auto",
                     help="decode72b: KV-head or batch sharding (auto: heads when N = 8)")
     ap.add_argument("--pool", type=int, default=4, help="decode72b: resident layers cycled over the 80")
@@ -722,7 +796,9 @@ def main():
                     help="build workload: layers per step (profiling cases only; the bench line uses 28)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"build": 20, "decode72b": 10}.get(args.workload, 2000)
+        args.steps = {"build": 20, "decode72b": 10, "decode_step": 200}.get(args.workload, 2000)
+    if args.workload == "decode_step":
+        return run_decode_step(args)
     if args.workload == "decode72b":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "metric": DEC72_METRIC,
