@@ -654,6 +654,81 @@ def run_decode_step(args):
     return 0
 
 
+# ---------------------------------------------------------------- config 3: end-to-end decode
+E2E_METRIC = "config3 e2e greedy decode tokens/s (LLaVA-NeXT-7B-shaped, fp16, 16384 visual tokens, 128 steps)"
+
+
+def run_e2e(args):
+    """Config 3: a random-init LLaVA-NeXT-7B-shaped decoder (32 layers, 32 MHA
+    heads, hidden 4096, FFN 11008, vocab 32000, fp16), visual span of 16384
+    synthetic tokens; prefill with the per-layer rotation build, then 128 greedy
+    steps, each one CUDA-graph replay of the whole 32-layer step."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    from rotatek_b200.kernels import rotatek_decode
+    from rotatek_b200.llama_e2e import DecoderConfig, RandomLlamaDecoder
+    cfg = DecoderConfig(max_new_tokens=args.e2e_tokens)
+    model = RandomLlamaDecoder(cfg, dev, seed=0)
+    batches = [args.batch] if args.batch else [1, 4, 8]
+    peak, peak_kind = load_peak_hbm()
+    for b in batches:
+        x = model.prompt_embeddings(b, seed=b)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        logits = model.prefill(x)
+        e1.record()
+        torch.cuda.synchronize()
+        prefill_ms = e0.elapsed_time(e1)
+        del x
+        model.init_decode(logits.argmax(-1))
+        model.decode_step()                      # warm-up (workspaces); token 1
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            model.decode_step()
+        steps = cfg.max_new_tokens - 1
+        sampler = ClockSampler(0)
+        with sampler:
+            e0.record()
+            for _ in range(steps):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+        decode_ms = e0.elapsed_time(e1)
+        # one layer's decode attention on its own (same static arguments)
+        q = torch.randn(b, cfg.heads, cfg.head_dim, device=dev, dtype=cfg.dtype)
+        la = model.cache.static_decode_args(cfg.layers - 1, model.mask)
+        for _ in range(5):
+            rotatek_decode(q_full=q, num_kv_groups=1, **la)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(50):
+            rotatek_decode(q_full=q, num_kv_groups=1, **la)
+        e1.record()
+        torch.cuda.synchronize()
+        attn_us = e0.elapsed_time(e1) * 1e3 / 50
+        attn_bytes = model.attention_bytes_per_step() // cfg.layers
+        line = {
+            "metric": E2E_METRIC, "value": b * steps / (decode_ms * 1e-3), "unit": "tokens/s",
+            "n_gpus": 1, "steps": steps, "warmup": 1, "higher_is_better": True, "dtype": "fp16",
+            "data": "random-init weights, synthetic visual-span embeddings, random prompt tokens",
+            "config": {"workload": "config3: LLaVA-NeXT-7B-shaped decoder (Vicuna: 32 layers, 32 MHA heads, "
+                                   "hidden 4096, FFN 11008, vocab 32000), 32 prompt + 16384 visual + 32 text "
+                                   "tokens, channel_ratio 0.75", "batch": b},
+            "decode_ms_per_step": decode_ms / steps, "prefill_ms_incl_rotation_build": prefill_ms,
+            "decode_attention_us_per_layer": attn_us,
+            "decode_attention_hbm": {"achieved": attn_bytes / (attn_us * 1e-6) / 1e9, "peak": peak,
+                                     "unit": "GB/s", "frac": attn_bytes / (attn_us * 1e-6) / 1e9 / peak,
+                                     "algorithmic_bytes_per_layer": attn_bytes, "peak_source": peak_kind},
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(line), flush=True)
+        del g, logits
+        model.cache = None
+        torch.cuda.empty_cache()
+    return 0
+
+
 # ---------------------------------------------------------------- config 5: multi-GPU decode
 DEC72_METRIC = "config5 decode step us/step (80 layers, B=64, 64/8 heads, 32k ctx, 25% K channels kept)"
 CFG5 = dict(layers=80, batch=64, q_heads=64, kv_heads=8, head_dim=128, keep=32, prompt=64, vision=31744,
@@ -786,12 +861,15 @@ def main():
                     help="override the batch (profiling cases only; the bench line uses 32)")
     ap.add_argument("--kernel-only", action="store_true",
                     help="decode launches only: no e2e, no CPU baseline, no JSON bench line")
-    ap.add_argument("--workload", choices=["decode", "build", "decode72b", "decode_step"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "build", "decode72b", "decode_step", "e2e"],
+                    default="decode",
                     help="decode: BASELINE config 2 (the headline); build: config 4 rotation build; "
-                         "decode72b: config 5 multi-GPU decode; decode_step: config 2 with cache appends")
+                         "decode72b: config 5 multi-GPU decode; decode_step: config 2 with cache appends; "
+                         "e2e: config 3 LLaVA-NeXT-7B-shaped end-to-end decode")
     ap.add_argument("--shard", choices=["auto", "heads", "batch"], default="auto",
                     help="decode72b: KV-head or batch sharding (auto: heads when N = 8)")
     ap.add_argument("--pool", type=int, default=4, help="decode72b: resident layers cycled over the 80")
+    ap.add_argument("--e2e-tokens", type=int, default=128, help="e2e: greedy tokens per sequence")
     ap.add_argument("--layers", type=int, default=None,
                     help="build workload: layers per step (profiling cases only; the bench line uses 28)")
     args = ap.parse_args()
@@ -799,6 +877,8 @@ def main():
         args.steps = {"build": 20, "decode72b": 10, "decode_step": 200}.get(args.workload, 2000)
     if args.workload == "decode_step":
         return run_decode_step(args)
+    if args.workload == "e2e":
+        return run_e2e(args)
     if args.workload == "decode72b":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "metric": DEC72_METRIC,

@@ -100,6 +100,32 @@ class SpanKVCache:
                     v_full=L.values[:, :, :s_f], mask_full=None, k_sparse=L.keys_rot,
                     v_sparse=L.values[:, :, L.s_prompt + L.t_max:])
 
+    # ---- static-shape decode (CUDA-graph capture): the append position and the
+    # validity mask live on the device, the views cover the whole capacity
+    def write_at(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
+                 index: torch.Tensor) -> None:
+        """Write n new tokens ([B, H, n, D]) at text slots ``index`` (device int64
+        [n], absolute positions in keys_full / values); host counters untouched."""
+        L = self.layers[layer_idx]
+        L.keys_full.index_copy_(2, index, key_states)
+        L.values.index_copy_(2, index, value_states)
+
+    def capacity_mask(self, layer_idx: int = 0) -> torch.Tensor:
+        """A [B, S_p + T_max] uint8 mask, 1 on the prompt and the text stored so far."""
+        L = self.layers[layer_idx]
+        m = torch.zeros(L.keys_full.shape[0], L.s_prompt + L.t_max, dtype=torch.uint8,
+                        device=L.keys_full.device)
+        m[:, :L.s_prompt + L.s_text] = 1
+        return m
+
+    def static_decode_args(self, layer_idx: int, mask: torch.Tensor) -> dict:
+        """``decode_args`` over the whole text capacity, unwritten slots masked."""
+        L = self.layers[layer_idx]
+        cap = L.s_prompt + L.t_max
+        return dict(R_partial=L.rotation, delta_mu=L.delta_mu, k_full=L.keys_full[:, :, :cap],
+                    v_full=L.values[:, :, :cap], mask_full=mask, k_sparse=L.keys_rot,
+                    v_sparse=L.values[:, :, cap:])
+
     def get_seq_length(self, layer_idx: int = 0) -> int:
         if len(self.layers) <= layer_idx:
             return 0

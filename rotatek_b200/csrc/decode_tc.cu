@@ -636,19 +636,30 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
           for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
           lsum[h] += lw;
         }
+        // kU slots per step with all their loads issued first: the L2 round
+        // trips overlap instead of running one slot at a time
+        constexpr int kU = kHeads <= 8 ? 4 : 1;
         const int nk = min(32, nslots - k0);
-        for (int k = 0; k < nk; ++k) {
-          const float4 *ok = reinterpret_cast<const float4 *>(s0 + (long long)(k0 + k) * p.slot_floats + 32) + lane;
-          float4 v[kHeads];
+        for (int k = 0; k < nk; k += kU) {
+          float4 v[kU][kHeads];
 #pragma unroll
-          for (int h = 0; h < kHeads; ++h) v[h] = __ldcg(ok + h * (kHeadDim / 4));
+          for (int u = 0; u < kU; ++u) {
+            const float4 *ok =
+                reinterpret_cast<const float4 *>(s0 + (long long)(k0 + k + u) * p.slot_floats + 32) + lane;
 #pragma unroll
-          for (int h = 0; h < kHeads; ++h) {
-            const float wk = __shfl_sync(0xffffffffu, w[h], k);
-            acc[h].x += v[h].x * wk;
-            acc[h].y += v[h].y * wk;
-            acc[h].z += v[h].z * wk;
-            acc[h].w += v[h].w * wk;
+            for (int h = 0; h < kHeads; ++h)
+              v[u][h] = k + u < nk ? __ldcg(ok + h * (kHeadDim / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int u = 0; u < kU; ++u) {
+#pragma unroll
+            for (int h = 0; h < kHeads; ++h) {
+              const float wk = __shfl_sync(0xffffffffu, w[h], (k + u) & 31);
+              acc[h].x += v[u][h].x * wk;
+              acc[h].y += v[u][h].y * wk;
+              acc[h].z += v[u][h].z * wk;
+              acc[h].w += v[u][h].w * wk;
+            }
           }
         }
       }
