@@ -245,6 +245,95 @@ __device__ __forceinline__ void load_header(unsigned char *hdr, const DecodePara
   cp_async_wait_all();
 }
 
+// Merge of one unit's partials (one per consumer warp of CTAs c_first..c_last),
+// in slot order (deterministic): per-head max, weights 2^(m_k - max), weighted
+// sums; output in the query dtype.  KH = heads merged (the first KH of the
+// slot's 8 or 16; a single-head unit -- G = 1 -- reads one head per slot).
+template <typename T, int KH, int kWarps>
+__device__ __forceinline__ void merge_unit(const DecodeParams &p, int unit, int c_first, int c_last,
+                                           int bk, int head0, int nheads, int lane) {
+
+  // every partial of the unit is in place: merge them in slot order.
+  // Pass 1: lane k holds slot k0 + k; per-head max and normaliser by shuffles.
+  __threadfence();
+  const float *s0 = p.partials + (long long)(unit + c_first) * kWarps * p.slot_floats;
+  const int nslots = kWarps * (c_last - c_first + 1);
+  float mx[KH];
+#pragma unroll
+  for (int h = 0; h < KH; ++h) mx[h] = kNegBig;
+  for (int k0 = 0; k0 < nslots; k0 += 32) {
+    const bool on = k0 + lane < nslots;
+    const float *sl = s0 + (long long)(k0 + lane) * p.slot_floats;
+#pragma unroll
+    for (int h = 0; h < KH; ++h) {
+      float v = on ? __ldcg(sl + h) : kNegBig;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+      mx[h] = fmaxf(mx[h], v);
+    }
+  }
+  // Pass 2: weights w[k][h] = 2^(m_k - max) (lane k), then acc over slots;
+  // lane owns channels 4*lane .. 4*lane+3 of every head.
+  float lsum[KH];
+  float4 acc[KH];
+#pragma unroll
+  for (int h = 0; h < KH; ++h) {
+    lsum[h] = 0.f;
+    acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int k0 = 0; k0 < nslots; k0 += 32) {
+    const bool on = k0 + lane < nslots;
+    const float *sl = s0 + (long long)(k0 + lane) * p.slot_floats;
+    float w[KH];
+#pragma unroll
+    for (int h = 0; h < KH; ++h) {
+      w[h] = on ? fast_exp2(__ldcg(sl + h) - mx[h]) : 0.f;
+      float lw = on ? __ldcg(sl + 16 + h) * w[h] : 0.f;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
+      lsum[h] += lw;
+    }
+    // kU slots per step with all their loads issued first: the L2 round
+    // trips overlap instead of running one slot at a time
+    constexpr int kU = KH == 1 ? 32 : (KH <= 8 ? 4 : 1);
+    const int nk = min(32, nslots - k0);
+    for (int k = 0; k < nk; k += kU) {
+      float4 v[kU][KH];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const float4 *ok =
+            reinterpret_cast<const float4 *>(s0 + (long long)(k0 + k + u) * p.slot_floats + 32) + lane;
+#pragma unroll
+        for (int h = 0; h < KH; ++h)
+          v[u][h] = k + u < nk ? __ldcg(ok + h * (kHeadDim / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+#pragma unroll
+        for (int h = 0; h < KH; ++h) {
+          const float wk = __shfl_sync(0xffffffffu, w[h], (k + u) & 31);
+          acc[h].x += v[u][h].x * wk;
+          acc[h].y += v[u][h].y * wk;
+          acc[h].z += v[u][h].z * wk;
+          acc[h].w += v[u][h].w * wk;
+        }
+      }
+    }
+  }
+  T *outb = reinterpret_cast<T *>(p.out) + (long long)bk * p.o_sb;
+#pragma unroll
+  for (int h = 0; h < KH; ++h) {
+    if (h < nheads) {
+      const float inv = 1.f / (lsum[h] + 1e-6f);
+      T *orow = outb + (long long)(head0 + h) * p.o_sh + lane * 4;
+      orow[0] = from_f32<T>(acc[h].x * inv);
+      orow[1] = from_f32<T>(acc[h].y * inv);
+      orow[2] = from_f32<T>(acc[h].z * inv);
+      orow[3] = from_f32<T>(acc[h].w * inv);
+    }
+  }
+}
+
 template <typename T, int NT, int DK>
 __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
     rotatek_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_kf,
@@ -574,6 +663,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int h = nt * 8 + 2 * t4 + c;
+        if (h >= nheads) continue;  // padding heads: never merged
         if (g8 == 0) {
           slot[h] = m_run[nt][c];
           slot[16 + h] = l_run[nt][c];
@@ -596,85 +686,10 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
     }
     last = __shfl_sync(0xffffffffu, last, 0);
     if (last) {
-      // every partial of the unit is in place: merge them in slot order.
-      // Pass 1: lane k holds slot k0 + k; per-head max and normaliser by shuffles.
-      __threadfence();
-      const float *s0 = p.partials + (long long)(unit + c_first) * kWarps * p.slot_floats;
-      const int nslots = kWarps * (c_last - c_first + 1);
-      float mx[kHeads];
-#pragma unroll
-      for (int h = 0; h < kHeads; ++h) mx[h] = kNegBig;
-      for (int k0 = 0; k0 < nslots; k0 += 32) {
-        const bool on = k0 + lane < nslots;
-        const float *sl = s0 + (long long)(k0 + lane) * p.slot_floats;
-#pragma unroll
-        for (int h = 0; h < kHeads; ++h) {
-          float v = on ? __ldcg(sl + h) : kNegBig;
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
-          mx[h] = fmaxf(mx[h], v);
-        }
-      }
-      // Pass 2: weights w[k][h] = 2^(m_k - max) (lane k), then acc over slots;
-      // lane owns channels 4*lane .. 4*lane+3 of every head.
-      float lsum[kHeads];
-      float4 acc[kHeads];
-#pragma unroll
-      for (int h = 0; h < kHeads; ++h) {
-        lsum[h] = 0.f;
-        acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      for (int k0 = 0; k0 < nslots; k0 += 32) {
-        const bool on = k0 + lane < nslots;
-        const float *sl = s0 + (long long)(k0 + lane) * p.slot_floats;
-        float w[kHeads];
-#pragma unroll
-        for (int h = 0; h < kHeads; ++h) {
-          w[h] = on ? fast_exp2(__ldcg(sl + h) - mx[h]) : 0.f;
-          float lw = on ? __ldcg(sl + 16 + h) * w[h] : 0.f;
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
-          lsum[h] += lw;
-        }
-        // kU slots per step with all their loads issued first: the L2 round
-        // trips overlap instead of running one slot at a time
-        constexpr int kU = kHeads <= 8 ? 4 : 1;
-        const int nk = min(32, nslots - k0);
-        for (int k = 0; k < nk; k += kU) {
-          float4 v[kU][kHeads];
-#pragma unroll
-          for (int u = 0; u < kU; ++u) {
-            const float4 *ok =
-                reinterpret_cast<const float4 *>(s0 + (long long)(k0 + k + u) * p.slot_floats + 32) + lane;
-#pragma unroll
-            for (int h = 0; h < kHeads; ++h)
-              v[u][h] = k + u < nk ? __ldcg(ok + h * (kHeadDim / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
-#pragma unroll
-          for (int u = 0; u < kU; ++u) {
-#pragma unroll
-            for (int h = 0; h < kHeads; ++h) {
-              const float wk = __shfl_sync(0xffffffffu, w[h], (k + u) & 31);
-              acc[h].x += v[u][h].x * wk;
-              acc[h].y += v[u][h].y * wk;
-              acc[h].z += v[u][h].z * wk;
-              acc[h].w += v[u][h].w * wk;
-            }
-          }
-        }
-      }
-      T *outb = reinterpret_cast<T *>(p.out) + (long long)bk * p.o_sb;
-#pragma unroll
-      for (int h = 0; h < kHeads; ++h) {
-        if (h < nheads) {
-          const float inv = 1.f / (lsum[h] + 1e-6f);
-          T *orow = outb + (long long)(head0 + h) * p.o_sh + lane * 4;
-          orow[0] = from_f32<T>(acc[h].x * inv);
-          orow[1] = from_f32<T>(acc[h].y * inv);
-          orow[2] = from_f32<T>(acc[h].z * inv);
-          orow[3] = from_f32<T>(acc[h].w * inv);
-        }
-      }
+      if (nheads == 1)
+        merge_unit<T, 1, kWarps>(p, unit, c_first, c_last, bk, head0, nheads, lane);
+      else
+        merge_unit<T, kHeads, kWarps>(p, unit, c_first, c_last, bk, head0, nheads, lane);
     }
     it = seg_end;
     ++unit;
