@@ -643,7 +643,11 @@ int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_
   jp.sweeps = sweeps;
   jp.rot_log = rot_log;
   jp.max_sweeps = rtk::kJacobiMaxSweeps;
-  jp.tol = 1e-6f;
+  // Converge as far as the output dtype can hold: R is rounded to the Keys'
+  // dtype, whose rounding alone moves span(R) by ~8e-3 (bf16) / ~2e-3 (fp16) in
+  // projector distance, while off(A) <= tol ||diag A|| leaves it ~20 tol from
+  // the exact eigenvectors.
+  jp.tol = dt == RTK_BF16 ? 1e-4f : dt == RTK_F16 ? 2.5e-5f : 1e-6f;
   e = rtk::launch_jacobi(jp, st);
   if (e != cudaSuccess) return cuda_fail(e, "rotation builder (eigensolver) launch");
 
