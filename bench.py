@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (the headline metric): one attention layer's
+Workload (benchmark config 2, the headline metric): one attention layer's
 single-token decode at the Qwen2.5-VL-7B attention shape -- bf16, B=32,
 28 query / 4 KV heads (G=7), head_dim 128, D_keep=32 (channel_ratio 0.75),
 64 prompt + 15 360 visual + 576 text tokens.  A step is one call of
@@ -493,7 +493,7 @@ def run_build(args):
             "metric": BUILD_METRIC, "value": us_per_step, "unit": "us/step", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": total_ms / args.steps,
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: seeded low-rank+noise Keys (BASELINE generator), N(0,1) queries",
+            "data": "synthetic: seeded low-rank+noise Keys (the benchmark generator), N(0,1) queries",
             "config": {"workload": BUILD_WORKLOAD, "layers": keys.shape[0] // CFG4["batch"],
                        "global_batch": CFG4["batch"] * world,
                        "seq_len": CFG4["vision"], "parallelism": f"replicas x{world} (no collective)",
@@ -863,7 +863,7 @@ def main():
                     help="decode launches only: no e2e, no CPU baseline, no JSON bench line")
     ap.add_argument("--workload", choices=["decode", "build", "decode72b", "decode_step", "e2e"],
                     default="decode",
-                    help="decode: BASELINE config 2 (the headline); build: config 4 rotation build; "
+                    help="decode: benchmark config 2 (the headline); build: config 4 rotation build; "
                          "decode72b: config 5 multi-GPU decode; decode_step: config 2 with cache appends; "
                          "e2e: config 3 LLaVA-NeXT-7B-shaped end-to-end decode")
     ap.add_argument("--shard", choices=["auto", "heads", "batch"], default="auto",

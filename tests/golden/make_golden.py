@@ -162,7 +162,7 @@ def main():
     def want(name):
         return args.only is None or args.only == name
     bf16 = torch.bfloat16
-    # fp32, B=2, 8/2 heads, 32 + 576 + 64, ratio 0.75
+    # benchmark config 1: fp32, B=2, 8/2 heads, 32 + 576 + 64, ratio 0.75
     if want("cfg1_fp32"):
         prefill_case("cfg1_fp32", mods, torch, synth, batch=2, q_heads=8, kv_heads=2, prompt=32,
                      vision=576, text=64, ratio=0.75, dtype=torch.float32, seed=1,

@@ -164,7 +164,7 @@ def bf16_half_ulp(x):
 
 
 def test_decode_config2_full_size():
-    """BASELINE config 2 at full size: B=32, 28/4 heads, 64+15360+576, keep 32, bf16.
+    """benchmark config 2 at full size: B=32, 28/4 heads, 64+15360+576, keep 32, bf16.
 
     The north-star bar is max-abs 2e-3 on the bf16 output.  Outputs here reach
     |x| ~ 4, where storing in bf16 alone moves a value by up to 2^-7, so the bar

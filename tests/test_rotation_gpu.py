@@ -158,7 +158,7 @@ def test_build_rotation_matches_reference(golden, case, inputs):
 
 
 def test_build_rotation_config4_layer():
-    """One layer of BASELINE config 4: B=8, 4 KV heads (G=7), S_v=15360, bf16, keep 32."""
+    """One layer of benchmark config 4: B=8, 4 KV heads (G=7), S_v=15360, bf16, keep 32."""
     B, H, G, S = 8, 4, 7, 15360
     k = syn.lowrank_keys(B, H, S, seed=44, device=DEV, dtype=torch.bfloat16)
     q = syn.normal((B, H * G, 32, 128), 45, DEV, torch.bfloat16)

@@ -30,7 +30,7 @@ def _static_decode(d, out):
 
 
 @pytest.mark.parametrize("dtype,B,Hq,Hkv,Sv,Sf", [
-    (torch.bfloat16, 32, 28, 4, 15360, 640),   # BASELINE config 2 (tensor-core kernel)
+    (torch.bfloat16, 32, 28, 4, 15360, 640),   # benchmark config 2 (tensor-core kernel)
     (torch.float32, 2, 8, 2, 576, 96),         # config-1 shape (generic kernel)
 ])
 def test_static_entry_matches_workspace_entry(dtype, B, Hq, Hkv, Sv, Sf):
