@@ -122,4 +122,42 @@ def full_channel_decode(
     return out
 
 
-__all__ = ["ROTATEK_KERNEL", "rotatek_decode", "full_channel_decode"]
+def think_selection(think_mask: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """R_sel [B, H_kv, D, D_keep] = the identity's columns of each head's kept
+    channels (in channel order): q . R_sel picks q's kept channels."""
+    b, h, d = think_mask.shape
+    keep = int(think_mask[0, 0].sum())
+    if not bool((think_mask.sum(-1) == keep).all()):
+        raise ValueError("every head must keep the same number of channels")
+    idx = think_mask.nonzero()[:, 2].view(b, h, keep)                    # kept channels, ascending
+    R = torch.zeros(b, h, d, keep, dtype=dtype, device=think_mask.device)
+    R.scatter_(2, idx.unsqueeze(2), 1)
+    return R
+
+
+def think_decode(
+    q_full: torch.Tensor,                # [B, H_q, D]
+    think_mask: torch.Tensor,            # [B, H_kv, D] bool, True = kept (ChannelPruner.current_think_mask)
+    key_pruned: torch.Tensor,            # [B, H_kv, S_vis, D_keep] kept channels, channel order
+    k_full: torch.Tensor,                # [B, H_kv, S_full, D]
+    v_full: torch.Tensor,                # [B, H_kv, S_full, D]
+    mask_full: Optional[torch.Tensor],   # [B, S_full] uint8
+    v_sparse: torch.Tensor,              # [B, H_kv, S_vis, D]
+    num_kv_groups: int,
+) -> torch.Tensor:
+    """The ThinK baseline's decode without recovering full-width Keys.
+
+    The adapters zero-fill the pruned channels of the visual Keys, concatenate
+    prompt, visual and text Keys and run ``full_channel_decode``
+    (llama_visionzip.py:217-240).  A zero channel adds nothing to q . k, so the
+    same logits are q[kept] . k_pruned on the visual span and q . k on the
+    prompt/text span -- the RotateK kernel with R = the kept channels'
+    selection and no delta_mu.  Returns [B, 1, H_q, D]."""
+    R = think_selection(think_mask, q_full.dtype)
+    out, _, _ = rotatek_decode(q_full=q_full, R_partial=R, delta_mu=None, k_full=k_full, v_full=v_full,
+                               mask_full=mask_full, k_sparse=key_pruned, v_sparse=v_sparse,
+                               num_kv_groups=num_kv_groups)
+    return out
+
+
+__all__ = ["ROTATEK_KERNEL", "rotatek_decode", "full_channel_decode", "think_decode", "think_selection"]

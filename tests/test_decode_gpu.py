@@ -249,3 +249,34 @@ def test_reference_value_errors():
         full_channel_decode(kw["q_full"][0], kw["k_full"], kw["v_full"], 4)
     with pytest.raises(ValueError, match="head_dim must match"):
         full_channel_decode(kw["q_full"], kw["k_full"][..., :64], kw["v_full"], 4)
+
+
+@pytest.mark.parametrize("dtype,G", [(torch.bfloat16, 7), (torch.float32, 1)])
+def test_think_decode_matches_recovered_dense(dtype, G):
+    """ThinK: the fused decode on the kept channels equals the dense decode on
+    Keys with the pruned channels zero-filled (llama_visionzip.py:217-240)."""
+    from rotatek_b200.kernels import think_decode
+    B, Hkv, Sv, Sf, D, keep = 2, 2, 300, 40, 128, 32
+    gen = torch.Generator().manual_seed(11)
+    k_vis = torch.randn(B, Hkv, Sv, D, generator=gen)
+    scores = torch.rand(B, Hkv, D, generator=gen)
+    think_mask = torch.zeros(B, Hkv, D, dtype=torch.bool)
+    think_mask.scatter_(2, scores.topk(keep, dim=-1).indices, True)
+    sel = think_mask.unsqueeze(2).expand(-1, -1, Sv, -1)
+    key_pruned = k_vis[sel].view(B, Hkv, Sv, keep)
+    recovered = torch.zeros_like(k_vis)
+    recovered[sel] = key_pruned.reshape(-1)
+    k_full = torch.randn(B, Hkv, Sf, D, generator=gen)
+    v_full = torch.randn(B, Hkv, Sf, D, generator=gen)
+    v_vis = torch.randn(B, Hkv, Sv, D, generator=gen)
+    q = torch.randn(B, Hkv * G, D, generator=gen)
+    cu = lambda t: t.to(DEV, dtype)  # noqa: E731
+    got = think_decode(cu(q), think_mask.to(DEV), cu(key_pruned), cu(k_full), cu(v_full), None, cu(v_vis), G)
+    # float64 restatement of the adapters' path, on the same (rounded) inputs:
+    # dense decode over [prompt/text | zero-filled visual Keys]
+    rnd = lambda t: np.asarray(t.to(dtype).float().numpy(), dtype=np.float64)  # noqa: E731
+    want = odec.full_channel_decode(rnd(q), rnd(torch.cat([k_full, recovered], -2)),
+                                    rnd(torch.cat([v_full, v_vis], -2)), G)
+    rel = 2.0 ** -8 if dtype == torch.bfloat16 else 1e-5
+    tol = (2e-3 if dtype == torch.bfloat16 else 1e-5) + rel * np.abs(want).max()
+    np.testing.assert_allclose(got.float().cpu().numpy(), want, rtol=0, atol=tol)

@@ -239,3 +239,22 @@ def test_pruner_update_rotatek_contract():
     assert pr.current_rotatek_R_partial.shape == (B, Hkv, 128, 32)
     assert pr.current_rotatek_delta_mu.shape == (B, Hkv, 128)
     assert update_rotatek is ChannelPruner.update_rotatek
+
+
+def test_build_rotation_cuda_graph_replay():
+    """The build runs on the caller's stream with no host synchronisation, so it
+    can be captured in a CUDA graph (after one eager call has sized the
+    workspace) and replayed with identical results."""
+    k = syn.lowrank_keys(2, 2, 777, seed=31, device=DEV, dtype=torch.bfloat16)
+    q = syn.normal((2, 8, 32, 128), 32, DEV, torch.bfloat16)
+    eager = rot.build_rotation(k, q, 32, 4)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = rot.build_rotation(k, q, 32, 4)
+    g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(eager, out):
+        assert torch.equal(a, b)
+    assert rot.read_build_status() == 0
+    del g
