@@ -654,6 +654,77 @@ def run_decode_step(args):
     return 0
 
 
+# ---------------------------------------------------------------- ThinK baseline at config 2
+THINK_METRIC = "ThinK decode step us/step, config 2 shape (bs32 16k ctx, 32 of 128 K channels kept per head)"
+
+
+def run_think(args):
+    """ThinK's decode at the config-2 shape: ``think_decode`` (the kept channels
+    through the fused kernel) against the adapters' path -- zero-filled
+    recovery of the visual Keys, concatenation and the dense decode
+    (llama_visionzip.py:217-240) -- both on this GPU."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    from rotatek_b200 import synthetic as syn
+    from rotatek_b200.kernels import full_channel_decode, think_decode
+    b, hkv, G, sp, sv, st = CFG["batch"], CFG["kv_heads"], CFG["q_heads"] // CFG["kv_heads"], CFG["prompt"], \
+        CFG["vision"], CFG["text"]
+    keep = CFG["keep"]
+    k_all = syn.lowrank_keys(b, hkv, sp + sv + st, seed=5, device=dev, dtype=torch.bfloat16)
+    values = syn.normal((b, hkv, sp + sv + st, 128), 6, dev, torch.bfloat16)
+    q = syn.normal((b, CFG["q_heads"], 128), 7, dev, torch.bfloat16)
+    score = torch.rand(b, hkv, 128, device=dev)
+    think_mask = torch.zeros(b, hkv, 128, dtype=torch.bool, device=dev)
+    think_mask.scatter_(2, score.topk(keep, dim=-1).indices, True)
+    k_vis = k_all[:, :, sp:sp + sv]
+    sel = think_mask.unsqueeze(2).expand(-1, -1, sv, -1)
+    key_pruned = k_vis[sel].view(b, hkv, sv, keep)
+    k_prompt, k_text = k_all[:, :, :sp].contiguous(), k_all[:, :, sp + sv:].contiguous()
+    k_full = torch.cat([k_prompt, k_text], dim=-2)
+    v_full = torch.cat([values[:, :, :sp], values[:, :, sp + sv:]], dim=-2)
+    v_vis = values[:, :, sp:sp + sv]
+
+    from rotatek_b200.kernels import think_selection
+    selection = think_selection(think_mask, keep, q.dtype)   # once per layer, after prefill
+
+    def fused():
+        think_decode(q, think_mask, key_pruned, k_full, v_full, None, v_vis, G, selection=selection)
+
+    def adapter():
+        recovered = torch.zeros(b, hkv, sv, 128, dtype=key_pruned.dtype, device=dev)
+        recovered[sel] = key_pruned.reshape(-1)
+        keys = torch.cat([k_prompt, recovered, k_text], dim=-2)
+        full_channel_decode(q, keys, values, num_kv_groups=G)
+
+    def timed(fn, n):
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / n
+
+    sampler = ClockSampler(0)
+    with sampler:
+        ours = timed(fused, args.steps)
+    theirs = timed(adapter, max(10, args.steps // 10))
+    nbytes = (key_pruned.numel() + v_vis.numel() + k_full.numel() + v_full.numel() + 2 * q.numel()) * 2
+    peak, peak_kind = load_peak_hbm()
+    print(json.dumps({"metric": THINK_METRIC, "value": ours, "unit": "us/step", "n_gpus": 1, "steps": args.steps,
+                      "higher_is_better": False, "dtype": "bf16", "data": DATA,
+                      "config": {"workload": WORKLOAD + "; ThinK channel selection instead of a rotation"},
+                      "adapter_path_us": theirs, "speedup_vs_adapter_path": theirs / ours,
+                      "roofline": {"bound": "hbm", "achieved": nbytes / ours / 1e3, "peak": peak, "unit": "GB/s",
+                                   "frac": nbytes / ours / 1e3 / peak, "peak_source": peak_kind,
+                                   "algorithmic_bytes_per_launch": nbytes},
+                      "clocks": sampler.summary()}), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------- config 3: end-to-end decode
 E2E_METRIC = "config3 e2e greedy decode tokens/s (LLaVA-NeXT-7B-shaped, fp16, 16384 visual tokens, 128 steps)"
 
@@ -861,11 +932,11 @@ def main():
                     help="override the batch (profiling cases only; the bench line uses 32)")
     ap.add_argument("--kernel-only", action="store_true",
                     help="decode launches only: no e2e, no CPU baseline, no JSON bench line")
-    ap.add_argument("--workload", choices=["decode", "build", "decode72b", "decode_step", "e2e"],
+    ap.add_argument("--workload", choices=["decode", "build", "decode72b", "decode_step", "e2e", "think"],
                     default="decode",
                     help="decode: benchmark config 2 (the headline); build: config 4 rotation build; "
                          "decode72b: config 5 multi-GPU decode; decode_step: config 2 with cache appends; "
-                         "e2e: config 3 LLaVA-NeXT-7B-shaped end-to-end decode")
+                         "e2e: config 3 LLaVA-NeXT-7B-shaped end-to-end decode; think: ThinK at config 2")
     ap.add_argument("--shard", choices=["auto", "heads", "batch"], default="auto",
                     help="decode72b: KV-head or batch sharding (auto: heads when N = 8)")
     ap.add_argument("--pool", type=int, default=4, help="decode72b: resident layers cycled over the 80")
@@ -874,11 +945,13 @@ def main():
                     help="build workload: layers per step (profiling cases only; the bench line uses 28)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"build": 20, "decode72b": 10, "decode_step": 200}.get(args.workload, 2000)
+        args.steps = {"build": 20, "decode72b": 10, "decode_step": 200, "think": 200}.get(args.workload, 2000)
     if args.workload == "decode_step":
         return run_decode_step(args)
     if args.workload == "e2e":
         return run_e2e(args)
+    if args.workload == "think":
+        return run_think(args)
     if args.workload == "decode72b":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "metric": DEC72_METRIC,

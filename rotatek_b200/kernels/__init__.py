@@ -122,16 +122,14 @@ def full_channel_decode(
     return out
 
 
-def think_selection(think_mask: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
-    """R_sel [B, H_kv, D, D_keep] = the identity's columns of each head's kept
-    channels (in channel order): q . R_sel picks q's kept channels."""
+def think_selection(think_mask: torch.Tensor, keep: int, dtype: torch.dtype) -> torch.Tensor:
+    """R_sel [B, H_kv, D, keep] = the identity's columns of each head's kept
+    channels in channel order (q . R_sel picks q's kept channels).  No host
+    synchronisation: the kept channels come from a stable sort of the mask."""
     b, h, d = think_mask.shape
-    keep = int(think_mask[0, 0].sum())
-    if not bool((think_mask.sum(-1) == keep).all()):
-        raise ValueError("every head must keep the same number of channels")
-    idx = think_mask.nonzero()[:, 2].view(b, h, keep)                    # kept channels, ascending
+    order = torch.sort((~think_mask).to(torch.uint8), dim=-1, stable=True).indices[..., :keep]
     R = torch.zeros(b, h, d, keep, dtype=dtype, device=think_mask.device)
-    R.scatter_(2, idx.unsqueeze(2), 1)
+    R.scatter_(2, order.unsqueeze(2), 1)
     return R
 
 
@@ -144,6 +142,7 @@ def think_decode(
     mask_full: Optional[torch.Tensor],   # [B, S_full] uint8
     v_sparse: torch.Tensor,              # [B, H_kv, S_vis, D]
     num_kv_groups: int,
+    selection: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """The ThinK baseline's decode without recovering full-width Keys.
 
@@ -152,9 +151,12 @@ def think_decode(
     (llama_visionzip.py:217-240).  A zero channel adds nothing to q . k, so the
     same logits are q[kept] . k_pruned on the visual span and q . k on the
     prompt/text span -- the RotateK kernel with R = the kept channels'
-    selection and no delta_mu.  Returns [B, 1, H_q, D]."""
-    R = think_selection(think_mask, q_full.dtype)
-    out, _, _ = rotatek_decode(q_full=q_full, R_partial=R, delta_mu=None, k_full=k_full, v_full=v_full,
+    selection and no delta_mu.  ``selection`` is ``think_selection(think_mask,
+    D_keep, q.dtype)``, built here when not given; the mask is fixed after
+    prefill, so a caller can build it once per layer.  Returns [B, 1, H_q, D]."""
+    if selection is None:
+        selection = think_selection(think_mask, key_pruned.shape[-1], q_full.dtype)
+    out, _, _ = rotatek_decode(q_full=q_full, R_partial=selection, delta_mu=None, k_full=k_full, v_full=v_full,
                                mask_full=mask_full, k_sparse=key_pruned, v_sparse=v_sparse,
                                num_kv_groups=num_kv_groups)
     return out
