@@ -194,6 +194,43 @@ int rtk_build_rotation(const rtk_tensor *keys_vision, const rtk_tensor *queries_
                        const rtk_tensor *eigvals_out, void *workspace, size_t workspace_bytes,
                        void *stream);
 
+/* The prefill Key path of the attention adapters, fused with the covariance
+ * sums.  Replaces k_proj -> view / transpose -> apply_rotary_pos_emb
+ * (integrations/lmms_eval/models/model_utils/llava_next/llama_visionzip.py:144-153;
+ * qwen/qwen2_5vl_visionzip.py:932-942 once the multimodal cos / sin sections are
+ * merged) and the covariance pass over its visual span (kv_pruning_utils.py:112-115):
+ *   keys_out[b, h, s] = k * cos + rotate_half(k) * sin,
+ *   k = hidden[b, s] . w_k[h*128 : h*128 + 128]^T + bias[h*128 : ...]
+ * rounded as torch rounds those bf16 / fp16 ops, for every token s; cov_out and
+ * ksum_out as rtk_key_covariance over the visual tokens
+ * [vis_start, vis_start + vis_len) of keys_out.  One pass on the tcgen05
+ * tensor cores.
+ *   hidden     [B, S, hidden]      bf16 | f16, hidden % 64 == 0, 16-byte aligned rows
+ *   w_k        [H_kv * 128, hidden]  same dtype (nn.Linear weight)
+ *   bias       [H_kv * 128]        same dtype, contiguous, nullable
+ *   cos, sin   [B or 1, S, 128]    same dtype, channel stride 1
+ *   keys_out   [B, H_kv, S, 128]   same dtype, channel stride 1
+ *   cov_out    [B, H_kv, 128, 128] f32 contiguous; ksum_out [B, H_kv, 128] f32 contiguous
+ *   workspace  >= 256 bytes whose first word is the device-status word        */
+int rtk_key_projection(const rtk_tensor *hidden, const rtk_tensor *w_k, const rtk_tensor *bias,
+                       const rtk_tensor *cos, const rtk_tensor *sin, int64_t vis_start, int64_t vis_len,
+                       const rtk_tensor *keys_out, const rtk_tensor *cov_out, const rtk_tensor *ksum_out,
+                       void *workspace, size_t workspace_bytes, void *stream);
+
+/* rtk_key_projection followed by the rest of rtk_build_rotation on the visual
+ * span of keys_out: from a layer's hidden states to what the split cache stores
+ * (K for every token; R, delta_mu and kept = K_vis . R for the visual span)
+ * with one pass over the Keys fewer than projection + rtk_build_rotation.
+ * Arguments as in the two calls; kept_out is [B, H_kv, vis_len, keep];
+ * workspace of rtk_build_rotation_workspace_size(B, H_kv, 128) bytes.         */
+int rtk_build_rotation_projected(const rtk_tensor *hidden, const rtk_tensor *w_k, const rtk_tensor *bias,
+                                 const rtk_tensor *cos, const rtk_tensor *sin, int64_t vis_start,
+                                 int64_t vis_len, const rtk_tensor *queries_recent, int64_t num_kv_groups,
+                                 int64_t keep, const rtk_tensor *keys_out, const rtk_tensor *kept_out,
+                                 const rtk_tensor *R_out, const rtk_tensor *delta_mu_out,
+                                 const rtk_tensor *eigvals_out, void *workspace, size_t workspace_bytes,
+                                 void *stream);
+
 /* Copy the workspace's device-status word to *status (RTK_DEVICE_TIMEOUT bits)
  * and clear it.  Synchronises `stream`.                                       */
 int rtk_read_status(void *workspace, void *stream, uint32_t *status);

@@ -26,6 +26,34 @@ cudaError_t launch_cov_tc(int dtype_is_bf16, const CUtensorMap &keys_map, const 
                           cudaStream_t stream);
 cudaError_t launch_cov_simt(const CovParams &p, cudaStream_t stream);
 
+// Fused Key projection (the prefill K path of the attention adapters, then the
+// covariance pass): for every (b, h) and every token s,
+//   K[b, h, s, :] = RoPE(X[b, s, :] W[h*128 : h*128 + 128, :]^T + bias)
+// in the Keys' dtype, rounded like torch's bf16 / fp16 ops (projection output,
+// k * cos, rotate_half(k) * sin, their sum), and over the visual tokens
+// [vis_start, vis_start + vis_len) the raw sums of CovParams from those K values.
+struct KProjParams {
+  int batch, heads, seq, hidden;  // hidden % 64 == 0
+  int vis_start, vis_len;
+  const void *bias;                       // [heads * 128] or NULL
+  const void *cos, *sin;                  // [B | 1, S, 128] (element strides below, channel stride 1)
+  long long cs_sb, cs_ss;                 // batch stride (0 = broadcast), token stride
+  float *cov;                             // [B * H][128][128]
+  float *ksum;                            // [B * H][128]
+  unsigned int *status;                   // device status word (bounded-wait timeouts)
+  int splits;                             // CTAs (one cluster) per (b, h)
+};
+
+// x: [B, S, hidden] 3-D map, box {64, 128, 1}; w: [H*128, hidden] 2-D map, box
+// {64, 128}; k_out[i]: the output [B, H, len_i, 128] of span i (prompt, visual,
+// text) as 4-D maps with box {64, 128, 1, 1}; all 128B-swizzled.
+struct KProjMaps {
+  CUtensorMap x, w, k_out[3];
+};
+
+cudaError_t launch_kproj_tc(int dtype_is_bf16, const KProjMaps &maps, const KProjParams &p,
+                            cudaStream_t stream);
+
 // Jacobi rotation log: the (c, s) of every rotation of every sweep, per matrix,
 // so that only the selected eigenvectors are ever formed.
 constexpr int kJacobiMaxSweeps = 15;

@@ -536,6 +536,199 @@ cudaError_t launch_rotation(const View4 &kv, int dt, int64_t keep, const rtk_ten
   return tma ? rtk::launch_rotate_tma(dt == RTK_BF16, kmap, rp, st)
              : rtc ? rtk::launch_rotate_tc(dt == RTK_BF16, rp, st) : rtk::launch_rotate_simt(rp, st);
 }
+
+// Build workspace: status word (256 B) | cov | ksum | sweeps | rotation log.
+struct BuildWs {
+  unsigned int *status;
+  float *cov, *ksum;
+  int *sweeps;
+  float2 *rot_log;
+};
+
+BuildWs build_ws(void *workspace, int64_t n, int64_t D) {
+  unsigned char *ws = static_cast<unsigned char *>(workspace);
+  BuildWs w;
+  w.status = reinterpret_cast<unsigned int *>(ws);
+  w.cov = reinterpret_cast<float *>(ws + kStatusBytes);
+  w.ksum = reinterpret_cast<float *>(ws + kStatusBytes + align_up((size_t)n * D * D * sizeof(float)));
+  w.sweeps = reinterpret_cast<int *>(reinterpret_cast<unsigned char *>(w.ksum) + align_up((size_t)n * D * sizeof(float)));
+  w.rot_log = reinterpret_cast<float2 *>(reinterpret_cast<unsigned char *>(w.sweeps) + align_up((size_t)n * sizeof(int)));
+  return w;
+}
+
+// Shapes and dtypes of the build's query and output arguments for B x H
+// matrices of S visual tokens (RTK_OK or a failure already recorded).
+int check_build_args(int64_t B, int64_t H, int64_t S, int64_t D, int dt, const rtk_tensor *queries,
+                     int64_t num_kv_groups, int64_t keep, const rtk_tensor *kept_out,
+                     const rtk_tensor *R_out, const rtk_tensor *delta_mu_out, const rtk_tensor *eigvals_out) {
+  if (keep < 1 || keep > D) return fail(RTK_ERR_INVALID, "keep must be in [1, head_dim] (got %lld)", (long long)keep);
+  if (queries != nullptr) {
+    if (queries->ndim != 4 || queries->shape[0] != B || queries->shape[3] != D ||
+        num_kv_groups <= 0 || queries->shape[1] != H * num_kv_groups)
+      return fail(RTK_ERR_INVALID, "queries_recent must be [B, H_kv * num_kv_groups, W, D]");
+    if (!dtype_ok(queries->dtype)) return fail(RTK_ERR_INVALID, "queries_recent dtype must be float32, bfloat16 or float16");
+  }
+  if (!same_dims(kept_out, 4, {B, H, S, keep}) || kept_out->dtype != dt)
+    return fail(RTK_ERR_INVALID, "kept_out must be [B, H_kv, S_v, keep] in the Keys' dtype");
+  if (!same_dims(R_out, 4, {B, H, D, keep}) || R_out->dtype != dt)
+    return fail(RTK_ERR_INVALID, "R_out must be [B, H_kv, D, keep] in the Keys' dtype");
+  if (delta_mu_out != nullptr && (!same_dims(delta_mu_out, 3, {B, H, D}) || delta_mu_out->dtype != dt))
+    return fail(RTK_ERR_INVALID, "delta_mu_out must be [B, H_kv, D] in the Keys' dtype");
+  if (eigvals_out != nullptr && (!same_dims(eigvals_out, 3, {B, H, D}) || eigvals_out->dtype != RTK_F32 ||
+                                 eigvals_out->stride[2] != 1 || eigvals_out->stride[1] != D ||
+                                 eigvals_out->stride[0] != H * D))
+    return fail(RTK_ERR_INVALID, "eigvals_out must be a contiguous float32 [B, H_kv, D]");
+  return RTK_OK;
+}
+
+// The build after the sums are in w.cov / w.ksum: centring, query weighting,
+// Jacobi, top-k R and delta_mu, then kept = K_vis . R.
+int finish_build(const View4 &kv, int dt, const rtk_tensor *queries, int64_t num_kv_groups, int64_t keep,
+                 const rtk_tensor *kept_out, const rtk_tensor *R_out, const rtk_tensor *delta_mu_out,
+                 const rtk_tensor *eigvals_out, const BuildWs &w, cudaStream_t st) {
+  const int64_t B = kv.n[0], H = kv.n[1], S = kv.n[2];
+  rtk::JacobiParams jp;
+  std::memset(&jp, 0, sizeof(jp));
+  jp.nmat = (int)(B * H); jp.heads = (int)H;
+  jp.cov = w.cov; jp.ksum = w.ksum; jp.count = (int)std::max<int64_t>(S, 1);
+  jp.center_dtype = dt;
+  if (queries != nullptr) {
+    jp.q = queries->data; jp.q_dtype = queries->dtype;
+    for (int i = 0; i < 4; ++i) jp.q_s[i] = queries->stride[i];
+    jp.window = (int)queries->shape[2];
+    jp.groups = (int)num_kv_groups;
+  }
+  jp.keep = (int)keep;
+  jp.R = R_out->data; jp.R_dtype = dt;
+  for (int i = 0; i < 4; ++i) jp.R_s[i] = R_out->stride[i];
+  if (delta_mu_out != nullptr) {
+    jp.dm = delta_mu_out->data;
+    for (int i = 0; i < 3; ++i) jp.dm_s[i] = delta_mu_out->stride[i];
+  }
+  jp.evals = eigvals_out ? static_cast<float *>(eigvals_out->data) : nullptr;
+  jp.sweeps = w.sweeps;
+  jp.rot_log = w.rot_log;
+  jp.max_sweeps = rtk::kJacobiMaxSweeps;
+  // Converge as far as the output dtype can hold: R is rounded to the Keys'
+  // dtype, whose rounding alone moves span(R) by ~8e-3 (bf16) / ~2e-3 (fp16) in
+  // projector distance, while off(A) <= tol ||diag A|| leaves it ~20 tol from
+  // the exact eigenvectors.
+  jp.tol = dt == RTK_BF16 ? 1e-4f : dt == RTK_F16 ? 2.5e-5f : 1e-6f;
+  cudaError_t e = rtk::launch_jacobi(jp, st);
+  if (e != cudaSuccess) return cuda_fail(e, "rotation builder (eigensolver) launch");
+  e = launch_rotation(kv, dt, keep, R_out, kept_out, w.status, st);
+  if (e != cudaSuccess) return cuda_fail(e, "rotation builder (rotate) launch");
+  return RTK_OK;
+}
+
+// A 16-bit tensor of rank 2 or 3 (innermost first in dims / box, byte strides
+// of the outer dimensions) as a 128B-swizzled TMA map.
+bool encode_map_rank(CUtensorMap *map, CUtensorMapDataType dt, int rank, const void *data,
+                     const cuuint64_t *dims, const cuuint64_t *strides, const cuuint32_t *box) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr || reinterpret_cast<uintptr_t>(data) % 16 != 0) return false;
+  for (int i = 0; i < rank; ++i)
+    if (dims[i] == 0 || dims[i] > (1ull << 31)) return false;
+  for (int i = 0; i < rank - 1; ++i)
+    if (strides[i] % 16 != 0 || strides[i] == 0) return false;
+  cuuint32_t estride[3] = {1, 1, 1};
+  return fn(map, dt, rank, const_cast<void *>(data), dims, strides, box, estride,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Validate and launch the fused projection; cov / ksum are B*H contiguous
+// fp32 blocks.  keys_out [B, H, S, 128].
+int run_key_projection(const rtk_tensor *x, const rtk_tensor *w, const rtk_tensor *bias,
+                       const rtk_tensor *cos, const rtk_tensor *sin, int64_t vis_start, int64_t vis_len,
+                       const rtk_tensor *keys_out, float *cov, float *ksum, unsigned int *status,
+                       cudaStream_t st) {
+  if (x == nullptr || x->ndim != 3) return fail(RTK_ERR_INVALID, "hidden_states must be [B, S, hidden]");
+  const int64_t B = x->shape[0], S = x->shape[1], Hd = x->shape[2];
+  const int dt = x->dtype;
+  if (!is_half_type(dt)) return fail(RTK_ERR_UNSUPPORTED, "the fused Key projection needs bfloat16 or float16 inputs");
+  if (w == nullptr || w->ndim != 2 || w->shape[1] != Hd || w->shape[0] % 128 != 0 || w->shape[0] == 0 ||
+      w->dtype != dt)
+    return fail(RTK_ERR_INVALID, "w_k must be [H_kv * 128, hidden] in the hidden states' dtype");
+  const int64_t H = w->shape[0] / 128;
+  if (bias != nullptr && (bias->ndim != 1 || bias->shape[0] != H * 128 || bias->dtype != dt || bias->stride[0] != 1))
+    return fail(RTK_ERR_INVALID, "bias must be a contiguous [H_kv * 128] vector in the hidden states' dtype");
+  for (const rtk_tensor *c : {cos, sin}) {
+    if (c == nullptr || c->ndim != 3 || (c->shape[0] != B && c->shape[0] != 1) || c->shape[1] != S ||
+        c->shape[2] != 128 || c->dtype != dt)
+      return fail(RTK_ERR_INVALID, "cos / sin must be [B or 1, S, 128] in the hidden states' dtype");
+  }
+  if (cos->stride[0] != sin->stride[0] || cos->stride[1] != sin->stride[1] || cos->shape[0] != sin->shape[0])
+    return fail(RTK_ERR_INVALID, "cos and sin must have the same shape and strides");
+  if (vis_start < 0 || vis_len < 0 || vis_start + vis_len > S)
+    return fail(RTK_ERR_INVALID, "the visual span [%lld, %lld) is not inside [0, %lld)", (long long)vis_start,
+                (long long)(vis_start + vis_len), (long long)S);
+  if (!same_dims(keys_out, 4, {B, H, S, 128}) || keys_out->dtype != dt)
+    return fail(RTK_ERR_INVALID, "keys_out must be [B, H_kv, S, 128] in the hidden states' dtype");
+  if (Hd % 64 != 0) return fail(RTK_ERR_UNSUPPORTED, "hidden size must be a multiple of 64 (got %lld)", (long long)Hd);
+  if (B * S >= (1ll << 31) || Hd >= (1ll << 31)) return fail(RTK_ERR_UNSUPPORTED, "tensor too large");
+  if (B == 0) return RTK_OK;
+  if (S == 0) {
+    cudaError_t e = cudaMemsetAsync(cov, 0, (size_t)B * H * 128 * 128 * sizeof(float), st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ksum, 0, (size_t)B * H * 128 * sizeof(float), st);
+    return e == cudaSuccess ? RTK_OK : cuda_fail(e, "key projection (empty sequence)");
+  }
+  // layouts: channel stride 1, 16-byte aligned rows for TMA and the cos / sin vector loads
+  const int64_t cs_sb = cos->shape[0] == 1 ? 0 : cos->stride[0];
+  const bool cs_ok = cos->stride[2] == 1 && sin->stride[2] == 1 && (cos->stride[1] * 2) % 16 == 0 &&
+                     (cs_sb * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(cos->data) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(sin->data) % 16 == 0;
+  if (!cs_ok || x->stride[2] != 1 || w->stride[1] != 1 || keys_out->stride[3] != 1)
+    return fail(RTK_ERR_UNSUPPORTED, "the fused Key projection needs channel-contiguous, 16-byte aligned rows");
+  const CUtensorMapDataType tdt = dt == RTK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  rtk::KProjMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  {
+    const cuuint64_t dims[3] = {(cuuint64_t)Hd, (cuuint64_t)S, (cuuint64_t)B};
+    const cuuint64_t strides[2] = {(cuuint64_t)(S == 1 ? Hd * 2 : x->stride[1] * 2),
+                                   (cuuint64_t)(B == 1 ? S * Hd * 2 : x->stride[0] * 2)};
+    const cuuint32_t box[3] = {64, 128, 1};
+    if (!encode_map_rank(&maps.x, tdt, 3, x->data, dims, strides, box))
+      return fail(RTK_ERR_UNSUPPORTED, "hidden_states layout is not describable by TMA (16-byte aligned strides needed)");
+  }
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)Hd, (cuuint64_t)(H * 128)};
+    const cuuint64_t strides[1] = {(cuuint64_t)(w->stride[0] * 2)};
+    const cuuint32_t box[2] = {64, 128};
+    if (!encode_map_rank(&maps.w, tdt, 2, w->data, dims, strides, box))
+      return fail(RTK_ERR_UNSUPPORTED, "w_k layout is not describable by TMA (16-byte aligned rows needed)");
+  }
+  const int64_t span_start[3] = {0, vis_start, vis_start + vis_len};
+  const int64_t span_len[3] = {vis_start, vis_len, S - vis_start - vis_len};
+  int64_t tiles = 0;
+  for (int i = 0; i < 3; ++i) {
+    tiles += cdiv(span_len[i], 128);
+    if (span_len[i] == 0) continue;
+    View4 v;
+    v.data = static_cast<const unsigned char *>(keys_out->data) + span_start[i] * keys_out->stride[2] * 2;
+    v.n[0] = B; v.n[1] = H; v.n[2] = span_len[i]; v.n[3] = 128;
+    for (int j = 0; j < 4; ++j) v.s[j] = keys_out->stride[j];
+    if (!encode_map(&maps.k_out[i], v, tdt, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+      return fail(RTK_ERR_UNSUPPORTED, "keys_out layout is not describable by TMA (16-byte aligned strides needed)");
+  }
+  rtk::KProjParams kp;
+  std::memset(&kp, 0, sizeof(kp));
+  kp.batch = (int)B; kp.heads = (int)H; kp.seq = (int)S; kp.hidden = (int)Hd;
+  kp.vis_start = (int)vis_start; kp.vis_len = (int)vis_len;
+  kp.bias = bias != nullptr ? bias->data : nullptr;
+  kp.cos = cos->data; kp.sin = sin->data;
+  kp.cs_sb = cs_sb; kp.cs_ss = cos->stride[1];
+  kp.cov = cov; kp.ksum = ksum;
+  kp.status = status;
+  // one CTA per SM: split each (b, h) over up to 8 CTAs while the grid fits one wave
+  const int64_t units = B * H;
+  int z = 8;
+  while (z > 1 && (units * z > (int64_t)sm_count(current_device()) || z > tiles)) z >>= 1;
+  kp.splits = z;
+  const cudaError_t e = rtk::launch_kproj_tc(dt == RTK_BF16, maps, kp, st);
+  if (e != cudaSuccess) return cuda_fail(e, "key projection launch");
+  return RTK_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -584,77 +777,77 @@ int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_
   const int64_t B = kv.n[0], H = kv.n[1], S = kv.n[2], D = kv.n[3];
   if (!dtype_ok(keys->dtype)) return fail(RTK_ERR_INVALID, "keys_vision dtype must be float32, bfloat16 or float16");
   if (D != 128) return fail(RTK_ERR_UNSUPPORTED, "the rotation builder supports head_dim 128 (got %lld)", (long long)D);
-  if (keep < 1 || keep > D) return fail(RTK_ERR_INVALID, "keep must be in [1, head_dim] (got %lld)", (long long)keep);
-  if (queries != nullptr) {
-    if (queries->ndim != 4 || queries->shape[0] != B || queries->shape[3] != D ||
-        num_kv_groups <= 0 || queries->shape[1] != H * num_kv_groups)
-      return fail(RTK_ERR_INVALID, "queries_recent must be [B, H_kv * num_kv_groups, W, D]");
-    if (!dtype_ok(queries->dtype)) return fail(RTK_ERR_INVALID, "queries_recent dtype must be float32, bfloat16 or float16");
-  }
-  if (!same_dims(kept_out, 4, {B, H, S, keep}) || kept_out->dtype != keys->dtype)
-    return fail(RTK_ERR_INVALID, "kept_out must be [B, H_kv, S_v, keep] in the Keys' dtype");
-  if (!same_dims(R_out, 4, {B, H, D, keep}) || R_out->dtype != keys->dtype)
-    return fail(RTK_ERR_INVALID, "R_out must be [B, H_kv, D, keep] in the Keys' dtype");
-  if (delta_mu_out != nullptr && (!same_dims(delta_mu_out, 3, {B, H, D}) || delta_mu_out->dtype != keys->dtype))
-    return fail(RTK_ERR_INVALID, "delta_mu_out must be [B, H_kv, D] in the Keys' dtype");
-  if (eigvals_out != nullptr && (!same_dims(eigvals_out, 3, {B, H, D}) || eigvals_out->dtype != RTK_F32 ||
-                                 eigvals_out->stride[2] != 1 || eigvals_out->stride[1] != D ||
-                                 eigvals_out->stride[0] != H * D))
-    return fail(RTK_ERR_INVALID, "eigvals_out must be a contiguous float32 [B, H_kv, D]");
+  const int rc = check_build_args(B, H, S, D, keys->dtype, queries, num_kv_groups, keep, kept_out, R_out,
+                                  delta_mu_out, eigvals_out);
+  if (rc != RTK_OK) return rc;
   if (B * H == 0) return RTK_OK;
   const size_t need = rtk_build_rotation_workspace_size(B, H, D);
   if (workspace == nullptr || workspace_bytes < need)
     return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, need);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  unsigned char *ws = static_cast<unsigned char *>(workspace);
-  unsigned int *status = reinterpret_cast<unsigned int *>(ws);
-  float *cov = reinterpret_cast<float *>(ws + kStatusBytes);
-  float *ksum = reinterpret_cast<float *>(ws + kStatusBytes + align_up((size_t)B * H * D * D * sizeof(float)));
-  int *sweeps = reinterpret_cast<int *>(reinterpret_cast<unsigned char *>(ksum) +
-                                        align_up((size_t)B * H * D * sizeof(float)));
-  float2 *rot_log = reinterpret_cast<float2 *>(reinterpret_cast<unsigned char *>(sweeps) +
-                                               align_up((size_t)B * H * sizeof(int)));
-  const int device = current_device();
-  const int dt = keys->dtype;
+  const BuildWs w = build_ws(workspace, B * H, D);
   // ---- covariance + channel sums
-  cudaError_t e = launch_covariance(kv, dt, cov, ksum, device, st);
+  const cudaError_t e = launch_covariance(kv, keys->dtype, w.cov, w.ksum, current_device(), st);
   if (e != cudaSuccess) return cuda_fail(e, "rotation builder (covariance) launch");
+  // ---- centring, query weighting, Jacobi, top-k R, delta_mu; kept = K_vis . R
+  return finish_build(kv, keys->dtype, queries, num_kv_groups, keep, kept_out, R_out, delta_mu_out,
+                      eigvals_out, w, st);
+}
 
-  // ---- centring, query weighting, Jacobi, top-k R and delta_mu
-  rtk::JacobiParams jp;
-  std::memset(&jp, 0, sizeof(jp));
-  jp.nmat = (int)(B * H); jp.heads = (int)H;
-  jp.cov = cov; jp.ksum = ksum; jp.count = (int)std::max<int64_t>(S, 1);
-  jp.center_dtype = dt;
-  if (queries != nullptr) {
-    jp.q = queries->data; jp.q_dtype = queries->dtype;
-    for (int i = 0; i < 4; ++i) jp.q_s[i] = queries->stride[i];
-    jp.window = (int)queries->shape[2];
-    jp.groups = (int)num_kv_groups;
-  }
-  jp.keep = (int)keep;
-  jp.R = R_out->data; jp.R_dtype = dt;
-  for (int i = 0; i < 4; ++i) jp.R_s[i] = R_out->stride[i];
-  if (delta_mu_out != nullptr) {
-    jp.dm = delta_mu_out->data;
-    for (int i = 0; i < 3; ++i) jp.dm_s[i] = delta_mu_out->stride[i];
-  }
-  jp.evals = eigvals_out ? static_cast<float *>(eigvals_out->data) : nullptr;
-  jp.sweeps = sweeps;
-  jp.rot_log = rot_log;
-  jp.max_sweeps = rtk::kJacobiMaxSweeps;
-  // Converge as far as the output dtype can hold: R is rounded to the Keys'
-  // dtype, whose rounding alone moves span(R) by ~8e-3 (bf16) / ~2e-3 (fp16) in
-  // projector distance, while off(A) <= tol ||diag A|| leaves it ~20 tol from
-  // the exact eigenvectors.
-  jp.tol = dt == RTK_BF16 ? 1e-4f : dt == RTK_F16 ? 2.5e-5f : 1e-6f;
-  e = rtk::launch_jacobi(jp, st);
-  if (e != cudaSuccess) return cuda_fail(e, "rotation builder (eigensolver) launch");
+int rtk_key_projection(const rtk_tensor *hidden, const rtk_tensor *w_k, const rtk_tensor *bias,
+                       const rtk_tensor *cos, const rtk_tensor *sin, int64_t vis_start, int64_t vis_len,
+                       const rtk_tensor *keys_out, const rtk_tensor *cov_out, const rtk_tensor *ksum_out,
+                       void *workspace, size_t workspace_bytes, void *stream) {
+  g_last_error.clear();
+  if (keys_out == nullptr || keys_out->ndim != 4) return fail(RTK_ERR_INVALID, "keys_out must be [B, H_kv, S, 128]");
+  const int64_t B = keys_out->shape[0], H = keys_out->shape[1];
+  if (!same_dims(cov_out, 4, {B, H, 128, 128}) || cov_out->dtype != RTK_F32 || cov_out->stride[3] != 1 ||
+      cov_out->stride[2] != 128 || cov_out->stride[1] != 128 * 128 || cov_out->stride[0] != H * 128 * 128)
+    return fail(RTK_ERR_INVALID, "cov_out must be a contiguous float32 [B, H_kv, 128, 128]");
+  if (!same_dims(ksum_out, 3, {B, H, 128}) || ksum_out->dtype != RTK_F32 || ksum_out->stride[2] != 1 ||
+      ksum_out->stride[1] != 128 || ksum_out->stride[0] != H * 128)
+    return fail(RTK_ERR_INVALID, "ksum_out must be a contiguous float32 [B, H_kv, 128]");
+  if (workspace == nullptr || workspace_bytes < kStatusBytes)
+    return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, kStatusBytes);
+  return run_key_projection(hidden, w_k, bias, cos, sin, vis_start, vis_len, keys_out,
+                            static_cast<float *>(cov_out->data), static_cast<float *>(ksum_out->data),
+                            static_cast<unsigned int *>(workspace), static_cast<cudaStream_t>(stream));
+}
 
-  // ---- kept = K_vis . R
-  e = launch_rotation(kv, dt, keep, R_out, kept_out, status, st);
-  if (e != cudaSuccess) return cuda_fail(e, "rotation builder (rotate) launch");
-  return RTK_OK;
+int rtk_build_rotation_projected(const rtk_tensor *hidden, const rtk_tensor *w_k, const rtk_tensor *bias,
+                                 const rtk_tensor *cos, const rtk_tensor *sin, int64_t vis_start,
+                                 int64_t vis_len, const rtk_tensor *queries, int64_t num_kv_groups,
+                                 int64_t keep, const rtk_tensor *keys_out, const rtk_tensor *kept_out,
+                                 const rtk_tensor *R_out, const rtk_tensor *delta_mu_out,
+                                 const rtk_tensor *eigvals_out, void *workspace, size_t workspace_bytes,
+                                 void *stream) {
+  g_last_error.clear();
+  if (keys_out == nullptr || keys_out->ndim != 4 || keys_out->shape[3] != 128)
+    return fail(RTK_ERR_INVALID, "keys_out must be [B, H_kv, S, 128]");
+  const int64_t B = keys_out->shape[0], H = keys_out->shape[1], S = keys_out->shape[2];
+  if (vis_start < 0 || vis_len < 0 || vis_start + vis_len > S)
+    return fail(RTK_ERR_INVALID, "the visual span [%lld, %lld) is not inside [0, %lld)", (long long)vis_start,
+                (long long)(vis_start + vis_len), (long long)S);
+  const int rc = check_build_args(B, H, vis_len, 128, keys_out->dtype, queries, num_kv_groups, keep, kept_out,
+                                  R_out, delta_mu_out, eigvals_out);
+  if (rc != RTK_OK) return rc;
+  if (B * H == 0) return RTK_OK;
+  const size_t need = rtk_build_rotation_workspace_size(B, H, 128);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, need);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const BuildWs w = build_ws(workspace, B * H, 128);
+  // ---- K = RoPE(X W^T + b) for every token, with the visual span's sums
+  const int prc = run_key_projection(hidden, w_k, bias, cos, sin, vis_start, vis_len, keys_out, w.cov, w.ksum,
+                                     w.status, st);
+  if (prc != RTK_OK) return prc;
+  // ---- the rest of the build on the visual Keys just written
+  View4 kv;
+  as4(keys_out, kv);
+  kv.data = static_cast<const unsigned char *>(keys_out->data) + vis_start * keys_out->stride[2] * 2;
+  kv.n[2] = vis_len;
+  return finish_build(kv, keys_out->dtype, queries, num_kv_groups, keep, kept_out, R_out, delta_mu_out,
+                      eigvals_out, w, st);
 }
 
 int rtk_rotate_keys(const rtk_tensor *keys, const rtk_tensor *R, const rtk_tensor *kept_out, void *workspace,

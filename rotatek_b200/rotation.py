@@ -171,5 +171,92 @@ def build_rotation(keys_vision: torch.Tensor, queries_recent: Optional[torch.Ten
     return kept, R, dm, mask
 
 
+def _check_projection_args(hidden_states: torch.Tensor, w_k: torch.Tensor) -> None:
+    """The shape checks the output allocation depends on (the library checks the rest)."""
+    if hidden_states.dim() != 3:
+        raise ValueError("hidden_states must be [B, S, hidden]")
+    if w_k.dim() != 2 or w_k.shape[0] % 128 != 0 or w_k.shape[0] == 0 or w_k.shape[1] != hidden_states.shape[2]:
+        raise ValueError("w_k must be [H_kv * 128, hidden] in the hidden states' dtype")
+
+
+def _cos_sin_3d(cos: torch.Tensor, sin: torch.Tensor):
+    """cos / sin as [B | 1, S, D] views (HF hands them over as [B, S, D]; a
+    [S, D] table broadcasts over the batch)."""
+    if cos.dim() == 2:
+        cos, sin = cos.unsqueeze(0), sin.unsqueeze(0)
+    if cos.dim() != 3 or sin.shape != cos.shape:
+        raise ValueError("cos / sin must be [B, S, D] (or [S, D]) tensors of the same shape")
+    return cos, sin
+
+
+def key_projection(hidden_states: torch.Tensor, w_k: torch.Tensor, bias: Optional[torch.Tensor],
+                   cos: torch.Tensor, sin: torch.Tensor, vis_start: int, vis_len: int):
+    """Post-RoPE Keys straight from the hidden states, with the covariance sums
+    of their visual span, in one tensor-core pass.
+
+    Equals ``apply_rotary_pos_emb(k_proj(hidden_states).view(B, S, H_kv, D)
+    .transpose(1, 2), cos, sin)`` -- llama_visionzip.py:144-153 -- (rounded as
+    torch rounds those ops; up to the projection's accumulation order) and
+    ``key_covariance`` of its tokens [vis_start, vis_start + vis_len).
+
+    hidden_states [B, S, hidden]; w_k [H_kv * 128, hidden] (``k_proj.weight``);
+    bias [H_kv * 128] or None; cos / sin [B | 1, S, 128] in the same dtype
+    (bf16 / fp16).  Returns (keys [B, H_kv, S, 128], cov [B, H_kv, 128, 128]
+    fp32, ksum [B, H_kv, 128] fp32)."""
+    _check_projection_args(hidden_states, w_k)
+    cos, sin = _cos_sin_3d(cos, sin)
+    _lib.require_cuda(hidden_states, w_k, bias, cos, sin)
+    b, s, _ = hidden_states.shape
+    h = w_k.shape[0] // 128
+    dev = hidden_states.device
+    keys = torch.empty(b, h, s, 128, dtype=hidden_states.dtype, device=dev)
+    cov = torch.empty(b, h, 128, 128, dtype=torch.float32, device=dev)
+    ksum = torch.empty(b, h, 128, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    ws = _workspace(dev, 256)
+    D = _lib.describe
+    _lib.check(lib.rtk_key_projection(D(hidden_states), D(w_k), D(bias), D(cos), D(sin), vis_start, vis_len,
+                                      D(keys), D(cov), D(ksum), ctypes.c_void_p(ws.data_ptr()), ws.numel(),
+                                      _stream(dev)))
+    return keys, cov, ksum
+
+
+def build_rotation_projected(hidden_states: torch.Tensor, w_k: torch.Tensor, bias: Optional[torch.Tensor],
+                             cos: torch.Tensor, sin: torch.Tensor, vis_start: int, vis_len: int,
+                             queries_recent: Optional[torch.Tensor], keep: int, num_kv_groups: int,
+                             query_aware: Optional[bool] = None):
+    """``key_projection`` + ``build_rotation`` on the visual span, without the
+    covariance pass over the Keys: from one layer's hidden states to the Keys
+    of every token and the RotateK state of the visual span.
+
+    Returns (keys [B, H_kv, S, 128], kept [B, H_kv, vis_len, keep], R_partial,
+    delta_mu, keep_mask) -- ``build_rotation``'s outputs for
+    ``keys[:, :, vis_start:vis_start + vis_len]`` preceded by the Keys."""
+    _check_projection_args(hidden_states, w_k)
+    if query_aware is None:
+        query_aware = _ROTATEK_QUERY_AWARE_ACTIVE
+    q = queries_recent if query_aware else None
+    cos, sin = _cos_sin_3d(cos, sin)
+    _lib.require_cuda(hidden_states, w_k, bias, cos, sin, q)
+    b, s, _ = hidden_states.shape
+    h, d = w_k.shape[0] // 128, 128
+    dev = hidden_states.device
+    dt = hidden_states.dtype
+    keys = torch.empty(b, h, s, d, dtype=dt, device=dev)
+    kept = torch.empty(b, h, vis_len, keep, dtype=dt, device=dev)
+    R = torch.empty(b, h, d, keep, dtype=dt, device=dev)
+    dm = torch.empty(b, h, d, dtype=dt, device=dev)
+    lib = _lib.load()
+    ws = _workspace(dev, lib.rtk_build_rotation_workspace_size(b, h, d))
+    D = _lib.describe
+    _lib.check(lib.rtk_build_rotation_projected(
+        D(hidden_states), D(w_k), D(bias), D(cos), D(sin), vis_start, vis_len, D(q), num_kv_groups, keep,
+        D(keys), D(kept), D(R), D(dm), None, ctypes.c_void_p(ws.data_ptr()), ws.numel(), _stream(dev)))
+    mask = torch.zeros(b, h, d, dtype=torch.bool, device=dev)
+    mask[..., :keep] = True
+    return keys, kept, R, dm, mask
+
+
 __all__ = ["_ROTATEK_QUERY_AWARE_ACTIVE", "power_iteration_gpu", "eigh_topk", "key_covariance",
-           "keep_count", "build_rotation", "rotate_keys", "read_build_status"]
+           "keep_count", "build_rotation", "rotate_keys", "read_build_status", "key_projection",
+           "build_rotation_projected"]

@@ -12,7 +12,11 @@ What runs:
   CUDA tensor, rotatek/rotation.py:87), with and without ROTATEK_QUERY_AWARE;
 * the `paper` decode kernels ``rotatek_decode_fused_triton`` and
   ``full_channel_decode_triton`` (rotatek/kernels/fused_decode.py,
-  full_channel_flash_decoding.py) under TRITON_INTERPRET=1.
+  full_channel_flash_decoding.py) under TRITON_INTERPRET=1;
+* the adapters' prefill Key path (llava_next/llama_visionzip.py:144-153):
+  torch's nn.Linear as k_proj and transformers' LlamaRotaryEmbedding /
+  apply_rotary_pos_emb, which the adapter imports (llama_visionzip.py:26-33),
+  on CPU (kproj_* fixtures).
 
 Inputs come from ``rotatek_b200.synthetic`` with fixed seeds.  Each case is one
 ``.npz`` holding inputs, reference outputs, and scalar metadata.  bf16 tensors
@@ -143,6 +147,36 @@ def dense_case(name, torch, synth, dense, *, batch, q_heads, kv_heads, seq, dtyp
     print(f"wrote {name}.npz")
 
 
+def kproj_case(name, torch, *, batch, seq, hidden, kv_heads, vis_start, vis_len, dtype, seed, bias=True):
+    """The adapters' prefill Key path (llama_visionzip.py:144-153) on CPU: nn.Linear
+    k_proj, view / transpose, transformers' LlamaRotaryEmbedding cos / sin and
+    apply_rotary_pos_emb.  (The visual span's sums follow from the stored Keys.)"""
+    from transformers.models.llama.configuration_llama import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding, apply_rotary_pos_emb
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(batch, seq, hidden, generator=g).to(dtype)
+    lin = torch.nn.Linear(hidden, kv_heads * 128, bias=bias)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(kv_heads * 128, hidden, generator=g) * hidden ** -0.5)
+        if bias:
+            lin.bias.copy_(torch.randn(kv_heads * 128, generator=g) * 0.1)
+    lin = lin.to(dtype)
+    cfg = LlamaConfig(hidden_size=kv_heads * 128, num_attention_heads=kv_heads, num_key_value_heads=kv_heads,
+                      head_dim=128, max_position_embeddings=4096, rope_theta=10000.0)
+    rope = LlamaRotaryEmbedding(cfg)
+    pos = torch.arange(seq).unsqueeze(0).expand(batch, seq)
+    with torch.no_grad():
+        cos, sin = rope(x, pos)
+        k = lin(x).view(batch, seq, kv_heads, 128).transpose(1, 2)
+        _, k = apply_rotary_pos_emb(k, k, cos, sin)
+    out = dict(hidden=_np(x), w_k=_np(lin.weight), cos=_np(cos), sin=_np(sin), keys=_np(k),
+               vis_start=vis_start, vis_len=vis_len, dtype=str(dtype).replace("torch.", ""))
+    if bias:
+        out["bias"] = _np(lin.bias)
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
+    print(f"wrote {name}.npz")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
@@ -204,6 +238,14 @@ def main():
     if want("tiny_solved_fp32"):
         solved_matrix_case("tiny_solved_fp32", mods, torch, synth, batch=1, q_heads=4, kv_heads=2,
                            prompt=8, vision=300, text=24, ratio=0.75, scale=1e-5, seed=12)
+
+    # prefill Key path: projection with bias + RoPE, ragged spans (20 | 230 | 50)
+    if want("kproj_bf16"):
+        kproj_case("kproj_bf16", torch, batch=2, seq=300, hidden=256, kv_heads=2, vis_start=20,
+                   vis_len=230, dtype=bf16, seed=13)
+    if want("kproj_f16_nobias"):
+        kproj_case("kproj_f16_nobias", torch, batch=1, seq=200, hidden=192, kv_heads=3, vis_start=0,
+                   vis_len=170, dtype=torch.float16, seed=14, bias=False)
 
 
 if __name__ == "__main__":

@@ -79,6 +79,31 @@ def test_c_validation_messages(lib):
     assert (code, lib.rtk_last_error().decode()) == (1, "k/v head_dim must match q's")
 
 
+def test_key_projection_validation(lib):
+    """rtk_key_projection rejects bad shapes before any device work."""
+    bf = 1   # RTK_BF16
+    x, w, bias = _fake((2, 300, 256), bf), _fake((256, 256), bf), _fake((256,), bf)
+    cs = _fake((2, 300, 128), bf)
+    keys, cov, ksum = _fake((2, 2, 300, 128), bf), _fake((2, 2, 128, 128), 0), _fake((2, 2, 128), 0)
+
+    def call(**kw):
+        a = dict(x=x, w=w, bias=bias, cos=cs, sin=cs, vs=20, vl=230, keys=keys, cov=cov, ksum=ksum)
+        a.update(kw)
+        code = lib.rtk_key_projection(a["x"], a["w"], a["bias"], a["cos"], a["sin"], a["vs"], a["vl"],
+                                      a["keys"], a["cov"], a["ksum"], ctypes.c_void_p(0x1000), 256, None)
+        return code, lib.rtk_last_error().decode()
+
+    assert call(x=_fake((300, 256), bf)) == (1, "hidden_states must be [B, S, hidden]")
+    assert call(x=_fake((2, 300, 256), 0))[0] == _lib.RTK_ERR_UNSUPPORTED
+    assert call(w=_fake((200, 256), bf)) == (1, "w_k must be [H_kv * 128, hidden] in the hidden states' dtype")
+    assert call(bias=_fake((128,), bf))[1].startswith("bias must be a contiguous [H_kv * 128] vector")
+    assert call(cos=_fake((2, 299, 128), bf))[1].startswith("cos / sin must be [B or 1, S, 128]")
+    assert call(vl=290) == (1, "the visual span [20, 310) is not inside [0, 300)")
+    assert call(keys=_fake((2, 2, 300, 64), bf))[1].startswith("keys_out must be [B, H_kv, S, 128]")
+    assert call(cov=_fake((2, 2, 128, 128), bf))[1] == "cov_out must be a contiguous float32 [B, H_kv, 128, 128]"
+    assert call(x=_fake((2, 300, 100), bf), w=_fake((256, 100), bf))[0] == _lib.RTK_ERR_UNSUPPORTED
+
+
 def test_python_errors_match_reference_and_no_cpu_fallback():
     q = torch.zeros(2, 8, 128)
     R = torch.zeros(2, 2, 128, 32)

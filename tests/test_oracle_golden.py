@@ -120,3 +120,24 @@ def test_solved_matrix_matches_reference_at_tiny_scale(golden):
     ref = g["solved"].astype(np.float64)
     assert np.abs(np.diagonal(ref, axis1=-2, axis2=-1)).mean(axis=-1).max() < 1e-2
     np.testing.assert_allclose(mat, ref, rtol=0, atol=2e-6 * np.abs(ref).max())
+
+
+@pytest.mark.parametrize("case", ["kproj_bf16", "kproj_f16_nobias"])
+def test_key_projection_oracle_matches_reference_path(golden, case):
+    """k_proj + apply_rotary_pos_emb as the adapters run them (nn.Linear and
+    transformers on CPU, llama_visionzip.py:144-153) against the oracle's
+    float64 restatement with torch's roundings: the same bits except where the
+    projection's accumulation order crosses a rounding boundary (<= 0.2 % of
+    the elements, each within 2 ulps of its RoPE pair's magnitude)."""
+    from oracle import projection as oproj
+    g = golden(case)
+    st = g["dtype"]
+    k = oproj.key_projection(g["hidden"], g["w_k"], g.get("bias"), g["cos"], g["sin"], st)
+    assert k.shape == g["keys"].shape
+    frac, worst = oproj.key_mismatch(k, g["keys"], st)
+    assert frac <= 2e-3 and worst <= 2.0, (frac, worst)
+    # the spans cover the sequence; the sums are those of the stored Keys
+    cov, ksum = oproj.visual_sums(g["keys"], g["vis_start"], g["vis_len"])
+    v = g["keys"][:, :, g["vis_start"]:g["vis_start"] + g["vis_len"]].astype(np.float64)
+    np.testing.assert_allclose(ksum, v.sum(axis=2))
+    np.testing.assert_allclose(cov[0, 0], v[0, 0].T @ v[0, 0])
