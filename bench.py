@@ -64,12 +64,12 @@ def load_peak_hbm():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_traffic_per_launch():
-    """dram bytes per launch of the decode kernel from the committed ncu summary."""
-    path = os.path.join(REPO, "profiles", "decode_tc_config2.txt")
+def ncu_traffic_per_launch(name="decode_tc_config2.txt", key="dram_bytes_per_launch"):
+    """dram bytes per launch of a kernel from its committed ncu summary."""
+    path = os.path.join(REPO, "profiles", name)
     try:
         for line in open(path):
-            if line.startswith("dram_bytes_per_launch"):
+            if line.startswith(key + " ") or line.startswith(key + "="):
                 return int(float(line.split("=")[1].split()[0]))
     except OSError:
         pass
@@ -725,6 +725,103 @@ def run_think(args):
     return 0
 
 
+# ---------------------------------------------------------------- fused Key projection (config 4 layer)
+KPROJ_METRIC = ("config4 layer prefill Key path + rotation build us/layer (Qwen2.5-VL-7B shape: B=8, "
+                "S=64+15360+576, hidden 3584, 4 KV heads, bf16)")
+KPROJ = dict(batch=8, prompt=64, vision=15360, text=576, hidden=3584)
+
+
+def run_kproj(args):
+    """One layer's prefill Key path as the adapters run it -- k_proj, RoPE,
+    then the rotation build of the visual span (llama_visionzip.py:144-165) --
+    from the layer's hidden states.  Ours: ``build_rotation_projected`` (fused
+    projection + RoPE + covariance sums, Jacobi, rotate).  Beside it on the same
+    GPU: cuBLAS k_proj + torch RoPE + ``build_rotation`` (the adapter path with
+    this build's builder)."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    from rotatek_b200 import rotation as rot
+    from rotatek_b200 import synthetic as syn
+    b, sp, sv, st, hid = KPROJ["batch"], KPROJ["prompt"], KPROJ["vision"], KPROJ["text"], KPROJ["hidden"]
+    if args.batch:                   # profiling cases only
+        b = args.batch
+    if args.kproj_vision:
+        sv = args.kproj_vision
+    hkv, G, keep = CFG4["kv_heads"], CFG4["q_heads"] // CFG4["kv_heads"], CFG4["keep"]
+    s = sp + sv + st
+    dt = torch.bfloat16
+    x = syn.normal((b, s, hid), 21, dev, dt)
+    w = (syn.normal((hkv * 128, hid), 22, dev, torch.float32) * hid ** -0.5).to(dt)
+    bias = (syn.normal((hkv * 128,), 23, dev, torch.float32) * 0.1).to(dt)
+    inv = 1.0 / 1e6 ** (torch.arange(0, 128, 2, device=dev, dtype=torch.float32) / 128)
+    ang = torch.arange(s, device=dev, dtype=torch.float32)[:, None] * inv[None]
+    ang = torch.cat([ang, ang], dim=-1)
+    cos = ang.cos().to(dt)[None].expand(b, -1, -1).contiguous()
+    sin = ang.sin().to(dt)[None].expand(b, -1, -1).contiguous()
+    q = syn.normal((b, CFG4["q_heads"], CFG4["window"], 128), 24, dev, dt)
+
+    def fused():
+        return rot.build_rotation_projected(x, w, bias, cos, sin, sp, sv, q, keep, G)
+
+    def projection():
+        return rot.key_projection(x, w, bias, cos, sin, sp, sv)
+
+    def adapter():
+        k = torch.nn.functional.linear(x, w, bias).view(b, s, hkv, 128).transpose(1, 2)
+        k = k * cos[:, None] + torch.cat([-k[..., 64:], k[..., :64]], dim=-1) * sin[:, None]
+        return rot.build_rotation(k[:, :, sp:sp + sv], q, keep, G)
+
+    def cublas():
+        return torch.nn.functional.linear(x, w, bias)
+
+    def timed(fn, n):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / n
+
+    sampler = ClockSampler(0)
+    with sampler:
+        ours = timed(fused, args.steps)
+        proj = timed(projection, args.steps)
+    status = rot.read_build_status(dev)
+    theirs = timed(adapter, max(3, args.steps // 4))
+    lin = timed(cublas, max(3, args.steps // 4))
+    flops = 2 * b * s * hid * hkv * 128 + 2 * b * hkv * sv * 128 * 128   # projection + K^T K
+    peak = None
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+        peak_kind = "measured (bf16 burst, MEASURED_PEAKS.json)"
+    except (OSError, KeyError, ValueError):
+        peak, peak_kind = 1590.0, "fallback 1.59 PFLOP/s"
+    achieved = flops / proj / 1e6
+    print(json.dumps({
+        "metric": KPROJ_METRIC, "value": ours, "unit": "us/layer", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "higher_is_better": False, "dtype": "bf16",
+        "data": "synthetic: N(0,1) hidden states, scaled N(0,1) k_proj weight and bias, RoPE theta 1e6",
+        "config": {"workload": f"config4 layer: hidden states -> post-RoPE Keys (all {s} tokens) + rotation "
+                               f"build of the {sv} visual tokens, B={b}, H_kv=4 (G=7), keep 32",
+                   "l2": f"hidden states {x.numel() * 2 / 1e9:.2f} GB > 126 MB L2; no flush"},
+        "phases_us": {"key_projection_fused": proj, "cublas_k_proj_alone": lin},
+        "adapter_path_us": theirs, "speedup_vs_adapter_path": theirs / ours,
+        "roofline": {"bound": "tensor", "kernel": "kproj_tc_kernel + kproj_reduce_kernel",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": peak_kind, "algorithmic_flops_per_launch": flops,
+                     "traffic": ncu_traffic_per_launch("kproj_tc_small_case.txt", "dram_bytes_per_launch_config4"),
+                     "algorithmic_bytes_per_launch": (x.numel() + w.numel() + bias.numel() + b * hkv * s * 128
+                                                      + 2 * cos.numel()) * 2 + b * hkv * (128 * 128 + 128) * 4,
+                     "cublas_k_proj_tflops": 2 * b * s * hid * hkv * 128 / lin / 1e6},
+        "gpu_launches": 4 * args.steps, "clocks": sampler.summary(), "device_status": status}), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------- config 3: end-to-end decode
 E2E_METRIC = "config3 e2e greedy decode tokens/s (LLaVA-NeXT-7B-shaped, fp16, 16384 visual tokens, 128 steps)"
 
@@ -932,26 +1029,38 @@ def main():
                     help="override the batch (profiling cases only; the bench line uses 32)")
     ap.add_argument("--kernel-only", action="store_true",
                     help="decode launches only: no e2e, no CPU baseline, no JSON bench line")
-    ap.add_argument("--workload", choices=["decode", "build", "decode72b", "decode_step", "e2e", "think"],
+    ap.add_argument("--workload", choices=["decode", "build", "decode72b", "decode_step", "e2e", "think", "kproj"],
                     default="decode",
                     help="decode: benchmark config 2 (the headline); build: config 4 rotation build; "
                          "decode72b: config 5 multi-GPU decode; decode_step: config 2 with cache appends; "
-                         "e2e: config 3 LLaVA-NeXT-7B-shaped end-to-end decode; think: ThinK at config 2")
+                         "e2e: config 3 LLaVA-NeXT-7B-shaped end-to-end decode; think: ThinK at config 2; "
+                         "kproj: one config-4 layer from hidden states (fused Key projection + build)")
     ap.add_argument("--shard", choices=["auto", "heads", "batch"], default="auto",
                     help="decode72b: KV-head or batch sharding (auto: heads when N = 8)")
     ap.add_argument("--pool", type=int, default=4, help="decode72b: resident layers cycled over the 80")
     ap.add_argument("--e2e-tokens", type=int, default=128, help="e2e: greedy tokens per sequence")
+    ap.add_argument("--kproj-vision", type=int, default=None,
+                    help="kproj workload: visual tokens (profiling cases only; the bench line uses 15360)")
     ap.add_argument("--layers", type=int, default=None,
                     help="build workload: layers per step (profiling cases only; the bench line uses 28)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"build": 20, "decode72b": 10, "decode_step": 200, "think": 200}.get(args.workload, 2000)
+        args.steps = {"build": 20, "decode72b": 10, "decode_step": 200, "think": 200,
+                      "kproj": 20}.get(args.workload, 2000)
     if args.workload == "decode_step":
         return run_decode_step(args)
     if args.workload == "e2e":
         return run_e2e(args)
     if args.workload == "think":
         return run_think(args)
+    if args.workload == "kproj":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "metric": KPROJ_METRIC,
+                              "unavailable": "measured for this build only; its line carries the adapter "
+                                             "path (cuBLAS k_proj + torch RoPE + build) timed beside it"}),
+                  flush=True)
+            return 0
+        return run_kproj(args)
     if args.workload == "decode72b":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "metric": DEC72_METRIC,

@@ -211,18 +211,30 @@ int rtk_build_rotation(const rtk_tensor *keys_vision, const rtk_tensor *queries_
  *   cos, sin   [B or 1, S, 128]    same dtype, channel stride 1
  *   keys_out   [B, H_kv, S, 128]   same dtype, channel stride 1
  *   cov_out    [B, H_kv, 128, 128] f32 contiguous; ksum_out [B, H_kv, 128] f32 contiguous
- *   workspace  >= 256 bytes whose first word is the device-status word        */
+ *   workspace  rtk_key_projection_workspace_size() bytes: the device-status word
+ *              (first 256 bytes, as in the build workspace) and per-CTA partial
+ *              sums (no zeroing needed)                                          */
 int rtk_key_projection(const rtk_tensor *hidden, const rtk_tensor *w_k, const rtk_tensor *bias,
                        const rtk_tensor *cos, const rtk_tensor *sin, int64_t vis_start, int64_t vis_len,
                        const rtk_tensor *keys_out, const rtk_tensor *cov_out, const rtk_tensor *ksum_out,
                        void *workspace, size_t workspace_bytes, void *stream);
+
+/* Bytes of workspace rtk_key_projection needs on `device` (its SM count sets
+ * the number of partial sums): 256 + about 132 KiB x (SMs + B * ceil(H_kv / 2)). */
+size_t rtk_key_projection_workspace_size(int64_t batch, int64_t kv_heads, int64_t seq, int64_t vis_start,
+                                         int64_t vis_len, int32_t device);
+
+/* Bytes of workspace rtk_build_rotation_projected needs: the build workspace
+ * followed by the projection's partial sums.                                */
+size_t rtk_build_rotation_projected_workspace_size(int64_t batch, int64_t kv_heads, int64_t seq,
+                                                   int64_t vis_start, int64_t vis_len, int32_t device);
 
 /* rtk_key_projection followed by the rest of rtk_build_rotation on the visual
  * span of keys_out: from a layer's hidden states to what the split cache stores
  * (K for every token; R, delta_mu and kept = K_vis . R for the visual span)
  * with one pass over the Keys fewer than projection + rtk_build_rotation.
  * Arguments as in the two calls; kept_out is [B, H_kv, vis_len, keep];
- * workspace of rtk_build_rotation_workspace_size(B, H_kv, 128) bytes.         */
+ * workspace of rtk_build_rotation_projected_workspace_size() bytes.          */
 int rtk_build_rotation_projected(const rtk_tensor *hidden, const rtk_tensor *w_k, const rtk_tensor *bias,
                                  const rtk_tensor *cos, const rtk_tensor *sin, int64_t vis_start,
                                  int64_t vis_len, const rtk_tensor *queries_recent, int64_t num_kv_groups,

@@ -48,6 +48,8 @@ SIGNATURES = {
     "rtk_build_rotation_workspace_size": (ctypes.c_size_t, [ctypes.c_int64] * 3),
     "rtk_build_rotation": (ctypes.c_int, [_P, _P, ctypes.c_int64, ctypes.c_int64, _P, _P, _P, _P,
                                           ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "rtk_key_projection_workspace_size": (ctypes.c_size_t, [ctypes.c_int64] * 5 + [ctypes.c_int32]),
+    "rtk_build_rotation_projected_workspace_size": (ctypes.c_size_t, [ctypes.c_int64] * 5 + [ctypes.c_int32]),
     "rtk_key_projection": (ctypes.c_int, [_P] * 5 + [ctypes.c_int64, ctypes.c_int64] + [_P] * 3 +
                            [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "rtk_build_rotation_projected": (ctypes.c_int, [_P] * 5 + [ctypes.c_int64, ctypes.c_int64, _P,

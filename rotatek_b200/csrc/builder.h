@@ -38,19 +38,31 @@ struct KProjParams {
   const void *bias;                       // [heads * 128] or NULL
   const void *cos, *sin;                  // [B | 1, S, 128] (element strides below, channel stride 1)
   long long cs_sb, cs_ss;                 // batch stride (0 = broadcast), token stride
+  float *part;                            // per-CTA partial sums (kproj_workspace_floats)
   float *cov;                             // [B * H][128][128]
   float *ksum;                            // [B * H][128]
   unsigned int *status;                   // device status word (bounded-wait timeouts)
-  int splits;                             // CTAs (one cluster) per (b, h)
+  int grid;                               // persistent CTAs (<= SMs)
 };
 
+// One (CTA, unit, head) partial: sum k k^T (128 x 128) then four per-warp
+// channel sums (4 x 128).  Slots are indexed (cta + unit) * 2 + head, unit =
+// b * ceil(H / 2) + head pair.
+constexpr int kKProjPartFloats = 128 * 128 + 4 * 128;
+
+inline long long kproj_units(long long batch, long long heads) { return batch * ((heads + 1) / 2); }
+inline long long kproj_workspace_floats(long long batch, long long heads, long long grid) {
+  return (grid + kproj_units(batch, heads)) * 2 * kKProjPartFloats;
+}
+
 // x: [B, S, hidden] 3-D map, box {64, 128, 1}; w: [H*128, hidden] 2-D map, box
-// {64, 128}; k_out[i]: the output [B, H, len_i, 128] of span i (prompt, visual,
+// {64, 256}; k_out[i]: the output [B, H, len_i, 128] of span i (prompt, visual,
 // text) as 4-D maps with box {64, 128, 1, 1}; all 128B-swizzled.
 struct KProjMaps {
   CUtensorMap x, w, k_out[3];
 };
 
+// The projection kernel (grid = p.grid), then the reduction of its partials into cov / ksum.
 cudaError_t launch_kproj_tc(int dtype_is_bf16, const KProjMaps &maps, const KProjParams &p,
                             cudaStream_t stream);
 

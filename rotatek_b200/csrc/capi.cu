@@ -637,12 +637,26 @@ bool encode_map_rank(CUtensorMap *map, CUtensorMapDataType dt, int rank, const v
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 128-token tiles of one (b, head pair) and the persistent grid of the projection.
+int64_t kproj_tiles_per_unit(int64_t S, int64_t vis_start, int64_t vis_len) {
+  return cdiv(vis_start, 128) + cdiv(vis_len, 128) + cdiv(S - vis_start - vis_len, 128);
+}
+int64_t kproj_grid(int64_t B, int64_t H, int64_t S, int64_t vis_start, int64_t vis_len, int device) {
+  const int64_t total = rtk::kproj_units(B, H) * kproj_tiles_per_unit(S, vis_start, vis_len);
+  return std::max<int64_t>(1, std::min<int64_t>(sm_count(device), total));
+}
+size_t kproj_part_bytes(int64_t B, int64_t H, int64_t S, int64_t vis_start, int64_t vis_len, int device) {
+  return align_up((size_t)rtk::kproj_workspace_floats(B, H, kproj_grid(B, H, S, vis_start, vis_len, device)) *
+                  sizeof(float));
+}
+
 // Validate and launch the fused projection; cov / ksum are B*H contiguous
-// fp32 blocks.  keys_out [B, H, S, 128].
+// fp32 blocks, `part` the partial-sum scratch of kproj_part_bytes.
+// keys_out [B, H, S, 128].
 int run_key_projection(const rtk_tensor *x, const rtk_tensor *w, const rtk_tensor *bias,
                        const rtk_tensor *cos, const rtk_tensor *sin, int64_t vis_start, int64_t vis_len,
-                       const rtk_tensor *keys_out, float *cov, float *ksum, unsigned int *status,
-                       cudaStream_t st) {
+                       const rtk_tensor *keys_out, float *cov, float *ksum, float *part, size_t part_bytes,
+                       unsigned int *status, cudaStream_t st) {
   if (x == nullptr || x->ndim != 3) return fail(RTK_ERR_INVALID, "hidden_states must be [B, S, hidden]");
   const int64_t B = x->shape[0], S = x->shape[1], Hd = x->shape[2];
   const int dt = x->dtype;
@@ -666,7 +680,9 @@ int run_key_projection(const rtk_tensor *x, const rtk_tensor *w, const rtk_tenso
   if (!same_dims(keys_out, 4, {B, H, S, 128}) || keys_out->dtype != dt)
     return fail(RTK_ERR_INVALID, "keys_out must be [B, H_kv, S, 128] in the hidden states' dtype");
   if (Hd % 64 != 0) return fail(RTK_ERR_UNSUPPORTED, "hidden size must be a multiple of 64 (got %lld)", (long long)Hd);
-  if (B * S >= (1ll << 31) || Hd >= (1ll << 31)) return fail(RTK_ERR_UNSUPPORTED, "tensor too large");
+  if (B * S >= (1ll << 31) || Hd >= (1ll << 31) ||
+      rtk::kproj_units(B, H) * kproj_tiles_per_unit(S, vis_start, vis_len) >= (1ll << 31))
+    return fail(RTK_ERR_UNSUPPORTED, "tensor too large");
   if (B == 0) return RTK_OK;
   if (S == 0) {
     cudaError_t e = cudaMemsetAsync(cov, 0, (size_t)B * H * 128 * 128 * sizeof(float), st);
@@ -694,15 +710,13 @@ int run_key_projection(const rtk_tensor *x, const rtk_tensor *w, const rtk_tenso
   {
     const cuuint64_t dims[2] = {(cuuint64_t)Hd, (cuuint64_t)(H * 128)};
     const cuuint64_t strides[1] = {(cuuint64_t)(w->stride[0] * 2)};
-    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t box[2] = {64, 256};
     if (!encode_map_rank(&maps.w, tdt, 2, w->data, dims, strides, box))
       return fail(RTK_ERR_UNSUPPORTED, "w_k layout is not describable by TMA (16-byte aligned rows needed)");
   }
   const int64_t span_start[3] = {0, vis_start, vis_start + vis_len};
   const int64_t span_len[3] = {vis_start, vis_len, S - vis_start - vis_len};
-  int64_t tiles = 0;
   for (int i = 0; i < 3; ++i) {
-    tiles += cdiv(span_len[i], 128);
     if (span_len[i] == 0) continue;
     View4 v;
     v.data = static_cast<const unsigned char *>(keys_out->data) + span_start[i] * keys_out->stride[2] * 2;
@@ -720,11 +734,13 @@ int run_key_projection(const rtk_tensor *x, const rtk_tensor *w, const rtk_tenso
   kp.cs_sb = cs_sb; kp.cs_ss = cos->stride[1];
   kp.cov = cov; kp.ksum = ksum;
   kp.status = status;
-  // one CTA per SM: split each (b, h) over up to 8 CTAs while the grid fits one wave
-  const int64_t units = B * H;
-  int z = 8;
-  while (z > 1 && (units * z > (int64_t)sm_count(current_device()) || z > tiles)) z >>= 1;
-  kp.splits = z;
+  // persistent: one CTA per SM, contiguous shares of the B * ceil(H / 2) * tiles tiles
+  const int device = current_device();
+  kp.grid = (int)kproj_grid(B, H, S, vis_start, vis_len, device);
+  const size_t need = kproj_part_bytes(B, H, S, vis_start, vis_len, device);
+  if (part == nullptr || part_bytes < need)
+    return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes for partial sums, needs %zu", part_bytes, need);
+  kp.part = part;
   const cudaError_t e = rtk::launch_kproj_tc(dt == RTK_BF16, maps, kp, st);
   if (e != cudaSuccess) return cuda_fail(e, "key projection launch");
   return RTK_OK;
@@ -808,10 +824,25 @@ int rtk_key_projection(const rtk_tensor *hidden, const rtk_tensor *w_k, const rt
       ksum_out->stride[1] != 128 || ksum_out->stride[0] != H * 128)
     return fail(RTK_ERR_INVALID, "ksum_out must be a contiguous float32 [B, H_kv, 128]");
   if (workspace == nullptr || workspace_bytes < kStatusBytes)
-    return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, kStatusBytes);
+    return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes, needs at least %zu", workspace_bytes, kStatusBytes);
+  unsigned char *ws = static_cast<unsigned char *>(workspace);
   return run_key_projection(hidden, w_k, bias, cos, sin, vis_start, vis_len, keys_out,
                             static_cast<float *>(cov_out->data), static_cast<float *>(ksum_out->data),
-                            static_cast<unsigned int *>(workspace), static_cast<cudaStream_t>(stream));
+                            reinterpret_cast<float *>(ws + kStatusBytes), workspace_bytes - kStatusBytes,
+                            reinterpret_cast<unsigned int *>(ws), static_cast<cudaStream_t>(stream));
+}
+
+size_t rtk_key_projection_workspace_size(int64_t batch, int64_t kv_heads, int64_t seq, int64_t vis_start,
+                                         int64_t vis_len, int32_t device) {
+  if (batch <= 0 || kv_heads <= 0 || seq <= 0 || vis_start < 0 || vis_len < 0 || vis_start + vis_len > seq)
+    return kStatusBytes;
+  return kStatusBytes + kproj_part_bytes(batch, kv_heads, seq, vis_start, vis_len, device);
+}
+
+size_t rtk_build_rotation_projected_workspace_size(int64_t batch, int64_t kv_heads, int64_t seq,
+                                                   int64_t vis_start, int64_t vis_len, int32_t device) {
+  return rtk_build_rotation_workspace_size(batch, kv_heads, 128) +
+         rtk_key_projection_workspace_size(batch, kv_heads, seq, vis_start, vis_len, device) - kStatusBytes;
 }
 
 int rtk_build_rotation_projected(const rtk_tensor *hidden, const rtk_tensor *w_k, const rtk_tensor *bias,
@@ -832,14 +863,16 @@ int rtk_build_rotation_projected(const rtk_tensor *hidden, const rtk_tensor *w_k
                                   R_out, delta_mu_out, eigvals_out);
   if (rc != RTK_OK) return rc;
   if (B * H == 0) return RTK_OK;
-  const size_t need = rtk_build_rotation_workspace_size(B, H, 128);
-  if (workspace == nullptr || workspace_bytes < need)
-    return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, need);
+  const size_t build_bytes = rtk_build_rotation_workspace_size(B, H, 128);
+  if (workspace == nullptr || workspace_bytes < build_bytes)
+    return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes,
+                rtk_build_rotation_projected_workspace_size(B, H, S, vis_start, vis_len, current_device()));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const BuildWs w = build_ws(workspace, B * H, 128);
   // ---- K = RoPE(X W^T + b) for every token, with the visual span's sums
   const int prc = run_key_projection(hidden, w_k, bias, cos, sin, vis_start, vis_len, keys_out, w.cov, w.ksum,
-                                     w.status, st);
+                                     reinterpret_cast<float *>(static_cast<unsigned char *>(workspace) + build_bytes),
+                                     workspace_bytes - build_bytes, w.status, st);
   if (prc != RTK_OK) return prc;
   // ---- the rest of the build on the visual Keys just written
   View4 kv;

@@ -8,26 +8,30 @@
 // the visual span -- the inputs of the Jacobi prologue -- so the covariance
 // pass over K disappears.
 //
-// Work: a cluster of Z CTAs owns one (b, h); its 128-token tiles (prompt tiles,
-// then visual, then text, each span tiled from its own start) are split into Z
-// contiguous ranges.  Per CTA (192 threads, one CTA per SM):
-//   warp 0     TMA producer: per tile and per 64-wide hidden chunk, an X box
-//              {64 hidden x 128 tokens} and a W box {64 hidden x 128 channels}
-//              (128B swizzle) into a 5-stage ring
+// Work: a unit is (b, pair of KV heads); its 128-token tiles run over the
+// prompt, visual and text spans, each span tiled from its own start.  The
+// U x T tiles are split into contiguous ranges over a persistent grid of one
+// CTA per SM (320 threads):
+//   warp 0     TMA producer: per tile and 64-wide hidden chunk an X box
+//              {64 x 128 tokens} and a W box {64 x 256 channels} (128B
+//              swizzle) into a 4-stage ring; W rows past H * 128 read as zero
 //   warp 1     TMEM owner (512 columns) and MMA issuer: per chunk four
-//              tcgen05.mma kind::f16 M=128 N=128 K=16, both operands K-major,
-//              into one of two fp32 projection accumulators (columns 0 / 128);
-//              after a visual tile has been staged, eight more MMAs add
-//              K_tile^T K_tile into the covariance accumulator (columns 256..383)
-//              from the staged tile read MN-major
-//   warps 2-5  epilogue, one token row per thread: TMEM -> registers, + bias,
-//              round, RoPE with torch's roundings, -> a 128B-swizzled staging
-//              tile that is at once the TMA-store source and the covariance
-//              MMA operand; channel sums of visual tiles from the staging tile
+//              tcgen05.mma kind::f16 M=128 N=256 K=16 (both operands K-major)
+//              into the projection accumulator (columns 0-255, head h of the
+//              pair in 128 h ...); each staged visual (tile, head) then gets
+//              eight M=128 N=128 K=16 MMAs adding K^T K into that head's
+//              covariance accumulator (columns 256 + 128 h) from the staging
+//              tile read MN-major, interleaved with the next tile's chunks
+//   warps 2-9  epilogue, one (token row, head) per thread: drain TMEM (+ bias,
+//              round) into registers and free the accumulator, then RoPE with
+//              torch's roundings, a 128B-swizzled staging tile (TMA-store
+//              source and covariance operand, used by the two heads in turn),
+//              channel sums of visual tiles; at the end of each unit in the
+//              range, the covariance and channel-sum partials go to the
+//              workspace
+// A second kernel sums each unit's partials in a fixed order (deterministic).
 // Rows past the end of their span are zeroed (no covariance contribution) and
-// clipped by the span's output tensor map.  At the end the cluster reduces the
-// Z partial sums through distributed shared memory (as the covariance kernel
-// does) and writes cov / ksum.
+// clipped by the span's output tensor map.
 #include <type_traits>
 
 #include "builder.h"
@@ -36,48 +40,69 @@
 namespace rtk {
 namespace {
 
-constexpr int kRows = 128;              // tokens per tile
-constexpr int kBox = 128 * 128;         // bytes of a {64 x 128} 16-bit box
-constexpr int kStages = 5;
-constexpr int kThreads = 192;
-constexpr int kDumpStride = 132;        // fp32 row stride of the covariance dump
-constexpr uint32_t kAccCols = 128;      // one projection accumulator
-constexpr uint32_t kCovCol = 256;       // covariance accumulator
+constexpr int kRows = 128;                   // tokens per tile
+constexpr int kXBox = 128 * 128;             // {64 hidden x 128 tokens}, 16-bit
+constexpr int kWBox = 256 * 128;             // {64 hidden x 256 channels}
+constexpr int kStageBytes = kXBox + kWBox;   // 48 KB
+constexpr int kStages = 4;
+constexpr int kOutBox = 128 * 128;           // {64 channels x 128 tokens}
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr uint32_t kCovCol = 256;            // head h: columns 256 + 128 h
 constexpr uint32_t kTmemCols = 512;
 
 struct KpSmem {
-  static constexpr int kRing = 0;                                 // stage: X box | W box
-  static constexpr int kStage = kRing + kStages * 2 * kBox;       // channels 0-63 | 64-127
-  static constexpr int kBar = kStage + 2 * kBox;
-  // full[kStages], empty[kStages], acc_full[2], acc_empty[2], staged, staging_free, cov_done
-  static constexpr int kNumBars = 2 * kStages + 7;
+  static constexpr int kRing = 0;
+  static constexpr int kStage = kRing + kStages * kStageBytes;   // channels 0-63 | 64-127
+  static constexpr int kBar = kStage + 2 * kOutBox;
+  // full[kStages], empty[kStages], acc_full, acc_empty, staged, staging_free, cov_done, cov_flushed
+  static constexpr int kNumBars = 2 * kStages + 6;
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
-  static constexpr int kBias = (kTmemSlot + 16 + 15) & ~15;       // fp32 [128]
-  static constexpr int kSums = kBias + 128 * 4;                   // fp32 [4 warps][128]
-  static constexpr int kColSum = kSums + 4 * 128 * 4;             // fp32 [128]
-  static constexpr int kBytes = kColSum + 128 * 4;
-  static_assert(kStages * 2 * kBox >= 128 * kDumpStride * 4, "dump must fit in the ring");
-  static_assert(kStage % 1024 == 0, "swizzled boxes need 1024-byte alignment");
+  static constexpr int kAbort = kTmemSlot + 4;                     // bounded-wait abort flag
+  static constexpr int kBias = (kAbort + 4 + 15) & ~15;           // fp32 [256]
+  static constexpr int kBytes = kBias + 256 * 4;
+  static_assert(kStage % 1024 == 0 && kStageBytes % 1024 == 0, "swizzled boxes need 1024-byte alignment");
+  // + 1024 alignment slack; no static shared memory in the kernel (it would
+  // sit in front of the 1024-aligned dynamic array)
+  static_assert(kBytes + 1024 <= 232448, "shared memory budget");
 };
 
-// The three spans of a (b, h) row of tokens and their 128-token tiles.
+// The three spans of a unit's tokens and their 128-token tiles.
 struct Spans {
-  int start[3], end[3], first_tile[4];
+  int start0, start1, start2, end0, end1, end2, first1, first2, total;
 
   __device__ void init(int seq, int vs, int vl) {
-    start[0] = 0;       end[0] = vs;
-    start[1] = vs;      end[1] = vs + vl;
-    start[2] = vs + vl; end[2] = seq;
-    first_tile[0] = 0;
-#pragma unroll
-    for (int i = 0; i < 3; ++i) first_tile[i + 1] = first_tile[i] + (end[i] - start[i] + kRows - 1) / kRows;
+    start0 = 0; end0 = vs;
+    start1 = vs; end1 = vs + vl;
+    start2 = vs + vl; end2 = seq;
+    first1 = (vs + kRows - 1) / kRows;
+    first2 = first1 + (vl + kRows - 1) / kRows;
+    total = first2 + (seq - vs - vl + kRows - 1) / kRows;
   }
-  __device__ int total() const { return first_tile[3]; }
-  __device__ int span_of(int tile) const {
-    return tile < first_tile[1] ? 0 : tile < first_tile[2] ? 1 : 2;
+  // span index, first token of the tile, end of its span, first token of its span
+  __device__ void locate(int tile, int &span, int &row0, int &end, int &start) const {
+    if (tile < first1) { span = 0; start = start0; end = end0; row0 = tile * kRows; }
+    else if (tile < first2) { span = 1; start = start1; end = end1; row0 = start1 + (tile - first1) * kRows; }
+    else { span = 2; start = start2; end = end2; row0 = start2 + (tile - first2) * kRows; }
   }
-  __device__ int row0(int tile, int span) const { return start[span] + (tile - first_tile[span]) * kRows; }
+  __device__ bool visual(int tile) const { return tile >= first1 && tile < first2; }
 };
+
+// A CTA's share of the U * T tiles, and the unit / tile behind an index.
+struct Range {
+  int begin, end, tiles_per_unit;
+  __device__ int unit(int j) const { return j / tiles_per_unit; }
+  __device__ int tile(int j) const { return j % tiles_per_unit; }
+  // last index of the range that belongs to unit(j)
+  __device__ int unit_last(int j) const {
+    const int u_end = (unit(j) + 1) * tiles_per_unit;
+    return (u_end < end ? u_end : end) - 1;
+  }
+};
+
+__host__ __device__ inline long long range_begin(int c, long long total, int grid) {
+  return (long long)c * total / grid;
+}
 
 template <typename T>
 __device__ __forceinline__ float round_to(float x) {
@@ -92,57 +117,60 @@ __device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
   unpack2<T>(v.w, f[6], f[7]);
 }
 
-// One token row of the epilogue: 128 fp32 projection values from TMEM ->
-// bias, rounding, RoPE -> 64 packed 16-bit pairs (channels 2j, 2j+1 in out[j]).
-//   k      = round(acc + bias)                     (the projection's output)
+// Drain one head's 128 accumulator columns of this thread's row:
+// k = round(acc + bias), packed in pairs (channels 2j, 2j+1 in k[j]).
+template <typename T>
+__device__ __forceinline__ void drain_row(uint32_t tmem_row, const float *bias, uint32_t (&k)[64]) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint32_t r[16];
+    tmem_ld16_nowait(tmem_row + 16 * c, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 16; e += 2)
+      k[8 * c + e / 2] = pack2<T>(__fadd_rn(__uint_as_float(r[e]), bias[16 * c + e]),
+                                  __fadd_rn(__uint_as_float(r[e + 1]), bias[16 * c + e + 1]));
+  }
+}
+
+// RoPE on a drained row, in place:
 //   out_lo = round(round(k_lo cos_lo) - round(k_hi sin_lo))   channels d < 64
 //   out_hi = round(round(k_hi cos_hi) + round(k_lo sin_hi))   channels d + 64
 // which is torch's  k * cos + rotate_half(k) * sin  in the Keys' dtype.
+// Rows past the end of their span become zero.
 template <typename T>
-__device__ __forceinline__ void rope_row(uint32_t tmem_row, const float *bias, const T *crow,
-                                         const T *srow, bool valid, uint32_t (&out)[64]) {
+__device__ __forceinline__ void rope_row(const T *crow, const T *srow, bool valid, uint32_t (&k)[64]) {
 #pragma unroll
-  for (int h2 = 0; h2 < 4; ++h2) {
-    uint32_t rlo[16], rhi[16];
-    tmem_ld16_nowait(tmem_row + 16 * h2, rlo);
-    tmem_ld16_nowait(tmem_row + 64 + 16 * h2, rhi);
-    tmem_wait_ld();
-    float lo[16], hi[16];
+  for (int q = 0; q < 8; ++q) {
+    const int d = 8 * q;
+    if (!valid) {
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      lo[e] = __uint_as_float(rlo[e]);
-      hi[e] = __uint_as_float(rhi[e]);
+      for (int e = 0; e < 4; ++e) {
+        k[d / 2 + e] = 0u;
+        k[(d + 64) / 2 + e] = 0u;
+      }
+      continue;
+    }
+    float cl[8], ch[8], sl[8], sh[8], lo[8], hi[8];
+    unpack8<T>(__ldg(reinterpret_cast<const uint4 *>(crow + d)), cl);
+    unpack8<T>(__ldg(reinterpret_cast<const uint4 *>(crow + d + 64)), ch);
+    unpack8<T>(__ldg(reinterpret_cast<const uint4 *>(srow + d)), sl);
+    unpack8<T>(__ldg(reinterpret_cast<const uint4 *>(srow + d + 64)), sh);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      unpack2<T>(k[(d + e) / 2], lo[e], lo[e + 1]);
+      unpack2<T>(k[(d + 64 + e) / 2], hi[e], hi[e + 1]);
+    }
+    float olo[8], ohi[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      olo[e] = __fsub_rn(round_to<T>(__fmul_rn(lo[e], cl[e])), round_to<T>(__fmul_rn(hi[e], sl[e])));
+      ohi[e] = __fadd_rn(round_to<T>(__fmul_rn(hi[e], ch[e])), round_to<T>(__fmul_rn(lo[e], sh[e])));
     }
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int d = 16 * h2 + 8 * q;
-      float cl[8], ch[8], sl[8], sh[8];
-      if (valid) {
-        unpack8<T>(__ldg(reinterpret_cast<const uint4 *>(crow + d)), cl);
-        unpack8<T>(__ldg(reinterpret_cast<const uint4 *>(crow + d + 64)), ch);
-        unpack8<T>(__ldg(reinterpret_cast<const uint4 *>(srow + d)), sl);
-        unpack8<T>(__ldg(reinterpret_cast<const uint4 *>(srow + d + 64)), sh);
-      }
-      float olo[8], ohi[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        if (valid) {
-          const float klo = round_to<T>(__fadd_rn(lo[8 * q + e], bias[d + e]));
-          const float khi = round_to<T>(__fadd_rn(hi[8 * q + e], bias[d + 64 + e]));
-          olo[e] = round_to<T>(__fsub_rn(round_to<T>(__fmul_rn(klo, cl[e])),
-                                         round_to<T>(__fmul_rn(khi, sl[e]))));
-          ohi[e] = round_to<T>(__fadd_rn(round_to<T>(__fmul_rn(khi, ch[e])),
-                                         round_to<T>(__fmul_rn(klo, sh[e]))));
-        } else {
-          olo[e] = 0.f;
-          ohi[e] = 0.f;
-        }
-      }
-#pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        out[(d + e) >> 1] = pack2<T>(olo[e], olo[e + 1]);
-        out[(d + 64 + e) >> 1] = pack2<T>(ohi[e], ohi[e + 1]);
-      }
+    for (int e = 0; e < 8; e += 2) {
+      k[(d + e) / 2] = pack2<T>(olo[e], olo[e + 1]);
+      k[(d + 64 + e) / 2] = pack2<T>(ohi[e], ohi[e + 1]);
     }
   }
 }
@@ -155,28 +183,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + KpSmem::kBar);
   uint64_t *empty_bar = full_bar + kStages;
-  uint64_t *acc_full = empty_bar + kStages;    // [2] accumulator ready for the epilogue
-  uint64_t *acc_empty = acc_full + 2;          // [2] accumulator drained (4 warp arrivals)
-  uint64_t *staged_bar = acc_empty + 2;        // a visual tile is in the staging buffer
-  uint64_t *free_bar = staged_bar + 1;         // its covariance MMAs have read it
-  uint64_t *cov_bar = free_bar + 1;            // every MMA of this CTA has completed
+  uint64_t *acc_full = empty_bar + kStages;   // projection accumulator ready
+  uint64_t *acc_empty = acc_full + 1;         // drained (one arrival per epilogue warp)
+  uint64_t *staged_bar = acc_empty + 1;       // staging use n written (phase n)
+  uint64_t *free_bar = staged_bar + 1;        // use n read by its TMA store and its MMAs
+  uint64_t *cov_done = free_bar + 1;          // a unit's covariance MMAs completed
+  uint64_t *cov_flushed = cov_done + 1;       // ... and its accumulators read out
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + KpSmem::kTmemSlot);
   float *bias_s = reinterpret_cast<float *>(smem + KpSmem::kBias);
-  float *sums = reinterpret_cast<float *>(smem + KpSmem::kSums);
-  float *colsum = reinterpret_cast<float *>(smem + KpSmem::kColSum);
-  float *dump = reinterpret_cast<float *>(smem + KpSmem::kRing);
   unsigned char *stage = smem + KpSmem::kStage;
-  __shared__ int abort_flag;
+  int &abort_flag = *reinterpret_cast<int *>(smem + KpSmem::kAbort);
 
-  const int Z = p.splits;
-  const int m = blockIdx.x / Z;
-  const int z = static_cast<int>(cluster_rank());
-  const int b = m / p.heads, h = m % p.heads;
+  const int pairs = (p.heads + 1) / 2;
   Spans sp;
   sp.init(p.seq, p.vis_start, p.vis_len);
-  const int tiles = sp.total();
-  const int t0 = static_cast<int>((long long)z * tiles / Z);
-  const int nt = static_cast<int>((long long)(z + 1) * tiles / Z) - t0;
+  const long long total = (long long)p.batch * pairs * sp.total;
+  Range rg;
+  rg.tiles_per_unit = sp.total;
+  rg.begin = static_cast<int>(range_begin(blockIdx.x, total, gridDim.x));
+  rg.end = static_cast<int>(range_begin(blockIdx.x + 1, total, gridDim.x));
+  const int nt = rg.end - rg.begin;
   const int nk = p.hidden / 64;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned int *status = p.status;
@@ -186,21 +212,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
-    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, kEpiWarps);
     mbar_init(staged_bar, 1);
-    mbar_init(free_bar, 1);
-    mbar_init(cov_bar, 1);
+    mbar_init(free_bar, 2);            // the use's TMA store + its MMA side
+    mbar_init(cov_done, 1);
+    mbar_init(cov_flushed, kEpiWarps);
     abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
-  if (threadIdx.x >= 64) {
-    const int c = threadIdx.x - 64;
-    bias_s[c] = p.bias != nullptr ? to_f32<T>(static_cast<const T *>(p.bias)[h * 128 + c]) : 0.f;
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -213,18 +234,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&maps.w);
       int it = 0;
       bool ok = true;
-      for (int i = 0; i < nt && ok; ++i) {
-        const int tile = t0 + i, span = sp.span_of(tile), r0 = sp.row0(tile, span);
+      for (int j = rg.begin; j < rg.end && ok; ++j) {
+        const int u = rg.unit(j);
+        const int b = u / pairs, hp = u % pairs;
+        int span, row0, end, start;
+        sp.locate(rg.tile(j), span, row0, end, start);
         for (int kc = 0; kc < nk; ++kc, ++it) {
           const int st = it % kStages;
           if (!mbar_wait_bounded(&empty_bar[st], ((it / kStages) & 1) ^ 1, &abort_flag, status)) {
             ok = false;
             break;
           }
-          unsigned char *dst = smem + KpSmem::kRing + st * 2 * kBox;
-          mbar_arrive_expect_tx(&full_bar[st], 2 * kBox);
-          tma_load_3d(dst, &maps.x, kc * 64, r0, b, &full_bar[st]);
-          tma_load_2d(dst + kBox, &maps.w, kc * 64, h * 128, &full_bar[st]);
+          unsigned char *dst = smem + KpSmem::kRing + st * kStageBytes;
+          mbar_arrive_expect_tx(&full_bar[st], kStageBytes);
+          tma_load_3d(dst, &maps.x, kc * 64, row0, b, &full_bar[st]);
+          tma_load_2d(dst + kXBox, &maps.w, kc * 64, hp * 256, &full_bar[st]);
         }
       }
     }
@@ -232,166 +256,231 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-      constexpr uint32_t kIdProj = idesc_f16(kFmt, 0u, 0u, 128u, 128u);   // X, W K-major
+      constexpr uint32_t kIdProj = idesc_f16(kFmt, 0u, 0u, 128u, 256u);   // X, W K-major
       constexpr uint32_t kIdCov = idesc_f16(kFmt, 1u, 1u, 128u, 128u);    // K^T, K MN-major
       const uint32_t stage_addr = smem_u32(stage);
-      int it = 0, ncov = 0;
-      auto issue_cov = [&]() {
-        mbar_wait_bounded(staged_bar, ncov & 1, &abort_flag, status);
-        tc_fence_after();
-#pragma unroll
-        for (int ks = 0; ks < kRows / 16; ++ks) {
-          const uint64_t d = smem_desc_sw128(stage_addr + ks * 2048, kBox, 1024);
-          umma_f16(tmem + kCovCol, d, d, kIdCov, (ncov > 0 || ks > 0) ? 1u : 0u);
+      // staging uses in order: tile uj, head uh; un uses done, nflush units done
+      int uj = rg.begin, uh = 0, un = 0, nflush = 0, cur_unit = -1;
+      bool started[2] = {false, false};
+      auto take_use = [&](bool block) -> bool {
+        if (block) {
+          mbar_wait_bounded(staged_bar, un & 1, &abort_flag, status);
+        } else if (!mbar_try_wait(staged_bar, un & 1)) {
+          return false;
         }
-        umma_commit(free_bar);
-        ++ncov;
+        const int u = rg.unit(uj), tile = rg.tile(uj);
+        if (u != cur_unit) {
+          // the previous unit's accumulators must have been read out
+          if (cur_unit >= 0) mbar_wait_bounded(cov_flushed, (nflush - 1) & 1, &abort_flag, status);
+          cur_unit = u;
+          started[0] = started[1] = false;
+        }
+        if (sp.visual(tile)) {
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < kRows / 16; ++ks) {
+            const uint64_t d = smem_desc_sw128(stage_addr + ks * 2048, kOutBox, 1024);
+            umma_f16(tmem + kCovCol + 128 * uh, d, d, kIdCov, (started[uh] || ks > 0) ? 1u : 0u);
+          }
+          started[uh] = true;
+          umma_commit(free_bar);
+        } else {
+          mbar_arrive(free_bar);
+        }
+        const int hp = u % pairs;
+        const int nh = p.heads - 2 * hp < 2 ? p.heads - 2 * hp : 2;
+        ++un;
+        if (uh + 1 >= nh) {
+          if (uj == rg.unit_last(uj)) {
+            umma_commit(cov_done);   // the unit's last use: its sums are complete
+            ++nflush;
+          }
+          ++uj;
+          uh = 0;
+        } else {
+          ++uh;
+        }
+        return true;
       };
+      int it = 0;
       for (int i = 0; i < nt; ++i) {
-        const int a = i & 1;
-        mbar_wait_bounded(&acc_empty[a], ((i >> 1) & 1) ^ 1, &abort_flag, status);
+        mbar_wait_bounded(acc_empty, (i & 1) ^ 1, &abort_flag, status);
         tc_fence_after();
-        const uint32_t d_acc = tmem + a * kAccCols;
         for (int kc = 0; kc < nk; ++kc, ++it) {
           const int st = it % kStages;
           mbar_wait_bounded(&full_bar[st], (it / kStages) & 1, &abort_flag, status);
           tc_fence_after();
-          const uint32_t base = smem_u32(smem + KpSmem::kRing + st * 2 * kBox);
+          const uint32_t base = smem_u32(smem + KpSmem::kRing + st * kStageBytes);
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
             const uint64_t da = smem_desc_sw128(base + ks * 32, 16, 1024);
-            const uint64_t db = smem_desc_sw128(base + kBox + ks * 32, 16, 1024);
-            umma_f16(d_acc, da, db, kIdProj, (kc > 0 || ks > 0) ? 1u : 0u);
+            const uint64_t db = smem_desc_sw128(base + kXBox + ks * 32, 16, 1024);
+            umma_f16(tmem, da, db, kIdProj, (kc > 0 || ks > 0) ? 1u : 0u);
           }
           umma_commit(&empty_bar[st]);   // stage free once these MMAs have read it
+          // covariance updates of earlier tiles, as their uses get staged
+          while (uj < rg.begin + i && take_use(false)) {
+          }
         }
-        // the previous tile's covariance update runs behind this tile's projection
-        if (i > 0 && sp.span_of(t0 + i - 1) == 1) issue_cov();
-        umma_commit(&acc_full[a]);
+        // the previous tile's uses go before this accumulator is handed over
+        while (uj < rg.begin + i) take_use(true);
+        umma_commit(acc_full);
       }
-      if (nt > 0 && sp.span_of(t0 + nt - 1) == 1) issue_cov();
-      umma_commit(cov_bar);
+      while (uj < rg.end) take_use(true);
     }
   } else {
-    // ---------------- epilogue: one token row per thread
-    const int et = threadIdx.x - 64;
+    // ---------------- epilogue: warp group hh handles head hh of the pair
+    const int e = warp - 2;
+    const int hh = e >> 2;
     const int quarter = warp & 3;                  // TMEM lanes this warp may read
-    const int row = 32 * quarter + lane;
+    const int row = 32 * quarter + lane;           // token row (projection) / channel (covariance)
+    const int gt = (e & 3) * 32 + lane;            // thread index inside the group
     const uint32_t tmem_lane = tmem + ((uint32_t)(32 * quarter) << 16);
-    const int chunk = et & 15, rg = et >> 4;       // channel sums: 8 channels x 16 rows
+    const int chunk = gt & 15, rgp = gt >> 4;      // channel sums: 8 channels x 16 rows
     float ks_acc[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) ks_acc[k] = 0.f;
-    const T *cos_b = static_cast<const T *>(p.cos) + (long long)b * p.cs_sb;
-    const T *sin_b = static_cast<const T *>(p.sin) + (long long)b * p.cs_sb;
-    int nvis = 0;
-    bool pending = false, stored = false;
+    const T *bias_g = static_cast<const T *>(p.bias);
+    int un = 0, nflush = 0, cur_unit = -1;
+    bool stored = false, unit_vis = false;
     for (int i = 0; i < nt; ++i) {
-      const int tile = t0 + i, span = sp.span_of(tile), r0 = sp.row0(tile, span);
-      const int a = i & 1;
-      const int t = r0 + row;
-      const bool valid = t < sp.end[span];
-      mbar_wait_bounded(&acc_full[a], (i >> 1) & 1, &abort_flag, status);
+      const int j = rg.begin + i;
+      const int u = rg.unit(j), tile = rg.tile(j);
+      const int b = u / pairs, hp = u % pairs;
+      const int nh = p.heads - 2 * hp < 2 ? p.heads - 2 * hp : 2;
+      const bool has = hh < nh;
+      const int head = 2 * hp + hh;
+      int span, row0, end, start;
+      sp.locate(tile, span, row0, end, start);
+      if (u != cur_unit) {   // this head's bias
+        named_barrier_sync(1 + hh, 128);
+        bias_s[128 * hh + gt] = (has && bias_g != nullptr) ? to_f32<T>(bias_g[head * 128 + gt]) : 0.f;
+        named_barrier_sync(1 + hh, 128);
+        cur_unit = u;
+        unit_vis = false;
+      }
+      mbar_wait_bounded(acc_full, i & 1, &abort_flag, status);
       tc_fence_after();
-      uint32_t out[64];
-      rope_row<T>(tmem_lane + a * kAccCols, bias_s, cos_b + (long long)t * p.cs_ss,
-                  sin_b + (long long)t * p.cs_ss, valid, out);
+      uint32_t kv[64];
+      if (has) drain_row<T>(tmem_lane + 128 * hh, bias_s + 128 * hh, kv);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[a]);
-      // the staging tile is reusable once the previous visual tile's MMAs and
-      // the previous TMA store have read it
-      if (pending) {
-        mbar_wait_bounded(free_bar, (nvis - 1) & 1, &abort_flag, status);
-        pending = false;
-      }
-      if (et == 0 && stored) bulk_wait_read_all();
-      named_barrier_sync(1, 128);
+      if (lane == 0) mbar_arrive(acc_empty);       // the accumulator may be overwritten
+      const int use = un + hh;
+      if (has) {
+        const int t = row0 + row;
+        const bool valid = t < end;
+        const long long cs = (long long)b * p.cs_sb + (long long)t * p.cs_ss;
+        rope_row<T>(static_cast<const T *>(p.cos) + cs, static_cast<const T *>(p.sin) + cs, valid, kv);
+        // the staging tile is free once the previous use's store and MMAs have read it
+        if (use > 0) mbar_wait_bounded(free_bar, (use - 1) & 1, &abort_flag, status);
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8)
-        *reinterpret_cast<uint4 *>(stage + (c8 >> 3) * kBox + swizzled_offset<128>(row, (c8 & 7) * 8)) =
-            make_uint4(out[4 * c8], out[4 * c8 + 1], out[4 * c8 + 2], out[4 * c8 + 3]);
-      fence_proxy_async_smem();
-      named_barrier_sync(1, 128);
-      if (et == 0) {
-        tma_store_4d(&maps.k_out[span], stage, 0, r0 - sp.start[span], h, b);
-        tma_store_4d(&maps.k_out[span], stage + kBox, 64, r0 - sp.start[span], h, b);
-        bulk_commit_group();
-        if (span == 1) mbar_arrive(staged_bar);
-      }
-      stored = true;
-      if (span == 1) {
-        pending = true;
-        ++nvis;
-        const unsigned char *box = stage + (chunk >> 3) * kBox;
+        for (int c8 = 0; c8 < 16; ++c8)
+          *reinterpret_cast<uint4 *>(stage + (c8 >> 3) * kOutBox + swizzled_offset<128>(row, (c8 & 7) * 8)) =
+              make_uint4(kv[4 * c8], kv[4 * c8 + 1], kv[4 * c8 + 2], kv[4 * c8 + 3]);
+        fence_proxy_async_smem();
+        named_barrier_sync(1 + hh, 128);
+        if (gt == 0) {
+          tma_store_4d(&maps.k_out[span], stage, 0, row0 - start, head, b);
+          tma_store_4d(&maps.k_out[span], stage + kOutBox, 64, row0 - start, head, b);
+          bulk_commit_group();
+          stored = true;
+          mbar_arrive(staged_bar);
+        }
+        if (span == 1) {
+          unit_vis = true;
+          const unsigned char *box = stage + (chunk >> 3) * kOutBox;
 #pragma unroll 4
-        for (int rr = 0; rr < 16; ++rr) {
-          const uint4 v = *reinterpret_cast<const uint4 *>(box + swizzled_offset<128>(rg * 16 + rr, (chunk & 7) * 8));
-          float f[8];
-          unpack8<T>(v, f);
+          for (int rr = 0; rr < 16; ++rr) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(box + swizzled_offset<128>(rgp * 16 + rr, (chunk & 7) * 8));
+            float f[8];
+            unpack8<T>(v, f);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) ks_acc[k] += f[k];
+            for (int k = 0; k < 8; ++k) ks_acc[k] += f[k];
+          }
+        }
+        named_barrier_sync(1 + hh, 128);           // every thread is done reading the staging tile
+        if (gt == 0) {
+          bulk_wait_read_all();
+          mbar_arrive(free_bar);
         }
       }
-    }
-    if (et == 0 && stored) bulk_wait_all();
+      un += nh;
+      if (j == rg.unit_last(j)) {
+        // end of this unit in the range: covariance and channel-sum partials out
+        mbar_wait_bounded(cov_done, nflush & 1, &abort_flag, status);
+        tc_fence_after();
+        if (has) {
+          float *part = p.part + ((long long)(blockIdx.x + u) * 2 + hh) * kKProjPartFloats;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) ks_acc[k] += __shfl_xor_sync(0xffffffffu, ks_acc[k], 16);
-    if ((lane & 16) == 0) {
+          for (int c = 0; c < 8; ++c) {
+            uint32_t r[16];
+            if (unit_vis) {
+              tmem_ld16_nowait(tmem_lane + kCovCol + 128 * hh + 16 * c, r);
+              tmem_wait_ld();
+            } else {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) sums[(warp - 2) * 128 + chunk * 8 + k] = ks_acc[k];
-    }
-    named_barrier_sync(1, 128);
-    colsum[et] = sums[et] + sums[128 + et] + sums[256 + et] + sums[384 + et];
-    // covariance accumulator -> shared memory (fp32 rows, stride 132); reuses the ring
-    mbar_wait_bounded(cov_bar, 0, &abort_flag, status);
-    tc_fence_after();
+              for (int k = 0; k < 16; ++k) r[k] = 0u;
+            }
 #pragma unroll
-    for (int c0 = 0; c0 < 128; c0 += 32) {
-      float v[32];
-      if (nvis > 0) {
-        tmem_ld32(tmem_lane + kCovCol + (uint32_t)c0, v);
-      } else {
+            for (int k = 0; k < 16; k += 4)
+              *reinterpret_cast<float4 *>(part + row * 128 + 16 * c + k) =
+                  make_float4(__uint_as_float(r[k]), __uint_as_float(r[k + 1]), __uint_as_float(r[k + 2]),
+                              __uint_as_float(r[k + 3]));
+          }
 #pragma unroll
-        for (int k = 0; k < 32; ++k) v[k] = 0.f;
+          for (int k = 0; k < 8; ++k) {
+            ks_acc[k] += __shfl_xor_sync(0xffffffffu, ks_acc[k], 16);
+            if ((lane & 16) == 0) part[128 * 128 + (e & 3) * 128 + chunk * 8 + k] = ks_acc[k];
+            ks_acc[k] = 0.f;
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(cov_flushed);
+        ++nflush;
       }
-#pragma unroll
-      for (int k = 0; k < 32; k += 4)
-        *reinterpret_cast<float4 *>(dump + row * kDumpStride + c0 + k) =
-            make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
     }
-    tc_fence_before();
+    if (gt == 0 && stored) bulk_wait_all();
   }
   __syncthreads();
-  cluster_sync();  // every CTA of the cluster has its partial in shared memory
-
-  // ---------------- cluster reduction: this CTA's share of rows, every peer summed
-  {
-    const int rows = 128 / Z;
-    const int q0 = z * rows;
-    float *out = p.cov + (long long)m * 128 * 128;
-    for (int e = threadIdx.x; e < rows * 32; e += kThreads) {
-      const int r = q0 + e / 32, c4 = (e % 32) * 4;
-      const uint32_t local = smem_u32(dump + r * kDumpStride + c4);
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int q = 0; q < Z; ++q) {
-        const float4 v = ld_cluster_f4(map_to_cta(local, q));
-        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-      }
-      *reinterpret_cast<float4 *>(out + r * 128 + c4) = acc;
-    }
-    if (z == 0 && threadIdx.x < 128) {
-      const uint32_t local = smem_u32(colsum + threadIdx.x);
-      float acc = 0.f;
-      for (int q = 0; q < Z; ++q) acc += ld_cluster_f32(map_to_cta(local, q));
-      p.ksum[(long long)m * 128 + threadIdx.x] = acc;
-    }
-  }
-  cluster_sync();  // peers are done reading this CTA's shared memory
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+}
+
+// cov / ksum of (b, h): the sum, in CTA order, of the partials of the CTAs
+// whose tile range meets unit u = b * pairs + h / 2.  Block (m, y) sums the
+// 1024 floats [1024 y, 1024 y + 1024) of matrix m; y == 0 also the channel sums.
+constexpr int kReduceSplit = 128 * 128 / 1024;
+
+__global__ void __launch_bounds__(256)
+    kproj_reduce_kernel(const KProjParams p, int tiles_per_unit) {
+  const int pairs = (p.heads + 1) / 2;
+  const int m = blockIdx.x;                 // b * heads + head
+  const int b = m / p.heads, head = m % p.heads;
+  const int u = b * pairs + head / 2, hh = head & 1;
+  const long long total = (long long)p.batch * pairs * tiles_per_unit;
+  const long long lo = (long long)u * tiles_per_unit, hi = lo + tiles_per_unit;
+  // CTAs c with range_begin(c) <= lo ... range_begin(c) < hi
+  const int c0 = static_cast<int>(((lo + 1) * p.grid + total - 1) / total) - 1;
+  const int c1 = static_cast<int>((hi * p.grid + total - 1) / total) - 1;
+  const int off = (blockIdx.y * 256 + threadIdx.x) * 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float ks = 0.f;
+  for (int c = c0 < 0 ? 0 : c0; c <= c1 && c < p.grid; ++c) {
+    if (range_begin(c + 1, total, p.grid) <= lo || range_begin(c, total, p.grid) >= hi) continue;
+    const float *part = p.part + ((long long)(c + u) * 2 + hh) * kKProjPartFloats;
+    const float4 v = *reinterpret_cast<const float4 *>(part + off);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    if (blockIdx.y == 0 && threadIdx.x < 128) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) ks += part[128 * 128 + w * 128 + threadIdx.x];
+    }
+  }
+  *reinterpret_cast<float4 *>(p.cov + (long long)m * 128 * 128 + off) = acc;
+  if (blockIdx.y == 0 && threadIdx.x < 128) p.ksum[(long long)m * 128 + threadIdx.x] = ks;
 }
 
 }  // namespace
@@ -399,31 +488,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 cudaError_t launch_kproj_tc(int dtype_is_bf16, const KProjMaps &maps, const KProjParams &p,
                             cudaStream_t stream) {
   const int smem = KpSmem::kBytes + 1024;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.batch * p.heads * p.splits);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = p.splits;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (dtype_is_bf16) {
-    cudaError_t err = cudaFuncSetAttribute(kproj_tc_kernel<__nv_bfloat16>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (err != cudaSuccess) return err;
-    err = cudaLaunchKernelEx(&cfg, kproj_tc_kernel<__nv_bfloat16>, maps, p);
-    if (err != cudaSuccess) return err;
-  } else {
-    cudaError_t err = cudaFuncSetAttribute(kproj_tc_kernel<__half>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (err != cudaSuccess) return err;
-    err = cudaLaunchKernelEx(&cfg, kproj_tc_kernel<__half>, maps, p);
-    if (err != cudaSuccess) return err;
-  }
+  auto kernel = dtype_is_bf16 ? kproj_tc_kernel<__nv_bfloat16> : kproj_tc_kernel<__half>;
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (err != cudaSuccess) return err;
+  kernel<<<p.grid, kThreads, smem, stream>>>(maps, p);
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return err;
+  const int tiles_per_unit = (p.vis_start + kRows - 1) / kRows + (p.vis_len + kRows - 1) / kRows +
+                             (p.seq - p.vis_start - p.vis_len + kRows - 1) / kRows;
+  kproj_reduce_kernel<<<dim3(p.batch * p.heads, kReduceSplit), 256, 0, stream>>>(p, tiles_per_unit);
   return cudaGetLastError();
 }
 

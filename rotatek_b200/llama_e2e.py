@@ -12,6 +12,12 @@ rotated-truncated visual Keys plus the full-width prompt/text Keys
 synthetic embeddings.  Weights are random (there is no checkpoint); the shapes
 are the model's, so every byte and FLOP of the real model is moved and done.
 
+Prefill computes each layer's Keys with ``build_rotation_projected`` (K
+projection, RoPE and the visual span's covariance sums in one tensor-core pass,
+then the rest of the build), Queries and Values with cuBLAS; set
+``fused_key_projection=False`` for the adapters' order (fused QKV GEMM, torch
+RoPE, ``build_rotation`` on the visual slice).
+
 Decode steps are static-shape -- the append slot, the RoPE position and the
 text-span mask live on the device -- so a whole step (32 layers) is one CUDA
 graph replay.  Linear layers are cuBLAS GEMMs (torch), prefill attention is
@@ -27,7 +33,7 @@ import torch.nn.functional as F
 
 from rotatek_b200.cache import SpanKVCache
 from rotatek_b200.kernels import rotatek_decode
-from rotatek_b200.rotation import QUERY_WINDOW, build_rotation, keep_count
+from rotatek_b200.rotation import QUERY_WINDOW, build_rotation, build_rotation_projected, keep_count
 
 
 @dataclass
@@ -47,6 +53,7 @@ class DecoderConfig:
     channel_ratio: float = 0.75
     max_new_tokens: int = 128
     dtype: torch.dtype = torch.float16
+    fused_key_projection: bool = True   # prefill K through key projection + build in one call
 
 
 class RandomLlamaDecoder:
@@ -127,17 +134,31 @@ class RandomLlamaDecoder:
         cos, sin = self.cos[:s_total], self.sin[:s_total]
         self.cache = SpanKVCache(max_new_tokens=c.max_new_tokens)
         groups = c.heads // c.kv_heads
+        b = x.shape[0]
+        hq, hk = c.heads * c.head_dim, c.kv_heads * c.head_dim
         for li, L in enumerate(self.layers):
-            q, k, v = self._qkv(L, x)
-            q, k = self._rope(q, cos, sin), self._rope(k, cos, sin)
-            k = k.contiguous()
-            v = v.contiguous()
+            if c.fused_key_projection:
+                # K = RoPE(x W_k^T) for every token with the visual span's sums in
+                # one tensor-core pass, then the rest of the build on those Keys
+                xn = self._rms(x, L["ln1"])
+                q = F.linear(xn, L["wqkv"][:hq]).view(b, s_total, c.heads, c.head_dim).transpose(1, 2)
+                v = F.linear(xn, L["wqkv"][hq + hk:]).view(b, s_total, c.kv_heads, c.head_dim)
+                v = v.transpose(1, 2).contiguous()
+                q = self._rope(q, cos, sin)
+                k, kept, R, dm, _ = build_rotation_projected(xn, L["wqkv"][hq:hq + hk], None, cos, sin, s_p, s_v,
+                                                             q[:, :, -QUERY_WINDOW:], self.keep, groups)
+                del xn
+            else:
+                q, k, v = self._qkv(L, x)
+                q, k = self._rope(q, cos, sin), self._rope(k, cos, sin)
+                k = k.contiguous()
+                v = v.contiguous()
+                # RotateK build of this layer (ChannelPruner.update_rotatek's body)
+                kept, R, dm, _ = build_rotation(k[:, :, s_p:s_p + s_v], q[:, :, -QUERY_WINDOW:], self.keep, groups)
             a = F.scaled_dot_product_attention(q, k.repeat_interleave(groups, 1) if groups > 1 else k,
                                                v.repeat_interleave(groups, 1) if groups > 1 else v, is_causal=True)
-            x = x + F.linear(a.transpose(1, 2).reshape(x.shape[0], s_total, -1), L["wo"])
+            x = x + F.linear(a.transpose(1, 2).reshape(b, s_total, -1), L["wo"])
             x = x + self._mlp(L, x)
-            # RotateK build of this layer (ChannelPruner.update_rotatek's body)
-            kept, R, dm, _ = build_rotation(k[:, :, s_p:s_p + s_v], q[:, :, -QUERY_WINDOW:], self.keep, groups)
             self.cache.store_pruned(kept, k[:, :, :s_p], k[:, :, s_p + s_v:], v, R, dm, li)
             del q, k, v, a
         self.seq_len = s_total

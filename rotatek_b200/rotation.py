@@ -213,7 +213,7 @@ def key_projection(hidden_states: torch.Tensor, w_k: torch.Tensor, bias: Optiona
     cov = torch.empty(b, h, 128, 128, dtype=torch.float32, device=dev)
     ksum = torch.empty(b, h, 128, dtype=torch.float32, device=dev)
     lib = _lib.load()
-    ws = _workspace(dev, 256)
+    ws = _workspace(dev, lib.rtk_key_projection_workspace_size(b, h, s, vis_start, vis_len, dev.index))
     D = _lib.describe
     _lib.check(lib.rtk_key_projection(D(hidden_states), D(w_k), D(bias), D(cos), D(sin), vis_start, vis_len,
                                       D(keys), D(cov), D(ksum), ctypes.c_void_p(ws.data_ptr()), ws.numel(),
@@ -247,7 +247,7 @@ def build_rotation_projected(hidden_states: torch.Tensor, w_k: torch.Tensor, bia
     R = torch.empty(b, h, d, keep, dtype=dt, device=dev)
     dm = torch.empty(b, h, d, dtype=dt, device=dev)
     lib = _lib.load()
-    ws = _workspace(dev, lib.rtk_build_rotation_workspace_size(b, h, d))
+    ws = _workspace(dev, lib.rtk_build_rotation_projected_workspace_size(b, h, s, vis_start, vis_len, dev.index))
     D = _lib.describe
     _lib.check(lib.rtk_build_rotation_projected(
         D(hidden_states), D(w_k), D(bias), D(cos), D(sin), vis_start, vis_len, D(q), num_kv_groups, keep,

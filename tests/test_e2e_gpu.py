@@ -60,3 +60,28 @@ def test_layer_attention_matches_oracle():
     got = out.float().cpu().numpy()
     np.testing.assert_allclose(got, want, rtol=0, atol=1e-3 + 2.0 ** -10 * np.abs(want).max())
     assert int(m.mask.sum()) == 2 * (c.prompt + c.text + 2)
+
+
+def test_fused_key_projection_prefill_matches_adapter_order():
+    """Prefill through build_rotation_projected (fused K projection + RoPE +
+    covariance sums) against the adapters' order (QKV GEMM, torch RoPE,
+    build_rotation): layer 0 stores the same Keys up to the projection's
+    accumulation order and spans the same subspace."""
+    from dataclasses import replace
+    from oracle import projection as oproj
+    outs = []
+    for fused in (True, False):
+        m = RandomLlamaDecoder(replace(CFG, fused_key_projection=fused), "cuda", seed=0)
+        logits = m.prefill(m.prompt_embeddings(2, seed=1))
+        outs.append((m.cache.layers[0], logits.float()))
+    (a, la), (b, lb) = outs
+    n = a.s_prompt + a.s_text                     # prompt | text stored so far
+    frac, worst = oproj.key_mismatch(a.keys_full[:, :, :n].float().cpu().numpy(),
+                                     b.keys_full[:, :, :n].float().cpu().numpy(), "float16")
+    assert frac <= 5e-3 and worst <= 4.0, (frac, worst)
+    rel = torch.linalg.vector_norm((a.keys_rot - b.keys_rot).float()) / torch.linalg.vector_norm(b.keys_rot.float())
+    assert float(rel) < 1e-2
+    Ra, Rb = a.rotation.double(), b.rotation.double()
+    dist = torch.linalg.matrix_norm(Ra @ Ra.transpose(-1, -2) - Rb @ Rb.transpose(-1, -2))
+    assert float(dist.max()) < 1e-2
+    assert float((la - lb).abs().max()) <= 2e-2 * float(lb.abs().max())

@@ -66,7 +66,8 @@ def test_key_projection_matches_reference_path(golden, case):
     (torch.bfloat16, 1, 100, 64, 1, 10, 80, False, False),      # shorter than one tile
     (torch.float16, 2, 700, 256, 2, 0, 700, True, False),       # no prompt, no text
     (torch.bfloat16, 1, 300, 128, 2, 0, 0, True, True),         # no visual span: zero sums
-    (torch.bfloat16, 2, 300, 64, 40, 20, 250, False, True),     # 80 units -> no cluster
+    (torch.bfloat16, 2, 300, 64, 40, 20, 250, False, True),     # 40 units of 4 tiles
+    (torch.bfloat16, 8, 300, 128, 15, 20, 250, True, True),     # odd H; CTA ranges cross units
     (torch.bfloat16, 1, 4000, 3584, 4, 32, 3900, True, False),  # Qwen2.5-VL-7B K projection width
 ])
 def test_key_projection_vs_oracle(dtype, B, S, hidden, H, vs, vl, bias, per_batch):
