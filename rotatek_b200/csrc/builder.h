@@ -38,21 +38,21 @@ struct KProjParams {
   const void *bias;                       // [heads * 128] or NULL
   const void *cos, *sin;                  // [B | 1, S, 128] (element strides below, channel stride 1)
   long long cs_sb, cs_ss;                 // batch stride (0 = broadcast), token stride
-  float *part;                            // per-CTA partial sums (kproj_workspace_floats)
+  float *part;                            // per-group partial sums (kproj_workspace_floats)
   float *cov;                             // [B * H][128][128]
   float *ksum;                            // [B * H][128]
   unsigned int *status;                   // device status word (bounded-wait timeouts)
-  int grid;                               // persistent CTAs (<= SMs)
+  int grid;                               // persistent CTAs: groups * ceil(H / 2)
 };
 
-// One (CTA, unit, head) partial: sum k k^T (128 x 128) then four per-warp
-// channel sums (4 x 128).  Slots are indexed (cta + unit) * 2 + head, unit =
-// b * ceil(H / 2) + head pair.
+// One (group, b, head) partial: sum k k^T (128 x 128) then four per-warp
+// channel sums (4 x 128).  Slots are indexed ((group + b) * P + pair) * 2 +
+// head-in-pair, P = ceil(H / 2); the grid is groups * P CTAs.
 constexpr int kKProjPartFloats = 128 * 128 + 4 * 128;
 
-inline long long kproj_units(long long batch, long long heads) { return batch * ((heads + 1) / 2); }
+inline long long kproj_pairs(long long heads) { return (heads + 1) / 2; }
 inline long long kproj_workspace_floats(long long batch, long long heads, long long grid) {
-  return (grid + kproj_units(batch, heads)) * 2 * kKProjPartFloats;
+  return (grid / kproj_pairs(heads) + batch) * kproj_pairs(heads) * 2 * kKProjPartFloats;
 }
 
 // x: [B, S, hidden] 3-D map, box {64, 128, 1}; w: [H*128, hidden] 2-D map, box

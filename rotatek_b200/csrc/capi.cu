@@ -641,9 +641,13 @@ bool encode_map_rank(CUtensorMap *map, CUtensorMapDataType dt, int rank, const v
 int64_t kproj_tiles_per_unit(int64_t S, int64_t vis_start, int64_t vis_len) {
   return cdiv(vis_start, 128) + cdiv(vis_len, 128) + cdiv(S - vis_start - vis_len, 128);
 }
+// groups of ceil(H / 2) CTAs (one per head pair), as many groups as fit one
+// CTA per SM and there are (b, tile) items
 int64_t kproj_grid(int64_t B, int64_t H, int64_t S, int64_t vis_start, int64_t vis_len, int device) {
-  const int64_t total = rtk::kproj_units(B, H) * kproj_tiles_per_unit(S, vis_start, vis_len);
-  return std::max<int64_t>(1, std::min<int64_t>(sm_count(device), total));
+  const int64_t pairs = rtk::kproj_pairs(H);
+  const int64_t items = B * kproj_tiles_per_unit(S, vis_start, vis_len);
+  const int64_t groups = std::max<int64_t>(1, std::min<int64_t>(sm_count(device) / pairs, items));
+  return groups * pairs;
 }
 size_t kproj_part_bytes(int64_t B, int64_t H, int64_t S, int64_t vis_start, int64_t vis_len, int device) {
   return align_up((size_t)rtk::kproj_workspace_floats(B, H, kproj_grid(B, H, S, vis_start, vis_len, device)) *
@@ -681,7 +685,7 @@ int run_key_projection(const rtk_tensor *x, const rtk_tensor *w, const rtk_tenso
     return fail(RTK_ERR_INVALID, "keys_out must be [B, H_kv, S, 128] in the hidden states' dtype");
   if (Hd % 64 != 0) return fail(RTK_ERR_UNSUPPORTED, "hidden size must be a multiple of 64 (got %lld)", (long long)Hd);
   if (B * S >= (1ll << 31) || Hd >= (1ll << 31) ||
-      rtk::kproj_units(B, H) * kproj_tiles_per_unit(S, vis_start, vis_len) >= (1ll << 31))
+      B * kproj_tiles_per_unit(S, vis_start, vis_len) >= (1ll << 31) || H >= (1ll << 20))
     return fail(RTK_ERR_UNSUPPORTED, "tensor too large");
   if (B == 0) return RTK_OK;
   if (S == 0) {
@@ -734,7 +738,7 @@ int run_key_projection(const rtk_tensor *x, const rtk_tensor *w, const rtk_tenso
   kp.cs_sb = cs_sb; kp.cs_ss = cos->stride[1];
   kp.cov = cov; kp.ksum = ksum;
   kp.status = status;
-  // persistent: one CTA per SM, contiguous shares of the B * ceil(H / 2) * tiles tiles
+  // persistent: groups x head pairs, one CTA per SM; contiguous shares of the B x tiles items
   const int device = current_device();
   kp.grid = (int)kproj_grid(B, H, S, vis_start, vis_len, device);
   const size_t need = kproj_part_bytes(B, H, S, vis_start, vis_len, device);

@@ -8,10 +8,13 @@
 // the visual span -- the inputs of the Jacobi prologue -- so the covariance
 // pass over K disappears.
 //
-// Work: a unit is (b, pair of KV heads); its 128-token tiles run over the
-// prompt, visual and text spans, each span tiled from its own start.  The
-// U x T tiles are split into contiguous ranges over a persistent grid of one
-// CTA per SM (320 threads):
+// Work: the 128-token tiles of a sequence run over the prompt, visual and
+// text spans, each span tiled from its own start.  The grid (one CTA per SM,
+// 320 threads) is groups x P CTAs, P = ceil(H / 2) head pairs: the B x T
+// (b, tile) items are split into contiguous ranges over the groups, and the P
+// CTAs of a group walk the same range in step, CTA p producing head pair p --
+// so a hidden-state tile comes from HBM once and from L2 for the other pairs.
+// A unit is (b, head pair): its sums are flushed when a range leaves a b.
 //   warp 0     TMA producer: per tile and 64-wide hidden chunk an X box
 //              {64 x 128 tokens} and a W box {64 x 256 channels} (128B
 //              swizzle) into a 4-stage ring; W rows past H * 128 read as zero
@@ -88,7 +91,7 @@ struct Spans {
   __device__ bool visual(int tile) const { return tile >= first1 && tile < first2; }
 };
 
-// A CTA's share of the U * T tiles, and the unit / tile behind an index.
+// A group's share of the B * T (b, tile) items, and the b / tile behind an index.
 struct Range {
   int begin, end, tiles_per_unit;
   __device__ int unit(int j) const { return j / tiles_per_unit; }
@@ -195,13 +198,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   int &abort_flag = *reinterpret_cast<int *>(smem + KpSmem::kAbort);
 
   const int pairs = (p.heads + 1) / 2;
+  const int groups = gridDim.x / pairs;
+  const int grp = blockIdx.x / pairs, hp = blockIdx.x % pairs;   // this CTA's group and head pair
+  const int nh = p.heads - 2 * hp < 2 ? p.heads - 2 * hp : 2;     // heads of the pair (2, or 1 if H is odd)
   Spans sp;
   sp.init(p.seq, p.vis_start, p.vis_len);
-  const long long total = (long long)p.batch * pairs * sp.total;
+  const long long total = (long long)p.batch * sp.total;
   Range rg;
   rg.tiles_per_unit = sp.total;
-  rg.begin = static_cast<int>(range_begin(blockIdx.x, total, gridDim.x));
-  rg.end = static_cast<int>(range_begin(blockIdx.x + 1, total, gridDim.x));
+  rg.begin = static_cast<int>(range_begin(grp, total, groups));
+  rg.end = static_cast<int>(range_begin(grp + 1, total, groups));
   const int nt = rg.end - rg.begin;
   const int nk = p.hidden / 64;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -235,8 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0;
       bool ok = true;
       for (int j = rg.begin; j < rg.end && ok; ++j) {
-        const int u = rg.unit(j);
-        const int b = u / pairs, hp = u % pairs;
+        const int b = rg.unit(j);
         int span, row0, end, start;
         sp.locate(rg.tile(j), span, row0, end, start);
         for (int kc = 0; kc < nk; ++kc, ++it) {
@@ -287,8 +292,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           mbar_arrive(free_bar);
         }
-        const int hp = u % pairs;
-        const int nh = p.heads - 2 * hp < 2 ? p.heads - 2 * hp : 2;
         ++un;
         if (uh + 1 >= nh) {
           if (uj == rg.unit_last(uj)) {
@@ -346,8 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < nt; ++i) {
       const int j = rg.begin + i;
       const int u = rg.unit(j), tile = rg.tile(j);
-      const int b = u / pairs, hp = u % pairs;
-      const int nh = p.heads - 2 * hp < 2 ? p.heads - 2 * hp : 2;
+      const int b = u;
       const bool has = hh < nh;
       const int head = 2 * hp + hh;
       int span, row0, end, start;
@@ -411,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait_bounded(cov_done, nflush & 1, &abort_flag, status);
         tc_fence_after();
         if (has) {
-          float *part = p.part + ((long long)(blockIdx.x + u) * 2 + hh) * kKProjPartFloats;
+          float *part = p.part + (((long long)(grp + b) * pairs + hp) * 2 + hh) * kKProjPartFloats;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             uint32_t r[16];
@@ -450,28 +452,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// cov / ksum of (b, h): the sum, in CTA order, of the partials of the CTAs
-// whose tile range meets unit u = b * pairs + h / 2.  Block (m, y) sums the
-// 1024 floats [1024 y, 1024 y + 1024) of matrix m; y == 0 also the channel sums.
+// cov / ksum of (b, h): the sum, in group order, of the partials of the
+// groups whose range meets b's items.  Block (m, y) sums the 1024 floats
+// [1024 y, 1024 y + 1024) of matrix m; y == 0 also the channel sums.
 constexpr int kReduceSplit = 128 * 128 / 1024;
 
 __global__ void __launch_bounds__(256)
     kproj_reduce_kernel(const KProjParams p, int tiles_per_unit) {
   const int pairs = (p.heads + 1) / 2;
+  const int groups = p.grid / pairs;
   const int m = blockIdx.x;                 // b * heads + head
   const int b = m / p.heads, head = m % p.heads;
-  const int u = b * pairs + head / 2, hh = head & 1;
-  const long long total = (long long)p.batch * pairs * tiles_per_unit;
-  const long long lo = (long long)u * tiles_per_unit, hi = lo + tiles_per_unit;
-  // CTAs c with range_begin(c) <= lo ... range_begin(c) < hi
-  const int c0 = static_cast<int>(((lo + 1) * p.grid + total - 1) / total) - 1;
-  const int c1 = static_cast<int>((hi * p.grid + total - 1) / total) - 1;
+  const int hp = head / 2, hh = head & 1;
+  const long long total = (long long)p.batch * tiles_per_unit;
+  const long long lo = (long long)b * tiles_per_unit, hi = lo + tiles_per_unit;
+  // groups g with range_begin(g) <= lo ... range_begin(g) < hi
+  const int c0 = static_cast<int>(((lo + 1) * groups + total - 1) / total) - 1;
+  const int c1 = static_cast<int>((hi * groups + total - 1) / total) - 1;
   const int off = (blockIdx.y * 256 + threadIdx.x) * 4;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   float ks = 0.f;
-  for (int c = c0 < 0 ? 0 : c0; c <= c1 && c < p.grid; ++c) {
-    if (range_begin(c + 1, total, p.grid) <= lo || range_begin(c, total, p.grid) >= hi) continue;
-    const float *part = p.part + ((long long)(c + u) * 2 + hh) * kKProjPartFloats;
+  for (int c = c0 < 0 ? 0 : c0; c <= c1 && c < groups; ++c) {
+    if (range_begin(c + 1, total, groups) <= lo || range_begin(c, total, groups) >= hi) continue;
+    const float *part = p.part + (((long long)(c + b) * pairs + hp) * 2 + hh) * kKProjPartFloats;
     const float4 v = *reinterpret_cast<const float4 *>(part + off);
     acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
     if (blockIdx.y == 0 && threadIdx.x < 128) {
