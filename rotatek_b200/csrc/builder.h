@@ -42,25 +42,30 @@ struct KProjParams {
   float *cov;                             // [B * H][128][128]
   float *ksum;                            // [B * H][128]
   unsigned int *status;                   // device status word (bounded-wait timeouts)
-  int grid;                               // persistent CTAs: groups * ceil(H / 2)
+  int grid;                               // CTAs: groups * ceil(H / 2) clusters of 2
 };
 
 // One (group, b, head) partial: sum k k^T (128 x 128) then four per-warp
 // channel sums (4 x 128).  Slots are indexed ((group + b) * P + pair) * 2 +
-// head-in-pair, P = ceil(H / 2); the grid is groups * P CTAs.
+// head-in-pair, P = ceil(H / 2); the grid is groups * P two-CTA clusters.
 constexpr int kKProjPartFloats = 128 * 128 + 4 * 128;
 
 inline long long kproj_pairs(long long heads) { return (heads + 1) / 2; }
 inline long long kproj_workspace_floats(long long batch, long long heads, long long grid) {
-  return (grid / kproj_pairs(heads) + batch) * kproj_pairs(heads) * 2 * kKProjPartFloats;
+  return (grid / (2 * kproj_pairs(heads)) + batch) * kproj_pairs(heads) * 2 * kKProjPartFloats;
 }
+// Pair steps (two 128-token tiles of one span) of one sequence.
+int kproj_steps_per_b(int seq, int vis_start, int vis_len);
 
 // x: [B, S, hidden] 3-D map, box {64, 128, 1}; w: [H*128, hidden] 2-D map, box
-// {64, 256}; k_out[i]: the output [B, H, len_i, 128] of span i (prompt, visual,
+// {64, 128}; k_out[i]: the output [B, H, len_i, 128] of span i (prompt, visual,
 // text) as 4-D maps with box {64, 128, 1, 1}; all 128B-swizzled.
 struct KProjMaps {
   CUtensorMap x, w, k_out[3];
 };
+
+// Two-CTA clusters of the projection kernel that fit the current device at once (0 if unknown).
+int kproj_max_clusters(int dtype_is_bf16);
 
 // The projection kernel (grid = p.grid), then the reduction of its partials into cov / ksum.
 cudaError_t launch_kproj_tc(int dtype_is_bf16, const KProjMaps &maps, const KProjParams &p,

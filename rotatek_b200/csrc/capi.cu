@@ -637,17 +637,31 @@ bool encode_map_rank(CUtensorMap *map, CUtensorMapDataType dt, int rank, const v
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// 128-token tiles of one (b, head pair) and the persistent grid of the projection.
+// Pair steps (two 128-token tiles of one span) of one sequence.
 int64_t kproj_tiles_per_unit(int64_t S, int64_t vis_start, int64_t vis_len) {
-  return cdiv(vis_start, 128) + cdiv(vis_len, 128) + cdiv(S - vis_start - vis_len, 128);
+  return (cdiv(vis_start, 128) + 1) / 2 + (cdiv(vis_len, 128) + 1) / 2 + (cdiv(S - vis_start - vis_len, 128) + 1) / 2;
 }
-// groups of ceil(H / 2) CTAs (one per head pair), as many groups as fit one
-// CTA per SM and there are (b, tile) items
+// Co-resident two-CTA clusters of the projection kernel on `device` (cached;
+// one CTA per SM, so at most SMs / 2).
+int64_t kproj_cluster_slots(int device) {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  if (device < 0 || device >= 64) return sm_count(device) / 2;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[device] == 0) {
+    int n = rtk::kproj_max_clusters(1);
+    if (n <= 0) n = sm_count(device) / 2;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+// groups of ceil(H / 2) two-CTA clusters (one per head pair), as many groups
+// as fit the device at once and there are (b, step) items
 int64_t kproj_grid(int64_t B, int64_t H, int64_t S, int64_t vis_start, int64_t vis_len, int device) {
   const int64_t pairs = rtk::kproj_pairs(H);
   const int64_t items = B * kproj_tiles_per_unit(S, vis_start, vis_len);
-  const int64_t groups = std::max<int64_t>(1, std::min<int64_t>(sm_count(device) / pairs, items));
-  return groups * pairs;
+  const int64_t groups = std::max<int64_t>(1, std::min<int64_t>(kproj_cluster_slots(device) / pairs, items));
+  return groups * pairs * 2;
 }
 size_t kproj_part_bytes(int64_t B, int64_t H, int64_t S, int64_t vis_start, int64_t vis_len, int device) {
   return align_up((size_t)rtk::kproj_workspace_floats(B, H, kproj_grid(B, H, S, vis_start, vis_len, device)) *
@@ -714,7 +728,7 @@ int run_key_projection(const rtk_tensor *x, const rtk_tensor *w, const rtk_tenso
   {
     const cuuint64_t dims[2] = {(cuuint64_t)Hd, (cuuint64_t)(H * 128)};
     const cuuint64_t strides[1] = {(cuuint64_t)(w->stride[0] * 2)};
-    const cuuint32_t box[2] = {64, 256};
+    const cuuint32_t box[2] = {64, 128};
     if (!encode_map_rank(&maps.w, tdt, 2, w->data, dims, strides, box))
       return fail(RTK_ERR_UNSUPPORTED, "w_k layout is not describable by TMA (16-byte aligned rows needed)");
   }
@@ -738,7 +752,7 @@ int run_key_projection(const rtk_tensor *x, const rtk_tensor *w, const rtk_tenso
   kp.cs_sb = cs_sb; kp.cs_ss = cos->stride[1];
   kp.cov = cov; kp.ksum = ksum;
   kp.status = status;
-  // persistent: groups x head pairs, one CTA per SM; contiguous shares of the B x tiles items
+  // persistent: groups x head pairs x 2 CTAs, one CTA per SM; contiguous shares of the B x steps items
   const int device = current_device();
   kp.grid = (int)kproj_grid(B, H, S, vis_start, vis_len, device);
   const size_t need = kproj_part_bytes(B, H, S, vis_start, vis_len, device);
