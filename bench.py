@@ -811,10 +811,10 @@ def run_kproj(args):
                    "l2": f"hidden states {x.numel() * 2 / 1e9:.2f} GB > 126 MB L2; no flush"},
         "phases_us": {"key_projection_fused": proj, "cublas_k_proj_alone": lin},
         "adapter_path_us": theirs, "speedup_vs_adapter_path": theirs / ours,
-        "roofline": {"bound": "tensor", "kernel": "kproj_tc_kernel + kproj_reduce_kernel",
+        "roofline": {"bound": "tensor", "kernel": "kproj_pair_kernel + kproj_reduce_kernel",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "algorithmic_flops_per_launch": flops,
-                     "traffic": ncu_traffic_per_launch("kproj_tc_small_case.txt", "dram_bytes_per_launch_config4"),
+                     "traffic": ncu_traffic_per_launch("kproj_pair_small_case.txt", "dram_bytes_per_launch_config4"),
                      "algorithmic_bytes_per_launch": (x.numel() + w.numel() + bias.numel() + b * hkv * s * 128
                                                       + 2 * cos.numel()) * 2 + b * hkv * (128 * 128 + 128) * 4,
                      "cublas_k_proj_tflops": 2 * b * s * hid * hkv * 128 / lin / 1e6},
@@ -839,6 +839,12 @@ def run_e2e(args):
     model = RandomLlamaDecoder(cfg, dev, seed=0)
     batches = [args.batch] if args.batch else [1, 4, 8]
     peak, peak_kind = load_peak_hbm()
+    # one untimed prefill first: the process's first calls load kernels and
+    # cuBLAS heuristics, which would otherwise land in the first batch's time
+    x = model.prompt_embeddings(1, seed=0)
+    model.prefill(x)
+    del x
+    torch.cuda.synchronize()
     for b in batches:
         x = model.prompt_embeddings(b, seed=b)
         torch.cuda.synchronize()
