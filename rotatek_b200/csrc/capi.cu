@@ -122,7 +122,7 @@ EncodeTiledFn encode_fn() {
 // Returns false when TMA cannot describe the layout (the caller then uses the
 // generic kernel).  Size-1 dimensions get a canonical stride.
 bool encode_map(CUtensorMap *map, const View4 &v, CUtensorMapDataType dt, int box_inner,
-                int box_rows, CUtensorMapSwizzle sw) {
+                int box_rows, CUtensorMapSwizzle sw, int esize = 2) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return false;
   if (v.s[3] != 1) return false;
@@ -130,10 +130,10 @@ bool encode_map(CUtensorMap *map, const View4 &v, CUtensorMapDataType dt, int bo
   cuuint64_t dims[4] = {(cuuint64_t)v.n[3], (cuuint64_t)v.n[2], (cuuint64_t)v.n[1],
                         (cuuint64_t)v.n[0]};
   cuuint64_t strides[3];
-  int64_t natural = v.n[3] * 2;
+  int64_t natural = v.n[3] * esize;
   for (int i = 0; i < 3; ++i) {
     const int dim = 2 - i;  // S, H, B
-    int64_t sb = v.s[dim] * 2;
+    int64_t sb = v.s[dim] * esize;
     if (v.n[dim] == 1) sb = (natural + 15) / 16 * 16;
     if (sb <= 0 || sb % 16 != 0) return false;
     strides[i] = (cuuint64_t)sb;
@@ -249,6 +249,7 @@ struct DecodeArgs {
   const rtk_tensor *q, *R, *dm, *kf, *vf, *mask, *ks, *vs, *out;
   int64_t groups;
   bool dense;  // full_channel_decode: no visual span, no mask
+  const rtk_tensor *ksc = nullptr, *vsc = nullptr;   // fp8 visual span: ks / vs are e4m3 (uint8)
 };
 
 int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cudaStream_t stream) {
@@ -281,6 +282,7 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
   unsigned int *status = reinterpret_cast<unsigned int *>(ws);
   const double scale_log2 = 1.4426950408889634 / std::sqrt((double)D);
 
+  const bool fp8 = a.ksc != nullptr;
   // ---------------- tensor-core path
   bool tc = is_half_type(dt) && D == 128 && (Sf + Sv) > 0 && a.q->stride[2] == 1 &&
             os[2] == 1 && (a.dense || ((DK == 16 || DK == 32 || DK == 64) && R.s[3] == 1 &&
@@ -293,10 +295,18 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
     if (Sf > 0)
       tc = encode_map(&maps.kf, kf, et, 64, kFullBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B) &&
            encode_map(&maps.vf, vf, et, 64, kFullBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (tc && Sv > 0)
+    if (tc && Sv > 0 && !fp8)
       tc = encode_map(&maps.ks, ks, et, (int)DK, kVisBlockTokens, swizzle_for_row_bytes((int)DK * 2)) &&
            encode_map(&maps.vs, vs, et, 64, kVisBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (tc && Sv > 0 && fp8)   // e4m3 rows of DK and 128 bytes
+      tc = encode_map(&maps.ks, ks, CU_TENSOR_MAP_DATA_TYPE_UINT8, (int)DK, kVisBlockTokens,
+                      DK == 16 ? CU_TENSOR_MAP_SWIZZLE_NONE : swizzle_for_row_bytes((int)DK), 1) &&
+           encode_map(&maps.vs, vs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, kVisBlockTokens,
+                      CU_TENSOR_MAP_SWIZZLE_128B, 1);
   }
+  if (fp8 && !tc)
+    return fail(RTK_ERR_UNSUPPORTED, "the fp8 visual span needs bf16 / fp16 queries, head_dim 128, D_keep 16, "
+                                     "32 or 64 and 16-byte aligned e4m3 rows");
   if (tc) {
     const TcShape t = tc_shape(B, Hkv, G, Sf, Sv, device);
     const WorkspacePlan w = plan_workspace(B, Hq, t.slots, t.slot_floats);
@@ -321,8 +331,17 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
     p.slot_floats = t.slot_floats;
     p.tickets = reinterpret_cast<int *>(ws + w.ticket_off);
     p.status = status;
-    const cudaError_t e = rtk::launch_decode_tc(dt == RTK_BF16, maps, p, t.heads_tile,
-                                                a.dense ? 32 : (int)DK, t.grid, stream);
+    cudaError_t e;
+    if (fp8) {
+      rtk::DecodeFp8 f;
+      f.k_scale = static_cast<const float *>(a.ksc->data);
+      f.ksc_sb = a.ksc->stride[0]; f.ksc_sh = a.ksc->stride[1];
+      f.v_scale = static_cast<const float *>(a.vsc->data);
+      f.vsc_sb = a.vsc->stride[0]; f.vsc_sh = a.vsc->stride[1]; f.vsc_ss = a.vsc->stride[2];
+      e = rtk::launch_decode_tc_fp8(dt == RTK_BF16, maps, p, f, t.heads_tile, (int)DK, t.grid, stream);
+    } else {
+      e = rtk::launch_decode_tc(dt == RTK_BF16, maps, p, t.heads_tile, a.dense ? 32 : (int)DK, t.grid, stream);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "rotatek decode (tensor-core kernel) launch");
     return RTK_OK;
   }
@@ -441,6 +460,104 @@ int rtk_rotatek_decode(const rtk_tensor *q_full, const rtk_tensor *R_partial,
   if (B * Hq == 0 || D == 0) return RTK_OK;
   DecodeArgs a{q_full, R_partial, delta_mu, k_full, v_full, mask_full, k_sparse, v_sparse, out, num_kv_groups, false};
   return run_decode(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int rtk_rotatek_decode_fp8(const rtk_tensor *q_full, const rtk_tensor *R_partial,
+                           const rtk_tensor *delta_mu, const rtk_tensor *k_full,
+                           const rtk_tensor *v_full, const rtk_tensor *mask_full,
+                           const rtk_tensor *k8, const rtk_tensor *k_scale, const rtk_tensor *v8,
+                           const rtk_tensor *v_scale, int64_t num_kv_groups, const rtk_tensor *out,
+                           void *workspace, size_t workspace_bytes, void *stream) {
+  g_last_error.clear();
+  if (q_full == nullptr || q_full->ndim != 3) return fail(RTK_ERR_INVALID, "q_full must be [B, H_q, D]");
+  if (R_partial == nullptr || R_partial->ndim != 4)
+    return fail(RTK_ERR_INVALID, "R_partial must be [B, H_kv, D, D_keep]");
+  if (mask_full != nullptr && mask_full->dtype != RTK_U8) return fail(RTK_ERR_INVALID, "mask_full must be uint8");
+  const int64_t B = q_full->shape[0], Hq = q_full->shape[1], D = q_full->shape[2];
+  const int64_t Hkv = R_partial->shape[1], DK = R_partial->shape[3];
+  if (num_kv_groups <= 0 || Hq != Hkv * num_kv_groups)
+    return fail(RTK_ERR_INVALID, "H_q=%lld is not H_kv=%lld * num_kv_groups=%lld", (long long)Hq,
+                (long long)Hkv, (long long)num_kv_groups);
+  if (!same_dims(R_partial, 4, {B, Hkv, D, -1}) || DK < 1 || DK > D)
+    return fail(RTK_ERR_INVALID, "R_partial must be [B, H_kv, D, D_keep]");
+  if (delta_mu != nullptr && !same_dims(delta_mu, 3, {B, Hkv, D}))
+    return fail(RTK_ERR_INVALID, "delta_mu must be [B, H_kv, D]");
+  if (!same_dims(k_full, 4, {B, Hkv, -1, D})) return fail(RTK_ERR_INVALID, "k_full must be [B, H_kv, S_full, D]");
+  const int64_t Sf = k_full->shape[2];
+  if (!same_dims(v_full, 4, {B, Hkv, Sf, D})) return fail(RTK_ERR_INVALID, "v_full must be [B, H_kv, S_full, D]");
+  if (mask_full != nullptr && !same_dims(mask_full, 2, {B, Sf})) return fail(RTK_ERR_INVALID, "mask_full must be [B, S_full]");
+  if (!same_dims(k8, 4, {B, Hkv, -1, DK}) || k8->dtype != RTK_U8)
+    return fail(RTK_ERR_INVALID, "k_sparse_fp8 must be a uint8 (e4m3) [B, H_kv, S_sparse, D_keep]");
+  const int64_t Sv = k8->shape[2];
+  if (!same_dims(v8, 4, {B, Hkv, Sv, D}) || v8->dtype != RTK_U8)
+    return fail(RTK_ERR_INVALID, "v_sparse_fp8 must be a uint8 (e4m3) [B, H_kv, S_sparse, D]");
+  if (!same_dims(k_scale, 3, {B, Hkv, DK}) || k_scale->dtype != RTK_F32 || k_scale->stride[2] != 1)
+    return fail(RTK_ERR_INVALID, "k_scale must be a float32 [B, H_kv, D_keep] with unit channel stride");
+  if (!same_dims(v_scale, 3, {B, Hkv, Sv}) || v_scale->dtype != RTK_F32)
+    return fail(RTK_ERR_INVALID, "v_scale must be a float32 [B, H_kv, S_sparse]");
+  for (const rtk_tensor *t : {R_partial, k_full, v_full, out})
+    if (t->dtype != q_full->dtype) return fail(RTK_ERR_INVALID, "q, R, k_full, v_full and out must share a dtype");
+  if (delta_mu != nullptr && delta_mu->dtype != q_full->dtype)
+    return fail(RTK_ERR_INVALID, "q, R, k_full, v_full and out must share a dtype");
+  int64_t os[3];
+  if (!out_view(out, B, Hq, D, os)) return fail(RTK_ERR_INVALID, "out must be [B, H_q, D] or [B, 1, H_q, D]");
+  if (B * Hq == 0 || D == 0) return RTK_OK;
+  DecodeArgs a{q_full, R_partial, delta_mu, k_full, v_full, mask_full, k8, v8, out, num_kv_groups, false,
+               k_scale, v_scale};
+  return run_decode(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int rtk_quantize_visual_fp8(const rtk_tensor *k_sparse, const rtk_tensor *v_sparse, const rtk_tensor *k8_out,
+                            const rtk_tensor *k_scale_out, const rtk_tensor *v8_out,
+                            const rtk_tensor *v_scale_out, void *stream) {
+  g_last_error.clear();
+  View4 ks, vs;
+  if (!as4(k_sparse, ks) || !as4(v_sparse, vs))
+    return fail(RTK_ERR_INVALID, "k_sparse must be [B, H_kv, S, D_keep] and v_sparse [B, H_kv, S, 128]");
+  const int64_t B = ks.n[0], H = ks.n[1], S = ks.n[2], DK = ks.n[3];
+  if (!is_half_type(k_sparse->dtype) || v_sparse->dtype != k_sparse->dtype)
+    return fail(RTK_ERR_UNSUPPORTED, "fp8 quantisation takes bfloat16 or float16 Keys and Values");
+  if (vs.n[0] != B || vs.n[1] != H || vs.n[2] != S || vs.n[3] != 128)
+    return fail(RTK_ERR_INVALID, "v_sparse must be [B, H_kv, S, 128]");
+  if (DK != 16 && DK != 32 && DK != 64) return fail(RTK_ERR_UNSUPPORTED, "D_keep must be 16, 32 or 64");
+  auto contiguous = [](const rtk_tensor *t, std::initializer_list<int64_t> dims) {
+    if (t == nullptr || t->ndim != (int)dims.size()) return false;
+    int64_t st = 1;
+    int i = (int)dims.size() - 1;
+    for (auto it = dims.end(); it != dims.begin(); --i) {
+      --it;
+      if (t->shape[i] != *it || (t->stride[i] != st && t->shape[i] != 1)) return false;
+      st *= *it;
+    }
+    return true;
+  };
+  if (!contiguous(k8_out, {B, H, S, DK}) || k8_out->dtype != RTK_U8)
+    return fail(RTK_ERR_INVALID, "k8_out must be a contiguous uint8 [B, H_kv, S, D_keep]");
+  if (!contiguous(v8_out, {B, H, S, 128}) || v8_out->dtype != RTK_U8)
+    return fail(RTK_ERR_INVALID, "v8_out must be a contiguous uint8 [B, H_kv, S, 128]");
+  if (!contiguous(k_scale_out, {B, H, DK}) || k_scale_out->dtype != RTK_F32)
+    return fail(RTK_ERR_INVALID, "k_scale_out must be a contiguous float32 [B, H_kv, D_keep]");
+  if (!contiguous(v_scale_out, {B, H, S}) || v_scale_out->dtype != RTK_F32)
+    return fail(RTK_ERR_INVALID, "v_scale_out must be a contiguous float32 [B, H_kv, S]");
+  const bool aligned = ks.s[3] == 1 && vs.s[3] == 1 && reinterpret_cast<uintptr_t>(ks.data) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(vs.data) % 16 == 0 && (ks.s[2] * 2) % 16 == 0 &&
+                       (ks.s[1] * 2) % 16 == 0 && (ks.s[0] * 2) % 16 == 0 && (vs.s[2] * 2) % 16 == 0 &&
+                       (vs.s[1] * 2) % 16 == 0 && (vs.s[0] * 2) % 16 == 0;
+  if (!aligned) return fail(RTK_ERR_UNSUPPORTED, "fp8 quantisation needs channel-contiguous, 16-byte aligned rows");
+  if (B * H == 0) return RTK_OK;
+  if (B * H * S >= (1ll << 31) / 128) return fail(RTK_ERR_UNSUPPORTED, "tensor too large");
+  rtk::QuantParams qp;
+  std::memset(&qp, 0, sizeof(qp));
+  qp.batch = (int)B; qp.heads = (int)H; qp.seq = (int)S; qp.keep = (int)DK;
+  qp.keys = ks.data; qp.values = vs.data;
+  for (int i = 0; i < 4; ++i) { qp.k_s[i] = ks.s[i]; qp.v_s[i] = vs.s[i]; }
+  qp.keys8 = static_cast<uint8_t *>(k8_out->data);
+  qp.k_scale = static_cast<float *>(k_scale_out->data);
+  qp.values8 = static_cast<uint8_t *>(v8_out->data);
+  qp.v_scale = static_cast<float *>(v_scale_out->data);
+  const cudaError_t e = rtk::launch_quantize_fp8(k_sparse->dtype == RTK_BF16, qp, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fp8 quantisation launch");
+  return RTK_OK;
 }
 
 int rtk_full_channel_decode(const rtk_tensor *q, const rtk_tensor *k, const rtk_tensor *v,

@@ -36,6 +36,32 @@ cudaError_t launch_decode_tc(int dtype_is_bf16, const DecodeTensorMaps &maps,
                              const DecodeParams &p, int heads_tile, int dk, int grid,
                              cudaStream_t stream);
 
+// fp8 visual span (decode_tc.cu with the fp8 flag): K~8 [B, H_kv, S_v, D_keep]
+// and V8 [B, H_kv, S_v, 128] e4m3, dequantised as k_scale[b, h, c] * K~8 and
+// v_scale[b, h, t] * V8 (quant_fp8.cu).
+struct DecodeFp8 {
+  const float *k_scale; long long ksc_sb, ksc_sh;               // [B, H_kv, D_keep]
+  const float *v_scale; long long vsc_sb, vsc_sh, vsc_ss;       // [B, H_kv, S_v]
+};
+
+// heads_tile 8 or 16, dk 16 / 32 / 64; maps.ks / maps.vs are uint8 maps.
+cudaError_t launch_decode_tc_fp8(int dtype_is_bf16, const DecodeTensorMaps &maps,
+                                 const DecodeParams &p, const DecodeFp8 &f, int heads_tile, int dk,
+                                 int grid, cudaStream_t stream);
+
+// Quantisation of a visual span to the layout above (quant_fp8.cu).
+struct QuantParams {
+  int batch, heads, seq, keep;
+  const void *keys; long long k_s[4];        // [B, H, S, keep], 16-bit, channel stride 1
+  const void *values; long long v_s[4];      // [B, H, S, 128], 16-bit, channel stride 1
+  uint8_t *keys8;                            // [B, H, S, keep] contiguous
+  float *k_scale;                            // [B, H, keep]
+  uint8_t *values8;                          // [B, H, S, 128] contiguous
+  float *v_scale;                            // [B, H, S]
+};
+
+cudaError_t launch_quantize_fp8(int dtype_is_bf16, const QuantParams &p, cudaStream_t stream);
+
 // Generic path (decode_simt.cu): any dtype, any strides, head_dim <= 256.
 struct SimtParams {
   int dtype;                              // rtk_dtype of q / K / V / out

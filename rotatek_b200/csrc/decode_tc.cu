@@ -35,6 +35,9 @@
 //             and takes a ticket; the warp that completes the unit's count
 //             merges all of the unit's partials in slot order (deterministic)
 //             and writes the output.  No warp waits on another warp's merge.
+#include <cstring>
+#include <type_traits>
+
 #include "common.cuh"
 #include "decode.h"
 
@@ -64,7 +67,8 @@ struct Cfg {
   static constexpr int kHdrDm = kHdrR + kHeadDim * DK * 2;
   static constexpr int kHdrMask = kHdrDm + kHeadDim * 2;
   static constexpr int kHdrMaskBytes = 1024;  // prompt/text masks up to this length live here
-  static constexpr int kHdrBytes = (kHdrMask + kHdrMaskBytes + 127) / 128 * 128;
+  static constexpr int kHdrKsc = kHdrMask + kHdrMaskBytes;   // fp8 visual span: Key scales, fp32 [DK]
+  static constexpr int kHdrBytes = (kHdrKsc + DK * 4 + 127) / 128 * 128;
   static constexpr int kHdrBufs = DK == 64 ? 1 : 2;
   static constexpr int kMaxStages = 16;
   // barriers: full[16], empty[16], hdr_full[2], hdr_empty[2]; then flags
@@ -88,11 +92,14 @@ __device__ __forceinline__ long long cta_of_block(long long blk, long long total
 // Online softmax over MT 16-token tiles of scores already in log2 units,
 // then O^T += V^T . P^T with P split hi + lo.  `valid[mt][r]` masks row g8 + 8r
 // of tile mt.  V tile: rows = tokens, two 64-d boxes `vbox` bytes apart.
+// With `vscale` the probabilities of row g8 + 8r of tile mt are multiplied by
+// vscale[mt][r] after the normaliser has taken them (per-token Value scales of
+// an fp8 visual span: sum_t p_t (s_t v8_t)).
 template <typename T, int NT, int MT>
 __device__ __forceinline__ void softmax_pv(float (&s)[MT][NT][4], const bool (&valid)[MT][2],
                                            float (&m_run)[NT][2], float (&l_run)[NT][2],
                                            float (&o)[8][NT][4], uint32_t vbase, uint32_t vbox,
-                                           int lane) {
+                                           int lane, const float (*vscale)[2] = nullptr) {
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
@@ -141,12 +148,18 @@ __device__ __forceinline__ void softmax_pv(float (&s)[MT][NT][4], const bool (&v
   for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const float p0 = fast_exp2(s[mt][nt][0] - m_run[nt][0]);
-      const float p1 = fast_exp2(s[mt][nt][1] - m_run[nt][1]);
-      const float p2 = fast_exp2(s[mt][nt][2] - m_run[nt][0]);
-      const float p3 = fast_exp2(s[mt][nt][3] - m_run[nt][1]);
+      float p0 = fast_exp2(s[mt][nt][0] - m_run[nt][0]);
+      float p1 = fast_exp2(s[mt][nt][1] - m_run[nt][1]);
+      float p2 = fast_exp2(s[mt][nt][2] - m_run[nt][0]);
+      float p3 = fast_exp2(s[mt][nt][3] - m_run[nt][1]);
       l_run[nt][0] += p0 + p2;
       l_run[nt][1] += p1 + p3;
+      if (vscale != nullptr) {
+        p0 *= vscale[mt][0];
+        p1 *= vscale[mt][0];
+        p2 *= vscale[mt][1];
+        p3 *= vscale[mt][1];
+      }
       float r0, r1, r2, r3;
       const uint32_t h01 = pack2<T>(p0, p1), h23 = pack2<T>(p2, p3);
       unpack2<T>(h01, r0, r1);
@@ -183,7 +196,8 @@ __device__ __forceinline__ void softmax_pv(float (&s)[MT][NT][4], const bool (&v
 // wait); the rest is staged through registers with every load issued first.
 template <typename T, int NT, int DK>
 __device__ __forceinline__ void load_header(unsigned char *hdr, const DecodeParams &p, int b,
-                                            int kvh, int head0, int nheads, int lane) {
+                                            int kvh, int head0, int nheads, int lane,
+                                            const float *ksc = nullptr) {
   using C = Cfg<NT, DK>;
   constexpr int kHeads = C::kHeads;
   constexpr int kRowChunks = kHeadDim / 8;  // 16-byte chunks of a 128-wide row
@@ -230,6 +244,10 @@ __device__ __forceinline__ void load_header(unsigned char *hdr, const DecodePara
                               : from_f32<T>(0.f);
 #pragma unroll
     for (int k = 0; k < kHeadDim / 32; ++k) hd[lane + 32 * k] = dv[k];
+  }
+  if (ksc != nullptr) {   // fp8 visual span: this unit's Key scales
+    float *hk = reinterpret_cast<float *>(hdr + C::kHdrKsc);
+    for (int c = lane; c < DK; c += 32) hk[c] = ksc[c];
   }
   if (p.mask != nullptr && p.seq_full <= C::kHdrMaskBytes) {
     const uint8_t *mrow = p.mask + (long long)b * p.mask_sb;
@@ -334,12 +352,83 @@ __device__ __forceinline__ void merge_unit(const DecodeParams &p, int unit, int 
   }
 }
 
-template <typename T, int NT, int DK>
+// 16 e4m3 -> 16 f16 (exact), low bytes first
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(static_cast<uint16_t>(two)));
+  return r;
+}
+__device__ __forceinline__ void e4m3x16_to_f16(const uint4 &in, uint4 &lo, uint4 &hi) {
+  lo = make_uint4(e4m3x2_to_f16x2(in.x), e4m3x2_to_f16x2(in.x >> 16), e4m3x2_to_f16x2(in.y),
+                  e4m3x2_to_f16x2(in.y >> 16));
+  hi = make_uint4(e4m3x2_to_f16x2(in.z), e4m3x2_to_f16x2(in.z >> 16), e4m3x2_to_f16x2(in.w),
+                  e4m3x2_to_f16x2(in.w >> 16));
+}
+// byte offset of 16-byte chunk c of row t in a TMA box of DK-byte rows
+template <int DK>
+__device__ __forceinline__ uint32_t k8_offset(int t, int c) {
+  if constexpr (DK == 16) return static_cast<uint32_t>(t) * 16;
+  else return swizzled_offset<DK>(t, c * 8);
+}
+
+// fp8 visual block: the stage holds K~8 (64 x DK bytes, at kKsBytes / 2) and
+// V8 (64 x 128 bytes, in the place of the second 16-bit V box); rewrite them in
+// place as the f16 tiles the 16-bit path reads (K~ rows of 2 DK bytes from 0,
+// V in two 64-channel boxes from kKsBytes).  32 rows per pass, one row per
+// lane; every lane reads the source bytes its pass overwrites before any lane
+// writes (K~ rows 32..63 land on K~8), and V box 1's row t is V8's row t.
+template <int DK>
+__device__ __forceinline__ void convert_fp8_stage(unsigned char *st, int lane) {
+  constexpr int kKs = kVisTokens * DK * 2;
+  unsigned char *k16 = st;
+  const unsigned char *k8 = st + kKs / 2;
+  unsigned char *v16 = st + kKs;
+  unsigned char *v8 = st + kKs + kVisBoxBytes;
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+    const int t = pass * 32 + lane;
+    uint4 kr[DK / 16], vr[4];
+#pragma unroll
+    for (int c = 0; c < DK / 16; ++c) kr[c] = *reinterpret_cast<const uint4 *>(k8 + k8_offset<DK>(t, c));
+#pragma unroll
+    for (int c = 0; c < 4; ++c) vr[c] = *reinterpret_cast<const uint4 *>(v8 + swizzled_offset<128>(t, c * 8));
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < DK / 16; ++c) {
+      uint4 lo, hi;
+      e4m3x16_to_f16(kr[c], lo, hi);
+      *reinterpret_cast<uint4 *>(k16 + swizzled_offset<DK * 2>(t, 16 * c)) = lo;
+      *reinterpret_cast<uint4 *>(k16 + swizzled_offset<DK * 2>(t, 16 * c + 8)) = hi;
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {     // channels 0-63 -> box 0
+      uint4 lo, hi;
+      e4m3x16_to_f16(vr[c], lo, hi);
+      *reinterpret_cast<uint4 *>(v16 + swizzled_offset<128>(t, 16 * c)) = lo;
+      *reinterpret_cast<uint4 *>(v16 + swizzled_offset<128>(t, 16 * c + 8)) = hi;
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) vr[c] = *reinterpret_cast<const uint4 *>(v8 + swizzled_offset<128>(t, (c + 4) * 8));
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {     // channels 64-127 -> box 1 (over V8 row t)
+      uint4 lo, hi;
+      e4m3x16_to_f16(vr[c], lo, hi);
+      *reinterpret_cast<uint4 *>(v8 + swizzled_offset<128>(t, 16 * c)) = lo;
+      *reinterpret_cast<uint4 *>(v8 + swizzled_offset<128>(t, 16 * c + 8)) = hi;
+    }
+    __syncwarp();
+  }
+}
+
+template <typename T, int NT, int DK, bool FP8>
 __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
     rotatek_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_kf,
                              const __grid_constant__ CUtensorMap tm_vf,
                              const __grid_constant__ CUtensorMap tm_ks,
-                             const __grid_constant__ CUtensorMap tm_vs, const DecodeParams p) {
+                             const __grid_constant__ CUtensorMap tm_vs, const DecodeParams p,
+                             const DecodeFp8 f8) {
+  // the visual span's MMAs run in f16 when it is stored in fp8 (e4m3 -> f16 is exact)
+  using TV = typename std::conditional<FP8, __half, T>::type;
   using C = Cfg<NT, DK>;
   constexpr int kHeads = C::kHeads;
   constexpr int kStages = C::kStages;
@@ -401,7 +490,9 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (ok)
           load_header<T, NT, DK>(smem + C::kHdrOff + buf * C::kHdrBytes, p, bk, kvh,
-                                 kvh * p.groups + hc * kHeads, min(kHeads, p.groups - hc * kHeads), lane);
+                                 kvh * p.groups + hc * kHeads, min(kHeads, p.groups - hc * kHeads), lane,
+                                 FP8 ? f8.k_scale + (long long)bk * f8.ksc_sb + (long long)kvh * f8.ksc_sh
+                                     : nullptr);
         __syncwarp();
         if (lane == 0) mbar_arrive(&hdr_full[buf]);
       }
@@ -418,10 +509,17 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
             tma_load_4d(st + 3 * kFullBoxBytes, &tm_vf, 64, tok, kvh, bk, &full_bar[stage]);
           } else {
             const int tok = (j - p.blocks_full) * kVisTokens;
-            mbar_arrive_expect_tx(&full_bar[stage], C::kKsBytes + 2 * kVisBoxBytes);
-            tma_load_4d(st, &tm_ks, 0, tok, kvh, bk, &full_bar[stage]);
-            tma_load_4d(st + C::kKsBytes, &tm_vs, 0, tok, kvh, bk, &full_bar[stage]);
-            tma_load_4d(st + C::kKsBytes + kVisBoxBytes, &tm_vs, 64, tok, kvh, bk, &full_bar[stage]);
+            if constexpr (FP8) {
+              // e4m3 tiles at the places convert_fp8_stage reads them from
+              mbar_arrive_expect_tx(&full_bar[stage], kVisTokens * DK + kVisBoxBytes);
+              tma_load_4d(st + C::kKsBytes / 2, &tm_ks, 0, tok, kvh, bk, &full_bar[stage]);
+              tma_load_4d(st + C::kKsBytes + kVisBoxBytes, &tm_vs, 0, tok, kvh, bk, &full_bar[stage]);
+            } else {
+              mbar_arrive_expect_tx(&full_bar[stage], C::kKsBytes + 2 * kVisBoxBytes);
+              tma_load_4d(st, &tm_ks, 0, tok, kvh, bk, &full_bar[stage]);
+              tma_load_4d(st + C::kKsBytes, &tm_vs, 0, tok, kvh, bk, &full_bar[stage]);
+              tma_load_4d(st + C::kKsBytes + kVisBoxBytes, &tm_vs, 64, tok, kvh, bk, &full_bar[stage]);
+            }
           }
           ++issued;
         }
@@ -508,12 +606,17 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
       for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          const float v0 = c[nt][2 * half], v1 = c[nt][2 * half + 1];
-          const uint32_t h = pack2<T>(v0, v1);
+          float v0 = c[nt][2 * half], v1 = c[nt][2 * half + 1];
+          if constexpr (FP8) {   // channel mt*16 + g8 + 8 half: fold its Key scale in
+            const float sc = reinterpret_cast<const float *>(hdr + C::kHdrKsc)[mt * 16 + (lane >> 2) + 8 * half];
+            v0 *= sc;
+            v1 *= sc;
+          }
+          const uint32_t h = pack2<TV>(v0, v1);
           float h0, h1;
-          unpack2<T>(h, h0, h1);
+          unpack2<TV>(h, h0, h1);
           qhi[mt][nt][half] = movmatrix_trans(h);
-          qlo[mt][nt][half] = movmatrix_trans(pack2<T>(v0 - h0, v1 - h1));
+          qlo[mt][nt][half] = movmatrix_trans(pack2<TV>(v0 - h0, v1 - h1));
         }
       }
     }
@@ -603,6 +706,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
         } else {
           // ---- visual block: 64 tokens, rotated-truncated Keys, (q~ . k~ + bias)
           const int tok0 = (j - p.blocks_full) * kVisTokens;
+          if constexpr (FP8) convert_fp8_stage<DK>(ring + stage * C::kStageBytes, lane);
           float s[4][NT][4];
 #pragma unroll
           for (int mt = 0; mt < 4; ++mt)
@@ -617,8 +721,8 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
                           a[1], a[2], a[3]);
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt) {
-                mma_16816<T>(s[mt][nt], a, qhi[ks][nt][0], qhi[ks][nt][1]);
-                mma_16816<T>(s[mt][nt], a, qlo[ks][nt][0], qlo[ks][nt][1]);
+                mma_16816<TV>(s[mt][nt], a, qhi[ks][nt][0], qhi[ks][nt][1]);
+                mma_16816<TV>(s[mt][nt], a, qlo[ks][nt][0], qlo[ks][nt][1]);
               }
             }
           }
@@ -635,9 +739,22 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
               s[mt][nt][3] = (s[mt][nt][3] + bias2[nt][1]) * p.scale_log2;
             }
           }
-          softmax_pv<T, NT, 4>(s, valid, m_run, l_run, o, sbase + C::kKsBytes, kVisBoxBytes, lane);
+          if constexpr (FP8) {
+            // per-token Value scales of the fp8 span fold into the probabilities
+            const float *vsc = f8.v_scale + (long long)bk * f8.vsc_sb + (long long)kvh * f8.vsc_sh;
+            float vs[4][2];
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+              for (int r = 0; r < 2; ++r)
+                vs[mt][r] = valid[mt][r] ? __ldg(vsc + (long long)(tok0 + mt * 16 + g8 + 8 * r) * f8.vsc_ss) : 0.f;
+            softmax_pv<TV, NT, 4>(s, valid, m_run, l_run, o, sbase + C::kKsBytes, kVisBoxBytes, lane, vs);
+          } else {
+            softmax_pv<T, NT, 4>(s, valid, m_run, l_run, o, sbase + C::kKsBytes, kVisBoxBytes, lane);
+          }
         }
       }
+      if constexpr (FP8) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // our writes, then TMA's
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[stage]);
     }
@@ -696,29 +813,29 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
   }
 }
 
-template <typename T, int NT, int DK>
-cudaError_t launch_tc(const DecodeTensorMaps &maps, const DecodeParams &p, int grid,
+template <typename T, int NT, int DK, bool FP8>
+cudaError_t launch_tc(const DecodeTensorMaps &maps, const DecodeParams &p, const DecodeFp8 &f8, int grid,
                       cudaStream_t stream) {
   using C = Cfg<NT, DK>;
   const int smem = C::kBytes + 1024;
-  auto kern = rotatek_decode_tc_kernel<T, NT, DK>;
+  auto kern = rotatek_decode_tc_kernel<T, NT, DK, FP8>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (err != cudaSuccess) return err;
-  kern<<<grid, C::kThreads, smem, stream>>>(maps.kf, maps.vf, maps.ks, maps.vs, p);
+  kern<<<grid, C::kThreads, smem, stream>>>(maps.kf, maps.vf, maps.ks, maps.vs, p, f8);
   return cudaGetLastError();
 }
 
-template <typename T>
-cudaError_t dispatch_nt_dk(const DecodeTensorMaps &maps, const DecodeParams &p, int nt, int dk,
-                           int grid, cudaStream_t stream) {
+template <typename T, bool FP8>
+cudaError_t dispatch_nt_dk(const DecodeTensorMaps &maps, const DecodeParams &p, const DecodeFp8 &f8, int nt,
+                           int dk, int grid, cudaStream_t stream) {
   if (nt == 1) {
-    if (dk == 16) return launch_tc<T, 1, 16>(maps, p, grid, stream);
-    if (dk == 32) return launch_tc<T, 1, 32>(maps, p, grid, stream);
-    if (dk == 64) return launch_tc<T, 1, 64>(maps, p, grid, stream);
+    if (dk == 16) return launch_tc<T, 1, 16, FP8>(maps, p, f8, grid, stream);
+    if (dk == 32) return launch_tc<T, 1, 32, FP8>(maps, p, f8, grid, stream);
+    if (dk == 64) return launch_tc<T, 1, 64, FP8>(maps, p, f8, grid, stream);
   } else {
-    if (dk == 16) return launch_tc<T, 2, 16>(maps, p, grid, stream);
-    if (dk == 32) return launch_tc<T, 2, 32>(maps, p, grid, stream);
-    if (dk == 64) return launch_tc<T, 2, 64>(maps, p, grid, stream);
+    if (dk == 16) return launch_tc<T, 2, 16, FP8>(maps, p, f8, grid, stream);
+    if (dk == 32) return launch_tc<T, 2, 32, FP8>(maps, p, f8, grid, stream);
+    if (dk == 64) return launch_tc<T, 2, 64, FP8>(maps, p, f8, grid, stream);
   }
   return cudaErrorInvalidValue;
 }
@@ -728,8 +845,17 @@ cudaError_t dispatch_nt_dk(const DecodeTensorMaps &maps, const DecodeParams &p, 
 cudaError_t launch_decode_tc(int dtype_is_bf16, const DecodeTensorMaps &maps, const DecodeParams &p,
                              int heads_tile, int dk, int grid, cudaStream_t stream) {
   const int nt = heads_tile / 8;
-  if (dtype_is_bf16) return dispatch_nt_dk<__nv_bfloat16>(maps, p, nt, dk, grid, stream);
-  return dispatch_nt_dk<__half>(maps, p, nt, dk, grid, stream);
+  DecodeFp8 none;
+  std::memset(&none, 0, sizeof(none));
+  if (dtype_is_bf16) return dispatch_nt_dk<__nv_bfloat16, false>(maps, p, none, nt, dk, grid, stream);
+  return dispatch_nt_dk<__half, false>(maps, p, none, nt, dk, grid, stream);
+}
+
+cudaError_t launch_decode_tc_fp8(int dtype_is_bf16, const DecodeTensorMaps &maps, const DecodeParams &p,
+                                 const DecodeFp8 &f, int heads_tile, int dk, int grid, cudaStream_t stream) {
+  const int nt = heads_tile / 8;
+  if (dtype_is_bf16) return dispatch_nt_dk<__nv_bfloat16, true>(maps, p, f, nt, dk, grid, stream);
+  return dispatch_nt_dk<__half, true>(maps, p, f, nt, dk, grid, stream);
 }
 
 }  // namespace rtk

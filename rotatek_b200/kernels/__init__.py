@@ -87,6 +87,65 @@ def rotatek_decode(
     return out, None, None
 
 
+def _as_u8(t: torch.Tensor) -> torch.Tensor:
+    return t.view(torch.uint8) if t.dtype == torch.float8_e4m3fn else t
+
+
+def quantize_visual_fp8(k_sparse: torch.Tensor, v_sparse: torch.Tensor):
+    """fp8 (e4m3) copy of a visual span for ``rotatek_decode_fp8``.
+
+    k_sparse [B, H_kv, S_v, D_keep] (D_keep 16 / 32 / 64) and v_sparse
+    [B, H_kv, S_v, 128], bf16 or fp16.  Returns (k8, k_scale, v8, v_scale):
+    e4m3 bytes as uint8 [B, H_kv, S_v, D_keep] / [B, H_kv, S_v, 128] and fp32
+    scales [B, H_kv, D_keep] (per rotated channel) / [B, H_kv, S_v] (per
+    token), with x ~= scale * e4m3(x8), scale = amax / 448."""
+    if k_sparse.dim() != 4 or v_sparse.dim() != 4:
+        raise ValueError("k_sparse must be [B, H_kv, S, D_keep] and v_sparse [B, H_kv, S, 128]")
+    _lib.require_cuda(k_sparse, v_sparse)
+    b, h, s, dk = k_sparse.shape
+    dev = k_sparse.device
+    k8 = torch.empty(b, h, s, dk, dtype=torch.uint8, device=dev)
+    v8 = torch.empty(b, h, s, v_sparse.shape[-1], dtype=torch.uint8, device=dev)
+    ksc = torch.empty(b, h, dk, dtype=torch.float32, device=dev)
+    vsc = torch.empty(b, h, s, dtype=torch.float32, device=dev)
+    D = _lib.describe
+    _lib.check(_lib.load().rtk_quantize_visual_fp8(D(k_sparse), D(v_sparse), D(k8), D(ksc), D(v8), D(vsc),
+                                                     _stream(dev)))
+    return k8, ksc, v8, vsc
+
+
+def rotatek_decode_fp8(q_full, R_partial, delta_mu, k_full, v_full, mask_full, k8, k_scale, v8, v_scale,
+                       num_kv_groups: int):
+    """``rotatek_decode`` with the visual span in fp8: the visual Keys are
+    k_scale[c] * e4m3(k8) and the visual Values v_scale[t] * e4m3(v8) (from
+    ``quantize_visual_fp8``; uint8 or float8_e4m3fn tensors); the prompt/text span
+    and the output stay in q's dtype.  Returns (out [B, 1, H_q, D], None, None)."""
+    if q_full.dim() != 3:
+        raise ValueError("q_full must be [B, H_q, D]")
+    if R_partial.dim() != 4:
+        raise ValueError("R_partial must be [B, H_kv, D, D_keep]")
+    k8, v8 = _as_u8(k8), _as_u8(v8)
+    _lib.require_cuda(q_full, R_partial, delta_mu, k_full, v_full, mask_full, k8, k_scale, v8, v_scale)
+    bsz, heads, head_dim = q_full.shape
+    h_kv = R_partial.shape[1]
+    lib = _lib.load()
+    dev = q_full.device
+    key = ("rk", _dtype_code(q_full), bsz, heads, h_kv, head_dim, R_partial.shape[-1],
+           k_full.shape[-2], k8.shape[-2], dev.index)
+    need = _ws_size_cache.get(key)
+    if need is None:
+        need = (lib.rtk_rotatek_decode_workspace_size(*key[1:-1], dev.index),
+                lib.rtk_decode_workspace_counter_bytes(bsz, heads))
+        _ws_size_cache[key] = need
+    ws = _lib.workspace(dev, *need)
+    out = torch.empty((bsz, 1, heads, head_dim), dtype=q_full.dtype, device=dev)
+    D = _lib.describe
+    _lib.check(lib.rtk_rotatek_decode_fp8(
+        D(q_full), D(R_partial), D(delta_mu), D(k_full), D(v_full), D(mask_full), D(k8), D(k_scale), D(v8),
+        D(v_scale), num_kv_groups, D(out), ctypes.c_void_p(ws.data_ptr()), ws.numel(), _stream(dev)))
+    return out, None, None
+
+
 def full_channel_decode(
     q: torch.Tensor,                   # [B, H_q, D]
     k: torch.Tensor,                   # [B, H_kv, S, D]
@@ -162,4 +221,5 @@ def think_decode(
     return out
 
 
-__all__ = ["ROTATEK_KERNEL", "rotatek_decode", "full_channel_decode", "think_decode", "think_selection"]
+__all__ = ["ROTATEK_KERNEL", "rotatek_decode", "full_channel_decode", "think_decode", "think_selection",
+           "quantize_visual_fp8", "rotatek_decode_fp8"]
