@@ -725,6 +725,61 @@ def run_think(args):
     return 0
 
 
+# ---------------------------------------------------------------- fp8 visual span (config 2 shape)
+FP8_METRIC = "fp8 visual-span decode us/step & HBM GB/s %peak, config 2 shape (bs32 16k ctx, 25% K channels kept)"
+
+
+def run_decode_fp8(args):
+    """The config-2 decode step with the visual span stored in e4m3
+    (``quantize_visual_fp8`` once after prefill, then ``rotatek_decode_fp8``);
+    the 16-bit decode of the same inputs timed beside it."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    from rotatek_b200.kernels import quantize_visual_fp8, rotatek_decode, rotatek_decode_fp8
+    d = make_inputs(dev, seed=0, batch=args.batch)
+    k8, ksc, v8, vsc = quantize_visual_fp8(d.k_sparse, d.v_sparse)
+    fp8_args = (d.q_full, d.R_partial, d.delta_mu, d.k_full, d.v_full, d.mask_full, k8, ksc, v8, vsc,
+                d.num_kv_groups)
+
+    def timed(fn, n):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / n
+
+    sampler = ClockSampler(0)
+    with sampler:
+        ours = timed(lambda: rotatek_decode_fp8(*fp8_args), args.steps)
+    bf16 = timed(lambda: rotatek_decode(**d.as_kwargs()), max(10, args.steps // 4))
+    out8, _, _ = rotatek_decode_fp8(*fp8_args)
+    ref, _, _ = rotatek_decode(**d.as_kwargs())
+    rel = float((out8.float() - ref.float()).norm() / ref.float().norm())
+    e = lambda t: t.numel() * t.element_size()  # noqa: E731
+    nbytes = (e(k8) + e(ksc) + e(v8) + e(vsc) + e(d.k_full) + e(d.v_full) + e(d.R_partial) + e(d.delta_mu)
+              + 2 * e(d.q_full))
+    peak, peak_kind = load_peak_hbm()
+    if args.kernel_only:
+        return 0
+    print(json.dumps({"metric": FP8_METRIC, "value": ours, "unit": "us/step", "n_gpus": 1, "steps": args.steps,
+                      "warmup": max(args.warmup, 3), "higher_is_better": False,
+                      "dtype": "e4m3 visual span (K~ per-channel, V per-token scales), bf16 prompt/text",
+                      "data": DATA, "config": {"workload": WORKLOAD + "; visual K~ and V stored in e4m3",
+                                               "l2": f"{nbytes / 1e6:.0f} MB per step > 126 MB L2; no flush"},
+                      "bf16_decode_us": bf16, "speedup_vs_bf16_decode": bf16 / ours,
+                      "rel_error_vs_bf16_decode": rel,
+                      "roofline": {"bound": "hbm", "achieved": nbytes / ours / 1e3, "peak": peak, "unit": "GB/s",
+                                   "frac": nbytes / ours / 1e3 / peak, "peak_source": peak_kind,
+                                   "algorithmic_bytes_per_launch": nbytes},
+                      "gpu_launches": args.steps, "clocks": sampler.summary()}), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------- fused Key projection (config 4 layer)
 KPROJ_METRIC = ("config4 layer prefill Key path + rotation build us/layer (Qwen2.5-VL-7B shape: B=8, "
                 "S=64+15360+576, hidden 3584, 4 KV heads, bf16)")
@@ -1035,12 +1090,14 @@ def main():
                     help="override the batch (profiling cases only; the bench line uses 32)")
     ap.add_argument("--kernel-only", action="store_true",
                     help="decode launches only: no e2e, no CPU baseline, no JSON bench line")
-    ap.add_argument("--workload", choices=["decode", "build", "decode72b", "decode_step", "e2e", "think", "kproj"],
+    ap.add_argument("--workload", choices=["decode", "build", "decode72b", "decode_step", "e2e", "think", "kproj",
+                                           "decode_fp8"],
                     default="decode",
                     help="decode: benchmark config 2 (the headline); build: config 4 rotation build; "
                          "decode72b: config 5 multi-GPU decode; decode_step: config 2 with cache appends; "
                          "e2e: config 3 LLaVA-NeXT-7B-shaped end-to-end decode; think: ThinK at config 2; "
-                         "kproj: one config-4 layer from hidden states (fused Key projection + build)")
+                         "kproj: one config-4 layer from hidden states (fused Key projection + build); "
+                         "decode_fp8: config 2 with the visual span in e4m3")
     ap.add_argument("--shard", choices=["auto", "heads", "batch"], default="auto",
                     help="decode72b: KV-head or batch sharding (auto: heads when N = 8)")
     ap.add_argument("--pool", type=int, default=4, help="decode72b: resident layers cycled over the 80")
@@ -1052,13 +1109,20 @@ def main():
     args = ap.parse_args()
     if args.steps is None:
         args.steps = {"build": 20, "decode72b": 10, "decode_step": 200, "think": 200,
-                      "kproj": 20}.get(args.workload, 2000)
+                      "kproj": 20, "decode_fp8": 1000}.get(args.workload, 2000)
     if args.workload == "decode_step":
         return run_decode_step(args)
     if args.workload == "e2e":
         return run_e2e(args)
     if args.workload == "think":
         return run_think(args)
+    if args.workload == "decode_fp8":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "metric": FP8_METRIC,
+                              "unavailable": "fp8 storage is this build's extension; the reference keeps the "
+                                             "visual span in the model dtype"}), flush=True)
+            return 0
+        return run_decode_fp8(args)
     if args.workload == "kproj":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "metric": KPROJ_METRIC,

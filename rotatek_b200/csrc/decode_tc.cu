@@ -94,8 +94,9 @@ __device__ __forceinline__ long long cta_of_block(long long blk, long long total
 // of tile mt.  V tile: rows = tokens, two 64-d boxes `vbox` bytes apart.
 // With `vscale` the probabilities of row g8 + 8r of tile mt are multiplied by
 // vscale[mt][r] after the normaliser has taken them (per-token Value scales of
-// an fp8 visual span: sum_t p_t (s_t v8_t)).
-template <typename T, int NT, int MT>
+// an fp8 visual span: sum_t p_t (s_t v8_t)).  PLO = false drops the low half of
+// P's split (11 bits of P are plenty against e4m3 Values' 4).
+template <typename T, int NT, int MT, bool PLO = true>
 __device__ __forceinline__ void softmax_pv(float (&s)[MT][NT][4], const bool (&valid)[MT][2],
                                            float (&m_run)[NT][2], float (&l_run)[NT][2],
                                            float (&o)[8][NT][4], uint32_t vbase, uint32_t vbox,
@@ -166,8 +167,10 @@ __device__ __forceinline__ void softmax_pv(float (&s)[MT][NT][4], const bool (&v
       unpack2<T>(h23, r2, r3);
       pb[mt][nt][0] = movmatrix_trans(h01);
       pb[mt][nt][1] = movmatrix_trans(h23);
-      pl[mt][nt][0] = movmatrix_trans(pack2<T>(p0 - r0, p1 - r1));
-      pl[mt][nt][1] = movmatrix_trans(pack2<T>(p2 - r2, p3 - r3));
+      if constexpr (PLO) {
+        pl[mt][nt][0] = movmatrix_trans(pack2<T>(p0 - r0, p1 - r1));
+        pl[mt][nt][1] = movmatrix_trans(pack2<T>(p2 - r2, p3 - r3));
+      }
     }
   }
   // O^T[d, head] += V^T[d, tok] . P^T[tok, head]   (ldmatrix.trans of V rows)
@@ -184,7 +187,7 @@ __device__ __forceinline__ void softmax_pv(float (&s)[MT][NT][4], const bool (&v
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         mma_16816<T>(o[d][nt], a, pb[kk][nt][0], pb[kk][nt][1]);
-        mma_16816<T>(o[d][nt], a, pl[kk][nt][0], pl[kk][nt][1]);
+        if constexpr (PLO) mma_16816<T>(o[d][nt], a, pl[kk][nt][0], pl[kk][nt][1]);
       }
     }
   }
@@ -659,8 +662,24 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
     const int first = it + ((cw - it) % kWarps + kWarps) % kWarps;
     for (int i = first; i < seg_end; i += kWarps) {
       const int stage = i % kStages;
-      const bool ready = mbar_wait_bounded(&full_bar[stage], (i / kStages) & 1, abort_flag, p.status);
       const int j = j0 + (i - it);
+      // fp8 span: this block's per-token Value scales, requested before the
+      // stage wait so that their L2 latency hides behind it and the conversion
+      float vs[4][2];
+      if constexpr (FP8) {
+        if (j >= p.blocks_full) {
+          const float *vsc = f8.v_scale + (long long)bk * f8.vsc_sb + (long long)kvh * f8.vsc_sh;
+          const int tv = (j - p.blocks_full) * kVisTokens + g8;
+#pragma unroll
+          for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+              const int tok = tv + mt * 16 + 8 * r;
+              vs[mt][r] = tok < p.seq_sparse ? __ldg(vsc + (long long)tok * f8.vsc_ss) : 0.f;
+            }
+        }
+      }
+      const bool ready = mbar_wait_bounded(&full_bar[stage], (i / kStages) & 1, abort_flag, p.status);
       const uint32_t sbase = smem_u32(ring + stage * C::kStageBytes);
       if (ready) {
         if (j < p.blocks_full) {
@@ -741,14 +760,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
           }
           if constexpr (FP8) {
             // per-token Value scales of the fp8 span fold into the probabilities
-            const float *vsc = f8.v_scale + (long long)bk * f8.vsc_sb + (long long)kvh * f8.vsc_sh;
-            float vs[4][2];
-#pragma unroll
-            for (int mt = 0; mt < 4; ++mt)
-#pragma unroll
-              for (int r = 0; r < 2; ++r)
-                vs[mt][r] = valid[mt][r] ? __ldg(vsc + (long long)(tok0 + mt * 16 + g8 + 8 * r) * f8.vsc_ss) : 0.f;
-            softmax_pv<TV, NT, 4>(s, valid, m_run, l_run, o, sbase + C::kKsBytes, kVisBoxBytes, lane, vs);
+            softmax_pv<TV, NT, 4, false>(s, valid, m_run, l_run, o, sbase + C::kKsBytes, kVisBoxBytes, lane, vs);
           } else {
             softmax_pv<T, NT, 4>(s, valid, m_run, l_run, o, sbase + C::kKsBytes, kVisBoxBytes, lane);
           }

@@ -3,8 +3,9 @@ decode against the float64 decode of the dequantised span.
 
 Tolerances (written out per dtype, as for the 16-bit decode): bf16 2e-3
 absolute + 2^-8 relative, fp16 1e-3 + 2^-10.  The fp8 path multiplies e4m3
-values (exact in f16) with the rotated query split into f16 hi + lo, so it is
-held to the same bar as the 16-bit path on the values it reads.  How far the
+values (exact in f16) with the rotated query split into f16 hi + lo and with
+the softmax weights rounded to f16 (11 bits; the Values they weight carry 4),
+so it is held to the same bar as the 16-bit path on the values it reads.  How far the
 quantisation itself moves the output from the 16-bit decode is measured, not
 gated tightly (the synthetic inputs say little about real attention).
 """
