@@ -780,6 +780,83 @@ def run_decode_fp8(args):
     return 0
 
 
+# ---------------------------------------------------------------- SparK baseline at config 2
+SPARK_METRIC = "SparK decode step us/step, config 2 shape (bs32 16k ctx, 32 of 128 K channels kept per token)"
+
+
+def run_spark(args):
+    """SparK's decode at the config-2 shape: ``spark_decode`` (kept values,
+    kept-channel indices and the pruned mean; Keys rebuilt block by block in
+    shared memory) against the adapters' path on the same GPU -- recovery of the
+    full-width visual Keys, concatenation and the dense decode
+    (llama_visionzip.py:226-242) -- and against the dense decode alone over Keys
+    recovered beforehand."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    from rotatek_b200 import synthetic as syn
+    from rotatek_b200.kernels import full_channel_decode, pack_spark_indices, spark_decode
+    b, hkv, G, sp, sv, st = CFG["batch"], CFG["kv_heads"], CFG["q_heads"] // CFG["kv_heads"], CFG["prompt"], \
+        CFG["vision"], CFG["text"]
+    if args.batch:                   # profiling cases only
+        b = args.batch
+    keep = CFG["keep"]
+    d = syn.make_spark(b, CFG["q_heads"], hkv, sv, sp + st, keep=keep, seed=0, device=dev, dtype=torch.bfloat16)
+    idx = pack_spark_indices(d.keep_mask, keep)          # once per layer, after prefill
+    k_prompt, k_text = d.k_full[:, :, :sp], d.k_full[:, :, sp:]
+    values = torch.cat([d.v_full[:, :, :sp], d.v_sparse, d.v_full[:, :, sp:]], dim=-2)
+
+    def fused():
+        spark_decode(d.q_full, d.k_full, d.v_full, None, d.k_kept, idx, d.pruned_mean, d.v_sparse, G)
+
+    def adapter():
+        rec = d.pruned_mean.expand(b, hkv, sv, 128).contiguous()
+        rec[d.keep_mask] = d.k_kept.reshape(-1)
+        keys = torch.cat([k_prompt, rec, k_text], dim=-2)
+        full_channel_decode(d.q_full, keys, values, num_kv_groups=G)
+
+    keys_rec = torch.cat([k_prompt, d.recovered(), k_text], dim=-2)
+
+    def dense_only():
+        full_channel_decode(d.q_full, keys_rec, values, num_kv_groups=G)
+
+    def timed(fn, n):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / n
+
+    sampler = ClockSampler(0)
+    with sampler:
+        ours = timed(fused, args.steps)
+    if args.kernel_only:
+        return 0
+    dense = timed(dense_only, max(10, args.steps // 4))
+    theirs = timed(adapter, max(10, args.steps // 20))
+    e = lambda t: t.numel() * t.element_size()  # noqa: E731
+    nbytes = (e(d.k_kept) + e(idx) + e(d.pruned_mean) + e(d.v_sparse) + e(d.k_full) + e(d.v_full)
+              + 2 * e(d.q_full))
+    peak, peak_kind = load_peak_hbm()
+    print(json.dumps({"metric": SPARK_METRIC, "value": ours, "unit": "us/step", "n_gpus": 1, "steps": args.steps,
+                      "warmup": max(args.warmup, 3), "higher_is_better": False, "dtype": "bf16",
+                      "data": "synthetic: seeded low-rank+noise Keys pruned per token (SparK scoring against a "
+                              "N(0,1) query window); N(0,1) Values/queries",
+                      "config": {"workload": WORKLOAD + "; SparK per-token channel pruning instead of a rotation",
+                                 "l2": f"{nbytes / 1e6:.0f} MB per step > 126 MB L2; no flush"},
+                      "adapter_path_us": theirs, "speedup_vs_adapter_path": theirs / ours,
+                      "dense_decode_of_recovered_keys_us": dense, "speedup_vs_dense_decode": dense / ours,
+                      "roofline": {"bound": "hbm", "achieved": nbytes / ours / 1e3, "peak": peak, "unit": "GB/s",
+                                   "frac": nbytes / ours / 1e3 / peak, "peak_source": peak_kind,
+                                   "algorithmic_bytes_per_launch": nbytes},
+                      "gpu_launches": args.steps, "clocks": sampler.summary()}), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------- fused Key projection (config 4 layer)
 KPROJ_METRIC = ("config4 layer prefill Key path + rotation build us/layer (Qwen2.5-VL-7B shape: B=8, "
                 "S=64+15360+576, hidden 3584, 4 KV heads, bf16)")
@@ -1091,13 +1168,13 @@ def main():
     ap.add_argument("--kernel-only", action="store_true",
                     help="decode launches only: no e2e, no CPU baseline, no JSON bench line")
     ap.add_argument("--workload", choices=["decode", "build", "decode72b", "decode_step", "e2e", "think", "kproj",
-                                           "decode_fp8"],
+                                           "decode_fp8", "spark"],
                     default="decode",
                     help="decode: benchmark config 2 (the headline); build: config 4 rotation build; "
                          "decode72b: config 5 multi-GPU decode; decode_step: config 2 with cache appends; "
                          "e2e: config 3 LLaVA-NeXT-7B-shaped end-to-end decode; think: ThinK at config 2; "
                          "kproj: one config-4 layer from hidden states (fused Key projection + build); "
-                         "decode_fp8: config 2 with the visual span in e4m3")
+                         "decode_fp8: config 2 with the visual span in e4m3; spark: SparK at config 2")
     ap.add_argument("--shard", choices=["auto", "heads", "batch"], default="auto",
                     help="decode72b: KV-head or batch sharding (auto: heads when N = 8)")
     ap.add_argument("--pool", type=int, default=4, help="decode72b: resident layers cycled over the 80")
@@ -1109,7 +1186,7 @@ def main():
     args = ap.parse_args()
     if args.steps is None:
         args.steps = {"build": 20, "decode72b": 10, "decode_step": 200, "think": 200,
-                      "kproj": 20, "decode_fp8": 1000}.get(args.workload, 2000)
+                      "kproj": 20, "decode_fp8": 1000, "spark": 1000}.get(args.workload, 2000)
     if args.workload == "decode_step":
         return run_decode_step(args)
     if args.workload == "e2e":
@@ -1123,6 +1200,14 @@ def main():
                                              "visual span in the model dtype"}), flush=True)
             return 0
         return run_decode_fp8(args)
+    if args.workload == "spark":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "metric": SPARK_METRIC,
+                              "unavailable": "measured for this build only; its line carries the adapter "
+                                             "path (recovery + concatenation + dense decode) timed beside it"}),
+                  flush=True)
+            return 0
+        return run_spark(args)
     if args.workload == "kproj":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "metric": KPROJ_METRIC,

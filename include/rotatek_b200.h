@@ -43,6 +43,7 @@ typedef enum rtk_status {
 
 /* Device-status bits a kernel may set in the workspace's status word. */
 #define RTK_DEVICE_TIMEOUT 1u /* a bounded wait gave up; outputs of that call are invalid */
+#define RTK_DEVICE_BAD_INPUT 2u /* rtk_spark_pack: a token's kept count differs from D_keep */
 
 typedef struct rtk_tensor {
   void *data;          /* device pointer; NULL only where a parameter says "nullable" */
@@ -159,6 +160,34 @@ size_t rtk_full_channel_decode_workspace_size(int32_t dtype, int64_t batch, int6
 int rtk_full_channel_decode(const rtk_tensor *q, const rtk_tensor *k, const rtk_tensor *v,
                             int64_t num_kv_groups, const rtk_tensor *out, void *workspace,
                             size_t workspace_bytes, void *stream);
+
+/* SparK baseline decode without materialising its recovered Keys.
+ * Replaces the adapters' SparK branch -- recovery
+ * (integrations/lmms_eval/models/model_utils/llava_next/llama_visionzip.py:226-230:
+ * every channel of a visual token takes its pruned-channel mean, the kept
+ * channels their values), concatenation (233-234) and full_channel_decode
+ * (237-242) -- with the arithmetic of that dense decode over
+ * [k_full ; recovered visual Keys], [v_full ; v_sparse]; mask_full (nullable)
+ * masks the prompt/text span as in rtk_rotatek_decode.
+ *   k_kept [B, H_kv, S_v, D_keep]   kept channels' values in channel order
+ *                                   (K_compact of rotatek/baselines/spark.py:15-58)
+ *   keep_idx [B, H_kv, S_v, D_keep] their channels, uint8 ascending (rtk_spark_pack)
+ *   pruned_mean [B, H_kv, S_v, 1]   per-token fill value (spark.py's pruned_mean)
+ * bf16 / fp16, head_dim 128, D_keep 16, 32 or 64; 16-byte aligned,
+ * channel-contiguous rows (else RTK_ERR_UNSUPPORTED).  Workspace: as for
+ * rtk_rotatek_decode (rtk_rotatek_decode_workspace_size with the same shapes). */
+int rtk_spark_decode(const rtk_tensor *q_full, const rtk_tensor *k_full, const rtk_tensor *v_full,
+                     const rtk_tensor *mask_full, const rtk_tensor *k_kept, const rtk_tensor *keep_idx,
+                     const rtk_tensor *pruned_mean, const rtk_tensor *v_sparse, int64_t num_kv_groups,
+                     const rtk_tensor *out, void *workspace, size_t workspace_bytes, void *stream);
+
+/* keep_idx_out [B, H_kv, S, D_keep] (uint8, contiguous) = each token's kept
+ * channels of keep_mask [B, H_kv, S, 128] (bool as uint8, unit channel stride;
+ * spark.py's keep_mask) in ascending order -- what the boolean-index
+ * assignment of llama_visionzip.py:230 walks.  Run once per layer after
+ * prefill.  A token whose kept count is not D_keep ORs RTK_DEVICE_BAD_INPUT
+ * into *status (a device uint32; nullable). */
+int rtk_spark_pack(const rtk_tensor *keep_mask, const rtk_tensor *keep_idx_out, void *status, void *stream);
 
 /* ------------------------------------------------------------------------
  * Prefill rotation builder (head_dim 128)

@@ -43,6 +43,8 @@ SIGNATURES = {
     "rtk_quantize_visual_fp8": (ctypes.c_int, [_P] * 6 + [ctypes.c_void_p]),
     "rtk_full_channel_decode_workspace_size": (ctypes.c_size_t, [ctypes.c_int32] + [ctypes.c_int64] * 5 + [ctypes.c_int32]),
     "rtk_full_channel_decode": (ctypes.c_int, [_P] * 3 + [ctypes.c_int64, _P, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "rtk_spark_decode": (ctypes.c_int, [_P] * 8 + [ctypes.c_int64, _P, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "rtk_spark_pack": (ctypes.c_int, [_P, _P, ctypes.c_void_p, ctypes.c_void_p]),
     "rtk_key_covariance": (ctypes.c_int, [_P, _P, _P, ctypes.c_void_p]),
     "rtk_rotate_keys": (ctypes.c_int, [_P, _P, _P, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "rtk_eigh_topk_workspace_size": (ctypes.c_size_t, [ctypes.c_int64]),

@@ -188,13 +188,14 @@ struct TcShape {
   int64_t slots;  // one per (unit + cta, consumer warp); <= 5 consumer warps per CTA
 };
 
-TcShape tc_shape(int64_t B, int64_t Hkv, int64_t G, int64_t Sf, int64_t Sv, int device) {
+TcShape tc_shape(int64_t B, int64_t Hkv, int64_t G, int64_t Sf, int64_t Sv, int device,
+                 int64_t vis_tokens = kVisBlockTokens) {
   TcShape t;
   t.heads_tile = G <= 8 ? 8 : 16;
   t.head_chunks = (int)cdiv(G, t.heads_tile);
   t.units = B * Hkv * t.head_chunks;
   t.blocks_full = cdiv(Sf, kFullBlockTokens);
-  t.blocks_sparse = cdiv(Sv, kVisBlockTokens);
+  t.blocks_sparse = cdiv(Sv, vis_tokens);
   t.blocks_per_unit = t.blocks_full + t.blocks_sparse;
   t.total = t.units * t.blocks_per_unit;
   t.grid = (int)std::max<int64_t>(1, std::min<int64_t>(t.total, sm_count(device)));
@@ -250,23 +251,33 @@ struct DecodeArgs {
   int64_t groups;
   bool dense;  // full_channel_decode: no visual span, no mask
   const rtk_tensor *ksc = nullptr, *vsc = nullptr;   // fp8 visual span: ks / vs are e4m3 (uint8)
+  // SparK visual span: ks = kept values [B, H_kv, S_v, D_keep], kidx = their
+  // channels (uint8), kmean = pruned-channel means [B, H_kv, S_v, 1]; R unused
+  const rtk_tensor *kidx = nullptr, *kmean = nullptr;
 };
 
 int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cudaStream_t stream) {
-  View4 kf{}, vf{}, ks{}, vs{}, R{};
+  View4 kf{}, vf{}, ks{}, vs{}, R{}, ki{}, km{};
   as4(a.kf, kf);
   as4(a.vf, vf);
   const int64_t B = a.q->shape[0], Hq = a.q->shape[1], D = a.q->shape[2];
   const int64_t Hkv = kf.n[1];
   const int64_t G = a.groups;
   const int64_t Sf = kf.n[2];
+  const bool spark = a.kidx != nullptr;
   int64_t Sv = 0, DK = 0;
   if (!a.dense) {
     as4(a.ks, ks);
     as4(a.vs, vs);
-    as4(a.R, R);
     Sv = ks.n[2];
-    DK = R.n[3];
+    if (spark) {
+      as4(a.kidx, ki);
+      as4(a.kmean, km);
+      DK = ks.n[3];
+    } else {
+      as4(a.R, R);
+      DK = R.n[3];
+    }
   }
   int64_t os[3];
   out_view(a.out, B, Hq, D, os);
@@ -285,7 +296,7 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
   const bool fp8 = a.ksc != nullptr;
   // ---------------- tensor-core path
   bool tc = is_half_type(dt) && D == 128 && (Sf + Sv) > 0 && a.q->stride[2] == 1 &&
-            os[2] == 1 && (a.dense || ((DK == 16 || DK == 32 || DK == 64) && R.s[3] == 1 &&
+            os[2] == 1 && (a.dense || ((DK == 16 || DK == 32 || DK == 64) && (spark || R.s[3] == 1) &&
                                        (a.dm == nullptr || a.dm->stride[2] == 1)));
   rtk::DecodeTensorMaps maps;
   std::memset(&maps, 0, sizeof(maps));
@@ -295,7 +306,12 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
     if (Sf > 0)
       tc = encode_map(&maps.kf, kf, et, 64, kFullBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B) &&
            encode_map(&maps.vf, vf, et, 64, kFullBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (tc && Sv > 0 && !fp8)
+    if (tc && Sv > 0 && spark)   // 32-token boxes; index rows of DK bytes
+      tc = encode_map(&maps.ks, ks, et, (int)DK, kFullBlockTokens, swizzle_for_row_bytes((int)DK * 2)) &&
+           encode_map(&maps.vs, vs, et, 64, kFullBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B) &&
+           encode_map(&maps.ki, ki, CU_TENSOR_MAP_DATA_TYPE_UINT8, (int)DK, kFullBlockTokens,
+                      DK == 16 ? CU_TENSOR_MAP_SWIZZLE_NONE : swizzle_for_row_bytes((int)DK), 1);
+    if (tc && Sv > 0 && !fp8 && !spark)
       tc = encode_map(&maps.ks, ks, et, (int)DK, kVisBlockTokens, swizzle_for_row_bytes((int)DK * 2)) &&
            encode_map(&maps.vs, vs, et, 64, kVisBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B);
     if (tc && Sv > 0 && fp8)   // e4m3 rows of DK and 128 bytes
@@ -307,8 +323,11 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
   if (fp8 && !tc)
     return fail(RTK_ERR_UNSUPPORTED, "the fp8 visual span needs bf16 / fp16 queries, head_dim 128, D_keep 16, "
                                      "32 or 64 and 16-byte aligned e4m3 rows");
+  if (spark && !tc)
+    return fail(RTK_ERR_UNSUPPORTED, "the SparK decode needs bf16 / fp16 tensors, head_dim 128, D_keep 16, 32 "
+                                     "or 64, and channel-contiguous, 16-byte aligned rows");
   if (tc) {
-    const TcShape t = tc_shape(B, Hkv, G, Sf, Sv, device);
+    const TcShape t = tc_shape(B, Hkv, G, Sf, Sv, device, spark ? kFullBlockTokens : kVisBlockTokens);
     const WorkspacePlan w = plan_workspace(B, Hq, t.slots, t.slot_floats);
     rtk::DecodeParams p;
     std::memset(&p, 0, sizeof(p));
@@ -322,7 +341,7 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
     p.scale_log2 = (float)scale_log2;
     p.q = a.q->data; p.q_sb = a.q->stride[0]; p.q_sh = a.q->stride[1];
     if (!a.dense) {
-      p.R = R.data; p.R_sb = R.s[0]; p.R_sh = R.s[1]; p.R_sd = R.s[2];
+      if (!spark) { p.R = R.data; p.R_sb = R.s[0]; p.R_sh = R.s[1]; p.R_sd = R.s[2]; }
       if (a.dm != nullptr) { p.dm = a.dm->data; p.dm_sb = a.dm->stride[0]; p.dm_sh = a.dm->stride[1]; }
       if (a.mask != nullptr) { p.mask = static_cast<const uint8_t *>(a.mask->data); p.mask_sb = a.mask->stride[0]; p.mask_ss = a.mask->stride[1]; }
     }
@@ -332,7 +351,11 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
     p.tickets = reinterpret_cast<int *>(ws + w.ticket_off);
     p.status = status;
     cudaError_t e;
-    if (fp8) {
+    if (spark) {
+      rtk::DecodeSpark sp;
+      sp.mean = km.data; sp.mean_sb = km.s[0]; sp.mean_sh = km.s[1]; sp.mean_ss = km.s[2];
+      e = rtk::launch_decode_tc_spark(dt == RTK_BF16, maps, p, sp, t.heads_tile, (int)DK, t.grid, stream);
+    } else if (fp8) {
       rtk::DecodeFp8 f;
       f.k_scale = static_cast<const float *>(a.ksc->data);
       f.ksc_sb = a.ksc->stride[0]; f.ksc_sh = a.ksc->stride[1];
@@ -583,6 +606,72 @@ int rtk_full_channel_decode(const rtk_tensor *q, const rtk_tensor *k, const rtk_
   if (B * Hq == 0 || D == 0) return RTK_OK;
   DecodeArgs a{q, nullptr, nullptr, k, v, nullptr, nullptr, nullptr, out, num_kv_groups, true};
   return run_decode(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int rtk_spark_decode(const rtk_tensor *q_full, const rtk_tensor *k_full, const rtk_tensor *v_full,
+                     const rtk_tensor *mask_full, const rtk_tensor *k_kept, const rtk_tensor *keep_idx,
+                     const rtk_tensor *pruned_mean, const rtk_tensor *v_sparse, int64_t num_kv_groups,
+                     const rtk_tensor *out, void *workspace, size_t workspace_bytes, void *stream) {
+  g_last_error.clear();
+  if (q_full == nullptr || q_full->ndim != 3) return fail(RTK_ERR_INVALID, "q_full must be [B, H_q, D]");
+  if (k_kept == nullptr || k_kept->ndim != 4)
+    return fail(RTK_ERR_INVALID, "k_kept must be [B, H_kv, S_sparse, D_keep]");
+  if (mask_full != nullptr && mask_full->dtype != RTK_U8) return fail(RTK_ERR_INVALID, "mask_full must be uint8");
+  const int64_t B = q_full->shape[0], Hq = q_full->shape[1], D = q_full->shape[2];
+  const int64_t Hkv = k_kept->shape[1], Sv = k_kept->shape[2], DK = k_kept->shape[3];
+  if (num_kv_groups <= 0 || Hq != Hkv * num_kv_groups)
+    return fail(RTK_ERR_INVALID, "H_q=%lld is not H_kv=%lld * num_kv_groups=%lld", (long long)Hq,
+                (long long)Hkv, (long long)num_kv_groups);
+  if (!same_dims(k_kept, 4, {B, Hkv, Sv, DK}) || DK < 1 || DK > D)
+    return fail(RTK_ERR_INVALID, "k_kept must be [B, H_kv, S_sparse, D_keep] with D_keep <= D");
+  if (!same_dims(keep_idx, 4, {B, Hkv, Sv, DK}) || keep_idx->dtype != RTK_U8)
+    return fail(RTK_ERR_INVALID, "keep_idx must be a uint8 [B, H_kv, S_sparse, D_keep]");
+  if (!same_dims(pruned_mean, 4, {B, Hkv, Sv, 1}))
+    return fail(RTK_ERR_INVALID, "pruned_mean must be [B, H_kv, S_sparse, 1]");
+  if (!same_dims(k_full, 4, {B, Hkv, -1, D})) return fail(RTK_ERR_INVALID, "k_full must be [B, H_kv, S_full, D]");
+  const int64_t Sf = k_full->shape[2];
+  if (!same_dims(v_full, 4, {B, Hkv, Sf, D})) return fail(RTK_ERR_INVALID, "v_full must be [B, H_kv, S_full, D]");
+  if (mask_full != nullptr && !same_dims(mask_full, 2, {B, Sf})) return fail(RTK_ERR_INVALID, "mask_full must be [B, S_full]");
+  if (!same_dims(v_sparse, 4, {B, Hkv, Sv, D})) return fail(RTK_ERR_INVALID, "v_sparse must be [B, H_kv, S_sparse, D]");
+  if (!dtype_ok(q_full->dtype)) return fail(RTK_ERR_INVALID, "q_full dtype must be float32, bfloat16 or float16");
+  for (const rtk_tensor *t : {k_full, v_full, k_kept, pruned_mean, v_sparse, out})
+    if (t->dtype != q_full->dtype)
+      return fail(RTK_ERR_INVALID, "all tensors but mask_full and keep_idx must share q_full's dtype");
+  int64_t os[3];
+  if (!out_view(out, B, Hq, D, os)) return fail(RTK_ERR_INVALID, "out must be [B, H_q, D] or [B, 1, H_q, D]");
+  if (B * Hq == 0 || D == 0) return RTK_OK;
+  DecodeArgs a{q_full, nullptr, nullptr, k_full, v_full, mask_full, k_kept, v_sparse, out, num_kv_groups, false};
+  a.kidx = keep_idx;
+  a.kmean = pruned_mean;
+  return run_decode(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int rtk_spark_pack(const rtk_tensor *keep_mask, const rtk_tensor *keep_idx_out, void *status, void *stream) {
+  g_last_error.clear();
+  if (keep_mask == nullptr || keep_mask->ndim != 4 || keep_mask->dtype != RTK_U8)
+    return fail(RTK_ERR_INVALID, "keep_mask must be a bool / uint8 [B, H_kv, S, D]");
+  const int64_t B = keep_mask->shape[0], H = keep_mask->shape[1], S = keep_mask->shape[2];
+  if (keep_mask->shape[3] != 128 || keep_mask->stride[3] != 1)
+    return fail(RTK_ERR_UNSUPPORTED, "keep_mask needs D = 128 with a unit channel stride");
+  if (keep_idx_out == nullptr || keep_idx_out->ndim != 4 || keep_idx_out->dtype != RTK_U8 ||
+      keep_idx_out->shape[0] != B || keep_idx_out->shape[1] != H || keep_idx_out->shape[2] != S)
+    return fail(RTK_ERR_INVALID, "keep_idx_out must be a uint8 [B, H_kv, S, D_keep]");
+  const int64_t DK = keep_idx_out->shape[3];
+  if (DK < 1 || DK > 128) return fail(RTK_ERR_INVALID, "D_keep must be in 1..128");
+  if (keep_idx_out->stride[3] != 1 || keep_idx_out->stride[2] != DK || keep_idx_out->stride[1] != S * DK ||
+      keep_idx_out->stride[0] != H * S * DK)
+    return fail(RTK_ERR_INVALID, "keep_idx_out must be contiguous");
+  if (B * H * S == 0) return RTK_OK;
+  if (B * H * S >= (1ll << 31) * 8) return fail(RTK_ERR_UNSUPPORTED, "tensor too large");
+  rtk::SparkPackParams p;
+  p.batch = (int)B; p.heads = (int)H; p.seq = (int)S; p.keep = (int)DK;
+  p.mask = static_cast<const uint8_t *>(keep_mask->data);
+  for (int i = 0; i < 3; ++i) p.m_s[i] = keep_mask->stride[i];
+  p.idx = static_cast<uint8_t *>(keep_idx_out->data);
+  p.status = static_cast<unsigned int *>(status);
+  const cudaError_t e = rtk::launch_spark_pack(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "SparK index packing launch");
+  return RTK_OK;
 }
 
 // ------------------------------------------------------------------ rotation builder

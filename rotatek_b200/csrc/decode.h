@@ -29,6 +29,7 @@ struct DecodeParams {
 
 struct DecodeTensorMaps {
   CUtensorMap kf, vf, ks, vs;             // [D|Dk, S, H_kv, B] views, 64-token boxes
+  CUtensorMap ki;                         // SparK: kept channel indices [Dk, S, H_kv, B] (uint8)
 };
 
 // heads_tile: 8 or 16 query heads per unit; dk: 16, 32 or 64.
@@ -48,6 +49,31 @@ struct DecodeFp8 {
 cudaError_t launch_decode_tc_fp8(int dtype_is_bf16, const DecodeTensorMaps &maps,
                                  const DecodeParams &p, const DecodeFp8 &f, int heads_tile, int dk,
                                  int grid, cudaStream_t stream);
+
+// SparK visual span (decode_tc.cu with the SparK flag): per token the kept
+// channels' values [B, H_kv, S_v, D_keep] (maps.ks, 32-token boxes), their
+// channel indices [B, H_kv, S_v, D_keep] uint8 ascending (maps.ki) and the
+// pruned channels' mean [B, H_kv, S_v] (16-bit, below); Values in maps.vs with
+// 32-token boxes.  The dense Keys are the adapters' recovery of those.
+struct DecodeSpark {
+  const void *mean; long long mean_sb, mean_sh, mean_ss;
+};
+
+cudaError_t launch_decode_tc_spark(int dtype_is_bf16, const DecodeTensorMaps &maps, const DecodeParams &p,
+                                   const DecodeSpark &sp, int heads_tile, int dk, int grid,
+                                   cudaStream_t stream);
+
+// Kept-channel indices of a SparK keep mask (spark_pack.cu): keep [B, H, S, 128]
+// bytes (nonzero = kept) -> idx [B, H, S, keep] uint8, ascending.  A token with
+// a kept count other than `keep` sets bit RTK_DEVICE_BAD_INPUT of *status.
+struct SparkPackParams {
+  int batch, heads, seq, keep;
+  const uint8_t *mask; long long m_s[3];     // channel stride 1
+  uint8_t *idx;                              // contiguous
+  unsigned int *status;
+};
+
+cudaError_t launch_spark_pack(const SparkPackParams &p, cudaStream_t stream);
 
 // Quantisation of a visual span to the layout above (quant_fp8.cu).
 struct QuantParams {

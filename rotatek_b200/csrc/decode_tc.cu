@@ -52,14 +52,29 @@ constexpr int kVisBoxBytes = kVisTokens * 128;    // one {64 d x 64 tokens} box
 constexpr int kSmemBudget = 232448;      // 227 KB opt-in per CTA
 constexpr float kNegBig = -1e30f;        // running-max floor (fused_decode.py:151)
 
-template <int NT, int DK>
+// What the visual span holds:
+//   kModeRotK   rotated-truncated Keys k~ [S_v, D_keep] and Values, 16-bit
+//   kModeFp8    the same in e4m3 with per-channel Key / per-token Value scales
+//   kModeSpark  SparK's per-token channel pruning: the kept channels' values
+//               [S_v, D_keep] (channel order), their channel indices [S_v, D_keep]
+//               (uint8, ascending) and the pruned channels' mean per token; the
+//               dense Keys are rebuilt in shared memory block by block
+enum : int { kModeRotK = 0, kModeFp8 = 1, kModeSpark = 2 };
+
+template <int NT, int DK, int MODE = kModeRotK>
 struct Cfg {
   static constexpr int kHeads = 8 * NT;
   static constexpr int kWarps = (NT == 1 && DK <= 32) ? 5 : 4;   // consumer warps
   static constexpr int kThreads = (kWarps + 1) * 32;             // + producer warp
   static_assert(kWarps <= 5, "the host sizes the workspace for at most 5 partial slots per CTA");
   static constexpr int kKsBytes = kVisTokens * DK * 2;           // visual Keys of a block
-  static constexpr int kStageBytes = (kKsBytes + 2 * kVisBoxBytes + 1023) / 1024 * 1024;
+  // SparK visual block (32 tokens): rebuilt dense Keys in two 64-channel boxes |
+  // Values in two boxes | kept values [32][DK] | kept channel indices [32][DK]
+  static constexpr int kSpValOff = 4 * kFullBoxBytes;
+  static constexpr int kSpIdxOff = kSpValOff + kFullTokens * DK * 2;
+  static constexpr int kStageRaw =
+      MODE == kModeSpark ? kSpIdxOff + kFullTokens * DK : kKsBytes + 2 * kVisBoxBytes;
+  static constexpr int kStageBytes = (kStageRaw + 1023) / 1024 * 1024;
   static_assert(kStageBytes >= 4 * kFullBoxBytes, "a stage must hold a prompt/text block");
   // per-unit header: q rows [H][128], R [128][DK], delta_mu [128] (16-bit), mask bytes
   static constexpr int kHdrQ = 0;
@@ -423,16 +438,57 @@ __device__ __forceinline__ void convert_fp8_stage(unsigned char *st, int lane) {
   }
 }
 
-template <typename T, int NT, int DK, bool FP8>
-__global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
+// SparK visual block: rebuild the 32 tokens' full-width Keys as the two
+// 128B-swizzled {64 channels x 32 tokens} boxes a prompt/text block has, from
+// the kept values and channel indices the TMA put at kSpValOff / kSpIdxOff --
+// the adapters' recovery (llama_visionzip.py:226-230): every channel first
+// takes the token's pruned-channel mean, then the kept channels their values.
+// Lane t owns token row t (its fill, its scatter), so only the caller's
+// __syncwarp before the MMAs orders lanes.  `mean2` is the token's mean (16-bit
+// bits) in both halves.  Indices are taken mod 128, so no write leaves the row.
+template <int DK>
+__device__ __forceinline__ void rebuild_spark_keys(unsigned char *st, int lane, uint32_t mean2) {
+  constexpr int kValOff = Cfg<1, DK, kModeSpark>::kSpValOff;
+  constexpr int kIdxOff = Cfg<1, DK, kModeSpark>::kSpIdxOff;
+  const uint32_t row = smem_u32(st) + static_cast<uint32_t>(lane) * 128;
+  const uint32_t x = static_cast<uint32_t>(lane & 7) << 4;   // the row's 128B-swizzle pattern
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    st_shared_v4(row + ((c << 4) ^ x), mean2, mean2, mean2, mean2);
+    st_shared_v4(row + kFullBoxBytes + ((c << 4) ^ x), mean2, mean2, mean2, mean2);
+  }
+  uint32_t val[DK / 2], idx[DK / 4];
+#pragma unroll
+  for (int c = 0; c < DK / 8; ++c) {
+    const uint4 v = *reinterpret_cast<const uint4 *>(st + kValOff + swizzled_offset<DK * 2>(lane, c * 8));
+    val[4 * c] = v.x; val[4 * c + 1] = v.y; val[4 * c + 2] = v.z; val[4 * c + 3] = v.w;
+  }
+#pragma unroll
+  for (int c = 0; c < DK / 16; ++c) {
+    const uint4 v = *reinterpret_cast<const uint4 *>(st + kIdxOff + k8_offset<DK>(lane, c));
+    idx[4 * c] = v.x; idx[4 * c + 1] = v.y; idx[4 * c + 2] = v.z; idx[4 * c + 3] = v.w;
+  }
+#pragma unroll
+  for (int k = 0; k < DK; ++k) {
+    const uint32_t b2 = ((idx[k >> 2] >> (8 * (k & 3))) & 127u) << 1;   // byte offset in a 256-byte row
+    const uint32_t addr = row + ((b2 & 128u) << 5) + ((b2 & 127u) ^ x);  // box 1 holds channels 64-127
+    st_shared_u16(addr, static_cast<uint16_t>(val[k >> 1] >> (16 * (k & 1))));
+  }
+}
+
+template <typename T, int NT, int DK, int MODE>
+__global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
     rotatek_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_kf,
                              const __grid_constant__ CUtensorMap tm_vf,
                              const __grid_constant__ CUtensorMap tm_ks,
-                             const __grid_constant__ CUtensorMap tm_vs, const DecodeParams p,
-                             const DecodeFp8 f8) {
+                             const __grid_constant__ CUtensorMap tm_vs,
+                             const __grid_constant__ CUtensorMap tm_ki, const DecodeParams p,
+                             const DecodeFp8 f8, const DecodeSpark sp) {
+  constexpr bool FP8 = MODE == kModeFp8;
+  constexpr bool SPARK = MODE == kModeSpark;
   // the visual span's MMAs run in f16 when it is stored in fp8 (e4m3 -> f16 is exact)
   using TV = typename std::conditional<FP8, __half, T>::type;
-  using C = Cfg<NT, DK>;
+  using C = Cfg<NT, DK, MODE>;
   constexpr int kHeads = C::kHeads;
   constexpr int kStages = C::kStages;
   constexpr int kWarps = C::kWarps;
@@ -475,6 +531,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
     if (lane == 0) {
       if (p.blocks_full > 0) { tma_prefetch_desc(&tm_kf); tma_prefetch_desc(&tm_vf); }
       if (p.blocks_sparse > 0) { tma_prefetch_desc(&tm_ks); tma_prefetch_desc(&tm_vs); }
+      if (SPARK && p.blocks_sparse > 0) tma_prefetch_desc(&tm_ki);
     }
     int unit = static_cast<int>(lo / bpu);
     int j = static_cast<int>(lo - (long long)unit * bpu);
@@ -510,6 +567,15 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
             tma_load_4d(st + kFullBoxBytes, &tm_kf, 64, tok, kvh, bk, &full_bar[stage]);
             tma_load_4d(st + 2 * kFullBoxBytes, &tm_vf, 0, tok, kvh, bk, &full_bar[stage]);
             tma_load_4d(st + 3 * kFullBoxBytes, &tm_vf, 64, tok, kvh, bk, &full_bar[stage]);
+          } else if constexpr (SPARK) {
+            // Values, kept values and kept channel indices; the Keys are rebuilt
+            // by the consumer in the first 2 * kFullBoxBytes
+            const int tok = (j - p.blocks_full) * kFullTokens;
+            mbar_arrive_expect_tx(&full_bar[stage], 2 * kFullBoxBytes + kFullTokens * DK * 3);
+            tma_load_4d(st + 2 * kFullBoxBytes, &tm_vs, 0, tok, kvh, bk, &full_bar[stage]);
+            tma_load_4d(st + 3 * kFullBoxBytes, &tm_vs, 64, tok, kvh, bk, &full_bar[stage]);
+            tma_load_4d(st + C::kSpValOff, &tm_ks, 0, tok, kvh, bk, &full_bar[stage]);
+            tma_load_4d(st + C::kSpIdxOff, &tm_ki, 0, tok, kvh, bk, &full_bar[stage]);
           } else {
             const int tok = (j - p.blocks_full) * kVisTokens;
             if constexpr (FP8) {
@@ -590,7 +656,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
     // fp32 result -> 16-bit hi + lo B fragments (k = channel, n = head)
     uint32_t qhi[DK / 16][NT][2], qlo[DK / 16][NT][2];
 #pragma unroll
-    for (int mt = 0; mt < DK / 16; ++mt) {
+    for (int mt = 0; mt < (SPARK ? 0 : DK / 16); ++mt) {
       float c[NT][4];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) c[nt][0] = c[nt][1] = c[nt][2] = c[nt][3] = 0.f;
@@ -625,7 +691,10 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
     }
     // bias = q . delta_mu per head: lane sums 4 channels, butterfly over the warp
     float bias2[NT][2];
-    {
+    if constexpr (SPARK) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) bias2[nt][0] = bias2[nt][1] = 0.f;
+    } else {
       float dmv[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) dmv[k] = to_f32(hdm[lane * 4 + k]);
@@ -679,12 +748,30 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
             }
         }
       }
+      // SparK span: this lane's token's pruned-channel mean, likewise early
+      uint32_t mean2 = 0;
+      if constexpr (SPARK) {
+        const int tok = (j - p.blocks_full) * kFullTokens + lane;
+        if (j >= p.blocks_full && tok < p.seq_sparse) {
+          const uint32_t m = __ldg(reinterpret_cast<const unsigned short *>(sp.mean) + (long long)bk * sp.mean_sb +
+                                   (long long)kvh * sp.mean_sh + (long long)tok * sp.mean_ss);
+          mean2 = m | (m << 16);
+        }
+      }
       const bool ready = mbar_wait_bounded(&full_bar[stage], (i / kStages) & 1, abort_flag, p.status);
       const uint32_t sbase = smem_u32(ring + stage * C::kStageBytes);
+      const bool spark_vis = SPARK && j >= p.blocks_full;
       if (ready) {
-        if (j < p.blocks_full) {
-          // ---- prompt/text block: 32 tokens at full width, q . k
-          const int tok0 = j * kFullTokens;
+        if (j < p.blocks_full || spark_vis) {
+          // ---- 32 tokens at full width, q . k: a prompt/text block, or a SparK
+          //      visual block once its Keys are rebuilt
+          const int tok0 = (spark_vis ? j - p.blocks_full : j) * kFullTokens;
+          if constexpr (SPARK) {
+            if (spark_vis) {
+              rebuild_spark_keys<DK>(ring + stage * C::kStageBytes, lane, mean2);
+              __syncwarp();
+            }
+          }
           float s[2][NT][4];
 #pragma unroll
           for (int mt = 0; mt < 2; ++mt)
@@ -708,8 +795,8 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
               const int tok = tok0 + mt * 16 + g8 + 8 * r;
-              bool v = tok < p.seq_full;
-              if (v && p.mask != nullptr)
+              bool v = tok < (spark_vis ? p.seq_sparse : p.seq_full);
+              if (v && !spark_vis && p.mask != nullptr)
                 v = (p.seq_full <= C::kHdrMaskBytes ? hmask[tok]
                                                     : p.mask[(long long)bk * p.mask_sb +
                                                              (long long)tok * p.mask_ss]) != 0;
@@ -722,7 +809,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
           }
           softmax_pv<T, NT, 2>(s, valid, m_run, l_run, o, sbase + 2 * kFullBoxBytes,
                                kFullBoxBytes, lane);
-        } else {
+        } else if constexpr (!SPARK) {
           // ---- visual block: 64 tokens, rotated-truncated Keys, (q~ . k~ + bias)
           const int tok0 = (j - p.blocks_full) * kVisTokens;
           if constexpr (FP8) convert_fp8_stage<DK>(ring + stage * C::kStageBytes, lane);
@@ -766,7 +853,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
           }
         }
       }
-      if constexpr (FP8) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // our writes, then TMA's
+      if constexpr (FP8 || SPARK) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // our writes, then TMA's
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[stage]);
     }
@@ -825,49 +912,65 @@ __global__ void __launch_bounds__(Cfg<NT, DK>::kThreads, 1)
   }
 }
 
-template <typename T, int NT, int DK, bool FP8>
-cudaError_t launch_tc(const DecodeTensorMaps &maps, const DecodeParams &p, const DecodeFp8 &f8, int grid,
-                      cudaStream_t stream) {
-  using C = Cfg<NT, DK>;
+template <typename T, int NT, int DK, int MODE>
+cudaError_t launch_tc(const DecodeTensorMaps &maps, const DecodeParams &p, const DecodeFp8 &f8,
+                      const DecodeSpark &sp, int grid, cudaStream_t stream) {
+  using C = Cfg<NT, DK, MODE>;
   const int smem = C::kBytes + 1024;
-  auto kern = rotatek_decode_tc_kernel<T, NT, DK, FP8>;
+  auto kern = rotatek_decode_tc_kernel<T, NT, DK, MODE>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (err != cudaSuccess) return err;
-  kern<<<grid, C::kThreads, smem, stream>>>(maps.kf, maps.vf, maps.ks, maps.vs, p, f8);
+  kern<<<grid, C::kThreads, smem, stream>>>(maps.kf, maps.vf, maps.ks, maps.vs, maps.ki, p, f8, sp);
   return cudaGetLastError();
 }
 
-template <typename T, bool FP8>
-cudaError_t dispatch_nt_dk(const DecodeTensorMaps &maps, const DecodeParams &p, const DecodeFp8 &f8, int nt,
-                           int dk, int grid, cudaStream_t stream) {
+template <typename T, int MODE>
+cudaError_t dispatch_nt_dk(const DecodeTensorMaps &maps, const DecodeParams &p, const DecodeFp8 &f8,
+                           const DecodeSpark &sp, int nt, int dk, int grid, cudaStream_t stream) {
   if (nt == 1) {
-    if (dk == 16) return launch_tc<T, 1, 16, FP8>(maps, p, f8, grid, stream);
-    if (dk == 32) return launch_tc<T, 1, 32, FP8>(maps, p, f8, grid, stream);
-    if (dk == 64) return launch_tc<T, 1, 64, FP8>(maps, p, f8, grid, stream);
+    if (dk == 16) return launch_tc<T, 1, 16, MODE>(maps, p, f8, sp, grid, stream);
+    if (dk == 32) return launch_tc<T, 1, 32, MODE>(maps, p, f8, sp, grid, stream);
+    if (dk == 64) return launch_tc<T, 1, 64, MODE>(maps, p, f8, sp, grid, stream);
   } else {
-    if (dk == 16) return launch_tc<T, 2, 16, FP8>(maps, p, f8, grid, stream);
-    if (dk == 32) return launch_tc<T, 2, 32, FP8>(maps, p, f8, grid, stream);
-    if (dk == 64) return launch_tc<T, 2, 64, FP8>(maps, p, f8, grid, stream);
+    if (dk == 16) return launch_tc<T, 2, 16, MODE>(maps, p, f8, sp, grid, stream);
+    if (dk == 32) return launch_tc<T, 2, 32, MODE>(maps, p, f8, sp, grid, stream);
+    if (dk == 64) return launch_tc<T, 2, 64, MODE>(maps, p, f8, sp, grid, stream);
   }
   return cudaErrorInvalidValue;
+}
+
+template <int MODE>
+cudaError_t dispatch(int dtype_is_bf16, const DecodeTensorMaps &maps, const DecodeParams &p,
+                     const DecodeFp8 &f8, const DecodeSpark &sp, int heads_tile, int dk, int grid,
+                     cudaStream_t stream) {
+  const int nt = heads_tile / 8;
+  if (dtype_is_bf16) return dispatch_nt_dk<__nv_bfloat16, MODE>(maps, p, f8, sp, nt, dk, grid, stream);
+  return dispatch_nt_dk<__half, MODE>(maps, p, f8, sp, nt, dk, grid, stream);
 }
 
 }  // namespace
 
 cudaError_t launch_decode_tc(int dtype_is_bf16, const DecodeTensorMaps &maps, const DecodeParams &p,
                              int heads_tile, int dk, int grid, cudaStream_t stream) {
-  const int nt = heads_tile / 8;
-  DecodeFp8 none;
-  std::memset(&none, 0, sizeof(none));
-  if (dtype_is_bf16) return dispatch_nt_dk<__nv_bfloat16, false>(maps, p, none, nt, dk, grid, stream);
-  return dispatch_nt_dk<__half, false>(maps, p, none, nt, dk, grid, stream);
+  DecodeFp8 f8;
+  DecodeSpark sp;
+  std::memset(&f8, 0, sizeof(f8));
+  std::memset(&sp, 0, sizeof(sp));
+  return dispatch<kModeRotK>(dtype_is_bf16, maps, p, f8, sp, heads_tile, dk, grid, stream);
 }
 
 cudaError_t launch_decode_tc_fp8(int dtype_is_bf16, const DecodeTensorMaps &maps, const DecodeParams &p,
                                  const DecodeFp8 &f, int heads_tile, int dk, int grid, cudaStream_t stream) {
-  const int nt = heads_tile / 8;
-  if (dtype_is_bf16) return dispatch_nt_dk<__nv_bfloat16, true>(maps, p, f, nt, dk, grid, stream);
-  return dispatch_nt_dk<__half, true>(maps, p, f, nt, dk, grid, stream);
+  DecodeSpark sp;
+  std::memset(&sp, 0, sizeof(sp));
+  return dispatch<kModeFp8>(dtype_is_bf16, maps, p, f, sp, heads_tile, dk, grid, stream);
+}
+
+cudaError_t launch_decode_tc_spark(int dtype_is_bf16, const DecodeTensorMaps &maps, const DecodeParams &p,
+                                   const DecodeSpark &sp, int heads_tile, int dk, int grid, cudaStream_t stream) {
+  DecodeFp8 f8;
+  std::memset(&f8, 0, sizeof(f8));
+  return dispatch<kModeSpark>(dtype_is_bf16, maps, p, f8, sp, heads_tile, dk, grid, stream);
 }
 
 }  // namespace rtk

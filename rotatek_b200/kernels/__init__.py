@@ -221,5 +221,78 @@ def think_decode(
     return out
 
 
+def pack_spark_indices(keep_mask: torch.Tensor, d_keep: int, validate: bool = True) -> torch.Tensor:
+    """Kept channels of a SparK keep mask, ascending: keep_mask [B, H_kv, S, 128]
+    bool (``ChannelPruner.current_spark_mask``, rotatek/baselines/spark.py:15-58)
+    -> keep_idx [B, H_kv, S, d_keep] uint8 for ``spark_decode``.  The mask is
+    fixed after prefill, so this runs once per layer.  ``validate`` checks on
+    the device that every token keeps exactly d_keep channels and raises
+    ValueError otherwise (one host synchronisation)."""
+    if keep_mask.dim() != 4:
+        raise ValueError("keep_mask must be [B, H_kv, S, D]")
+    _lib.require_cuda(keep_mask)
+    b, h, s, _ = keep_mask.shape
+    dev = keep_mask.device
+    mask = keep_mask.view(torch.uint8) if keep_mask.dtype == torch.bool else keep_mask
+    idx = torch.empty(b, h, s, d_keep, dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev) if validate else None
+    D = _lib.describe
+    _lib.check(_lib.load().rtk_spark_pack(D(mask), D(idx),
+                                          ctypes.c_void_p(status.data_ptr() if validate else 0), _stream(dev)))
+    if validate and int(status.item()) != 0:
+        raise ValueError(f"keep_mask: some token does not keep exactly {d_keep} channels")
+    return idx
+
+
+def spark_decode(
+    q_full: torch.Tensor,                # [B, H_q, D]
+    k_full: torch.Tensor,                # [B, H_kv, S_full, D]
+    v_full: torch.Tensor,                # [B, H_kv, S_full, D]
+    mask_full: Optional[torch.Tensor],   # [B, S_full] uint8 or None
+    k_kept: torch.Tensor,                # [B, H_kv, S_vis, D_keep] kept channels, channel order
+    keep_idx: torch.Tensor,              # [B, H_kv, S_vis, D_keep] uint8 (pack_spark_indices)
+    pruned_mean: torch.Tensor,           # [B, H_kv, S_vis, 1]
+    v_sparse: torch.Tensor,              # [B, H_kv, S_vis, D]
+    num_kv_groups: int,
+) -> torch.Tensor:
+    """The SparK baseline's decode without recovering full-width Keys.
+
+    The adapters fill a [B, H_kv, S_vis, D] buffer with each token's
+    ``pruned_mean``, write the kept values into the kept channels, concatenate
+    prompt, visual and text Keys and run ``full_channel_decode``
+    (llama_visionzip.py:226-242).  This computes that decode in one kernel that
+    rebuilds each 32-token block of recovered Keys in shared memory, so the
+    visual Keys cost D_keep values + D_keep index bytes + one mean per token in
+    HBM instead of 128 values.  ``mask_full`` masks the prompt/text span as in
+    ``rotatek_decode``.  Returns [B, 1, H_q, D] in q's dtype."""
+    if q_full.dim() != 3:
+        raise ValueError("q_full must be [B, H_q, D]")
+    if k_kept.dim() != 4:
+        raise ValueError("k_kept must be [B, H_kv, S_vis, D_keep]")
+    if mask_full is not None and mask_full.dtype != torch.uint8:
+        raise ValueError("mask_full must be uint8")
+    if pruned_mean.dim() == 3:
+        pruned_mean = pruned_mean.unsqueeze(-1)
+    _lib.require_cuda(q_full, k_full, v_full, mask_full, k_kept, keep_idx, pruned_mean, v_sparse)
+    bsz, heads, head_dim = q_full.shape
+    h_kv = k_kept.shape[1]
+    lib = _lib.load()
+    dev = q_full.device
+    key = ("rk", _dtype_code(q_full), bsz, heads, h_kv, head_dim, k_kept.shape[-1],
+           k_full.shape[-2], k_kept.shape[-2], dev.index)
+    need = _ws_size_cache.get(key)
+    if need is None:
+        need = (lib.rtk_rotatek_decode_workspace_size(*key[1:-1], dev.index),
+                lib.rtk_decode_workspace_counter_bytes(bsz, heads))
+        _ws_size_cache[key] = need
+    ws = _lib.workspace(dev, *need)
+    out = torch.empty((bsz, 1, heads, head_dim), dtype=q_full.dtype, device=dev)
+    D = _lib.describe
+    _lib.check(lib.rtk_spark_decode(
+        D(q_full), D(k_full), D(v_full), D(mask_full), D(k_kept), D(keep_idx), D(pruned_mean), D(v_sparse),
+        num_kv_groups, D(out), ctypes.c_void_p(ws.data_ptr()), ws.numel(), _stream(dev)))
+    return out
+
+
 __all__ = ["ROTATEK_KERNEL", "rotatek_decode", "full_channel_decode", "think_decode", "think_selection",
-           "quantize_visual_fp8", "rotatek_decode_fp8"]
+           "quantize_visual_fp8", "rotatek_decode_fp8", "pack_spark_indices", "spark_decode"]

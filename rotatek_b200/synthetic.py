@@ -142,3 +142,60 @@ def make_decode(batch: int, q_heads: int, kv_heads: int, vision_len: int, full_l
     mask_full = torch.ones(batch, full_len, dtype=torch.uint8, device=device)
     return DecodeInputs(q_full, r_cast.contiguous(), delta_mu, k_full, v_full, mask_full,
                         k_sparse.contiguous(), v_sparse, groups)
+
+
+@dataclass
+class SparkInputs:
+    """Arguments of ``spark_decode`` for one layer: SparK's per-token channel
+    pruning (rotatek/baselines/spark.py:15-58) of low-rank visual Keys."""
+    q_full: torch.Tensor        # [B, H_q, D]
+    k_full: torch.Tensor        # [B, H_kv, S_f, D]
+    v_full: torch.Tensor        # [B, H_kv, S_f, D]
+    mask_full: torch.Tensor     # [B, S_f] uint8
+    k_kept: torch.Tensor        # [B, H_kv, S_v, D_keep] kept values, channel order
+    keep_mask: torch.Tensor     # [B, H_kv, S_v, D] bool
+    pruned_mean: torch.Tensor   # [B, H_kv, S_v, 1]
+    v_sparse: torch.Tensor      # [B, H_kv, S_v, D]
+    num_kv_groups: int
+
+    def recovered(self) -> torch.Tensor:
+        """Full-width visual Keys as the adapters rebuild them
+        (llama_visionzip.py:228-230)."""
+        b, h, s, _ = self.k_kept.shape
+        rec = self.pruned_mean.expand(b, h, s, self.keep_mask.shape[-1]).contiguous()
+        rec[self.keep_mask] = self.k_kept.reshape(-1)
+        return rec
+
+
+def spark_prune(queries: torch.Tensor, keys: torch.Tensor, keep: int):
+    """(K_compact, keep_mask, pruned_mean) of spark.py:15-58 for queries
+    [B, H, Q, D] (grouped to the KV heads) and keys [B, H, S, D], in the keys'
+    dtype: score k^2 * ||Q||_2, keep the top `keep` channels per token (ties
+    broken by torch.topk), kept values in channel order, mean of the rest."""
+    q_norm = torch.norm(queries, dim=-2, p=2).unsqueeze(-2)
+    scores = torch.pow(keys, 2) * q_norm
+    top = torch.topk(scores, keep, dim=-1).indices.sort(dim=-1).values
+    k_kept = torch.gather(keys, -1, top)
+    mask = torch.zeros_like(keys, dtype=torch.bool)
+    mask.scatter_(-1, top, True)
+    pruned_mean = (keys.float().sum(-1, keepdim=True) - k_kept.float().sum(-1, keepdim=True)) / (
+        keys.shape[-1] - keep)
+    return k_kept.contiguous(), mask, pruned_mean.to(keys.dtype)
+
+
+def make_spark(batch: int, q_heads: int, kv_heads: int, vision_len: int, full_len: int, keep: int = 32,
+               head_dim: int = 128, seed: int = 0, device="cpu", dtype=torch.float32) -> SparkInputs:
+    """SparK decode-step inputs: low-rank visual Keys pruned per token against a
+    N(0,1) query window (grouped by the mean over each KV head's queries, as
+    ChannelPruner.update_spark does), N(0,1) Values and decode queries."""
+    groups = q_heads // kv_heads
+    k_vis = lowrank_keys(batch, kv_heads, vision_len, head_dim, seed=seed, device=device, dtype=dtype)
+    window = normal((batch, q_heads, QUERY_WINDOW, head_dim), seed + 1, device, dtype)
+    grouped = window.view(batch, kv_heads, groups, QUERY_WINDOW, head_dim).mean(2)
+    k_kept, mask, mean = spark_prune(grouped, k_vis, keep)
+    k_full = lowrank_keys(batch, kv_heads, full_len, head_dim, seed=seed + 3, device=device, dtype=dtype)
+    v_full = normal((batch, kv_heads, full_len, head_dim), seed + 4, device, dtype)
+    v_sparse = normal((batch, kv_heads, vision_len, head_dim), seed + 5, device, dtype)
+    q_full = normal((batch, q_heads, head_dim), seed + 6, device, dtype)
+    mask_full = torch.ones(batch, full_len, dtype=torch.uint8, device=device)
+    return SparkInputs(q_full, k_full, v_full, mask_full, k_kept, mask, mean, v_sparse, groups)

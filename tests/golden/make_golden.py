@@ -16,7 +16,10 @@ What runs:
 * the adapters' prefill Key path (llava_next/llama_visionzip.py:144-153):
   torch's nn.Linear as k_proj and transformers' LlamaRotaryEmbedding /
   apply_rotary_pos_emb, which the adapter imports (llama_visionzip.py:26-33),
-  on CPU (kproj_* fixtures).
+  on CPU (kproj_* fixtures);
+* ``ChannelPruner.update_spark`` (the SparK baseline, rotatek/baselines/spark.py)
+  and the adapters' SparK decode branch: recovery, concatenation and
+  ``full_channel_decode_triton`` (spark_* fixtures).
 
 Inputs come from ``rotatek_b200.synthetic`` with fixed seeds.  Each case is one
 ``.npz`` holding inputs, reference outputs, and scalar metadata.  bf16 tensors
@@ -147,6 +150,34 @@ def dense_case(name, torch, synth, dense, *, batch, q_heads, kv_heads, seq, dtyp
     print(f"wrote {name}.npz")
 
 
+def spark_case(name, mods, torch, synth, dense, *, batch, q_heads, kv_heads, prompt, vision, text, ratio,
+               dtype, seed):
+    """SparK: the reference's ``ChannelPruner.update_spark`` on a prefill, then
+    the adapters' decode branch for one query token -- recovery (fill every
+    channel with the token's pruned_mean, the kept values into the kept
+    channels; llama_visionzip.py:226-230, restated here with the same torch
+    operations), concatenation [prompt | recovered | text] and the reference's
+    ``full_channel_decode_triton`` over the whole cache."""
+    pre = synth.make_prefill(batch, q_heads, kv_heads, prompt, vision, text, seed=seed, dtype=dtype)
+    groups = q_heads // kv_heads
+    pruner = mods[True].ChannelPruner(ratio=ratio, prompt_seqlen=prompt, query_seqlen=text)
+    kc, kv_prompt, kv_text, _, values = pruner.update_spark(
+        pre.keys, pre.queries, pre.values, None, num_key_value_groups=groups)
+    mask = pruner.current_spark_mask
+    mean = pruner.current_spark_pruned_mean
+    b, h, s_v = kc.shape[:3]
+    rec = mean.expand(b, h, s_v, pre.keys.shape[-1]).contiguous()
+    rec[mask] = kc.reshape(-1)
+    q_dec = synth.normal((batch, q_heads, pre.keys.shape[-1]), seed + 11, dtype=dtype)
+    o = dense(q_dec, torch.cat([kv_prompt, rec, kv_text], dim=-2), values, num_kv_groups=groups)
+    out = dict(keys=_np(pre.keys), values=_np(values), queries_window=_np(pre.queries[:, :, -32:]), k_compact=_np(kc),
+               keep_mask=mask.numpy(), pruned_mean=_np(mean), recovered=_np(rec), q_decode=_np(q_dec),
+               out_spark=_np(o), prompt_len=prompt, vision_len=vision, text_len=text, ratio=ratio,
+               num_kv_groups=groups, dtype=str(dtype).replace("torch.", ""))
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
+    print(f"wrote {name}.npz")
+
+
 def kproj_case(name, torch, *, batch, seq, hidden, kv_heads, vis_start, vis_len, dtype, seed, bias=True):
     """The adapters' prefill Key path (llama_visionzip.py:144-153) on CPU: nn.Linear
     k_proj, view / transpose, transformers' LlamaRotaryEmbedding cos / sin and
@@ -238,6 +269,15 @@ def main():
     if want("tiny_solved_fp32"):
         solved_matrix_case("tiny_solved_fp32", mods, torch, synth, batch=1, q_heads=4, kv_heads=2,
                            prompt=8, vision=300, text=24, ratio=0.75, scale=1e-5, seed=12)
+
+    # SparK baseline: prune (fp32, benchmark config-1 shape) and bf16 with a
+    # ragged visual span and D_keep 64
+    if want("spark_fp32"):
+        spark_case("spark_fp32", mods, torch, synth, dense, batch=2, q_heads=8, kv_heads=2, prompt=32,
+                   vision=576, text=64, ratio=0.75, dtype=torch.float32, seed=15)
+    if want("spark_bf16"):
+        spark_case("spark_bf16", mods, torch, synth, dense, batch=1, q_heads=4, kv_heads=2, prompt=8,
+                   vision=200, text=24, ratio=0.5, dtype=bf16, seed=16)
 
     # prefill Key path: projection with bias + RoPE, ragged spans (20 | 230 | 50)
     if want("kproj_bf16"):

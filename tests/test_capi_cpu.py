@@ -79,6 +79,32 @@ def test_c_validation_messages(lib):
     assert (code, lib.rtk_last_error().decode()) == (1, "k/v head_dim must match q's")
 
 
+def test_spark_validation_messages(lib):
+    q, kf, vf = _fake((2, 8, 128)), _fake((2, 2, 10, 128)), _fake((2, 2, 10, 128))
+    kk, idx, mean = _fake((2, 2, 50, 32)), _fake((2, 2, 50, 32), dtype=3), _fake((2, 2, 50, 1))
+    vs, out = _fake((2, 2, 50, 128)), _fake((2, 1, 8, 128))
+
+    def call(**kw):
+        a = dict(q=q, kf=kf, vf=vf, mask=None, kk=kk, idx=idx, mean=mean, vs=vs, g=4, out=out)
+        a.update(kw)
+        code = lib.rtk_spark_decode(a["q"], a["kf"], a["vf"], a["mask"], a["kk"], a["idx"], a["mean"],
+                                    a["vs"], a["g"], a["out"], None, 0, None)
+        return code, lib.rtk_last_error().decode()
+
+    assert call(q=_fake((8, 128))) == (1, "q_full must be [B, H_q, D]")
+    assert call(g=3) == (1, "H_q=8 is not H_kv=2 * num_kv_groups=3")
+    assert call(idx=_fake((2, 2, 50, 32)))[1] == "keep_idx must be a uint8 [B, H_kv, S_sparse, D_keep]"
+    assert call(mean=_fake((2, 2, 50)))[1] == "pruned_mean must be [B, H_kv, S_sparse, 1]"
+    assert call(vs=_fake((2, 2, 49, 128)))[1] == "v_sparse must be [B, H_kv, S_sparse, D]"
+    assert call(mean=_fake((2, 2, 50, 1), dtype=2))[1].startswith("all tensors but mask_full and keep_idx")
+    code, _ = call()                        # valid shapes, but no workspace
+    assert code in (_lib.RTK_ERR_WORKSPACE, _lib.RTK_ERR_CUDA)
+    code = lib.rtk_spark_pack(_fake((2, 2, 50, 64), dtype=3), _fake((2, 2, 50, 32), dtype=3), None, None)
+    assert (code, lib.rtk_last_error().decode()) == (2, "keep_mask needs D = 128 with a unit channel stride")
+    code = lib.rtk_spark_pack(_fake((2, 2, 50, 128), dtype=3), _fake((2, 2, 49, 32), dtype=3), None, None)
+    assert (code, lib.rtk_last_error().decode()) == (1, "keep_idx_out must be a uint8 [B, H_kv, S, D_keep]")
+
+
 def test_key_projection_validation(lib):
     """rtk_key_projection rejects bad shapes before any device work."""
     bf = 1   # RTK_BF16

@@ -141,3 +141,39 @@ def test_key_projection_oracle_matches_reference_path(golden, case):
     v = g["keys"][:, :, g["vis_start"]:g["vis_start"] + g["vis_len"]].astype(np.float64)
     np.testing.assert_allclose(ksum, v.sum(axis=2))
     np.testing.assert_allclose(cov[0, 0], v[0, 0].T @ v[0, 0])
+
+
+def _spark_spans(g):
+    p, v = g["prompt_len"], g["vision_len"]
+    keys, values = g["keys"], g["values"]
+    return (keys[:, :, p:p + v], np.concatenate([keys[:, :, :p], keys[:, :, p + v:]], axis=2),
+            np.concatenate([values[:, :, :p], values[:, :, p + v:]], axis=2), values[:, :, p:p + v])
+
+
+def test_spark_prune_oracle_matches_update_spark(golden):
+    """fp32 (no score ties): the same kept channels and values as the reference's
+    ChannelPruner.update_spark, the pruned mean within fp32 summation order."""
+    from oracle import spark as osp
+    g = golden("spark_fp32")
+    k_vis = _spark_spans(g)[0]
+    q = osp.update_spark_queries(g["queries_window"], g["num_kv_groups"])
+    kc, mask, mean = osp.per_token_channel_prune(q, k_vis, g["ratio"])
+    np.testing.assert_array_equal(mask, g["keep_mask"])
+    np.testing.assert_array_equal(kc, g["k_compact"])
+    np.testing.assert_allclose(mean, g["pruned_mean"], rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("case", ["spark_fp32", "spark_bf16"])
+def test_spark_recovery_and_decode_oracle(golden, case):
+    """Packing the mask to ascending channels and recovering gives the
+    adapters' recovered Keys bit for bit; the decode over them matches the
+    reference's dense Triton decode."""
+    from oracle import spark as osp
+    g = golden(case)
+    _, k_full, v_full, v_vis = _spark_spans(g)
+    idx = osp.pack_indices(g["keep_mask"])
+    assert idx.shape[-1] == 128 - int(128 * g["ratio"])
+    np.testing.assert_array_equal(osp.recover(g["k_compact"], idx, g["pruned_mean"]), g["recovered"])
+    out = osp.spark_decode(g["q_decode"], k_full, v_full, None, g["k_compact"], idx, g["pruned_mean"], v_vis,
+                           g["num_kv_groups"])
+    assert_matches_reference(out, g["out_spark"], g["dtype"])
