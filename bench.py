@@ -358,6 +358,13 @@ def run_ours(args):
             "clocks": clocks,
             "device_status": status,
         }
+        if world == 1:
+            dense_us, dense_bytes = dense_same_context(d, max(50, args.steps // 4))
+            line["dense_same_context"] = {
+                "value": dense_us, "unit": UNIT, "speedup": dense_us / us_per_step,
+                "algorithmic_bytes_per_launch": dense_bytes,
+                "hbm_frac": dense_bytes / dense_us / 1e3 / peak,
+                "what": "full_channel_decode over the same 16000-token context with full-width visual Keys"}
         if world == 1 and not args.no_cpu_baseline:
             us_cpu, sample, threads = cpu_baseline_sample()
             line["cpu_baseline"] = {"value": us_cpu, "unit": UNIT, "cores": threads,
@@ -367,6 +374,31 @@ def run_ours(args):
         pg.barrier()
         pg.destroy_process_group()
     return 0
+
+
+def dense_same_context(d, steps):
+    """Config 2's comparison: a full-channel flash-decode of the same context
+    (prompt/text Keys plus the visual Keys at full width, rotated back as K~ R^T)
+    through ``full_channel_decode``; CUDA events over ``steps`` back-to-back calls.
+    Returns (us per call, algorithmic bytes per call)."""
+    from rotatek_b200.kernels import full_channel_decode
+    G = CFG["q_heads"] // CFG["kv_heads"]
+    k_vis = torch.matmul(d.k_sparse, d.R_partial.transpose(-1, -2))
+    keys = torch.cat([d.k_full, k_vis], dim=2)
+    values = torch.cat([d.v_full, d.v_sparse], dim=2)
+    del k_vis
+    e = lambda t: t.numel() * t.element_size()  # noqa: E731
+    nbytes = e(keys) + e(values) + 2 * e(d.q_full)
+    for _ in range(5):
+        full_channel_decode(d.q_full, keys, values, num_kv_groups=G)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        full_channel_decode(d.q_full, keys, values, num_kv_groups=G)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / steps, nbytes
 
 
 # ---------------------------------------------------------------- config 4: the rotation build
