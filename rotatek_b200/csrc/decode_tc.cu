@@ -34,7 +34,10 @@
 //             unit it stores its partial (m, l, acc) to its own workspace slot
 //             and takes a ticket; the warp that completes the unit's count
 //             merges all of the unit's partials in slot order (deterministic)
-//             and writes the output.  No warp waits on another warp's merge.
+//             and writes the output.  No warp waits on another warp's merge,
+//             except at the end of the CTA's range: the unit of its last
+//             segment is merged by all consumer warps together, each taking a
+//             share of the heads, after one named barrier among them.
 #include <cstring>
 #include <type_traits>
 
@@ -283,11 +286,13 @@ __device__ __forceinline__ void load_header(unsigned char *hdr, const DecodePara
 
 // Merge of one unit's partials (one per consumer warp of CTAs c_first..c_last),
 // in slot order (deterministic): per-head max, weights 2^(m_k - max), weighted
-// sums; output in the query dtype.  KH = heads merged (the first KH of the
-// slot's 8 or 16; a single-head unit -- G = 1 -- reads one head per slot).
+// sums; output in the query dtype.  KH = heads merged: the slot's heads
+// hb .. hb+KH-1 (a single-head unit -- G = 1 -- reads one head per slot).  Each
+// head's sums run in slot order whatever KH, so warps that split a unit's
+// heads among them write the same bits as one warp merging them all.
 template <typename T, int KH, int kWarps>
 __device__ __forceinline__ void merge_unit(const DecodeParams &p, int unit, int c_first, int c_last,
-                                           int bk, int head0, int nheads, int lane) {
+                                           int bk, int head0, int nheads, int lane, int hb = 0) {
 
   // every partial of the unit is in place: merge them in slot order.
   // Pass 1: lane k holds slot k0 + k; per-head max and normaliser by shuffles.
@@ -302,7 +307,7 @@ __device__ __forceinline__ void merge_unit(const DecodeParams &p, int unit, int 
     const float *sl = s0 + (long long)(k0 + lane) * p.slot_floats;
 #pragma unroll
     for (int h = 0; h < KH; ++h) {
-      float v = on ? __ldcg(sl + h) : kNegBig;
+      float v = on ? __ldcg(sl + hb + h) : kNegBig;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
       mx[h] = fmaxf(mx[h], v);
@@ -323,15 +328,15 @@ __device__ __forceinline__ void merge_unit(const DecodeParams &p, int unit, int 
     float w[KH];
 #pragma unroll
     for (int h = 0; h < KH; ++h) {
-      w[h] = on ? fast_exp2(__ldcg(sl + h) - mx[h]) : 0.f;
-      float lw = on ? __ldcg(sl + 16 + h) * w[h] : 0.f;
+      w[h] = on ? fast_exp2(__ldcg(sl + hb + h) - mx[h]) : 0.f;
+      float lw = on ? __ldcg(sl + 16 + hb + h) * w[h] : 0.f;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
       lsum[h] += lw;
     }
     // kU slots per step with all their loads issued first: the L2 round
     // trips overlap instead of running one slot at a time
-    constexpr int kU = KH == 1 ? 32 : (KH <= 8 ? 4 : 1);
+    constexpr int kU = KH == 1 ? 32 : KH == 2 ? 16 : KH == 4 ? 8 : KH == 8 ? 4 : 1;
     const int nk = min(32, nslots - k0);
     for (int k = 0; k < nk; k += kU) {
       float4 v[kU][KH];
@@ -341,7 +346,7 @@ __device__ __forceinline__ void merge_unit(const DecodeParams &p, int unit, int 
             reinterpret_cast<const float4 *>(s0 + (long long)(k0 + k + u) * p.slot_floats + 32) + lane;
 #pragma unroll
         for (int h = 0; h < KH; ++h)
-          v[u][h] = k + u < nk ? __ldcg(ok + h * (kHeadDim / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          v[u][h] = k + u < nk ? __ldcg(ok + (hb + h) * (kHeadDim / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
@@ -359,9 +364,9 @@ __device__ __forceinline__ void merge_unit(const DecodeParams &p, int unit, int 
   T *outb = reinterpret_cast<T *>(p.out) + (long long)bk * p.o_sb;
 #pragma unroll
   for (int h = 0; h < KH; ++h) {
-    if (h < nheads) {
+    if (hb + h < nheads) {
       const float inv = 1.f / (lsum[h] + 1e-6f);
-      T *orow = outb + (long long)(head0 + h) * p.o_sh + lane * 4;
+      T *orow = outb + (long long)(head0 + hb + h) * p.o_sh + lane * 4;
       orow[0] = from_f32<T>(acc[h].x * inv);
       orow[1] = from_f32<T>(acc[h].y * inv);
       orow[2] = from_f32<T>(acc[h].z * inv);
@@ -502,6 +507,9 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
   uint64_t *hdr_full = empty_bar + C::kMaxStages;
   uint64_t *hdr_empty = hdr_full + 2;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kFlagOff);
+  // the unit whose merge the consumer warps share at the end (unit, c_first,
+  // c_last; unit -1 = none)
+  volatile int *pending = abort_flag + 1;
   unsigned char *ring = smem + C::kRingOff;
 
   const int warp = threadIdx.x >> 5;
@@ -522,6 +530,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
       mbar_init(&hdr_empty[b], kWarps);
     }
     *abort_flag = 0;
+    pending[0] = -1;
     fence_barrier_init();
   }
   __syncthreads();
@@ -902,13 +911,38 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
     }
     last = __shfl_sync(0xffffffffu, last, 0);
     if (last) {
-      if (nheads == 1)
+      if (nheads == 1) {
         merge_unit<T, 1, kWarps>(p, unit, c_first, c_last, bk, head0, nheads, lane);
-      else
+      } else if (seg_end == nblk) {
+        // the CTA's last segment: every consumer warp is about to finish, so
+        // the unit's heads are merged by all of them below
+        if (lane == 0) {
+          pending[1] = c_first;
+          pending[2] = c_last;
+          pending[0] = unit;
+        }
+      } else {
         merge_unit<T, kHeads, kWarps>(p, unit, c_first, c_last, bk, head0, nheads, lane);
+      }
     }
     it = seg_end;
     ++unit;
+  }
+
+  // ---- shared merge of the last segment's unit: warp cw merges heads
+  //      cw*KS .. cw*KS+KS-1 (every consumer warp reaches this barrier: none
+  //      returns early and every wait above is bounded)
+  named_barrier_sync(1, kWarps * 32);
+  const int pu = pending[0];
+  if (pu >= 0) {
+    constexpr int KS = (kHeads + kWarps - 1) / kWarps;
+    const int hc = pu % p.head_chunks;
+    const int kvh = (pu / p.head_chunks) % p.kv_heads;
+    const int bk = pu / (p.kv_heads * p.head_chunks);
+    const int nheads = min(kHeads, p.groups - hc * kHeads);
+    if (cw * KS < nheads)
+      merge_unit<T, KS, kWarps>(p, pu, pending[1], pending[2], bk, kvh * p.groups + hc * kHeads, nheads, lane,
+                                cw * KS);
   }
 }
 
