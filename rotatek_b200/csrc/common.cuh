@@ -110,6 +110,21 @@ __device__ __forceinline__ void cp_async_16(void *smem_dst, const void *gmem_src
                : "memory");
 }
 
+// 16-byte cp.async of which only the first `src_bytes` are read; the rest of the
+// 16 shared-memory bytes are zero-filled
+__device__ __forceinline__ void cp_async_16_zfill(void *smem_dst, const void *gmem_src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src),
+               "r"(src_bytes)
+               : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued before has landed.  The
+// barrier's pending count goes up by one now and down by one at that arrival, so
+// the barrier's expected count is unchanged.
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t *bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }

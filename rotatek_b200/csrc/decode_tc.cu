@@ -212,9 +212,11 @@ __device__ __forceinline__ void softmax_pv(float (&s)[MT][NT][4], const bool (&v
 }
 
 // Copy one unit's small operands into a header buffer (producer warp, all
-// lanes): the unit's query rows, R[b, kvh], delta_mu[b, kvh] and mask row.
-// Aligned rows go by cp.async (16 B, global -> shared, all issued before one
-// wait); the rest is staged through registers with every load issued first.
+// lanes): the unit's query rows, R[b, kvh], delta_mu[b, kvh], mask row and (fp8)
+// Key scales.  16-byte aligned rows go by cp.async and are not waited for here:
+// the caller has each lane arrive on the header's barrier when its copies land,
+// so the producer goes back to issuing tiles at once.  The rest is staged
+// through registers (every load issued first) and stored before returning.
 template <typename T, int NT, int DK>
 __device__ __forceinline__ void load_header(unsigned char *hdr, const DecodeParams &p, int b,
                                             int kvh, int head0, int nheads, int lane,
@@ -256,22 +258,33 @@ __device__ __forceinline__ void load_header(unsigned char *hdr, const DecodePara
       for (int e = lane; e < kHeadDim * DK; e += 32) hrt[e] = Rb[(long long)(e / DK) * p.R_sd + e % DK];
     }
   }
-  {
+  const T *dmr = p.dm != nullptr
+                     ? reinterpret_cast<const T *>(p.dm) + (long long)b * p.dm_sb + (long long)kvh * p.dm_sh
+                     : nullptr;
+  if (dmr != nullptr && (reinterpret_cast<uintptr_t>(dmr) & 15) == 0) {
+    if (lane < kHeadDim / 8) cp_async_16(hd + lane * 8, dmr + lane * 8);
+  } else {
     T dv[kHeadDim / 32];
 #pragma unroll
-    for (int k = 0; k < kHeadDim / 32; ++k)
-      dv[k] = p.dm != nullptr ? reinterpret_cast<const T *>(p.dm)[(long long)b * p.dm_sb +
-                                                                  (long long)kvh * p.dm_sh + lane + 32 * k]
-                              : from_f32<T>(0.f);
+    for (int k = 0; k < kHeadDim / 32; ++k) dv[k] = dmr != nullptr ? dmr[lane + 32 * k] : from_f32<T>(0.f);
 #pragma unroll
     for (int k = 0; k < kHeadDim / 32; ++k) hd[lane + 32 * k] = dv[k];
   }
   if (ksc != nullptr) {   // fp8 visual span: this unit's Key scales
     float *hk = reinterpret_cast<float *>(hdr + C::kHdrKsc);
-    for (int c = lane; c < DK; c += 32) hk[c] = ksc[c];
+    if ((reinterpret_cast<uintptr_t>(ksc) & 15) == 0) {
+      for (int c = lane; c < DK / 4; c += 32) cp_async_16(hk + 4 * c, ksc + 4 * c);
+    } else {
+      for (int c = lane; c < DK; c += 32) hk[c] = ksc[c];
+    }
   }
-  if (p.mask != nullptr && p.seq_full <= C::kHdrMaskBytes) {
-    const uint8_t *mrow = p.mask + (long long)b * p.mask_sb;
+  const uint8_t *mrow = p.mask != nullptr ? p.mask + (long long)b * p.mask_sb : nullptr;
+  if (mrow != nullptr && p.seq_full <= C::kHdrMaskBytes && p.mask_ss == 1 &&
+      (reinterpret_cast<uintptr_t>(mrow) & 15) == 0) {
+    // the row's bytes only: the last chunk's tail is zero-filled, not read
+    for (int c = lane; c * 16 < p.seq_full; c += 32)
+      cp_async_16_zfill(hm + 16 * c, mrow + 16 * c, min(16, p.seq_full - 16 * c));
+  } else if (mrow != nullptr && p.seq_full <= C::kHdrMaskBytes) {
     uint8_t mv[C::kHdrMaskBytes / 32];
 #pragma unroll
     for (int k = 0; k < C::kHdrMaskBytes / 32; ++k) {
@@ -281,7 +294,6 @@ __device__ __forceinline__ void load_header(unsigned char *hdr, const DecodePara
 #pragma unroll
     for (int k = 0; k < C::kHdrMaskBytes / 32; ++k) hm[lane + 32 * k] = mv[k];
   }
-  cp_async_wait_all();
 }
 
 // Merge of one unit's partials (one per consumer warp of CTAs c_first..c_last),
@@ -562,8 +574,11 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
                                  kvh * p.groups + hc * kHeads, min(kHeads, p.groups - hc * kHeads), lane,
                                  FP8 ? f8.k_scale + (long long)bk * f8.ksc_sb + (long long)kvh * f8.ksc_sh
                                      : nullptr);
+        // not waited for: tiles keep streaming while it lands (a wait here left
+        // a ~5 us gap in the tile stream at each unit switch)
+        cp_async_mbar_arrive(&hdr_full[buf]);   // this lane's copies, when they land
         __syncwarp();
-        if (lane == 0) mbar_arrive(&hdr_full[buf]);
+        if (lane == 0) mbar_arrive(&hdr_full[buf]);   // the staged stores
       }
       if (lane == 0) {
         const int stage = i % kStages;
@@ -607,6 +622,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
         ++unit;
       }
     }
+    cp_async_wait_all();   // no header copy in flight when the warp exits
     if (lane == 0 && *abort_flag) {
       // leave no copy in flight: wait (bounded) for the stages still loading
       const int first = issued > kStages ? issued - kStages : 0;
