@@ -125,6 +125,13 @@ __device__ __forceinline__ void cp_async_mbar_arrive(uint64_t *bar) {
   asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// load with acquire semantics at GPU scope
+__device__ __forceinline__ int ld_acquire_gpu(const int *ptr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }

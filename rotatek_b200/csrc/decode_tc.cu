@@ -304,11 +304,12 @@ __device__ __forceinline__ void load_header(unsigned char *hdr, const DecodePara
 // heads among them write the same bits as one warp merging them all.
 template <typename T, int KH, int kWarps>
 __device__ __forceinline__ void merge_unit(const DecodeParams &p, int unit, int c_first, int c_last,
-                                           int bk, int head0, int nheads, int lane, int hb = 0) {
+                                           int bk, int head0, int nheads, int lane, int hb = 0,
+                                           bool acquire = true) {
 
   // every partial of the unit is in place: merge them in slot order.
   // Pass 1: lane k holds slot k0 + k; per-head max and normaliser by shuffles.
-  __threadfence();
+  if (acquire) __threadfence();
   const float *s0 = p.partials + (long long)(unit + c_first) * kWarps * p.slot_floats;
   const int nslots = kWarps * (c_last - c_first + 1);
   float mx[KH];
@@ -520,7 +521,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
   uint64_t *hdr_empty = hdr_full + 2;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kFlagOff);
   // the unit whose merge the consumer warps share at the end (unit, c_first,
-  // c_last; unit -1 = none)
+  // c_last, whether the CTA released its partials; unit -1 = none)
   volatile int *pending = abort_flag + 1;
   unsigned char *ring = smem + C::kRingOff;
 
@@ -916,6 +917,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
         }
       }
     }
+    if (seg_end == nblk) break;   // the CTA's last segment: one ticket for all warps, below
     __threadfence();
     __syncwarp();
     int last = 0;
@@ -927,27 +929,41 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
     }
     last = __shfl_sync(0xffffffffu, last, 0);
     if (last) {
-      if (nheads == 1) {
+      if (nheads == 1)
         merge_unit<T, 1, kWarps>(p, unit, c_first, c_last, bk, head0, nheads, lane);
-      } else if (seg_end == nblk) {
-        // the CTA's last segment: every consumer warp is about to finish, so
-        // the unit's heads are merged by all of them below
-        if (lane == 0) {
-          pending[1] = c_first;
-          pending[2] = c_last;
-          pending[0] = unit;
-        }
-      } else {
+      else
         merge_unit<T, kHeads, kWarps>(p, unit, c_first, c_last, bk, head0, nheads, lane);
-      }
     }
     it = seg_end;
     ++unit;
   }
 
-  // ---- shared merge of the last segment's unit: warp cw merges heads
-  //      cw*KS .. cw*KS+KS-1 (every consumer warp reaches this barrier: none
-  //      returns early and every wait above is bounded)
+  // ---- the CTA's last segment (unit `unit`): every consumer warp has stored
+  //      its partial (the barrier: no warp returns early and every wait above
+  //      is bounded).  One ticket for the CTA: when the unit's other CTAs have
+  //      all taken theirs -- the usual case, their pieces came at the start of
+  //      their ranges -- this CTA merges without releasing its own partials to
+  //      the GPU (its warps see them through the barrier), so no warp waits for
+  //      its stores to drain.  Otherwise one fence and one add of W.  The merge
+  //      is shared: warp cw takes heads cw*KS .. cw*KS+KS-1.
+  named_barrier_sync(1, kWarps * 32);
+  if (cw == 0 && lane == 0) {
+    const long long ublk0 = (long long)unit * bpu;
+    const int c_first = static_cast<int>(cta_of_block(ublk0, total, gridDim.x));
+    const int c_last = static_cast<int>(cta_of_block(ublk0 + bpu - 1, total, gridDim.x));
+    const int others = kWarps * (c_last - c_first);
+    bool last = ld_acquire_gpu(&p.tickets[unit]) == others;
+    const bool released = !last;
+    if (!last) {
+      __threadfence();
+      last = atomicAdd(&p.tickets[unit], kWarps) == others;
+    }
+    if (last) p.tickets[unit] = 0;  // ready for the next call
+    pending[1] = c_first;
+    pending[2] = c_last;
+    pending[3] = released;
+    pending[0] = last ? unit : -1;
+  }
   named_barrier_sync(1, kWarps * 32);
   const int pu = pending[0];
   if (pu >= 0) {
@@ -956,9 +972,15 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
     const int kvh = (pu / p.head_chunks) % p.kv_heads;
     const int bk = pu / (p.kv_heads * p.head_chunks);
     const int nheads = min(kHeads, p.groups - hc * kHeads);
-    if (cw * KS < nheads)
-      merge_unit<T, KS, kWarps>(p, pu, pending[1], pending[2], bk, kvh * p.groups + hc * kHeads, nheads, lane,
-                                cw * KS);
+    const int head0 = kvh * p.groups + hc * kHeads;
+    // the acquiring fence only after the CTA's own add; after the acquire load
+    // above the barrier orders every warp's loads
+    const bool acq = pending[3] != 0;
+    if (nheads == 1) {
+      if (cw == 0) merge_unit<T, 1, kWarps>(p, pu, pending[1], pending[2], bk, head0, nheads, lane, 0, acq);
+    } else if (cw * KS < nheads) {
+      merge_unit<T, KS, kWarps>(p, pu, pending[1], pending[2], bk, head0, nheads, lane, cw * KS, acq);
+    }
   }
 }
 
