@@ -186,7 +186,14 @@ struct TcShape {
   int grid;
   int slot_floats;
   int64_t slots;  // one per (unit + cta, consumer warp); <= 5 consumer warps per CTA
+  int phantom;    // blocks each unit counts extra in the split among CTAs
 };
+
+// What a CTA's switch from one unit to the next costs, in blocks of streaming
+// (measured at config 2: ranges that cross a unit start finished ~5 us, about
+// 12 blocks, after those that do not).  Used only where every CTA has at least
+// 16 times as many blocks, so that no range is left without real blocks.
+constexpr int kUnitSwitchBlocks = 12;
 
 TcShape tc_shape(int64_t B, int64_t Hkv, int64_t G, int64_t Sf, int64_t Sv, int device,
                  int64_t vis_tokens = kVisBlockTokens) {
@@ -201,6 +208,7 @@ TcShape tc_shape(int64_t B, int64_t Hkv, int64_t G, int64_t Sf, int64_t Sv, int 
   t.grid = (int)std::max<int64_t>(1, std::min<int64_t>(t.total, sm_count(device)));
   t.slot_floats = 32 + 16 * 128;
   t.slots = (t.units + t.grid) * 5;
+  t.phantom = t.total / t.grid >= 16 * kUnitSwitchBlocks ? kUnitSwitchBlocks : 0;
   return t;
 }
 
@@ -338,6 +346,7 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
     p.blocks_full = (int)t.blocks_full; p.blocks_sparse = (int)t.blocks_sparse;
     p.blocks_per_unit = (int)t.blocks_per_unit;
     p.total_blocks = t.total;
+    p.phantom = t.phantom;
     p.scale_log2 = (float)scale_log2;
     p.q = a.q->data; p.q_sb = a.q->stride[0]; p.q_sh = a.q->stride[1];
     if (!a.dense) {

@@ -16,6 +16,8 @@ struct DecodeParams {
   int head_chunks;                        // ceil(groups / heads_tile)
   int blocks_full, blocks_sparse, blocks_per_unit;
   long long total_blocks;                 // units * blocks_per_unit
+  int phantom;                            // blocks each unit counts extra when the
+                                          // units are split among CTAs (0 = even split)
   float scale_log2;                       // log2(e) / sqrt(head_dim)
   const void *q;  long long q_sb, q_sh;
   const void *R;  long long R_sb, R_sh, R_sd;

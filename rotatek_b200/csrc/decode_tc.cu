@@ -102,10 +102,29 @@ struct Cfg {
   static constexpr int kBytes = kRingOff + kStages * kStageBytes;
 };
 
-__device__ __forceinline__ long long cta_of_block(long long blk, long long total, int grid) {
-  // the CTA whose range [floor(c*T/P), floor((c+1)*T/P)) holds block `blk`
-  return ((blk + 1) * grid - 1) / total;
-}
+// The split of the U * bpu blocks among the CTAs.  A CTA whose range crosses
+// from one unit into the next pays for the switch (partial store and ticket,
+// new query fragments, the new unit's first tiles), so each unit counts `ph`
+// phantom blocks at its start: CTA c takes the virtual blocks
+// [floor(c*Tv/P), floor((c+1)*Tv/P)) of Tv = U * (bpu + ph), and a virtual
+// block maps to the real one at or after it.  ph = 0 is the even split.
+struct Split {
+  long long vtotal;
+  int bpu, ph;
+  __device__ __forceinline__ long long real_of(long long v) const {
+    const long long u = v / (bpu + ph);
+    const long long off = v - u * (bpu + ph) - ph;
+    return u * bpu + (off > 0 ? off : 0);
+  }
+  // [lo, hi) of CTA c
+  __device__ __forceinline__ long long lo(int c, int grid) const { return real_of((long long)c * vtotal / grid); }
+  // the CTA whose range holds real block `blk`
+  __device__ __forceinline__ int cta_of(long long blk) const {
+    const long long u = blk / bpu;
+    const long long v = u * (bpu + ph) + ph + (blk - u * bpu);
+    return static_cast<int>(((v + 1) * gridDim.x - 1) / vtotal);
+  }
+};
 
 // Online softmax over MT 16-token tiles of scores already in log2 units,
 // then O^T += V^T . P^T with P split hi + lo.  `valid[mt][r]` masks row g8 + 8r
@@ -527,11 +546,11 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const long long total = p.total_blocks;
-  const long long lo = (long long)blockIdx.x * total / gridDim.x;
-  const long long hi = (long long)(blockIdx.x + 1) * total / gridDim.x;
-  const int nblk = static_cast<int>(hi - lo);
   const int bpu = p.blocks_per_unit;
+  const Split split{p.total_blocks / bpu * (bpu + p.phantom), bpu, p.phantom};
+  const long long lo = split.lo(blockIdx.x, gridDim.x);
+  const long long hi = split.lo(blockIdx.x + 1, gridDim.x);
+  const int nblk = static_cast<int>(hi - lo);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -897,8 +916,8 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
       }
     }
     const long long ublk0 = (long long)unit * bpu;
-    const int c_first = static_cast<int>(cta_of_block(ublk0, total, gridDim.x));
-    const int c_last = static_cast<int>(cta_of_block(ublk0 + bpu - 1, total, gridDim.x));
+    const int c_first = split.cta_of(ublk0);
+    const int c_last = split.cta_of(ublk0 + bpu - 1);
     float *slot = p.partials + ((long long)(unit + blockIdx.x) * kWarps + cw) * p.slot_floats;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -949,8 +968,8 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
   named_barrier_sync(1, kWarps * 32);
   if (cw == 0 && lane == 0) {
     const long long ublk0 = (long long)unit * bpu;
-    const int c_first = static_cast<int>(cta_of_block(ublk0, total, gridDim.x));
-    const int c_last = static_cast<int>(cta_of_block(ublk0 + bpu - 1, total, gridDim.x));
+    const int c_first = split.cta_of(ublk0);
+    const int c_last = split.cta_of(ublk0 + bpu - 1);
     const int others = kWarps * (c_last - c_first);
     bool last = ld_acquire_gpu(&p.tickets[unit]) == others;
     const bool released = !last;
