@@ -104,6 +104,24 @@ __device__ __forceinline__ void tma_load_4d(void *smem_dst, const CUtensorMap *m
       : "memory");
 }
 
+// tma_load_4d with an L2 cache policy (createpolicy) for the copied lines
+__device__ __forceinline__ void tma_load_4d_hint(void *smem_dst, const CUtensorMap *map, int c0, int c1,
+                                                 int c2, int c3, uint64_t *bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// L2 policy: lines read once, first to go when L2 needs room
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 // 16-byte global -> shared copy that bypasses registers (both addresses 16-B aligned).
 __device__ __forceinline__ void cp_async_16(void *smem_dst, const void *gmem_src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src)

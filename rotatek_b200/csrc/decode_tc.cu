@@ -577,6 +577,9 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
     int unit = static_cast<int>(lo / bpu);
     int j = static_cast<int>(lo - (long long)unit * bpu);
     int seg = -1, bk = 0, kvh = 0, issued = 0;
+    // K/V tiles are read once: let them leave L2 first, so that the split
+    // partials (written early, merged at the end) stay there
+    const uint64_t stream_pol = l2_evict_first_policy();
     for (int i = 0; i < nblk; ++i) {
       if (i == 0 || j == 0) {
         // a new unit: its header goes into buffer seg % kNB once the consumers
@@ -607,31 +610,31 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
           if (j < p.blocks_full) {
             const int tok = j * kFullTokens;
             mbar_arrive_expect_tx(&full_bar[stage], 4 * kFullBoxBytes);
-            tma_load_4d(st, &tm_kf, 0, tok, kvh, bk, &full_bar[stage]);
-            tma_load_4d(st + kFullBoxBytes, &tm_kf, 64, tok, kvh, bk, &full_bar[stage]);
-            tma_load_4d(st + 2 * kFullBoxBytes, &tm_vf, 0, tok, kvh, bk, &full_bar[stage]);
-            tma_load_4d(st + 3 * kFullBoxBytes, &tm_vf, 64, tok, kvh, bk, &full_bar[stage]);
+            tma_load_4d_hint(st, &tm_kf, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
+            tma_load_4d_hint(st + kFullBoxBytes, &tm_kf, 64, tok, kvh, bk, &full_bar[stage], stream_pol);
+            tma_load_4d_hint(st + 2 * kFullBoxBytes, &tm_vf, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
+            tma_load_4d_hint(st + 3 * kFullBoxBytes, &tm_vf, 64, tok, kvh, bk, &full_bar[stage], stream_pol);
           } else if constexpr (SPARK) {
             // Values, kept values and kept channel indices; the Keys are rebuilt
             // by the consumer in the first 2 * kFullBoxBytes
             const int tok = (j - p.blocks_full) * kFullTokens;
             mbar_arrive_expect_tx(&full_bar[stage], 2 * kFullBoxBytes + kFullTokens * DK * 3);
-            tma_load_4d(st + 2 * kFullBoxBytes, &tm_vs, 0, tok, kvh, bk, &full_bar[stage]);
-            tma_load_4d(st + 3 * kFullBoxBytes, &tm_vs, 64, tok, kvh, bk, &full_bar[stage]);
-            tma_load_4d(st + C::kSpValOff, &tm_ks, 0, tok, kvh, bk, &full_bar[stage]);
-            tma_load_4d(st + C::kSpIdxOff, &tm_ki, 0, tok, kvh, bk, &full_bar[stage]);
+            tma_load_4d_hint(st + 2 * kFullBoxBytes, &tm_vs, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
+            tma_load_4d_hint(st + 3 * kFullBoxBytes, &tm_vs, 64, tok, kvh, bk, &full_bar[stage], stream_pol);
+            tma_load_4d_hint(st + C::kSpValOff, &tm_ks, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
+            tma_load_4d_hint(st + C::kSpIdxOff, &tm_ki, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
           } else {
             const int tok = (j - p.blocks_full) * kVisTokens;
             if constexpr (FP8) {
               // e4m3 tiles at the places convert_fp8_stage reads them from
               mbar_arrive_expect_tx(&full_bar[stage], kVisTokens * DK + kVisBoxBytes);
-              tma_load_4d(st + C::kKsBytes / 2, &tm_ks, 0, tok, kvh, bk, &full_bar[stage]);
-              tma_load_4d(st + C::kKsBytes + kVisBoxBytes, &tm_vs, 0, tok, kvh, bk, &full_bar[stage]);
+              tma_load_4d_hint(st + C::kKsBytes / 2, &tm_ks, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
+              tma_load_4d_hint(st + C::kKsBytes + kVisBoxBytes, &tm_vs, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
             } else {
               mbar_arrive_expect_tx(&full_bar[stage], C::kKsBytes + 2 * kVisBoxBytes);
-              tma_load_4d(st, &tm_ks, 0, tok, kvh, bk, &full_bar[stage]);
-              tma_load_4d(st + C::kKsBytes, &tm_vs, 0, tok, kvh, bk, &full_bar[stage]);
-              tma_load_4d(st + C::kKsBytes + kVisBoxBytes, &tm_vs, 64, tok, kvh, bk, &full_bar[stage]);
+              tma_load_4d_hint(st, &tm_ks, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
+              tma_load_4d_hint(st + C::kKsBytes, &tm_vs, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
+              tma_load_4d_hint(st + C::kKsBytes + kVisBoxBytes, &tm_vs, 64, tok, kvh, bk, &full_bar[stage], stream_pol);
             }
           }
           ++issued;
