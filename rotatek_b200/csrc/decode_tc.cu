@@ -12,18 +12,20 @@
 //            once per group, not once per query head.
 //   block  = 32 prompt/text tokens or 64 visual tokens of one unit: first the
 //            ceil(S_f/32) full-width blocks, then the ceil(S_v/64) visual ones.
-//   The U * blocks_per_unit blocks are cut into `grid` equal contiguous ranges,
-//   one per CTA (one CTA per SM).  Inside a CTA, block i goes to consumer warp
-//   i % W and ring stage i % S (S a multiple of W: every stage belongs to one
-//   warp, so its parity waits are exact).
+//   The U * blocks_per_unit blocks are cut into `grid` contiguous ranges, one
+//   per CTA (one CTA per SM), equal except that a range holding a unit start
+//   gives up a few blocks for the switch (`Split`).  Inside a CTA, block i goes
+//   to consumer warp i % W and ring stage i % S (S a multiple of W: every stage
+//   belongs to one warp, so its parity waits are exact).
 //
 // Warps: one producer, W consumers, no CTA-wide barrier after the prologue.
 //   producer  streams each block's K and V tiles with 4-D TMA tensor copies
-//             (128B/64B/32B swizzle, no multicast) into a ring of ~20 KB stages
-//             sized to fill shared memory (10 stages = 200 KB in flight per SM
-//             at D_keep <= 32); at every unit change its lanes also copy the
-//             unit's query rows, R, delta_mu and mask row into a double-buffered
-//             header.
+//             (128B/64B/32B swizzle, no multicast, L2 evict-first: read once)
+//             into a ring of ~20 KB stages sized to fill shared memory (10
+//             stages = 200 KB in flight per SM at D_keep <= 32); at every unit
+//             change its lanes also start cp.async copies of the unit's query
+//             rows, R, delta_mu and mask row into a double-buffered header,
+//             which arrive on the header's barrier as they land.
 //   consumer  builds its own query fragments from the header -- q~^T = R^T q^T
 //             on the tensor cores, split into a 16-bit hi + lo pair -- then for
 //             each of its blocks
