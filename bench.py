@@ -1021,9 +1021,7 @@ def run_e2e(args):
         del x
         model.init_decode(logits.argmax(-1))
         model.decode_step()                      # warm-up (workspaces); token 1
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            model.decode_step()
+        g = model.capture_decode_graph()
         steps = cfg.max_new_tokens - 1
         sampler = ClockSampler(0)
         with sampler:

@@ -113,7 +113,9 @@ int rtk_rotatek_decode(const rtk_tensor *q_full, const rtk_tensor *R_partial,
  * call on a device resolves the array's address (cudaGetSymbolAddress): make
  * it before any stream capture.  All calls on a device share the array; each
  * clears its counters first, and calls that overlap on the GPU race.
- * Arguments, outputs and errors are those of rtk_rotatek_decode.             */
+ * Arguments, outputs and errors are those of rtk_rotatek_decode; the device
+ * status of these calls accumulates in the array's status word, which
+ * rtk_read_static_status reads.                                              */
 int rtk_rotatek_decode_static(const rtk_tensor *q_full, const rtk_tensor *R_partial,
                               const rtk_tensor *delta_mu, const rtk_tensor *k_full,
                               const rtk_tensor *v_full, const rtk_tensor *mask_full,
@@ -302,6 +304,19 @@ int rtk_build_rotation_projected(const rtk_tensor *hidden, const rtk_tensor *w_k
 /* Copy the workspace's device-status word to *status (RTK_DEVICE_TIMEOUT bits)
  * and clear it.  Synchronises `stream`.                                       */
 int rtk_read_status(void *workspace, void *stream, uint32_t *status);
+
+/* rtk_read_status for rtk_rotatek_decode_static's fixed scratch on the current
+ * device: the status bits its calls set since the last read, then cleared.
+ * No counterpart in the reference.  Synchronises `stream`.                    */
+int rtk_read_static_status(void *stream, uint32_t *status);
+
+/* Diagnostic, no counterpart in the reference: launches one small kernel that
+ * waits on an mbarrier nothing arrives on, with the bounded wait every kernel
+ * here uses and a limit of limit_ns (at most 2e9) nanoseconds.  The wait gives
+ * up, RTK_DEVICE_TIMEOUT is ORed into the status word at `workspace` (read it
+ * with rtk_read_status), and the kernel returns: the error path of a lost TMA
+ * transaction, without a copy in flight.                                      */
+int rtk_selftest_wait_timeout(void *workspace, uint64_t limit_ns, void *stream);
 
 #ifdef __cplusplus
 }

@@ -61,6 +61,8 @@ SIGNATURES = {
                                                               ctypes.c_int64, ctypes.c_int64] + [_P] * 5 +
                                      [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "rtk_read_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
+    "rtk_read_static_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
+    "rtk_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]),
 }
 
 _lib = None
@@ -162,3 +164,23 @@ def read_status(device: Optional[torch.device] = None) -> int:
     check(load().rtk_read_status(ctypes.c_void_p(buf.data_ptr()), ctypes.c_void_p(stream),
                                  ctypes.byref(out)))
     return out.value
+
+
+def read_static_status() -> int:
+    """Device-status bits that rtk_rotatek_decode_static's calls on the current
+    device set since the last read (its fixed scratch's status word); clears them."""
+    out = ctypes.c_uint32(0)
+    stream = torch.cuda.current_stream().cuda_stream
+    check(load().rtk_read_static_status(ctypes.c_void_p(stream), ctypes.byref(out)))
+    return out.value
+
+
+def selftest_wait_timeout(limit_ns: int = 1_000_000, device: Optional[torch.device] = None) -> None:
+    """Run the bounded-wait self-test kernel against this device's decode
+    workspace: its wait on a barrier nothing arrives on gives up after
+    ``limit_ns`` and sets RTK_DEVICE_TIMEOUT, which ``read_status`` then reports."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    buf = workspace(dev, 1 << 20, 256)
+    stream = torch.cuda.current_stream(buf.device).cuda_stream
+    check(load().rtk_selftest_wait_timeout(ctypes.c_void_p(buf.data_ptr()), ctypes.c_uint64(limit_ns),
+                                           ctypes.c_void_p(stream)))

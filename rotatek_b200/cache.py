@@ -74,6 +74,12 @@ class SpanKVCache:
         v[:, :, :s_p].copy_(value_states[:, :, :s_p])
         v[:, :, s_p:s_p + s_t].copy_(value_states[:, :, s_p + s_v:])
         v[:, :, s_p + t_max:].copy_(value_states[:, :, s_p:s_p + s_v])
+        # The text slots not written yet are read by static_decode_args' full-capacity
+        # views and only masked out of the logits: the P.V product still multiplies
+        # their Values by a zero weight, so they must hold finite numbers (0 * NaN
+        # is NaN).  Zero them once here.
+        kf[:, :, s_p + s_t:].zero_()
+        v[:, :, s_p + s_t:s_p + t_max].zero_()
         if layer_idx == 0:
             self._seen_tokens += s_p + s_v + s_t
         self.layers.append(_Layer(kf, v, key_states_pruned.contiguous(), rotation, delta_mu, s_p, s_v, s_t, t_max))

@@ -64,9 +64,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // Wait for phase `parity` of `bar` to complete.  Returns false -- without
 // having waited for the phase -- once `*abort` is set (by this or another warp)
 // or the time limit passes; on a timeout it sets `*abort` and ORs
-// RTK_DEVICE_TIMEOUT into `*status`.
+// RTK_DEVICE_TIMEOUT into `*status`.  `limit_ns` is kWaitLimitNs everywhere but
+// in the self-test kernel, which runs a wait out on purpose.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
-                                                  volatile int *abort, unsigned int *status) {
+                                                  volatile int *abort, unsigned int *status,
+                                                  unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   // the clock is read only after many unsuccessful polls, so ordinary waits
   // never pay for it; the limit counts from that first reading
@@ -78,7 +80,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
       const unsigned long long now = globaltimer_ns();
       if (t0 == 0) {
         t0 = now;
-      } else if (now - t0 > kWaitLimitNs) {
+      } else if (now - t0 > limit_ns) {
         *abort = 1;
         atomicOr(status, 1u);
         return false;

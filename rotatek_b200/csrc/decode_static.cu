@@ -18,9 +18,14 @@
 //    (cudaGetSymbolAddress, with that device current) and caches it; make that
 //    first call before any stream capture.
 //  * Every call on a device shares the one array and leaves its contents for
-//    the next call; each call first clears the counter bytes that must start
-//    at zero (an async memset on the caller's stream).  Calls that overlap on
-//    the GPU -- different streams without ordering -- race on the array.
+//    the next call; each call first clears the ticket counters, which must
+//    start at zero (an async memset on the caller's stream).  Calls that
+//    overlap on the GPU -- different streams without ordering -- race on the
+//    array.
+//  * The array's first 256 bytes are the device-status word of rtk_read_status
+//    (RTK_DEVICE_TIMEOUT when a bounded wait gave up).  It is cleared once, by
+//    the first call on the device, and then keeps what the calls set until
+//    rtk_read_static_status reads and clears it.
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -38,16 +43,22 @@ constexpr int kMaxDevices = 64;
 // its device address comes from cudaGetSymbolAddress (per device).
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
+// The status word (and the counters after it) start at zero on each device.
+constexpr size_t kStatusBytes = 256;
+
 // Device address of the scratch on `device` (the current device), looked up
-// once per device and cached.
-cudaError_t scratch_address(int device, void **out) {
+// once per device and cached.  The first lookup also clears the status word,
+// on `stream`.
+cudaError_t scratch_address(int device, cudaStream_t stream, void **out) {
   static std::mutex mu;
   static void *addr[kMaxDevices] = {nullptr};
   if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(mu);
   if (addr[device] == nullptr) {
     void *p = nullptr;
-    const cudaError_t err = cudaGetSymbolAddress(&p, g_static_scratch);
+    cudaError_t err = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (err != cudaSuccess) return err;
+    err = cudaMemsetAsync(p, 0, kStatusBytes, stream);
     if (err != cudaSuccess) return err;
     addr[device] = p;
   }
@@ -91,13 +102,29 @@ extern "C" int rtk_rotatek_decode_static(const rtk_tensor *q_full, const rtk_ten
     return rtk::report_error(RTK_ERR_WORKSPACE, buf);
   }
   void *scratch = nullptr;
-  err = scratch_address(device, &scratch);
+  err = scratch_address(device, static_cast<cudaStream_t>(stream), &scratch);
   if (err != cudaSuccess) return cuda_error("cudaGetSymbolAddress", err);
-  // the status word and ticket counters must start at zero; the rest is
-  // overwritten by the kernels
-  const size_t zero = rtk::decode_counter_bytes(q_full->shape[0], q_full->shape[1]);
-  err = cudaMemsetAsync(scratch, 0, zero < need ? zero : need, static_cast<cudaStream_t>(stream));
-  if (err != cudaSuccess) return cuda_error("clearing the counters", err);
+  // the ticket counters after the status word must start at zero; the status
+  // word keeps what earlier calls set until rtk_read_static_status; the rest
+  // is overwritten by the kernels
+  size_t zero = rtk::decode_counter_bytes(q_full->shape[0], q_full->shape[1]);
+  if (zero > need) zero = need;
+  if (zero > kStatusBytes) {
+    err = cudaMemsetAsync(static_cast<unsigned char *>(scratch) + kStatusBytes, 0, zero - kStatusBytes,
+                          static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_error("clearing the counters", err);
+  }
   return rtk_rotatek_decode(q_full, R_partial, delta_mu, k_full, v_full, mask_full, k_sparse,
                             v_sparse, num_kv_groups, out, scratch, kStaticScratchBytes, stream);
+}
+
+extern "C" int rtk_read_static_status(void *stream, uint32_t *status) {
+  if (status == nullptr) return rtk::report_error(RTK_ERR_INVALID, "status must be non-NULL");
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return cuda_error("cudaGetDevice", err);
+  void *scratch = nullptr;
+  err = scratch_address(device, static_cast<cudaStream_t>(stream), &scratch);
+  if (err != cudaSuccess) return cuda_error("cudaGetSymbolAddress", err);
+  return rtk_read_status(scratch, stream, status);
 }

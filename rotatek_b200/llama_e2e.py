@@ -167,12 +167,23 @@ class RandomLlamaDecoder:
     # ------------------------------------------------------------------ decode
     def init_decode(self, first_token: torch.Tensor):
         """Static decode state after prefill: token [B], RoPE position, cache slot
-        and the text-span mask, all on the device."""
+        and the text-span mask, all on the device.  The cache has room for
+        ``max_new_tokens`` appends; ``steps`` counts the steps run on the host."""
         c = self.cfg
         self.token = first_token.view(-1).clone()
         self.pos = torch.tensor([self.seq_len], device=self.device, dtype=torch.long)
         self.slot = torch.tensor([c.prompt + c.text], device=self.device, dtype=torch.long)
+        self._slot_last = c.prompt + c.text + c.max_new_tokens - 1
         self.mask = self.cache.capacity_mask(0)
+        self.steps = StepBudget(c.max_new_tokens)
+
+    def capture_decode_graph(self) -> "DecodeGraph":
+        """``decode_step`` captured in a CUDA graph; each ``replay`` is one step and
+        counts against the cache's room like an eager step."""
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            logits = self.decode_step()
+        return DecodeGraph(g, logits, self.steps)
 
     @torch.no_grad()
     def decode_step(self) -> torch.Tensor:
@@ -180,15 +191,21 @@ class RandomLlamaDecoder:
         next token into it, advances the device position / slot / mask.
         Static shapes only (CUDA-graph capturable).  Returns the logits."""
         c = self.cfg
+        if not torch.cuda.is_current_stream_capturing():
+            self.steps.take()          # a captured step is counted at each replay
         b = self.token.shape[0]
         x = self.embed[self.token].view(b, 1, c.hidden)
         cos, sin = self.cos.index_select(0, self.pos), self.sin.index_select(0, self.pos)
-        self.mask.index_fill_(1, self.slot, 1)
+        # the host count above keeps the slot in range; the clamp keeps a replay
+        # that bypassed it from indexing past the text capacity into the Values'
+        # visual span (or out of the tensor)
+        slot = self.slot.clamp_max(self._slot_last)
+        self.mask.index_fill_(1, slot, 1)
         groups = c.heads // c.kv_heads
         for li, L in enumerate(self.layers):
             q, k, v = self._qkv(L, x)
             q, k = self._rope(q, cos, sin), self._rope(k, cos, sin)
-            self.cache.write_at(k, v, li, self.slot)
+            self.cache.write_at(k, v, li, slot)
             o, _, _ = rotatek_decode(q_full=q[:, :, 0], num_kv_groups=groups,
                                      **self.cache.static_decode_args(li, self.mask))
             x = x + F.linear(o.view(b, 1, -1), L["wo"])
@@ -210,4 +227,31 @@ class RandomLlamaDecoder:
         return per_layer * c.layers
 
 
-__all__ = ["DecoderConfig", "RandomLlamaDecoder"]
+class StepBudget:
+    """Host-side count of the decode steps a cache has room for: ``take`` raises
+    once ``limit`` steps have run, before the step writes past the text span."""
+
+    def __init__(self, limit: int):
+        self.limit = limit
+        self.used = 0
+
+    def take(self) -> None:
+        if self.used >= self.limit:
+            raise RuntimeError(f"decode step {self.used + 1} exceeds max_new_tokens={self.limit}: "
+                               "the cache has no room for another token")
+        self.used += 1
+
+
+class DecodeGraph:
+    """A captured decode step.  ``replay`` checks the step budget first."""
+
+    def __init__(self, graph: "torch.cuda.CUDAGraph", logits: torch.Tensor, steps: StepBudget):
+        self.graph, self.logits, self.steps = graph, logits, steps
+
+    def replay(self) -> torch.Tensor:
+        self.steps.take()
+        self.graph.replay()
+        return self.logits
+
+
+__all__ = ["DecoderConfig", "RandomLlamaDecoder", "StepBudget", "DecodeGraph"]

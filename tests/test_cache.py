@@ -83,3 +83,36 @@ def test_gpu_decode_through_cache_is_bit_identical(dtype):
                                     mask_full=torch.ones(B, kf.shape[2], dtype=torch.uint8, device="cuda"),
                                     k_sparse=k_rot, v_sparse=vs, num_kv_groups=HQ // HKV)
         assert torch.equal(got, want)
+
+
+def test_capacity_slots_zeroed_at_store():
+    """Text slots past the stored tokens hold zeros, whatever the allocator
+    handed out: the full-capacity decode views read them (masked logits, but
+    their Values still enter P.V with weight 0, and 0 * NaN is NaN)."""
+    k_prompt, k_text, k_rot, values, R, dm = _prefill()
+    cache = SpanKVCache(max_new_tokens=7)
+    empty = torch.empty
+    torch.empty = lambda *a, **k: empty(*a, **k).fill_(float("nan"))  # uninitialised = NaN
+    try:
+        cache.store_pruned(k_rot, k_prompt, k_text, values, R, dm, 0)
+    finally:
+        torch.empty = empty
+    L = cache.layers[0]
+    cap = L.s_prompt + L.t_max
+    assert not torch.isnan(L.keys_full).any() and not torch.isnan(L.values).any()
+    assert torch.count_nonzero(L.keys_full[:, :, SP + ST:cap]) == 0
+    assert torch.count_nonzero(L.values[:, :, SP + ST:cap]) == 0
+    args = cache.static_decode_args(0, cache.capacity_mask(0))
+    assert args["k_full"].shape[2] == cap and args["mask_full"].shape == (B, cap)
+
+
+def test_step_budget_raises_past_capacity():
+    """The e2e decoder's host-side step count: the (max_new_tokens + 1)-th step
+    raises before it would write past the cache's text capacity."""
+    from rotatek_b200.llama_e2e import StepBudget
+    budget = StepBudget(3)
+    for _ in range(3):
+        budget.take()
+    with pytest.raises(RuntimeError, match="exceeds max_new_tokens=3"):
+        budget.take()
+    assert budget.used == 3

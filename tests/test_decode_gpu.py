@@ -280,3 +280,94 @@ def test_think_decode_matches_recovered_dense(dtype, G):
     rel = 2.0 ** -8 if dtype == torch.bfloat16 else 1e-5
     tol = (2e-3 if dtype == torch.bfloat16 else 1e-5) + rel * np.abs(want).max()
     np.testing.assert_allclose(got.float().cpu().numpy(), want, rtol=0, atol=tol)
+
+
+def _rows(kw, rows):
+    """The decode arguments restricted to batch rows `rows`, on the CPU (batch
+    rows are independent units, so the oracle of a subset is a subset of the oracle)."""
+    idx = torch.as_tensor(rows, device=DEV)
+    out = {}
+    for k, x in kw.items():
+        out[k] = x.index_select(0, idx).cpu() if torch.is_tensor(x) else x
+    return out
+
+
+@pytest.mark.parametrize("sf", [1025, 3000])
+def test_decode_long_masked_full_span(sf):
+    """Prompt/text spans longer than the kernel's 1024-byte header mask: the
+    mask is read per token from global memory (fused_decode.py:254-258 honours
+    it at any length).  ~40 % of the tokens masked, plus a row with none kept."""
+    d = make(torch.bfloat16, 3, 28, 4, 2000, sf, seed=40 + sf)
+    g = torch.Generator(device=DEV).manual_seed(sf)
+    mask = (torch.rand(3, sf, generator=g, device=DEV) < 0.6).to(torch.uint8)
+    mask[2].zero_()
+    run_and_check(d, torch.bfloat16, mask=mask)
+    assert_status_clean()
+
+
+@pytest.mark.parametrize("sf", [333, 1024, 1500])
+def test_decode_strided_mask(sf):
+    """mask_full as a strided view (every other column of a wider buffer) and as
+    an unaligned slice: the header's register-staged path (S_f <= 1024) and the
+    global-memory path (S_f > 1024)."""
+    d = make(torch.bfloat16, 2, 28, 4, 900, sf, seed=sf, bias=False)
+    g = torch.Generator(device=DEV).manual_seed(7 + sf)
+    wide = (torch.rand(2, 2 * sf + 3, generator=g, device=DEV) < 0.55).to(torch.uint8)
+    strided = wide[:, 1:1 + 2 * sf:2]
+    assert strided.stride(-1) == 2
+    run_and_check(d, torch.bfloat16, mask=strided)
+    shifted = wide[:, 3:3 + sf]
+    assert shifted.data_ptr() % 16 != 0
+    run_and_check(d, torch.bfloat16, mask=shifted)
+    assert_status_clean()
+
+
+def test_decode_config5_shape():
+    """Benchmark config 5 on one GPU at full size: B=64, 64 query / 8 KV heads
+    (G=8), 64 prompt + 31 744 visual + 960 text tokens (S_f = 1024, the header
+    mask's limit), keep 32, bf16, with a partial mask.  Four batch rows, spread
+    over the batch, are checked against the float64 oracle."""
+    d = make(torch.bfloat16, 64, 64, 8, 31744, 1024, seed=72)
+    g = torch.Generator(device=DEV).manual_seed(72)
+    mask = (torch.rand(64, 1024, generator=g, device=DEV) < 0.9).to(torch.uint8)
+    kw = {**d.as_kwargs(), "mask_full": mask}
+    out, _, _ = rotatek_decode(**kw)
+    rows = [0, 21, 42, 63]
+    want = odec.rotatek_decode(**_rows(kw, rows))
+    check(out[rows], want, torch.bfloat16)
+    assert torch.isfinite(out).all()
+    assert_status_clean()
+
+
+def test_decode_config3_layer_shape():
+    """One layer of benchmark config 3 at full size: fp16, 32 query = 32 KV heads
+    (G=1, MHA), batch 8, 16 384 visual tokens, and the span-split cache's
+    prompt | text capacity (32 + 128 tokens) with the unwritten text slots
+    masked, as a CUDA-graph decode step passes them.  Three rows checked."""
+    sp, cap = 32, 128
+    d = make(torch.float16, 8, 32, 32, 16384, sp + cap, seed=33)
+    mask = torch.zeros(8, sp + cap, dtype=torch.uint8, device=DEV)
+    mask[:, :sp + 40] = 1            # 40 text tokens written so far
+    kw = {**d.as_kwargs(), "mask_full": mask}
+    out, _, _ = rotatek_decode(**kw)
+    rows = [0, 3, 7]
+    want = odec.rotatek_decode(**_rows(kw, rows))
+    check(out[rows], want, torch.float16)
+    assert_status_clean()
+
+
+def test_bounded_wait_timeout_is_reported_and_recoverable():
+    """The error path of every bounded wait: a wait on an mbarrier that nothing
+    arrives on (no copy in flight) gives up after 1 ms, the kernel returns,
+    rtk_read_status reports RTK_DEVICE_TIMEOUT once and clears it, and the
+    next decode on the same workspace and context matches the oracle."""
+    d = make(torch.bfloat16, 2, 28, 4, 700, 90, seed=123)
+    run_and_check(d, torch.bfloat16)                 # the device's workspace exists
+    assert_status_clean()
+    _lib.selftest_wait_timeout(limit_ns=1_000_000)
+    assert _lib.read_status() == _lib.RTK_DEVICE_TIMEOUT
+    assert _lib.read_status() == 0                   # read clears it
+    run_and_check(d, torch.bfloat16)
+    assert_status_clean()
+    with pytest.raises(ValueError, match="limit_ns"):
+        _lib.selftest_wait_timeout(limit_ns=0)

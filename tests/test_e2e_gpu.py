@@ -27,18 +27,60 @@ def test_graph_replay_matches_eager():
     toks_eager = m.token.clone()
     m = _model()
     first = m.decode_step().clone()              # warm-up: workspaces, cuBLAS handles
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        out = m.decode_step()
+    g = m.capture_decode_graph()
     got = [first]
     for _ in range(2):
-        g.replay()
-        got.append(out.clone())
+        got.append(g.replay().clone())
     torch.cuda.synchronize()
     for a, b in zip(eager, got):
         assert torch.equal(a, b)
     assert torch.equal(toks_eager, m.token)
+    # the cache holds max_new_tokens = 4 appends: one more replay, then no more
+    g.replay()
+    with pytest.raises(RuntimeError, match="exceeds max_new_tokens"):
+        g.replay()
+    with pytest.raises(RuntimeError, match="exceeds max_new_tokens"):
+        m.decode_step()
+    torch.cuda.synchronize()
+    assert int(m.slot) == CFG.prompt + CFG.text + CFG.max_new_tokens
     del g
+
+
+def test_unwritten_text_slots_cannot_poison_the_output(monkeypatch):
+    """The full-capacity decode views cover text slots not written yet; they
+    are masked out of the logits, and the cache zeroes them so that the P.V
+    product never multiplies a leftover NaN by its zero weight.  NaN put into
+    the memory the cache is about to take must not reach the output."""
+    from rotatek_b200.cache import SpanKVCache
+    from rotatek_b200.kernels import rotatek_decode
+    # every tensor the cache takes uninitialised starts as NaN here
+    store, empty = SpanKVCache.store_pruned, torch.empty
+
+    def nan_empty(*a, **k):
+        return empty(*a, **k).fill_(float("nan"))
+
+    def poisoned_store(self, *a, **k):
+        torch.empty = nan_empty
+        try:
+            return store(self, *a, **k)
+        finally:
+            torch.empty = empty
+
+    monkeypatch.setattr(SpanKVCache, "store_pruned", poisoned_store)
+    m = RandomLlamaDecoder(CFG, "cuda", seed=0)
+    logits = m.prefill(m.prompt_embeddings(2, seed=1))
+    m.init_decode(logits.argmax(-1))
+    L = m.cache.layers[0]
+    cap = L.s_prompt + L.t_max
+    assert torch.count_nonzero(L.keys_full[:, :, L.s_prompt + L.s_text:cap]) == 0
+    assert torch.count_nonzero(L.values[:, :, L.s_prompt + L.s_text:cap]) == 0
+    q = torch.randn(2, CFG.heads, CFG.head_dim, device="cuda", dtype=CFG.dtype)
+    args = m.cache.static_decode_args(0, m.mask)
+    out, _, _ = rotatek_decode(q_full=q, num_kv_groups=1, **args)
+    assert torch.isfinite(out).all()
+    want = odec.rotatek_decode(q_full=q, num_kv_groups=1, **args)
+    np.testing.assert_allclose(out.float().cpu().numpy(), want, rtol=0,
+                               atol=1e-3 + 2.0 ** -10 * np.abs(want).max())
 
 
 def test_layer_attention_matches_oracle():

@@ -43,6 +43,7 @@ def test_static_entry_matches_workspace_entry(dtype, B, Hq, Hkv, Sv, Sf):
         got = out.float().cpu().numpy()
         ref = want.float().cpu().numpy()
         assert np.all(np.abs(got - ref) <= atol + rtol * np.abs(ref))
+        assert _lib.read_static_status() == 0       # no bounded wait gave up
     torch.cuda.synchronize()
 
 
