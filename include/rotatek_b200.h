@@ -214,12 +214,13 @@ int rtk_rotate_keys(const rtk_tensor *keys, const rtk_tensor *R, const rtk_tenso
                     size_t workspace_bytes, void *stream);
 
 /* Bytes of workspace rtk_eigh_topk needs for n matrices: a 256-byte head (as
- * in the build workspace) and the solver's rotation log, about 0.93 MiB per
- * matrix.  No zeroing required. */
+ * in the build workspace); the solver keeps everything else in shared memory.
+ * No zeroing required. */
 size_t rtk_eigh_topk_workspace_size(int64_t n);
 
 /* Top-k eigenvectors of symmetric matrices, descending eigenvalue, each
- * column's largest-magnitude component positive (batched 128 x 128 Jacobi).
+ * column's largest-magnitude component positive (batched 128 x 128 solver:
+ * Householder tridiagonalisation, Sturm multisection, inverse iteration).
  * Replaces rotatek.rotation.power_iteration_gpu (rotatek/rotation.py:68-91),
  * which returns an unconverged basis of approximately the same subspace.
  *   cov [N, 128, 128] f32 contiguous, vecs_out [N, 128, k] f32,
@@ -231,7 +232,7 @@ int rtk_eigh_topk(const rtk_tensor *cov, int64_t k, const rtk_tensor *vecs_out,
 /* Bytes of workspace rtk_build_rotation needs: a device-status word in the
  * first 256 bytes (zero it once before first use; rtk_read_status reads and
  * clears it, a bounded wait that gave up sets RTK_DEVICE_TIMEOUT), then the
- * fp32 sums and the eigensolver's rotation log, about 1 MiB per (b, h). */
+ * fp32 sums (Sum k k^T and Sum k), 66 KB per (b, h). */
 size_t rtk_build_rotation_workspace_size(int64_t batch, int64_t kv_heads, int64_t head_dim);
 
 /* The RotateK prefill build for one layer: replaces the body of

@@ -20,7 +20,7 @@ CSRC = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(CSRC)
 REPO = os.path.dirname(PKG)
 LIB_NAME = "librotatek_b200.so"
-SOURCES = ["capi.cu", "decode_tc.cu", "decode_simt.cu", "decode_static.cu", "quant_fp8.cu", "spark_pack.cu", "cov_tc.cu", "kproj_tc.cu", "jacobi.cu",
+SOURCES = ["capi.cu", "decode_tc.cu", "decode_simt.cu", "decode_static.cu", "quant_fp8.cu", "spark_pack.cu", "cov_tc.cu", "kproj_tc.cu", "eigen.cu",
            "rotate.cu", "selftest.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

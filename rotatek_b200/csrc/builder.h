@@ -1,5 +1,5 @@
-// Parameters of the prefill rotation-builder kernels (covariance, Jacobi
-// eigensolver + top-k + delta_mu, rotation of the visual Keys).
+// Parameters of the prefill rotation-builder kernels (covariance, eigensolver
+// + top-k + delta_mu, rotation of the visual Keys).
 #pragma once
 
 #include <cuda.h>
@@ -71,15 +71,11 @@ int kproj_max_clusters(int dtype_is_bf16);
 cudaError_t launch_kproj_tc(int dtype_is_bf16, const KProjMaps &maps, const KProjParams &p,
                             cudaStream_t stream);
 
-// Jacobi rotation log: the (c, s) of every rotation of every sweep, per matrix,
-// so that only the selected eigenvectors are ever formed.
-constexpr int kJacobiMaxSweeps = 15;
-constexpr size_t kJacobiLogBytes = sizeof(float2) * kJacobiMaxSweeps * (kBuildDim - 1) * (kBuildDim / 2);
-
 // Eigensolver: per matrix, the covariance (centred if ksum is given), optionally
-// weighted by the query norms, diagonalised by cyclic Jacobi; the top `keep`
-// eigenvectors (descending eigenvalue) go out as R, plus delta_mu.
-struct JacobiParams {
+// weighted by the query norms, reduced to tridiagonal form by Householder
+// reflections; the top `keep` eigenvectors (descending eigenvalue) go out as R,
+// plus delta_mu.  No global scratch.
+struct EighParams {
   int nmat, heads;              // matrix m = b * heads + h
   const float *cov;             // [nmat][128][128]
   const float *ksum;            // [nmat][128] or NULL: `cov` is already the matrix to solve
@@ -89,17 +85,13 @@ struct JacobiParams {
   const void *q; int q_dtype; long long q_s[4];  // [B, H_q, W, 128]
   int window, groups;
   // outputs
-  int keep;
+  int keep;                                       // 1..128
   void *R; int R_dtype; long long R_s[4];        // [B, H, 128, keep]
   void *dm; long long dm_s[3];                    // [B, H, 128] (R's dtype), nullable
   float *evals;                                   // [nmat][128] descending, nullable
-  int *sweeps;                                    // [nmat] sweeps used, nullable
-  float2 *rot_log;                                // [nmat][kJacobiLogBytes / 8] scratch
-  int max_sweeps;
-  float tol;                                      // stop when off(A) <= tol * ||diag(A)||
 };
 
-cudaError_t launch_jacobi(const JacobiParams &p, cudaStream_t stream);
+cudaError_t launch_eigh(const EighParams &p, cudaStream_t stream);
 
 // Rotation: kept = K_vis . R (uncentred), stored in the Keys' dtype.
 struct RotateParams {

@@ -752,12 +752,10 @@ cudaError_t launch_rotation(const View4 &kv, int dt, int64_t keep, const rtk_ten
              : rtc ? rtk::launch_rotate_tc(dt == RTK_BF16, rp, st) : rtk::launch_rotate_simt(rp, st);
 }
 
-// Build workspace: status word (256 B) | cov | ksum | sweeps | rotation log.
+// Build workspace: status word (256 B) | cov | ksum.
 struct BuildWs {
   unsigned int *status;
   float *cov, *ksum;
-  int *sweeps;
-  float2 *rot_log;
 };
 
 BuildWs build_ws(void *workspace, int64_t n, int64_t D) {
@@ -766,8 +764,6 @@ BuildWs build_ws(void *workspace, int64_t n, int64_t D) {
   w.status = reinterpret_cast<unsigned int *>(ws);
   w.cov = reinterpret_cast<float *>(ws + kStatusBytes);
   w.ksum = reinterpret_cast<float *>(ws + kStatusBytes + align_up((size_t)n * D * D * sizeof(float)));
-  w.sweeps = reinterpret_cast<int *>(reinterpret_cast<unsigned char *>(w.ksum) + align_up((size_t)n * D * sizeof(float)));
-  w.rot_log = reinterpret_cast<float2 *>(reinterpret_cast<unsigned char *>(w.sweeps) + align_up((size_t)n * sizeof(int)));
   return w;
 }
 
@@ -797,12 +793,12 @@ int check_build_args(int64_t B, int64_t H, int64_t S, int64_t D, int dt, const r
 }
 
 // The build after the sums are in w.cov / w.ksum: centring, query weighting,
-// Jacobi, top-k R and delta_mu, then kept = K_vis . R.
+// eigensolver, top-k R and delta_mu, then kept = K_vis . R.
 int finish_build(const View4 &kv, int dt, const rtk_tensor *queries, int64_t num_kv_groups, int64_t keep,
                  const rtk_tensor *kept_out, const rtk_tensor *R_out, const rtk_tensor *delta_mu_out,
                  const rtk_tensor *eigvals_out, const BuildWs &w, cudaStream_t st) {
   const int64_t B = kv.n[0], H = kv.n[1], S = kv.n[2];
-  rtk::JacobiParams jp;
+  rtk::EighParams jp;
   std::memset(&jp, 0, sizeof(jp));
   jp.nmat = (int)(B * H); jp.heads = (int)H;
   jp.cov = w.cov; jp.ksum = w.ksum; jp.count = (int)std::max<int64_t>(S, 1);
@@ -821,15 +817,7 @@ int finish_build(const View4 &kv, int dt, const rtk_tensor *queries, int64_t num
     for (int i = 0; i < 3; ++i) jp.dm_s[i] = delta_mu_out->stride[i];
   }
   jp.evals = eigvals_out ? static_cast<float *>(eigvals_out->data) : nullptr;
-  jp.sweeps = w.sweeps;
-  jp.rot_log = w.rot_log;
-  jp.max_sweeps = rtk::kJacobiMaxSweeps;
-  // Converge as far as the output dtype can hold: R is rounded to the Keys'
-  // dtype, whose rounding alone moves span(R) by ~8e-3 (bf16) / ~2e-3 (fp16) in
-  // projector distance, while off(A) <= tol ||diag A|| leaves it ~20 tol from
-  // the exact eigenvectors.
-  jp.tol = dt == RTK_BF16 ? 1e-4f : dt == RTK_F16 ? 2.5e-5f : 1e-6f;
-  cudaError_t e = rtk::launch_jacobi(jp, st);
+  cudaError_t e = rtk::launch_eigh(jp, st);
   if (e != cudaSuccess) return cuda_fail(e, "rotation builder (eigensolver) launch");
   e = launch_rotation(kv, dt, keep, R_out, kept_out, w.status, st);
   if (e != cudaSuccess) return cuda_fail(e, "rotation builder (rotate) launch");
@@ -1006,14 +994,14 @@ int rtk_key_covariance(const rtk_tensor *keys, const rtk_tensor *cov_out, const 
 size_t rtk_build_rotation_workspace_size(int64_t batch, int64_t kv_heads, int64_t head_dim) {
   const int64_t n = batch * kv_heads;
   return kStatusBytes + align_up((size_t)n * head_dim * head_dim * sizeof(float)) +
-         align_up((size_t)n * head_dim * sizeof(float)) + align_up((size_t)n * sizeof(int)) +
-         align_up((size_t)n * rtk::kJacobiLogBytes);
+         align_up((size_t)n * head_dim * sizeof(float));
 }
 
-// [0, 256) status word (unused by the solver, kept so that one buffer can
-// serve both entry points), then the rotation log
+// [0, 256) status word, unused by the solver (which needs no global scratch);
+// kept so that one buffer can serve every builder entry point
 size_t rtk_eigh_topk_workspace_size(int64_t n) {
-  return kStatusBytes + align_up((size_t)std::max<int64_t>(n, 0) * rtk::kJacobiLogBytes);
+  (void)n;
+  return kStatusBytes;
 }
 
 int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_t num_kv_groups,
@@ -1038,7 +1026,7 @@ int rtk_build_rotation(const rtk_tensor *keys, const rtk_tensor *queries, int64_
   // ---- covariance + channel sums
   const cudaError_t e = launch_covariance(kv, keys->dtype, w.cov, w.ksum, current_device(), st);
   if (e != cudaSuccess) return cuda_fail(e, "rotation builder (covariance) launch");
-  // ---- centring, query weighting, Jacobi, top-k R, delta_mu; kept = K_vis . R
+  // ---- centring, query weighting, eigensolver, top-k R, delta_mu; kept = K_vis . R
   return finish_build(kv, keys->dtype, queries, num_kv_groups, keep, kept_out, R_out, delta_mu_out,
                       eigvals_out, w, st);
 }
@@ -1159,7 +1147,7 @@ int rtk_eigh_topk(const rtk_tensor *cov, int64_t k, const rtk_tensor *vecs_out,
   const size_t need = rtk_eigh_topk_workspace_size(N);
   if (workspace == nullptr || workspace_bytes < need)
     return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, need);
-  rtk::JacobiParams jp;
+  rtk::EighParams jp;
   std::memset(&jp, 0, sizeof(jp));
   jp.nmat = (int)N; jp.heads = 1;
   jp.cov = static_cast<const float *>(cov->data);
@@ -1168,10 +1156,7 @@ int rtk_eigh_topk(const rtk_tensor *cov, int64_t k, const rtk_tensor *vecs_out,
   jp.R = vecs_out->data; jp.R_dtype = RTK_F32;
   jp.R_s[0] = vecs_out->stride[0]; jp.R_s[1] = 0; jp.R_s[2] = vecs_out->stride[1]; jp.R_s[3] = vecs_out->stride[2];
   jp.evals = vals_out ? static_cast<float *>(vals_out->data) : nullptr;
-  jp.rot_log = reinterpret_cast<float2 *>(static_cast<unsigned char *>(workspace) + kStatusBytes);
-  jp.max_sweeps = rtk::kJacobiMaxSweeps;
-  jp.tol = 1e-6f;
-  const cudaError_t e = rtk::launch_jacobi(jp, static_cast<cudaStream_t>(stream));
+  const cudaError_t e = rtk::launch_eigh(jp, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "eigensolver launch");
   return RTK_OK;
 }

@@ -3,7 +3,7 @@
 // For every matrix m = (b, h) of visual Keys K [S x 128] (bf16 / fp16):
 //   cov[m]  = sum_s k_s k_s^T   (fp32, 128 x 128, uncentred)
 //   ksum[m] = sum_s k_s          (fp32, 128)
-// -- the raw sums behind kv_pruning_utils.py:112-115 (the Jacobi prologue
+// -- the raw sums behind kv_pruning_utils.py:112-115 (the eigensolver prologue
 // centres them).
 //
 // A cluster of Z CTAs (Z in {1, 2, 4, 8}) owns one matrix; CTA z of the

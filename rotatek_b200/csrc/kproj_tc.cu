@@ -5,7 +5,7 @@
 // and ChannelPruner.update_rotatek then reads the visual Keys again for their
 // mean and covariance (kv_pruning_utils.py:112-115).  This kernel produces the
 // post-RoPE Keys and, in the same pass, the raw sums sum_s k k^T and sum_s k of
-// the visual span -- the inputs of the Jacobi prologue -- so the covariance
+// the visual span -- the inputs of the eigensolver prologue -- so the covariance
 // pass over K disappears.
 //
 // CTA pairs.  A cluster of two CTAs computes a {256 tokens x 256 channels}

@@ -40,6 +40,8 @@ def rotatek_decode(
     k_sparse: torch.Tensor,              # [B, H_kv, S_sparse, D_keep]
     v_sparse: torch.Tensor,              # [B, H_kv, S_sparse, D]
     num_kv_groups: int,
+    *,
+    out: Optional[torch.Tensor] = None,  # [B, 1, H_q, D] to write into (any strides, channel stride 1)
 ) -> Tuple[torch.Tensor, None, None]:
     """RotateK decode of one query token; returns (out [B, 1, H_q, D], None, None).
 
@@ -48,8 +50,10 @@ def rotatek_decode(
     query q.R and the q.delta_mu bias, prompt/text logits the full query, both
     spans share one softmax, tokens with mask_full == 0 are skipped, and the
     output is acc / (l + 1e-6) in q's dtype.  Unlike the reference the output
-    is a fresh tensor, never an alias of a cached buffer.  Inputs may be strided
-    views (e.g. the adapters' ``value_states[:, :, s_p:s_p + s_v]``); nothing is
+    is a fresh tensor, never an alias of a cached buffer -- unless the caller
+    passes ``out`` (an extension: e.g. a head-major view of a collective's send
+    buffer, so that no copy precedes the gather).  Inputs may be strided views
+    (e.g. the adapters' ``value_states[:, :, s_p:s_p + s_v]``); nothing is
     copied.
     """
     if q_full.dim() != 3:
@@ -78,7 +82,10 @@ def rotatek_decode(
                 lib.rtk_decode_workspace_counter_bytes(bsz, heads))
         _ws_size_cache[key] = need
     ws = _lib.workspace(dev, *need)
-    out = torch.empty((bsz, 1, heads, head_dim), dtype=q_full.dtype, device=dev)
+    if out is None:
+        out = torch.empty((bsz, 1, heads, head_dim), dtype=q_full.dtype, device=dev)
+    elif out.shape != (bsz, 1, heads, head_dim) or out.dtype != q_full.dtype or out.device != dev:
+        raise ValueError(f"out must be [B, 1, H_q, D] = {(bsz, 1, heads, head_dim)} in q's dtype on q's device")
     D = _lib.describe
     _lib.check(lib.rtk_rotatek_decode(
         D(q_full), D(R_partial), D(delta_mu), D(k_full), D(v_full), D(mask_full), D(k_sparse),

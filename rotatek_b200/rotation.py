@@ -4,14 +4,15 @@ plus the fused prefill build that ``ChannelPruner.update_rotatek`` performs.
 ``power_iteration_gpu`` keeps the reference's signature (rotatek/rotation.py:
 68-91) and the ``_ROTATEK_QUERY_AWARE_ACTIVE`` flag (rotation.py:18), but
 returns the *converged* top-k eigenvectors (descending eigenvalue) from a
-batched 128x128 Jacobi eigensolver instead of five unconverged subspace
+batched 128x128 eigensolver (Householder tridiagonalisation, Sturm
+multisection, inverse iteration) instead of five unconverged subspace
 iterations from a random start; ``num_iters`` and ``seed`` are accepted and
 unused.  The subspace is the one the iteration approaches, and decode depends
 only on that subspace (logits equal q . (P k + (I - P) mu), P = R R^T).
 
 ``build_rotation`` runs the whole build of kv_pruning_utils.py:105-160 for one
-layer in three kernels: tcgen05 covariance of the visual Keys, Jacobi with the
-centring / query weighting / top-k / delta_mu fused in, and the rotation
+layer in three kernels: tcgen05 covariance of the visual Keys, the eigensolver
+with the centring / query weighting / top-k / delta_mu fused in, and the rotation
 K_vis . R.
 """
 from __future__ import annotations
