@@ -21,8 +21,7 @@ region is bracketed by barriers and the max over ranks is reported.
 
 --impl reference times the reference's own math on the host CPU: the eager
 PyTorch restatement of rotatek/kernels/fused_decode.py (the reference has no
-CPU decode of its own; its kernels are Triton-only), on a batch sample scaled
-to the full batch.
+CPU decode of its own; its kernels are Triton-only), on the full batch.
 """
 from __future__ import annotations
 
@@ -158,6 +157,37 @@ def dist_env():
     return rank, world, local
 
 
+def ramp_clocks(fn, min_s: float = 0.3) -> int:
+    """Untimed calls of ``fn`` until ``min_s`` seconds of device work have run:
+    an idle GPU needs some hundreds of milliseconds of load to reach its
+    working SM and memory clocks, more than a few warm-up steps of a 0.1 ms
+    kernel give it.  Returns the number of calls."""
+    n, t0 = 0, time.perf_counter()
+    while True:
+        for _ in range(20):
+            fn()
+        n += 20
+        torch.cuda.synchronize()
+        if time.perf_counter() - t0 >= min_s:
+            return n
+
+
+def lead_in(cycles: int = 2_000_000) -> None:
+    """Queue ~1 ms of device idling before a timed region's start event, so that
+    the host has already queued the first timed launches when the GPU reaches
+    them: the first step then measures the kernel, not the host's launch
+    latency after an idle, synchronised stream."""
+    torch.cuda._sleep(cycles)
+
+
+def step_stats(per_step_ms) -> dict:
+    """Percentiles of per-step device times (us) and the first five steps."""
+    xs = sorted(per_step_ms)
+    pick = lambda q: xs[min(len(xs) - 1, int(q * (len(xs) - 1) + 0.5))] * 1e3  # noqa: E731
+    return {"p10_us": pick(0.1), "p50_us": pick(0.5), "p90_us": pick(0.9), "min_us": xs[0] * 1e3,
+            "max_us": xs[-1] * 1e3, "first5_us": [x * 1e3 for x in per_step_ms[:5]]}
+
+
 def make_inputs(device, dtype=torch.bfloat16, seed=0, batch=None):
     from rotatek_b200 import synthetic as syn
     b = CFG["batch"] if batch is None else batch
@@ -182,8 +212,7 @@ def cpu_baseline_sample(target_s: float = 12.0):
     batch sample; returns (us per full batch-32 step, sample description, threads)."""
     from oracle.eager_torch import rotatek_decode_eager
     threads = use_all_host_threads()
-    b = 1
-    d = make_inputs("cpu", batch=b, seed=1)
+    d = make_inputs("cpu", seed=1)
     kw = d.as_kwargs()
     rotatek_decode_eager(**kw)                       # warm-up
     t0 = time.perf_counter()
@@ -193,10 +222,9 @@ def cpu_baseline_sample(target_s: float = 12.0):
     t0 = time.perf_counter()
     for _ in range(reps):
         rotatek_decode_eager(**kw)
-    per = (time.perf_counter() - t0) / reps
-    us_full = per * 1e6 * CFG["batch"] / b
-    sample = (f"batch {b} of {CFG['batch']} (other dims full), {reps} reps, eager torch fp32 "
-              f"restatement of fused_decode.py, scaled x{CFG['batch'] // b} to the batch-32 step")
+    us_full = (time.perf_counter() - t0) / reps * 1e6
+    sample = (f"the full batch-32 step (bf16 inputs, fp32 math), {reps} reps, eager torch "
+              f"restatement of fused_decode.py")
     return us_full, sample, threads
 
 
@@ -206,8 +234,7 @@ def run_reference(args):
         return 0
     from oracle.eager_torch import rotatek_decode_eager
     threads = use_all_host_threads()
-    b = 1
-    d = make_inputs("cpu", batch=b, seed=1)
+    d = make_inputs("cpu", seed=1)
     kw = d.as_kwargs()
     for _ in range(args.warmup):
         rotatek_decode_eager(**kw)
@@ -216,9 +243,9 @@ def run_reference(args):
         t0 = time.perf_counter()
         rotatek_decode_eager(**kw)
         times.append(time.perf_counter() - t0)
-    per_full_us = statistics.mean(times) * 1e6 * CFG["batch"] / b
-    sample = (f"batch {b} of {CFG['batch']} per step (other dims full), eager torch fp32 "
-              f"restatement of fused_decode.py, scaled x{CFG['batch'] // b}")
+    per_full_us = statistics.mean(times) * 1e6
+    sample = ("the full batch-32 step per step (bf16 inputs, fp32 math), eager torch restatement "
+              "of fused_decode.py")
     line = {
         "impl": "reference", "metric": METRIC, "value": per_full_us, "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -262,6 +289,7 @@ def run_ours(args):
     for _ in range(max(args.warmup, 3)):
         rotatek_decode(**kw)
     torch.cuda.synchronize()
+    ramp_calls = ramp_clocks(lambda: rotatek_decode(**kw))
 
     # ---- device-timed region: inputs resident in HBM
     events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
@@ -269,6 +297,7 @@ def run_ours(args):
     barrier()
     torch.cuda.synchronize()
     with sampler:
+        lead_in()
         events[0].record(stream)
         for i in range(args.steps):
             rotatek_decode(**kw)
@@ -357,6 +386,10 @@ def run_ours(args):
             "gpu_launches": args.steps,
             "clocks": clocks,
             "device_status": status,
+            "step_stats": step_stats(per_step_ms),
+            "warmup_calls": {"steps": max(args.warmup, 3), "clock_ramp": ramp_calls,
+                             "why": "untimed calls until 0.3 s of device work, so that an idle GPU's "
+                                    "clocks have ramped before the timed steps"},
         }
         if world == 1:
             dense_us, dense_bytes = dense_same_context(d, max(50, args.steps // 4))
@@ -365,15 +398,79 @@ def run_ours(args):
                 "algorithmic_bytes_per_launch": dense_bytes,
                 "hbm_frac": dense_bytes / dense_us / 1e3 / peak,
                 "what": "full_channel_decode over the same 16000-token context with full-width visual Keys"}
+        if world == 1 and not args.no_extras:
+            ours_out, _, _ = rotatek_decode(**kw)
+            line["reference_gpu_same_box"] = reference_gpu_decode(d, us_per_step, ours_out, 50)
         if world == 1 and not args.no_cpu_baseline:
             us_cpu, sample, threads = cpu_baseline_sample()
             line["cpu_baseline"] = {"value": us_cpu, "unit": UNIT, "cores": threads,
                                     "kind": "port", "sample": sample}
+    # ---- the other benchmark configurations, measured in the same run
+    if not args.no_extras:
+        del d, kw, host, dev_in
+        torch.cuda.empty_cache()
+        extras = {}
+        if world == 1:
+            extras["build_config4"] = build_summary(dev, steps=10, warmup=3)
+        else:
+            extras["strong_config2"] = strong_config2(dev, pg, rank, world, steps=200)
+        extras["config5"] = config5_step(dev, pg, rank, world, steps=5, warmup=2)
+        if rank == 0:
+            line.update(extras)
+    if rank == 0:
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()
     return 0
+
+
+REF_DIR = os.path.join(REPO, "baseline", "_ref")
+
+
+def reference_gpu_decode(d, ours_us: float, ours_out: torch.Tensor, steps: int) -> dict:
+    """The reference's own Triton decode kernels on this GPU at the same inputs:
+    ``rotatek_decode_fused_triton`` (ROTATEK_KERNEL=paper, fused_decode.py:303-420)
+    and ``rotatek_decode_gqa`` (gqa_decode.py:280-321), imported unmodified from
+    baseline/_ref.  CUDA events over ``steps`` back-to-back calls after warm-up;
+    each output is compared with ours (max abs difference).  A comparison
+    outside the product path, reported beside the headline."""
+    pkg = os.path.join(REF_DIR, "rotatek")
+    if not os.path.isdir(pkg):
+        return {"unavailable": "baseline/_ref/rotatek is absent (the reference is not pip-installable; "
+                               "its rotatek/ package is copied there unmodified)"}
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    res = {}
+    try:
+        import triton
+        from rotatek.kernels.fused_decode import rotatek_decode_fused_triton
+        from rotatek.kernels.gqa_decode import rotatek_decode_gqa
+        res["triton"] = triton.__version__
+    except Exception as exc:  # noqa: BLE001
+        return {"unavailable": f"import failed: {type(exc).__name__}: {exc}"[:300]}
+    kw = d.as_kwargs()
+    for name, fn in (("paper", rotatek_decode_fused_triton), ("gqa", rotatek_decode_gqa)):
+        try:
+            for _ in range(3):
+                out = fn(**kw)[0]
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            lead_in()
+            e0.record()
+            for _ in range(steps):
+                fn(**kw)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / steps
+            out = fn(**kw)[0].float()
+            res[name] = {"us_per_step": us, "speedup_of_ours": us / ours_us,
+                         "max_abs_diff_vs_ours": float((out.reshape(d.q_full.shape) -
+                                                        ours_out.float().reshape(d.q_full.shape)).abs().max())}
+        except Exception as exc:  # noqa: BLE001
+            res[name] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+    return res
+
 
 
 def dense_same_context(d, steps):
@@ -393,6 +490,7 @@ def dense_same_context(d, steps):
         full_channel_decode(d.q_full, keys, values, num_kv_groups=G)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    lead_in()
     e0.record()
     for _ in range(steps):
         full_channel_decode(d.q_full, keys, values, num_kv_groups=G)
@@ -416,6 +514,61 @@ def build_inputs(device, seed=0, layers=None, batch=None):
     queries = syn.normal((nb, CFG4["q_heads"], CFG4["window"], CFG4["head_dim"]), seed + 1, device,
                          torch.bfloat16)
     return keys, queries
+
+
+# Minimum HBM traffic of one config-4 build step: the visual Keys read twice
+# (covariance pass, rotation pass) and the rotated-truncated Keys written once.
+def build_min_bytes(keys, keep) -> int:
+    kbytes = keys.numel() * keys.element_size()
+    return 2 * kbytes + kbytes * keep // keys.shape[-1]
+
+
+def build_summary(dev, steps: int, warmup: int, seed: int = 100) -> dict:
+    """The config-4 build measured on its own (CUDA events): the whole step, its
+    HBM fraction on the minimum bytes, each kernel's time and share, the
+    eigensolver's time per 128x128 solve and the one-layer (32-matrix) build."""
+    from rotatek_b200 import rotation as rot
+    G = CFG4["q_heads"] // CFG4["kv_heads"]
+    keep = CFG4["keep"]
+    keys, queries = build_inputs(dev, seed=seed)
+    nmat = keys.shape[0] * keys.shape[1]
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, reps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+        lead_in()
+        ev[0].record(stream)
+        for i in range(reps):
+            fn()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+        return [ev[i].elapsed_time(ev[i + 1]) for i in range(reps)]
+
+    step = lambda: rot.build_rotation(keys, queries, keep, G)  # noqa: E731
+    for _ in range(max(warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    step_ms = statistics.mean(timed(step, steps))
+    kept, R, dm, _ = step()
+    cov_ms = statistics.mean(timed(lambda: rot.key_covariance(keys), 3))
+    rot_ms = statistics.mean(timed(lambda: rot.rotate_keys(keys, R), 3))
+    layer = lambda: rot.build_rotation(keys[:CFG4["batch"]], queries[:CFG4["batch"]], keep, G)  # noqa: E731
+    layer()
+    layer_ms = statistics.mean(timed(layer, 5))
+    eig_ms = max(step_ms - cov_ms - rot_ms, 0.0)
+    peak, peak_kind = load_peak_hbm()
+    nbytes = build_min_bytes(keys, keep)
+    out = {"what": BUILD_WORKLOAD, "us_per_step": step_ms * 1e3, "steps": steps,
+           "hbm": {"achieved": nbytes / step_ms / 1e6, "peak": peak, "unit": "GB/s",
+                   "frac": nbytes / step_ms / 1e6 / peak, "min_bytes": nbytes, "peak_source": peak_kind},
+           "phases_us": {"covariance": cov_ms * 1e3, "eigensolver": eig_ms * 1e3, "rotate": rot_ms * 1e3},
+           "share": {"covariance": cov_ms / step_ms, "eigensolver": eig_ms / step_ms, "rotate": rot_ms / step_ms},
+           "eigensolver_us_per_128x128_solve": eig_ms * 1e3 / nmat,
+           "one_layer_build_us": layer_ms * 1e3,
+           "device_status": rot.read_build_status(dev)}
+    del keys, queries, kept, R, dm
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_build(args):
@@ -446,6 +599,7 @@ def run_build(args):
 
     def timed(fn, reps):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+        lead_in()
         ev[0].record(stream)
         for i in range(reps):
             fn()
@@ -535,9 +689,12 @@ def run_build(args):
                           "eigensolve_us_per_128x128_solve": jac_ms * 1e3 / nmat,
                           "one_layer_build": layer_ms * 1e3,
                           "per_layer_sequential_28": layer_ms * 1e3 * CFG4["layers"]},
-            "roofline": {"bound": "fp32", "kernel": "jacobi_kernel (batched 128x128 Jacobi, CUDA cores)",
-                         "achieved": None, "peak": None, "unit": None, "frac": None, "traffic": None,
-                         "note": "no byte or tensor roofline applies; reported as time per solve"},
+            "roofline": {"bound": "hbm", "kernel": "whole build step (covariance + eigensolver + rotate)",
+                         "achieved": build_min_bytes(keys, keep) / (total_ms / args.steps * 1e-3) / 1e9, "peak": peak,
+                         "unit": "GB/s", "frac": build_min_bytes(keys, keep) / (total_ms / args.steps * 1e-3) / 1e9 / peak,
+                         "min_bytes": build_min_bytes(keys, keep), "traffic": None,
+                         "note": "the eigensolver (eigh_kernel) moves ~0.07 MB per matrix and is bound by "
+                                 "its sequential steps; reported as time per solve"},
             "hbm_kernels": {
                 "covariance": {"bound": "hbm", "achieved": cov_bytes / cov_ms / 1e6, "peak": peak,
                                "unit": "GB/s", "frac": cov_bytes / cov_ms / 1e6 / peak,
@@ -1073,6 +1230,135 @@ DEC72_WORKLOAD = ("config5: 72B-class GQA decode attention, bf16, 80 layers, B=6
                   "D=128, D_keep=32, S = 64 prompt + 31744 visual + 960 text")
 
 
+def config5_step(dev, pg, rank: int, world: int, steps: int, warmup: int, pool: int = 2) -> dict:
+    """One config-5 decode step (all 80 layers, one new token for the batch of
+    64) on this rank's share.  N = 1: the whole step on one GPU.  N > 1: KV heads
+    sharded (8 / N per rank, their query groups for the whole batch); every
+    layer's decode writes its heads head-major straight into that layer's
+    all_gather send buffer, and one NCCL all_gather (issued asynchronously, so
+    it runs beside the next layer's decode) leaves every rank with all 64
+    heads.  Device time per step (CUDA events, max over ranks), also without
+    the gathers, to show what the collective costs."""
+    from rotatek_b200 import sharding, synthetic as syn
+    from rotatek_b200.kernels import rotatek_decode
+    G = CFG5["q_heads"] // CFG5["kv_heads"]
+    p = sharding.plan(rank, world, CFG5["batch"], CFG5["kv_heads"], G, mode="heads" if world > 1 else "batch")
+    full_len = CFG5["prompt"] + CFG5["text"]
+    layers = []
+    for j in range(pool):
+        d = syn.make_decode(p.local_batch, p.local_q_heads, p.local_kv_heads, CFG5["vision"], full_len,
+                            keep=CFG5["keep"], seed=500 + 10 * j + rank, device=dev, dtype=torch.bfloat16)
+        kw = d.as_kwargs()
+        kw.pop("q_full")
+        layers.append(kw)
+        layer_bytes = d.nbytes()
+        del d
+    B, Hl, D = p.local_batch, p.local_q_heads, CFG5["head_dim"]
+    qs = [syn.normal((B, Hl, D), 900 + l, dev, torch.bfloat16) for l in range(CFG5["layers"])]
+    # send [H_loc, B, D] per layer (the decode's output, head-major); recv [H_q, B, D]
+    send = [torch.empty((Hl, B, D), dtype=torch.bfloat16, device=dev) for _ in range(CFG5["layers"])]
+    outs = [t.permute(1, 0, 2).unsqueeze(1) for t in send]          # [B, 1, H_loc, D] views
+    recv = [torch.empty((world * Hl, B, D), dtype=torch.bfloat16, device=dev) for _ in range(CFG5["layers"])]
+    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize()
+
+    def step(gather: bool):
+        works = []
+        for l in range(CFG5["layers"]):
+            rotatek_decode(q_full=qs[l], **layers[l % pool], out=outs[l])
+            if gather and world > 1:
+                works.append(pg.all_gather_into_tensor(recv[l], send[l], async_op=True))
+        for w in works:
+            w.wait()
+
+    def timed(gather: bool) -> float:
+        for _ in range(max(warmup, 3)):
+            step(gather)
+        torch.cuda.synchronize()
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        lead_in()
+        e0.record(stream)
+        for _ in range(steps):
+            step(gather)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        if pg is not None:
+            t = torch.tensor([ms], device=dev)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    decode_only = timed(False)
+    with_gather = timed(True) if world > 1 else decode_only
+    ok = True
+    if world > 1:
+        # the gathered heads are every rank's own outputs, in rank order
+        mine = recv[-1][rank * Hl:(rank + 1) * Hl]
+        ok = bool(torch.equal(mine, send[-1]))
+    peak, peak_kind = load_peak_hbm()
+    rank_bytes = layer_bytes * CFG5["layers"]
+    out = {"what": DEC72_WORKLOAD, "plan": (f"KV heads {p.h0}..{p.h1 - 1} per rank, NCCL all_gather of the "
+                                            f"outputs per layer" if world > 1 else "whole batch on one GPU"),
+           "ms_per_step": with_gather, "decode_only_ms_per_step": decode_only,
+           "tokens_per_s": CFG5["batch"] / (with_gather * 1e-3), "steps": steps, "layers_resident": pool,
+           "hbm_rank": {"achieved": rank_bytes / (with_gather * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                        "frac": rank_bytes / (with_gather * 1e-3) / 1e9 / peak, "bytes_per_rank_step": rank_bytes,
+                        "peak_source": peak_kind},
+           "gather_ok": ok}
+    del layers, qs, send, outs, recv
+    torch.cuda.empty_cache()
+    return out
+
+
+def strong_config2(dev, pg, rank: int, world: int, steps: int) -> dict:
+    """Config 2's global batch of 32 split over the ranks (32 / N rows each, no
+    collective): device time per global step, max over ranks.  Each rank cycles
+    over enough input copies that a step's inputs are not left in L2 by the
+    previous steps (>= 3 x 126 MB per rank)."""
+    from rotatek_b200.kernels import rotatek_decode
+    if CFG["batch"] % world:
+        return {"unavailable": f"batch {CFG['batch']} does not split over {world} ranks"}
+    b = CFG["batch"] // world
+    d1 = make_inputs(dev, seed=2000 + rank, batch=b)
+    per_rank = algorithmic_bytes(d1)
+    del d1
+    sets = max(1, math.ceil(3 * 126e6 / per_rank))
+    d = make_inputs(dev, seed=2000 + rank, batch=b * sets)
+    kw = d.as_kwargs()
+    views = [{k: (v[i * b:(i + 1) * b] if torch.is_tensor(v) else v) for k, v in kw.items()} for i in range(sets)]
+    for _ in range(5):
+        for v in views:
+            rotatek_decode(**v)
+    torch.cuda.synchronize()
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    lead_in()
+    e0.record(stream)
+    for i in range(steps):
+        rotatek_decode(**views[i % sets])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    mine = us
+    if pg is not None:
+        t = torch.tensor([us], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        us = float(t.item())
+    peak, _ = load_peak_hbm()
+    del d, kw, views
+    torch.cuda.empty_cache()
+    return {"what": f"config 2, global batch {CFG['batch']} split {b} rows per rank (strong scaling, no collective)",
+            "us_per_step": us, "rows_per_rank": b, "input_sets_cycled": sets, "steps": steps,
+            "hbm_frac_rank0": per_rank / (mine * 1e-6) / 1e9 / peak}
+
+
 def run_decode72b(args):
     """Config 5: one step = the decode attention of all 80 layers for one new
     token of the whole batch (strong scaling: the batch is fixed, ranks split
@@ -1193,6 +1479,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="decode workload: skip the same-box reference kernels, config 4 build, config-2 strong "
+                         "scaling and config 5 measurements that ride along the headline line")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the batch (profiling cases only; the bench line uses 32)")
     ap.add_argument("--kernel-only", action="store_true",
