@@ -414,7 +414,10 @@ def run_ours(args):
             extras["build_config4"] = build_summary(dev, steps=10, warmup=3)
         else:
             extras["strong_config2"] = strong_config2(dev, pg, rank, world, steps=200)
-        extras["config5"] = config5_step(dev, pg, rank, world, steps=5, warmup=2)
+        # measured: at 2 GPUs the all_gather hides behind a 0.4 ms layer decode with no
+        # reserve; at 8 GPUs (0.1 ms per layer) leaving it 8 SMs is fastest
+        extras["config5"] = config5_step(dev, pg, rank, world, steps=5, warmup=2,
+                                         sm_reserve=0 if world <= 2 else 8)
         if rank == 0:
             line.update(extras)
     if rank == 0:
@@ -1230,7 +1233,8 @@ DEC72_WORKLOAD = ("config5: 72B-class GQA decode attention, bf16, 80 layers, B=6
                   "D=128, D_keep=32, S = 64 prompt + 31744 visual + 960 text")
 
 
-def config5_step(dev, pg, rank: int, world: int, steps: int, warmup: int, pool: int = 2) -> dict:
+def config5_step(dev, pg, rank: int, world: int, steps: int, warmup: int, pool: int = 2,
+                 mode: str = "heads", sm_reserve: int = 0) -> dict:
     """One config-5 decode step (all 80 layers, one new token for the batch of
     64) on this rank's share.  N = 1: the whole step on one GPU.  N > 1: KV heads
     sharded (8 / N per rank, their query groups for the whole batch); every
@@ -1239,10 +1243,11 @@ def config5_step(dev, pg, rank: int, world: int, steps: int, warmup: int, pool: 
     it runs beside the next layer's decode) leaves every rank with all 64
     heads.  Device time per step (CUDA events, max over ranks), also without
     the gathers, to show what the collective costs."""
-    from rotatek_b200 import sharding, synthetic as syn
+    from rotatek_b200 import _lib, sharding, synthetic as syn
     from rotatek_b200.kernels import rotatek_decode
     G = CFG5["q_heads"] // CFG5["kv_heads"]
-    p = sharding.plan(rank, world, CFG5["batch"], CFG5["kv_heads"], G, mode="heads" if world > 1 else "batch")
+    p = sharding.plan(rank, world, CFG5["batch"], CFG5["kv_heads"], G, mode=mode if world > 1 else "batch")
+    gather = world > 1 and p.mode == "heads"
     full_len = CFG5["prompt"] + CFG5["text"]
     layers = []
     for j in range(pool):
@@ -1262,11 +1267,11 @@ def config5_step(dev, pg, rank: int, world: int, steps: int, warmup: int, pool: 
     stream = torch.cuda.current_stream(dev)
     torch.cuda.synchronize()
 
-    def step(gather: bool):
+    def step(with_gather: bool):
         works = []
         for l in range(CFG5["layers"]):
             rotatek_decode(q_full=qs[l], **layers[l % pool], out=outs[l])
-            if gather and world > 1:
+            if with_gather:
                 works.append(pg.all_gather_into_tensor(recv[l], send[l], async_op=True))
         for w in works:
             w.wait()
@@ -1292,17 +1297,25 @@ def config5_step(dev, pg, rank: int, world: int, steps: int, warmup: int, pool: 
             ms = float(t.item())
         return ms
 
+    _lib.set_decode_sm_reserve(sm_reserve if gather else 0)
     decode_only = timed(False)
-    with_gather = timed(True) if world > 1 else decode_only
+    with_gather = timed(True) if gather else decode_only
+    _lib.set_decode_sm_reserve(0)
     ok = True
-    if world > 1:
+    if gather:
         # the gathered heads are every rank's own outputs, in rank order
         mine = recv[-1][rank * Hl:(rank + 1) * Hl]
         ok = bool(torch.equal(mine, send[-1]))
+    if world > 1:
+        t = torch.tensor([float(ok)], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MIN)
+        ok = bool(t.item() > 0)
     peak, peak_kind = load_peak_hbm()
     rank_bytes = layer_bytes * CFG5["layers"]
-    out = {"what": DEC72_WORKLOAD, "plan": (f"KV heads {p.h0}..{p.h1 - 1} per rank, NCCL all_gather of the "
-                                            f"outputs per layer" if world > 1 else "whole batch on one GPU"),
+    plan = ("whole batch on one GPU" if world == 1 else
+            f"KV heads {p.h0}..{p.h1 - 1} per rank, NCCL all_gather of the outputs per layer" if gather else
+            f"batch rows {p.b0}..{p.b1 - 1} per rank (no collective)")
+    out = {"what": DEC72_WORKLOAD, "plan": plan, "decode_sm_reserve": sm_reserve if gather else 0,
            "ms_per_step": with_gather, "decode_only_ms_per_step": decode_only,
            "tokens_per_s": CFG5["batch"] / (with_gather * 1e-3), "steps": steps, "layers_resident": pool,
            "hbm_rank": {"achieved": rank_bytes / (with_gather * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
@@ -1360,10 +1373,10 @@ def strong_config2(dev, pg, rank: int, world: int, steps: int) -> dict:
 
 
 def run_decode72b(args):
-    """Config 5: one step = the decode attention of all 80 layers for one new
-    token of the whole batch (strong scaling: the batch is fixed, ranks split
-    it).  One KV head per GPU at N = 8 (outputs all_gathered along heads each
-    layer, overlapped with the next layer), batch-sharded at N = 2 and 4."""
+    """Config 5 on its own line: one step = the decode attention of all 80 layers
+    for one new token of the whole batch (strong scaling: the batch is fixed,
+    ranks split it), KV heads sharded (``--shard heads``, NCCL all_gather of the
+    outputs per layer) or batch rows (``--shard batch``, no collective)."""
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -1373,96 +1386,25 @@ def run_decode72b(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
         pg = dist
-    from rotatek_b200 import sharding, synthetic as syn
-    from rotatek_b200.kernels import rotatek_decode
-    G = CFG5["q_heads"] // CFG5["kv_heads"]
-    p = sharding.plan(rank, world, CFG5["batch"], CFG5["kv_heads"], G, mode=args.shard)
-    full_len = CFG5["prompt"] + CFG5["text"]
-    # A pool of resident layers, cycled over the 80 layer calls: 80 layers of
-    # this shard (55-437 GB) need not fit, and every layer's K/V exceed the L2,
-    # so each call still streams its full bytes from HBM.
-    pool = []
-    for j in range(args.pool):
-        d = syn.make_decode(p.local_batch, p.local_q_heads, p.local_kv_heads, CFG5["vision"], full_len,
-                            keep=CFG5["keep"], seed=500 + 10 * j + rank, device=dev, dtype=torch.bfloat16)
-        kw = d.as_kwargs()
-        kw.pop("q_full")
-        pool.append(kw)
-        layer_bytes = d.nbytes()
-    qs = [syn.normal((p.local_batch, p.local_q_heads, CFG5["head_dim"]), 900 + l, dev, torch.bfloat16)
-          for l in range(CFG5["layers"])]
-    torch.cuda.synchronize()
-    stream = torch.cuda.current_stream(dev)
-
-    def step():
-        works = []
-        for l in range(CFG5["layers"]):
-            out, _, _ = rotatek_decode(q_full=qs[l], **pool[l % len(pool)])
-            if p.needs_gather:
-                works.append(sharding.gather_output(p, out, async_op=True)[1])
-        for w in works:
-            w.wait()
-
-    def barrier():
-        if pg is not None:
-            pg.barrier()
-
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
+    mode = args.shard if args.shard != "auto" else "heads"
     sampler = ClockSampler(local)
-    barrier()
-    torch.cuda.synchronize()
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     with sampler:
-        ev[0].record(stream)
-        for i in range(args.steps):
-            step()
-            ev[i + 1].record(stream)
-        torch.cuda.synchronize()
-    barrier()
-    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
-    total_ms = sum(per)
-    mine = total_ms
-    if pg is not None:
-        t = torch.tensor([total_ms], device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        total_ms = float(t.item())
+        r = config5_step(dev, pg, rank, world, args.steps, args.warmup, pool=args.pool, mode=mode,
+                         sm_reserve=args.sm_reserve)
     clocks = sampler.summary()
-    if pg is not None:
-        per_rank = [None] * world
-        pg.all_gather_object(per_rank, clocks)
-        mhz = [c["sm_mhz"] for c in per_rank if c["sm_mhz"] is not None]
-        clocks = {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": per_rank[0]["sm_max_mhz"],
-                  "reasons": sorted({x for c in per_rank for x in c["reasons"]}),
-                  "samples": sum(c["samples"] for c in per_rank), "per_rank": per_rank}
     from rotatek_b200 import _lib
     status = _lib.read_status(dev)
     if rank == 0:
-        peak, peak_kind = load_peak_hbm()
-        step_us = total_ms * 1e3 / args.steps
-        rank_bytes = layer_bytes * CFG5["layers"]
-        achieved = rank_bytes / (mine * 1e-3 / args.steps) / 1e9
-        line = {
-            "metric": DEC72_METRIC, "value": step_us, "unit": "us/step", "n_gpus": world,
-            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": step_us / 1e3,
-            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: seeded low-rank+noise Keys rotated to a top-32 basis; N(0,1) Values/queries",
-            "config": {"workload": DEC72_WORKLOAD, "global_batch": CFG5["batch"],
-                       "seq_len": CFG5["prompt"] + CFG5["vision"] + CFG5["text"],
-                       "parallelism": (f"KV heads {p.h0}..{p.h1 - 1} of {CFG5['kv_heads']} per rank, all_gather "
-                                       f"of outputs per layer" if p.mode == "heads" else
-                                       f"batch-sharded x{world} (no collective)"),
-                       "layers_resident": len(pool),
-                       "l2": f"{layer_bytes / 1e9:.2f} GB per layer per rank > 126 MB L2; no flush"},
-            "tokens_per_s": CFG5["batch"] / (step_us * 1e-6),
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_source": peak_kind,
-                         "algorithmic_bytes_per_rank_step": rank_bytes, "traffic": None,
-                         "note": "rank 0's bytes over rank 0's own step time"},
-            "gpu_launches": CFG5["layers"] * args.steps * (3 if p.needs_gather else 1),
-            "clocks": clocks, "device_status": status,
-        }
+        line = {"metric": DEC72_METRIC, "value": r["ms_per_step"] * 1e3, "unit": "us/step", "n_gpus": world,
+                "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": r["ms_per_step"],
+                "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic: seeded low-rank+noise Keys rotated to a top-32 basis; N(0,1) Values/queries",
+                "config": {"workload": DEC72_WORKLOAD, "global_batch": CFG5["batch"],
+                           "seq_len": CFG5["prompt"] + CFG5["vision"] + CFG5["text"], "parallelism": r["plan"],
+                           "layers_resident": r["layers_resident"],
+                           "l2": "each layer's K/V per rank > 126 MB L2; no flush"},
+                "detail": r, "clocks": clocks, "device_status": status,
+                "gpu_launches": CFG5["layers"] * args.steps * (2 if world > 1 and mode == "heads" else 1)}
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.barrier()
@@ -1496,7 +1438,9 @@ def main():
                          "decode_fp8: config 2 with the visual span in e4m3; spark: SparK at config 2")
     ap.add_argument("--shard", choices=["auto", "heads", "batch"], default="auto",
                     help="decode72b: KV-head or batch sharding (auto: heads when N = 8)")
-    ap.add_argument("--pool", type=int, default=4, help="decode72b: resident layers cycled over the 80")
+    ap.add_argument("--pool", type=int, default=2, help="decode72b: resident layers cycled over the 80")
+    ap.add_argument("--sm-reserve", type=int, default=8,
+                    help="config 5 with heads sharded: SMs the decode leaves to the concurrent all_gather")
     ap.add_argument("--e2e-tokens", type=int, default=128, help="e2e: greedy tokens per sequence")
     ap.add_argument("--kproj-vision", type=int, default=None,
                     help="kproj workload: visual tokens (profiling cases only; the bench line uses 15360)")

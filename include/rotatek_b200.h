@@ -59,6 +59,16 @@ int rtk_abi_version(void);
 /* Message of the last failed call made by this thread ("" if none). */
 const char *rtk_last_error(void);
 
+/* Leave `sms` SMs (0..64, default 0) free of the tensor-core decode kernels
+ * of rtk_rotatek_decode, rtk_rotatek_decode_fp8, rtk_full_channel_decode and
+ * rtk_spark_decode, which otherwise launch one persistent CTA per SM.  A
+ * communication kernel issued beside them -- e.g. the all_gather of one
+ * layer's head-sharded outputs while the next layer decodes -- then finds SMs
+ * to run on instead of waiting for the decode to finish.  Process-wide, all
+ * devices; takes effect at the next call (workspaces sized with the default
+ * stay large enough).  No counterpart in the reference.                       */
+int rtk_decode_set_sm_reserve(int sms);
+
 /* ------------------------------------------------------------------------
  * Decode attention
  * ------------------------------------------------------------------------ */

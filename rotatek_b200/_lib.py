@@ -34,6 +34,7 @@ _P = ctypes.POINTER(RtkTensor)
 SIGNATURES = {
     "rtk_abi_version": (ctypes.c_int, []),
     "rtk_last_error": (ctypes.c_char_p, []),
+    "rtk_decode_set_sm_reserve": (ctypes.c_int, [ctypes.c_int]),
     "rtk_rotatek_decode_workspace_size": (ctypes.c_size_t, [ctypes.c_int32] + [ctypes.c_int64] * 7 + [ctypes.c_int32]),
     "rtk_decode_workspace_counter_bytes": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64]),
     "rtk_rotatek_decode": (ctypes.c_int, [_P] * 8 + [ctypes.c_int64, _P, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
@@ -184,3 +185,9 @@ def selftest_wait_timeout(limit_ns: int = 1_000_000, device: Optional[torch.devi
     stream = torch.cuda.current_stream(buf.device).cuda_stream
     check(load().rtk_selftest_wait_timeout(ctypes.c_void_p(buf.data_ptr()), ctypes.c_uint64(limit_ns),
                                            ctypes.c_void_p(stream)))
+
+
+def set_decode_sm_reserve(sms: int) -> None:
+    """Leave ``sms`` SMs free of the persistent decode kernels (process-wide),
+    for a collective that runs beside them; 0 restores one CTA per SM."""
+    check(load().rtk_decode_set_sm_reserve(int(sms)))

@@ -13,6 +13,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -58,6 +59,15 @@ int sm_count(int device) {
     cache[device] = n;
   }
   return cache[device];
+}
+
+// SMs the tensor-core decode kernels leave free (rtk_decode_set_sm_reserve).
+std::atomic<int> g_decode_sm_reserve{0};
+
+// CTAs of a persistent decode launch on `device`: one per SM not reserved.
+int decode_ctas(int device) {
+  const int n = sm_count(device) - g_decode_sm_reserve.load(std::memory_order_relaxed);
+  return n > 1 ? n : 1;
 }
 
 int current_device() {
@@ -205,7 +215,7 @@ TcShape tc_shape(int64_t B, int64_t Hkv, int64_t G, int64_t Sf, int64_t Sv, int 
   t.blocks_sparse = cdiv(Sv, vis_tokens);
   t.blocks_per_unit = t.blocks_full + t.blocks_sparse;
   t.total = t.units * t.blocks_per_unit;
-  t.grid = (int)std::max<int64_t>(1, std::min<int64_t>(t.total, sm_count(device)));
+  t.grid = (int)std::max<int64_t>(1, std::min<int64_t>(t.total, decode_ctas(device)));
   t.slot_floats = 32 + 16 * 128;
   t.slots = (t.units + t.grid) * 5;
   t.phantom = t.total / t.grid >= 16 * kUnitSwitchBlocks ? kUnitSwitchBlocks : 0;
@@ -429,6 +439,13 @@ bool dtype_ok(int dt) { return dt == RTK_F32 || dt == RTK_BF16 || dt == RTK_F16;
 extern "C" {
 
 int rtk_abi_version(void) { return RTK_ABI_VERSION; }
+
+int rtk_decode_set_sm_reserve(int sms) {
+  g_last_error.clear();
+  if (sms < 0 || sms > 64) return fail(RTK_ERR_INVALID, "sms must be in [0, 64] (got %d)", sms);
+  g_decode_sm_reserve.store(sms, std::memory_order_relaxed);
+  return RTK_OK;
+}
 
 const char *rtk_last_error(void) { return g_last_error.c_str(); }
 
