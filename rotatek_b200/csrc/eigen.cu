@@ -347,25 +347,27 @@ __global__ void __launch_bounds__(kThreads, KMAX <= 32 ? 2 : 1) eigh_kernel(cons
 #pragma unroll 1
   for (int k = 0; k < kN - 2; ++k) {
     const int cur = k & 1, nxt = cur ^ 1;
-    // the reflector of column k: x = A[k+1:, k], H x = alpha e_1
-    const float x0 = sm.rowbuf[cur][k];           // A[k+1][k]
+    // the reflector of column k: x = A[k+1:, k], H x = alpha e_1, needed when
+    // the tail of x (its sum of squares ss) is not zero
     const float ss = sm.ssbuf[cur][0] + sm.ssbuf[cur][1] + sm.ssbuf[cur][2] + sm.ssbuf[cur][3];
-    float tk = 0.f, alpha = x0, v0 = 0.f;
-    if (ss > 0.f) {
-      const float nrm = sqrtf(fmaf(x0, x0, ss));
-      alpha = x0 >= 0.f ? -nrm : nrm;
-      v0 = x0 - alpha;
-      tk = 2.f / fmaf(v0, v0, ss);
-    }
-    if (tid == 0) {
-      sm.e[k] = alpha;
-      sm.tau[k] = tk;
-    }
     const int k1 = k + 1;
     const bool live_rows = r0 + 31 >= k1;          // this quarter holds rows of the trailing block
-    if (tk != 0.f) {                                // uniform across the CTA
-      // v_k -> row k of the shared matrix (for the back-transform)
-      if (tid < kN) A[k * kAS + tid] = tid == k1 ? v0 : sm.xbuf[cur][tid];
+    if (ss > 0.f) {                                 // uniform across the CTA
+      // only warps 0-3, which form p below, need the reflector's scalars
+      float tk = 0.f, v0 = 0.f;
+      if (warp < 4) {
+        const float x0 = sm.rowbuf[cur][k];         // A[k+1][k]
+        const float nrm = sqrtf(fmaf(x0, x0, ss));
+        const float alpha = x0 >= 0.f ? -nrm : nrm;
+        v0 = x0 - alpha;
+        tk = 2.f / fmaf(v0, v0, ss);
+        if (tid == 0) {
+          sm.e[k] = alpha;
+          sm.tau[k] = tk;
+        }
+        // v_k -> row k of the shared matrix (for the back-transform)
+        A[k * kAS + tid] = tid == k1 ? v0 : sm.xbuf[cur][tid];
+      }
       // p = tau A22 v: this thread's rows; row k+1 (v = v0) is added from rowbuf below
       float acc = 0.f;
       if (live_rows && col > k) {
@@ -402,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, KMAX <= 32 ? 2 : 1) eigh_kernel(cons
       // A22 <- A22 - v w^T - w v^T, w = p - K v, K = (tau / 2) p.v:
       // A_jc -= v_j (p_c - 2 K v_c) + p_j v_c
       if (live_rows && col > k) {
-        const float K = 0.5f * tk * (sm.red[0][0] + sm.red[0][1] + sm.red[0][2] + sm.red[0][3]);
+        const float K = 0.5f * sm.tau[k] * (sm.red[0][0] + sm.red[0][1] + sm.red[0][2] + sm.red[0][3]);
         const float vc = sm.xbuf[cur][col];
         const float cc = fmaf(-2.f * K, vc, sm.pbuf[col]);
 #pragma unroll
@@ -415,17 +417,23 @@ __global__ void __launch_bounds__(kThreads, KMAX <= 32 ? 2 : 1) eigh_kernel(cons
           a[r + 3] = fmaf(-xv.w, cc, fmaf(-pv4.w, vc, a[r + 3]));
         }
       }
+    } else if (tid == 0) {                          // column k is already reduced
+      sm.e[k] = sm.rowbuf[cur][k];
+      sm.tau[k] = 0.f;
     }
     // column k+1 and row k+2 for the next step
     const int k2 = k + 2;
     if (col == k1) {
       float ssn = 0.f;
 #pragma unroll
-      for (int r = 0; r < 32; ++r) {
-        const int j = r0 + r;
-        const float t = j > k2 ? a[r] : 0.f;
-        sm.xbuf[nxt][j] = t;
-        ssn = fmaf(t, t, ssn);
+      for (int r = 0; r < 32; r += 4) {
+        float4 t;
+        t.x = r0 + r > k2 ? a[r] : 0.f;
+        t.y = r0 + r + 1 > k2 ? a[r + 1] : 0.f;
+        t.z = r0 + r + 2 > k2 ? a[r + 2] : 0.f;
+        t.w = r0 + r + 3 > k2 ? a[r + 3] : 0.f;
+        *reinterpret_cast<float4 *>(&sm.xbuf[nxt][r0 + r]) = t;
+        ssn = fmaf(t.x, t.x, fmaf(t.y, t.y, fmaf(t.z, t.z, fmaf(t.w, t.w, ssn))));
       }
       sm.ssbuf[nxt][qtr] = ssn;
     }
