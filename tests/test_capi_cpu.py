@@ -150,3 +150,14 @@ def test_python_errors_match_reference_and_no_cpu_fallback():
         rotatek_decode(**kw)
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         full_channel_decode(q, kf, kf, 4)
+
+
+def test_decode_sm_reserve_validation(lib):
+    """rtk_decode_set_sm_reserve takes 0..64 SMs; anything else is refused
+    before it changes the setting."""
+    assert lib.rtk_decode_set_sm_reserve(-1) == _lib.RTK_ERR_INVALID
+    assert "sms must be in [0, 64]" in lib.rtk_last_error().decode()
+    assert lib.rtk_decode_set_sm_reserve(65) == _lib.RTK_ERR_INVALID
+    assert lib.rtk_decode_set_sm_reserve(0) == _lib.RTK_OK
+    with pytest.raises(ValueError, match="sms must be"):
+        _lib.set_decode_sm_reserve(100)

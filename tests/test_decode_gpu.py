@@ -371,3 +371,40 @@ def test_bounded_wait_timeout_is_reported_and_recoverable():
     assert_status_clean()
     with pytest.raises(ValueError, match="limit_ns"):
         _lib.selftest_wait_timeout(limit_ns=0)
+
+
+def test_decode_into_a_caller_buffer():
+    """out= writes the result into the caller's tensor -- here the head-major
+    send buffer of a head-sharded all_gather, viewed as [B, 1, H_q, D] -- and
+    returns it; the values are those of a fresh output."""
+    d = make(torch.bfloat16, 3, 28, 4, 900, 70, seed=31)
+    kw = d.as_kwargs()
+    want = odec.rotatek_decode(**{k: (x.cpu() if torch.is_tensor(x) else x) for k, x in kw.items()})
+    send = torch.full((28, 3, 128), float("nan"), dtype=torch.bfloat16, device=DEV)
+    view = send.permute(1, 0, 2).unsqueeze(1)
+    out, _, _ = rotatek_decode(**kw, out=view)
+    assert out.data_ptr() == send.data_ptr()
+    check(out, want, torch.bfloat16)
+    check(send.permute(1, 0, 2).unsqueeze(1), want, torch.bfloat16)
+    fresh, _, _ = rotatek_decode(**kw)
+    torch.testing.assert_close(out, fresh, rtol=0, atol=0)
+    with pytest.raises(ValueError, match="out must be"):
+        rotatek_decode(**kw, out=torch.empty(3, 1, 28, 64, dtype=torch.bfloat16, device=DEV))
+
+
+@pytest.mark.parametrize("reserve", [8, 64])
+def test_decode_with_sms_left_free(reserve):
+    """With SMs left to a concurrent collective the decode runs on fewer CTAs
+    (a different split of the same blocks): same results within the tolerance,
+    and the workspace sized for all SMs still serves it."""
+    d = make(torch.bfloat16, 4, 28, 4, 3000, 200, seed=37)
+    try:
+        _lib.set_decode_sm_reserve(reserve)
+        run_and_check(d, torch.bfloat16)
+        full_channel = d.as_kwargs()
+        dense = full_channel_decode(full_channel["q_full"], full_channel["k_full"], full_channel["v_full"], 7)
+        check(dense, odec.full_channel_decode(full_channel["q_full"].cpu(), full_channel["k_full"].cpu(),
+                                              full_channel["v_full"].cpu(), 7), torch.bfloat16)
+    finally:
+        _lib.set_decode_sm_reserve(0)
+    assert_status_clean()
