@@ -143,6 +143,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           acc[2 * k + 1] += hi;
         }
       }
+      // the generic-proxy reads above must be ordered before the TMA write
+      // that refills this stage (async proxy): without the proxy fence a
+      // refill overwrote tiles still being read when two CTAs shared an SM
+      fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[st]);
     }

@@ -903,7 +903,9 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
           }
         }
       }
-      if constexpr (FP8 || SPARK) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // our writes, then TMA's
+      // this warp's reads (and, for fp8 / SparK, in-place writes) of the stage
+      // are ordered before the TMA write that refills it (async proxy)
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[stage]);
     }

@@ -297,12 +297,12 @@ __global__ void __launch_bounds__(128, 1)
           *reinterpret_cast<uint32_t *>(ob + (row + 8) * C::kOutStride + ch) = pack2<T>(acc[j][nn][2], acc[j][nn][3]);
         }
     }
+    // the tile has been read: every lane orders its reads before the TMA
+    // write (async proxy) that refills the stage with this warp's unit
+    // kStages ahead
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
-    // the tile has been read: refill the stage with this warp's unit kStages ahead
-    if (lane == 0 && ic.i < n) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(ic);
-    }
+    if (lane == 0 && ic.i < n) issue(ic);
     advance(ic, C::kWarps);
     T *og = reinterpret_cast<T *>(p.out) + (long long)b * p.o_s[0] + (long long)h * p.o_s[1];
     constexpr int kChunks = kTile * KEEP / 8;                   // 16-byte chunks of the tile

@@ -49,6 +49,27 @@ def test_key_covariance(dtype, B, H, S):
     np.testing.assert_allclose(f64(ksum), kk.sum(axis=2), rtol=1e-5, atol=1e-3)
 
 
+@pytest.mark.parametrize("B,H,S", [
+    (8, 4, 8000),    # 32 matrices x 8-CTA clusters = 256 CTAs: two per SM, 16 tiles per CTA
+    (74, 4, 512),    # 296 matrices, no cluster: two CTAs per SM, 8 tiles (the ring wraps)
+])
+def test_key_covariance_two_ctas_per_sm(B, H, S):
+    """Channel sums when two CTAs share an SM and every stage is refilled.
+    The sums are read from the TMA-filled stages by ordinary loads; a stage
+    released without a proxy fence was overwritten while being read (sums off
+    by tens of percent, the covariance unaffected).  Reference: torch float64
+    on the same device."""
+    full = torch.randn(B, H, S + 640, 128, device=DEV, generator=torch.Generator(DEV).manual_seed(B + S))
+    view = full.to(torch.bfloat16)[:, :, 64:64 + S]
+    for keys in (view, view.contiguous()):
+        cov, ksum = rot.key_covariance(keys)
+        k64 = keys.double()
+        want_ks = k64.sum(2)
+        want_cov = torch.einsum("bhsd,bhse->bhde", k64, k64)
+        assert ((ksum.double() - want_ks).abs().amax() / want_ks.abs().amax()).item() < 1e-5
+        assert ((cov.double() - want_cov).norm() / want_cov.norm()).item() < 1e-5
+
+
 def test_key_covariance_strided_view():
     """The visual span is a slice of the full Keys [B, H, S_total, D]."""
     full = syn.lowrank_keys(2, 4, 64 + 3000 + 100, seed=3, device=DEV, dtype=torch.bfloat16)
