@@ -26,36 +26,24 @@ cudaError_t launch_cov_tc(int dtype_is_bf16, const CUtensorMap &keys_map, const 
                           cudaStream_t stream);
 cudaError_t launch_cov_simt(const CovParams &p, cudaStream_t stream);
 
-// Fused Key projection (the prefill K path of the attention adapters, then the
-// covariance pass): for every (b, h) and every token s,
+// Key projection (the prefill K path of the attention adapters): for every
+// (b, h) and every token s,
 //   K[b, h, s, :] = RoPE(X[b, s, :] W[h*128 : h*128 + 128, :]^T + bias)
 // in the Keys' dtype, rounded like torch's bf16 / fp16 ops (projection output,
-// k * cos, rotate_half(k) * sin, their sum), and over the visual tokens
-// [vis_start, vis_start + vis_len) the raw sums of CovParams from those K values.
+// k * cos, rotate_half(k) * sin, their sum).  The visual span's sums of
+// CovParams are taken afterwards from the K values written (L2-warm).
 struct KProjParams {
   int batch, heads, seq, hidden;  // hidden % 64 == 0
   int vis_start, vis_len;
   const void *bias;                       // [heads * 128] or NULL
   const void *cos, *sin;                  // [B | 1, S, 128] (element strides below, channel stride 1)
   long long cs_sb, cs_ss;                 // batch stride (0 = broadcast), token stride
-  float *part;                            // per-group partial sums (kproj_workspace_floats)
-  float *cov;                             // [B * H][128][128]
-  float *ksum;                            // [B * H][128]
+  int cs_wide;                            // cos / sin rows 32-byte aligned: 256-bit loads
   unsigned int *status;                   // device status word (bounded-wait timeouts)
   int grid;                               // CTAs: groups * ceil(H / 2) clusters of 2
 };
 
-// One (group, b, head) partial: sum k k^T (128 x 128) then four per-warp
-// channel sums (4 x 128).  Slots are indexed ((group + b) * P + pair) * 2 +
-// head-in-pair, P = ceil(H / 2); the grid is groups * P two-CTA clusters.
-constexpr int kKProjPartFloats = 128 * 128 + 4 * 128;
-
 inline long long kproj_pairs(long long heads) { return (heads + 1) / 2; }
-inline long long kproj_workspace_floats(long long batch, long long heads, long long grid) {
-  return (grid / (2 * kproj_pairs(heads)) + batch) * kproj_pairs(heads) * 2 * kKProjPartFloats;
-}
-// Pair steps (two 128-token tiles of one span) of one sequence.
-int kproj_steps_per_b(int seq, int vis_start, int vis_len);
 
 // x: [B, S, hidden] 3-D map, box {64, 128, 1}; w: [H*128, hidden] 2-D map, box
 // {64, 128}; k_out[i]: the output [B, H, len_i, 128] of span i (prompt, visual,
@@ -67,7 +55,7 @@ struct KProjMaps {
 // Two-CTA clusters of the projection kernel that fit the current device at once (0 if unknown).
 int kproj_max_clusters(int dtype_is_bf16);
 
-// The projection kernel (grid = p.grid), then the reduction of its partials into cov / ksum.
+// The projection kernel (grid = p.grid).
 cudaError_t launch_kproj_tc(int dtype_is_bf16, const KProjMaps &maps, const KProjParams &p,
                             cudaStream_t stream);
 

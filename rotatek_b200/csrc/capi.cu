@@ -883,18 +883,12 @@ int64_t kproj_grid(int64_t B, int64_t H, int64_t S, int64_t vis_start, int64_t v
   const int64_t groups = std::max<int64_t>(1, std::min<int64_t>(kproj_cluster_slots(device) / pairs, items));
   return groups * pairs * 2;
 }
-size_t kproj_part_bytes(int64_t B, int64_t H, int64_t S, int64_t vis_start, int64_t vis_len, int device) {
-  return align_up((size_t)rtk::kproj_workspace_floats(B, H, kproj_grid(B, H, S, vis_start, vis_len, device)) *
-                  sizeof(float));
-}
-
-// Validate and launch the fused projection; cov / ksum are B*H contiguous
-// fp32 blocks, `part` the partial-sum scratch of kproj_part_bytes.
+// Validate and launch the projection, then the visual span's sums from the
+// Keys just written; cov / ksum are B*H contiguous fp32 blocks.
 // keys_out [B, H, S, 128].
 int run_key_projection(const rtk_tensor *x, const rtk_tensor *w, const rtk_tensor *bias,
                        const rtk_tensor *cos, const rtk_tensor *sin, int64_t vis_start, int64_t vis_len,
-                       const rtk_tensor *keys_out, float *cov, float *ksum, float *part, size_t part_bytes,
-                       unsigned int *status, cudaStream_t st) {
+                       const rtk_tensor *keys_out, float *cov, float *ksum, unsigned int *status, cudaStream_t st) {
   if (x == nullptr || x->ndim != 3) return fail(RTK_ERR_INVALID, "hidden_states must be [B, S, hidden]");
   const int64_t B = x->shape[0], S = x->shape[1], Hd = x->shape[2];
   const int dt = x->dtype;
@@ -970,17 +964,26 @@ int run_key_projection(const rtk_tensor *x, const rtk_tensor *w, const rtk_tenso
   kp.bias = bias != nullptr ? bias->data : nullptr;
   kp.cos = cos->data; kp.sin = sin->data;
   kp.cs_sb = cs_sb; kp.cs_ss = cos->stride[1];
-  kp.cov = cov; kp.ksum = ksum;
+  kp.cs_wide = (cos->stride[1] * 2) % 32 == 0 && (cs_sb * 2) % 32 == 0 &&
+               reinterpret_cast<uintptr_t>(cos->data) % 32 == 0 && reinterpret_cast<uintptr_t>(sin->data) % 32 == 0;
   kp.status = status;
   // persistent: groups x head pairs x 2 CTAs, one CTA per SM; contiguous shares of the B x steps items
   const int device = current_device();
   kp.grid = (int)kproj_grid(B, H, S, vis_start, vis_len, device);
-  const size_t need = kproj_part_bytes(B, H, S, vis_start, vis_len, device);
-  if (part == nullptr || part_bytes < need)
-    return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes for partial sums, needs %zu", part_bytes, need);
-  kp.part = part;
-  const cudaError_t e = rtk::launch_kproj_tc(dt == RTK_BF16, maps, kp, st);
+  cudaError_t e = rtk::launch_kproj_tc(dt == RTK_BF16, maps, kp, st);
   if (e != cudaSuccess) return cuda_fail(e, "key projection launch");
+  // sum k k^T and sum k over the visual span, read back while the Keys are in L2
+  if (vis_len == 0) {
+    e = cudaMemsetAsync(cov, 0, (size_t)B * H * 128 * 128 * sizeof(float), st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ksum, 0, (size_t)B * H * 128 * sizeof(float), st);
+  } else {
+    View4 kv;
+    as4(keys_out, kv);
+    kv.data = static_cast<const unsigned char *>(keys_out->data) + vis_start * keys_out->stride[2] * 2;
+    kv.n[2] = vis_len;
+    e = launch_covariance(kv, dt, cov, ksum, device, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "key projection (visual-span sums) launch");
   return RTK_OK;
 }
 }  // namespace
@@ -1063,24 +1066,22 @@ int rtk_key_projection(const rtk_tensor *hidden, const rtk_tensor *w_k, const rt
     return fail(RTK_ERR_INVALID, "ksum_out must be a contiguous float32 [B, H_kv, 128]");
   if (workspace == nullptr || workspace_bytes < kStatusBytes)
     return fail(RTK_ERR_WORKSPACE, "workspace has %zu bytes, needs at least %zu", workspace_bytes, kStatusBytes);
-  unsigned char *ws = static_cast<unsigned char *>(workspace);
   return run_key_projection(hidden, w_k, bias, cos, sin, vis_start, vis_len, keys_out,
                             static_cast<float *>(cov_out->data), static_cast<float *>(ksum_out->data),
-                            reinterpret_cast<float *>(ws + kStatusBytes), workspace_bytes - kStatusBytes,
-                            reinterpret_cast<unsigned int *>(ws), static_cast<cudaStream_t>(stream));
+                            static_cast<unsigned int *>(workspace), static_cast<cudaStream_t>(stream));
 }
 
 size_t rtk_key_projection_workspace_size(int64_t batch, int64_t kv_heads, int64_t seq, int64_t vis_start,
                                          int64_t vis_len, int32_t device) {
-  if (batch <= 0 || kv_heads <= 0 || seq <= 0 || vis_start < 0 || vis_len < 0 || vis_start + vis_len > seq)
-    return kStatusBytes;
-  return kStatusBytes + kproj_part_bytes(batch, kv_heads, seq, vis_start, vis_len, device);
+  // the projection needs no scratch beyond the status word
+  (void)batch; (void)kv_heads; (void)seq; (void)vis_start; (void)vis_len; (void)device;
+  return kStatusBytes;
 }
 
 size_t rtk_build_rotation_projected_workspace_size(int64_t batch, int64_t kv_heads, int64_t seq,
                                                    int64_t vis_start, int64_t vis_len, int32_t device) {
-  return rtk_build_rotation_workspace_size(batch, kv_heads, 128) +
-         rtk_key_projection_workspace_size(batch, kv_heads, seq, vis_start, vis_len, device) - kStatusBytes;
+  (void)seq; (void)vis_start; (void)vis_len; (void)device;
+  return rtk_build_rotation_workspace_size(batch, kv_heads, 128);
 }
 
 int rtk_build_rotation_projected(const rtk_tensor *hidden, const rtk_tensor *w_k, const rtk_tensor *bias,
@@ -1109,8 +1110,7 @@ int rtk_build_rotation_projected(const rtk_tensor *hidden, const rtk_tensor *w_k
   const BuildWs w = build_ws(workspace, B * H, 128);
   // ---- K = RoPE(X W^T + b) for every token, with the visual span's sums
   const int prc = run_key_projection(hidden, w_k, bias, cos, sin, vis_start, vis_len, keys_out, w.cov, w.ksum,
-                                     reinterpret_cast<float *>(static_cast<unsigned char *>(workspace) + build_bytes),
-                                     workspace_bytes - build_bytes, w.status, st);
+                                     w.status, st);
   if (prc != RTK_OK) return prc;
   // ---- the rest of the build on the visual Keys just written
   View4 kv;

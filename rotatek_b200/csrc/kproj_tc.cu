@@ -25,15 +25,24 @@
 //              staging tiles read MN-major) into columns 256-511 -- issued
 //              right after the next tile's projection, while its accumulator
 //              drains
-//   warps 2-9  epilogue, group h = head h of the pair, one token row per
-//              thread: drain TMEM (+ bias, round) into registers, free the
-//              accumulator, RoPE with torch's roundings, then write the row
-//              into head h's staging tile -- in CTA h, through DSMEM when that
-//              is the other CTA.  CTA h's staging thus holds head h for all
-//              256 tokens: the TMA-store source, the covariance operand (D's
-//              rows in CTA h are head h's channels, and its columns 128 h ...
-//              hold cov(head h); the other 128 columns get cross terms that are
-//              never read), and the source of head h's channel sums.
+//   warps 2-9  epilogue, one token row per thread; warp group c (warps 2-5,
+//              6-9) takes channel half c of BOTH heads: the channels
+//              [32 c, 32 c + 32) and their RoPE partners + 64.  Drain TMEM
+//              (+ bias, round) into registers, free the accumulator, fetch the
+//              row's cos / sin once for both heads, RoPE with torch's
+//              roundings, then write head h's part of the row into head h's
+//              staging tile -- which lives in CTA h, so one head goes through
+//              DSMEM.  CTA h's staging thus holds head h for all 256 tokens:
+//              the TMA-store source, the covariance operand (D's rows in CTA h
+//              are head h's channels, and its columns 128 h ... hold
+//              cov(head h); the other 128 columns get cross terms that are
+//              never read), and the source of head h's channel sums, which
+//              all eight warps of CTA h read.
+//
+//              The epilogue shares the SM's L1 / shared-memory data path with
+//              the tensor core's operand reads and the TMA writes, so what it
+//              costs there is what it takes from the GEMM: cos / sin are read
+//              once per row (not once per head) and 32 bytes per lane.
 //
 // Work split: each span (prompt, visual, text) is tiled from its own start in
 // 128-token tiles, and its tiles are taken two at a time (CTA 0, CTA 1) -- a
@@ -57,19 +66,20 @@ constexpr int kXBox = 128 * 128;             // {64 hidden x 128 tokens}, 16-bit
 constexpr int kWBox = 128 * 128;             // {64 hidden x 128 channels}
 constexpr int kStageBytes = kXBox + kWBox;   // 32 KB
 constexpr int kStages = 5;
-constexpr int kStageTile = 256 * 128;        // {64 channels x 256 tokens} staging box
+constexpr int kBox = 128 * 128;              // {64 channels x 128 tokens} staging / store box
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr uint32_t kCovCol = 256;            // covariance accumulator columns 256-511
-constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAccCols = 256;           // one accumulator: 128 tokens x (2 heads x 128 channels)
+constexpr uint32_t kTmemCols = 2 * kAccCols; // double-buffered
 constexpr uint16_t kPairMask = 0x3;          // both CTAs of the (two-CTA) cluster
 
 struct KpSmem {
   static constexpr int kRing = 0;
-  static constexpr int kStage = kRing + kStages * kStageBytes;   // channels 0-63 | 64-127, 256 rows each
-  static constexpr int kBar = kStage + 2 * kStageTile;
-  // full[S], empty[S], acc_full, acc_empty, staged, filled, free[2], cov_done, cov_flushed
-  static constexpr int kNumBars = 2 * kStages + 8;
+  // this CTA's 128 tokens of both heads: boxes [head][channels 0-63 | 64-127]
+  static constexpr int kStage = kRing + kStages * kStageBytes;
+  static constexpr int kBar = kStage + 4 * kBox;
+  // full[S], empty[S], acc_full[2], acc_empty[2]
+  static constexpr int kNumBars = 2 * kStages + 4;
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemSlot + 4;                     // bounded-wait abort flag
   static constexpr int kBias = (kAbort + 4 + 15) & ~15;           // fp32 [2][128]
@@ -128,11 +138,6 @@ struct Range {
   int begin, end, steps_per_b;
   __device__ int unit(int j) const { return j / steps_per_b; }
   __device__ int step(int j) const { return j % steps_per_b; }
-  // last index of the range that belongs to unit(j)
-  __device__ int unit_last(int j) const {
-    const int u_end = (unit(j) + 1) * steps_per_b;
-    return (u_end < end ? u_end : end) - 1;
-  }
 };
 
 __host__ __device__ inline long long range_begin(int c, long long total, int grid) {
@@ -152,65 +157,84 @@ __device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
   unpack2<T>(v.w, f[6], f[7]);
 }
 
-// Drain one head's 128 accumulator columns of this thread's row:
-// k = round(acc + bias), packed in pairs (channels 2j, 2j+1 in k[j]).
+// An epilogue thread owns one token row and one half of the channel pairs
+// that RoPE couples: channels [32 c, 32 c + 32) and [64 + 32 c, 96 + 32 c) of
+// BOTH heads of the pair (c = 0, 1 for the two warp groups).  Per head it
+// keeps 64 values packed in 32 words: k[0..15] the low channels, k[16..31]
+// the high ones.  The row's cos / sin for those channels (256 bytes) are
+// fetched once and serve both heads.
+
+// Drain one head's 64 accumulator columns of this thread's row:
+// k = round(acc + bias).  `cols` addresses channel 32 c of the head.
 template <typename T>
-__device__ __forceinline__ void drain_row(uint32_t tmem_row, const float *bias, uint32_t (&k)[64]) {
-  // two batches of four loads per wait: the accumulator is released sooner
+__device__ __forceinline__ void drain_half(uint32_t cols, const float *bias, uint32_t (&k)[32]) {
+  uint32_t r[4][16];
+  tmem_ld16_nowait(cols, r[0]);
+  tmem_ld16_nowait(cols + 16, r[1]);
+  tmem_ld16_nowait(cols + 64, r[2]);
+  tmem_ld16_nowait(cols + 80, r[3]);
+  tmem_wait_ld();
 #pragma unroll
-  for (int c4 = 0; c4 < 8; c4 += 4) {
-    uint32_t r[4][16];
+  for (int c = 0; c < 4; ++c) {
+    const float *bc = bias + (c & 1) * 16 + (c >> 1) * 64;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) tmem_ld16_nowait(tmem_row + 16 * (c4 + c), r[c]);
-    tmem_wait_ld();
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-#pragma unroll
-      for (int e = 0; e < 16; e += 2)
-        k[8 * (c4 + c) + e / 2] = pack2<T>(__fadd_rn(__uint_as_float(r[c][e]), bias[16 * (c4 + c) + e]),
-                                           __fadd_rn(__uint_as_float(r[c][e + 1]), bias[16 * (c4 + c) + e + 1]));
+    for (int e = 0; e < 16; e += 2)
+      k[8 * c + e / 2] = pack2<T>(__fadd_rn(__uint_as_float(r[c][e]), bc[e]),
+                                  __fadd_rn(__uint_as_float(r[c][e + 1]), bc[e + 1]));
   }
 }
 
-// RoPE on a drained row, in place:
+__device__ __forceinline__ void ldg_v8(const void *ptr, uint4 &a, uint4 &b) {
+  asm("ld.global.nc.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w), "=r"(b.x), "=r"(b.y), "=r"(b.z), "=r"(b.w)
+      : "l"(ptr));
+}
+
+// 16 channels (two 8-channel groups) of a cos / sin row: one 256-bit load
+// when the row is 32-byte aligned (one L1 wavefront per 32 bytes, where
+// 16-byte loads of different rows take one per 16), else two 128-bit loads.
+template <typename T>
+__device__ __forceinline__ void ldg_16ch(const T *ptr, bool wide, uint4 &a, uint4 &b) {
+  if (wide) {
+    ldg_v8(ptr, a, b);
+  } else {
+    a = __ldg(reinterpret_cast<const uint4 *>(ptr));
+    b = __ldg(reinterpret_cast<const uint4 *>(ptr + 8));
+  }
+}
+
+// RoPE on 8 channel pairs of a half row (group u: low channels k[4u .. 4u+3],
+// their partners + 64 in k[16 + 4u ...]), in place, for both heads (the
+// second only when `both`):
 //   out_lo = round(round(k_lo cos_lo) - round(k_hi sin_lo))   channels d < 64
 //   out_hi = round(round(k_hi cos_hi) + round(k_lo sin_hi))   channels d + 64
 // which is torch's  k * cos + rotate_half(k) * sin  in the Keys' dtype.
-// Rows past the end of their span become zero.
+// cos / sin are unpacked two channels at a time, so few values are live.
 template <typename T>
-__device__ __forceinline__ void rope_row(const T *crow, const T *srow, bool valid, uint32_t (&k)[64]) {
+__device__ __forceinline__ void rope_pair(uint32_t cl, uint32_t ch, uint32_t sl, uint32_t sh, uint32_t &klo,
+                                          uint32_t &khi) {
+  float c0, c1, d0, d1, s0, s1, t0, t1, l0, l1, h0, h1;
+  unpack2<T>(cl, c0, c1);
+  unpack2<T>(ch, d0, d1);
+  unpack2<T>(sl, s0, s1);
+  unpack2<T>(sh, t0, t1);
+  unpack2<T>(klo, l0, l1);
+  unpack2<T>(khi, h0, h1);
+  klo = pack2<T>(__fsub_rn(round_to<T>(__fmul_rn(l0, c0)), round_to<T>(__fmul_rn(h0, s0))),
+                 __fsub_rn(round_to<T>(__fmul_rn(l1, c1)), round_to<T>(__fmul_rn(h1, s1))));
+  khi = pack2<T>(__fadd_rn(round_to<T>(__fmul_rn(h0, d0)), round_to<T>(__fmul_rn(l0, t0))),
+                 __fadd_rn(round_to<T>(__fmul_rn(h1, d1)), round_to<T>(__fmul_rn(l1, t1))));
+}
+
+template <typename T>
+__device__ __forceinline__ void rope_group(const uint4 &clo, const uint4 &chi, const uint4 &slo, const uint4 &shi,
+                                           int u, bool both, uint32_t (&k0)[32], uint32_t (&k1)[32]) {
+  const uint32_t c[4] = {clo.x, clo.y, clo.z, clo.w}, d[4] = {chi.x, chi.y, chi.z, chi.w};
+  const uint32_t s[4] = {slo.x, slo.y, slo.z, slo.w}, t[4] = {shi.x, shi.y, shi.z, shi.w};
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const int d = 8 * q;
-    if (!valid) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        k[d / 2 + e] = 0u;
-        k[(d + 64) / 2 + e] = 0u;
-      }
-      continue;
-    }
-    float cl[8], ch[8], sl[8], sh[8], lo[8], hi[8];
-    unpack8<T>(__ldg(reinterpret_cast<const uint4 *>(crow + d)), cl);
-    unpack8<T>(__ldg(reinterpret_cast<const uint4 *>(crow + d + 64)), ch);
-    unpack8<T>(__ldg(reinterpret_cast<const uint4 *>(srow + d)), sl);
-    unpack8<T>(__ldg(reinterpret_cast<const uint4 *>(srow + d + 64)), sh);
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      unpack2<T>(k[(d + e) / 2], lo[e], lo[e + 1]);
-      unpack2<T>(k[(d + 64 + e) / 2], hi[e], hi[e + 1]);
-    }
-    float olo[8], ohi[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      olo[e] = __fsub_rn(round_to<T>(__fmul_rn(lo[e], cl[e])), round_to<T>(__fmul_rn(hi[e], sl[e])));
-      ohi[e] = __fadd_rn(round_to<T>(__fmul_rn(hi[e], ch[e])), round_to<T>(__fmul_rn(lo[e], sh[e])));
-    }
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      k[(d + e) / 2] = pack2<T>(olo[e], olo[e + 1]);
-      k[(d + 64 + e) / 2] = pack2<T>(ohi[e], ohi[e + 1]);
-    }
+  for (int w = 0; w < 4; ++w) {
+    rope_pair<T>(c[w], d[w], s[w], t[w], k0[4 * u + w], k0[16 + 4 * u + w]);
+    if (both) rope_pair<T>(c[w], d[w], s[w], t[w], k1[4 * u + w], k1[16 + 4 * u + w]);
   }
 }
 
@@ -222,13 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + KpSmem::kBar);   // rank 0's is used
   uint64_t *empty_bar = full_bar + kStages;
-  uint64_t *acc_full = empty_bar + kStages;   // projection accumulator ready (both CTAs)
-  uint64_t *acc_empty = acc_full + 1;         // rank 0: drained, one arrival per epilogue warp of the pair
-  uint64_t *staged_bar = acc_empty + 1;       // rank 0: both staging tiles written (4 group arrivals)
-  uint64_t *filled_bar = staged_bar + 1;      // this CTA's staging tile written by both CTAs
-  uint64_t *free_bar = filled_bar + 1;        // [2]: staging tile of head h read by its store and MMAs
-  uint64_t *cov_done = free_bar + 2;          // a unit's covariance MMAs completed (both CTAs)
-  uint64_t *cov_flushed = cov_done + 1;       // rank 0: ... and read out by both CTAs
+  uint64_t *acc_full = empty_bar + kStages;   // [2] accumulator ready (both CTAs)
+  uint64_t *acc_empty = acc_full + 2;         // [2] rank 0: drained, one arrival per epilogue warp of the pair
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + KpSmem::kTmemSlot);
   float *bias_s = reinterpret_cast<float *>(smem + KpSmem::kBias);
   unsigned char *stage = smem + KpSmem::kStage;
@@ -258,14 +277,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 2 * kEpiWarps);
-    mbar_init(staged_bar, 4);
-    mbar_init(filled_bar, 2);
-    mbar_init(&free_bar[0], 2);    // the tile's MMA side + its store
-    mbar_init(&free_bar[1], 2);
-    mbar_init(cov_done, 1);
-    mbar_init(cov_flushed, 2 * kEpiWarps);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * kEpiWarps);
+    }
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -301,52 +316,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer (rank 0)
+    // ---------------- MMA issuer (rank 0): tile i accumulates into buffer i & 1
     if (lane == 0 && r == 0) {
       constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
       constexpr uint32_t kIdProj = idesc_f16(kFmt, 0u, 0u, 256u, 256u);   // X, W K-major
-      constexpr uint32_t kIdCov = idesc_f16(kFmt, 1u, 1u, 256u, 256u);    // staging MN-major
-      const uint32_t stage_addr = smem_u32(stage);
-      uint32_t free_at[2][2];                        // [head][cta]
-      for (int h = 0; h < 2; ++h)
-        for (int c = 0; c < 2; ++c) free_at[h][c] = map_to_cta(smem_u32(&free_bar[h]), c);
-      // staging uses (one per pair step) in order
-      int uj = rg.begin, un = 0, nflush = 0, cur_unit = -1;
-      bool started = false;
-      auto take_use = [&]() {
-        mbar_wait_cluster_bounded(staged_bar, un & 1, &abort_flag, status);
-        const int u = rg.unit(uj);
-        if (u != cur_unit) {
-          // the previous unit's accumulators must have been read out
-          if (cur_unit >= 0) mbar_wait_cluster_bounded(cov_flushed, (nflush - 1) & 1, &abort_flag, status);
-          cur_unit = u;
-          started = false;
-        }
-        if (sp.span_of(rg.step(uj)) == 1) {
-          tc_fence_after();
-#pragma unroll
-          for (int ks = 0; ks < 2 * kRows / 16; ++ks) {
-            const uint64_t d = smem_desc_sw128(stage_addr + ks * 2048, kStageTile, 1024);
-            umma_pair_f16(tmem + kCovCol, d, d, kIdCov, (started || ks > 0) ? 1u : 0u);
-          }
-          started = true;
-          umma_pair_commit(&free_bar[0], kPairMask);
-          umma_pair_commit(&free_bar[1], kPairMask);
-        } else {
-          for (int h = 0; h < 2; ++h)
-            for (int c = 0; c < 2; ++c) mbar_arrive_cluster(free_at[h][c]);
-        }
-        ++un;
-        if (uj == rg.unit_last(uj)) {
-          umma_pair_commit(cov_done, kPairMask);   // the unit's last use: its sums are complete
-          ++nflush;
-        }
-        ++uj;
-      };
       int it = 0;
       for (int i = 0; i < nt; ++i) {
-        mbar_wait_cluster_bounded(acc_empty, (i & 1) ^ 1, &abort_flag, status);
+        const int a = i & 1;
+        if (!mbar_wait_cluster_bounded(&acc_empty[a], ((i >> 1) & 1) ^ 1, &abort_flag, status)) break;
         tc_fence_after();
+        const uint32_t acc = tmem + kAccCols * a;
         for (int kc = 0; kc < nk; ++kc, ++it) {
           const int st = it % kStages;
           mbar_wait_cluster_bounded(&full_bar[st], (it / kStages) & 1, &abort_flag, status);
@@ -356,152 +335,98 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int ks = 0; ks < 4; ++ks) {
             const uint64_t da = smem_desc_sw128(base + ks * 32, 16, 1024);
             const uint64_t db = smem_desc_sw128(base + kXBox + ks * 32, 16, 1024);
-            umma_pair_f16(tmem, da, db, kIdProj, (kc > 0 || ks > 0) ? 1u : 0u);
+            umma_pair_f16(acc, da, db, kIdProj, (kc > 0 || ks > 0) ? 1u : 0u);
           }
           umma_pair_commit(&empty_bar[st], kPairMask);   // both CTAs' stages free once read
         }
-        umma_pair_commit(acc_full, kPairMask);
-        // the previous step's covariance MMAs keep the tensor pipe busy while
-        // the epilogue drains this accumulator
-        while (uj < rg.begin + i) take_use();
+        umma_pair_commit(&acc_full[a], kPairMask);
       }
-      while (uj < rg.end) take_use();
     }
   } else {
-    // ---------------- epilogue: warp group hh handles head hh of the pair
-    const int e = warp - 2;
-    const int hh = e >> 2;
+    // ---------------- epilogue: warp group c handles channel half c of both heads
+    const int e = warp - 2;                        // 0..7
+    const int ch = e >> 2;                         // channel half
     const int quarter = warp & 3;                  // TMEM lanes this warp may read
-    const int row = 32 * quarter + lane;           // token row (projection) / channel (covariance)
-    const int gt = (e & 3) * 32 + lane;            // thread index inside the group
+    const int row = 32 * quarter + lane;           // token row of this CTA's tile
+    const int tid = e * 32 + lane;                 // 0..255
     const uint32_t tmem_lane = tmem + ((uint32_t)(32 * quarter) << 16);
-    const bool owner = hh == static_cast<int>(r);   // head hh's staging tile lives in this CTA
-    const bool has = hh < nh;
-    const int head = 2 * hp + hh;
-    const uint32_t stage_hh = map_to_cta(smem_u32(stage), hh);
-    const uint32_t filled_hh = map_to_cta(smem_u32(filled_bar), hh);
-    const uint32_t staged0 = map_to_cta(smem_u32(staged_bar), 0);
+    const bool has1 = nh > 1;
     const uint32_t acc_empty0 = map_to_cta(smem_u32(acc_empty), 0);
-    const uint32_t cov_flushed0 = map_to_cta(smem_u32(cov_flushed), 0);
-    const uint32_t free_mine = map_to_cta(smem_u32(&free_bar[hh]), r);
-    const uint32_t free_peer = map_to_cta(smem_u32(&free_bar[hh]), r ^ 1u);
-    const int chunk = gt & 15, rgp = gt >> 4;      // channel sums: 8 channels x 32 rows
-    float ks_acc[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) ks_acc[k] = 0.f;
+    const uint32_t stage_u32 = smem_u32(stage);
     const T *bias_g = static_cast<const T *>(p.bias);
-    int nflush = 0, cur_unit = -1;
-    bool stored = false, unit_vis = false;
+    const bool wide = p.cs_wide != 0;
+    int cur_unit = -1;
+    bool stored = false;
     for (int i = 0; i < nt; ++i) {
       const int j = rg.begin + i;
       const int b = rg.unit(j), step = rg.step(j);
+      const int a = i & 1;
       const StepTile mine = step_tile(sp, step, static_cast<int>(r));
-      if (b != cur_unit) {   // this head's bias
-        named_barrier_sync(1 + hh, 128);
-        bias_s[128 * hh + gt] = (has && bias_g != nullptr) ? to_f32<T>(bias_g[head * 128 + gt]) : 0.f;
-        named_barrier_sync(1 + hh, 128);
+      if (b != cur_unit) {   // both heads' bias
+        named_barrier_sync(1, 256);
+        const int hb = tid >> 7;
+        bias_s[tid] = ((hb == 0 || has1) && bias_g != nullptr) ? to_f32<T>(bias_g[(2 * hp + hb) * 128 + (tid & 127)])
+                                                               : 0.f;
+        named_barrier_sync(1, 256);
         cur_unit = b;
-        unit_vis = false;
       }
-      mbar_wait_cluster_bounded(acc_full, i & 1, &abort_flag, status);
+      mbar_wait_cluster_bounded(&acc_full[a], (i >> 1) & 1, &abort_flag, status);
       tc_fence_after();
-      uint32_t kv[64];
-      if (has) drain_row<T>(tmem_lane + 128 * hh, bias_s + 128 * hh, kv);
+      uint32_t kv[2][32];
+      const uint32_t acc = tmem_lane + kAccCols * a;
+      drain_half<T>(acc + 32 * ch, bias_s + 32 * ch, kv[0]);
+      if (has1) drain_half<T>(acc + 128 + 32 * ch, bias_s + 128 + 32 * ch, kv[1]);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(acc_empty0);   // the accumulator may be overwritten
-      if (has) {
-        const int t = mine.row0 + row;
-        const bool valid = mine.exists && t < mine.end;
-        const long long cs = (long long)b * p.cs_sb + (long long)t * p.cs_ss;
-        rope_row<T>(static_cast<const T *>(p.cos) + cs, static_cast<const T *>(p.sin) + cs, valid, kv);
-      }
-      // head hh's staging tile is free once the previous step's store and MMAs have read it
-      if (i > 0) mbar_wait_cluster_bounded(&free_bar[hh], (i - 1) & 1, &abort_flag, status);
-      if (has) {
-        const int srow = static_cast<int>(r) * kRows + row;
+      if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * a);   // this buffer may be overwritten
+      const int t = mine.row0 + row;
+      const bool valid = mine.exists && t < mine.end;   // rows past the span's end become zero
+      // the staging boxes are free once the previous step's stores have read them
+      if (tid == 0 && stored) bulk_wait_read_all();
+      named_barrier_sync(1, 256);
+      const long long cs = (long long)b * p.cs_sb + (long long)(valid ? t : 0) * p.cs_ss + 32 * ch;
+      const T *crow = static_cast<const T *>(p.cos) + cs, *srow = static_cast<const T *>(p.sin) + cs;
+      // two rounds of 16 channel pairs: the row's cos / sin serve both heads
 #pragma unroll
-        for (int c8 = 0; c8 < 16; ++c8)
-          st_cluster_v4(stage_hh + (c8 >> 3) * kStageTile + swizzled_offset<128>(srow, (c8 & 7) * 8),
-                        make_uint4(kv[4 * c8], kv[4 * c8 + 1], kv[4 * c8 + 2], kv[4 * c8 + 3]));
-      }
-      fence_proxy_async_cluster();
-      named_barrier_sync(1 + hh, 128);
-      if (gt == 0) {
-        mbar_arrive_cluster(staged0);
-        mbar_arrive_cluster(filled_hh);
-      }
-      if (owner) {
-        // both CTAs' rows of head hh are in this CTA's staging tile
-        mbar_wait_cluster_bounded(filled_bar, i & 1, &abort_flag, status);
-        fence_proxy_async_smem();
-        if (gt == 0 && has) {
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const StepTile tl = step_tile(sp, step, half);
-            if (!tl.exists) continue;
-            for (int c = 0; c < 2; ++c)
-              tma_store_4d(&maps.k_out[tl.span], stage + c * kStageTile + half * kRows * 128, 64 * c,
-                           tl.row0 - tl.start, head, b);
-          }
-          bulk_commit_group();
-          stored = true;
+      for (int half = 0; half < 2; ++half) {
+        uint4 clo[2], chi[2], slo[2], shi[2];
+        if (valid) {
+          ldg_16ch<T>(crow + 16 * half, wide, clo[0], clo[1]);
+          ldg_16ch<T>(crow + 64 + 16 * half, wide, chi[0], chi[1]);
+          ldg_16ch<T>(srow + 16 * half, wide, slo[0], slo[1]);
+          ldg_16ch<T>(srow + 64 + 16 * half, wide, shi[0], shi[1]);
         }
-        if (has && mine.span == 1) {
-          unit_vis = true;
-          const unsigned char *box = stage + (chunk >> 3) * kStageTile;
-#pragma unroll 4
-          for (int rr = 0; rr < 32; ++rr) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(box + swizzled_offset<128>(rgp * 32 + rr, (chunk & 7) * 8));
-            float f[8];
-            unpack8<T>(v, f);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) ks_acc[k] += f[k];
-          }
-        }
-        named_barrier_sync(1 + hh, 128);           // every thread is done reading the staging tile
-        if (gt == 0) {
-          if (stored) bulk_wait_read_all();
-          mbar_arrive_cluster(free_mine);
-          mbar_arrive_cluster(free_peer);
-        }
-      }
-      if (j == rg.unit_last(j)) {
-        // end of this b in the range: head hh's covariance and channel-sum partials out
-        mbar_wait_cluster_bounded(cov_done, nflush & 1, &abort_flag, status);
-        tc_fence_after();
-        if (owner && has) {
-          float *part = p.part + (((long long)(grp + b) * pairs + hp) * 2 + hh) * kKProjPartFloats;
+        for (int q = 0; q < 2; ++q) {
+          const int u = 2 * half + q;
+          if (valid) {
+            rope_group<T>(clo[q], chi[q], slo[q], shi[q], u, has1, kv[0], kv[1]);
+          } else {
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint32_t v[16];
-            if (unit_vis) {
-              tmem_ld16_nowait(tmem_lane + kCovCol + 128 * hh + 16 * c, v);
-              tmem_wait_ld();
-            } else {
-#pragma unroll
-              for (int k = 0; k < 16; ++k) v[k] = 0u;
-            }
-#pragma unroll
-            for (int k = 0; k < 16; k += 4)
-              *reinterpret_cast<float4 *>(part + row * 128 + 16 * c + k) =
-                  make_float4(__uint_as_float(v[k]), __uint_as_float(v[k + 1]), __uint_as_float(v[k + 2]),
-                              __uint_as_float(v[k + 3]));
+            for (int k = 0; k < 4; ++k)
+              kv[0][4 * u + k] = kv[0][16 + 4 * u + k] = kv[1][4 * u + k] = kv[1][16 + 4 * u + k] = 0u;
           }
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            ks_acc[k] += __shfl_xor_sync(0xffffffffu, ks_acc[k], 16);
-            if ((lane & 16) == 0) part[128 * 128 + (e & 3) * 128 + chunk * 8 + k] = ks_acc[k];
-            ks_acc[k] = 0.f;
+          for (int h = 0; h < 2; ++h) {
+            if (h == 1 && !has1) continue;
+            const uint32_t cbase = stage_u32 + (2 * h) * kBox + swizzled_offset<128>(row, (4 * ch + u) * 8);
+            st_shared_v4(cbase, kv[h][4 * u], kv[h][4 * u + 1], kv[h][4 * u + 2], kv[h][4 * u + 3]);
+            st_shared_v4(cbase + kBox, kv[h][16 + 4 * u], kv[h][17 + 4 * u], kv[h][18 + 4 * u], kv[h][19 + 4 * u]);
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(cov_flushed0);
-        ++nflush;
+      }
+      fence_proxy_async_smem();   // generic-proxy writes -> the TMA store
+      named_barrier_sync(1, 256);
+      if (tid == 0 && mine.exists) {
+        for (int h = 0; h < nh; ++h)
+          for (int c = 0; c < 2; ++c)
+            tma_store_4d(&maps.k_out[mine.span], stage + (2 * h + c) * kBox, 64 * c, mine.row0 - mine.start,
+                         2 * hp + h, b);
+        bulk_commit_group();
+        stored = true;
       }
     }
-    if (gt == 0 && stored) bulk_wait_all();
+    if (tid == 0 && stored) bulk_wait_all();
   }
   __syncthreads();
   cluster_sync();   // the peer is done with this CTA's shared and tensor memory
@@ -511,47 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// cov / ksum of (b, h): the sum, in group order, of the partials of the
-// groups whose range meets b's items.  Block (m, y) sums the 1024 floats
-// [1024 y, 1024 y + 1024) of matrix m; y == 0 also the channel sums.
-constexpr int kReduceSplit = 128 * 128 / 1024;
-
-__global__ void __launch_bounds__(256)
-    kproj_reduce_kernel(const KProjParams p, int steps_per_b) {
-  const int pairs = (p.heads + 1) / 2;
-  const int groups = p.grid / (2 * pairs);
-  const int m = blockIdx.x;                 // b * heads + head
-  const int b = m / p.heads, head = m % p.heads;
-  const int hp = head / 2, hh = head & 1;
-  const long long total = (long long)p.batch * steps_per_b;
-  const long long lo = (long long)b * steps_per_b, hi = lo + steps_per_b;
-  // groups g with range_begin(g) <= lo ... range_begin(g) < hi
-  const int c0 = static_cast<int>(((lo + 1) * groups + total - 1) / total) - 1;
-  const int c1 = static_cast<int>((hi * groups + total - 1) / total) - 1;
-  const int off = (blockIdx.y * 256 + threadIdx.x) * 4;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float ks = 0.f;
-  for (int c = c0 < 0 ? 0 : c0; c <= c1 && c < groups; ++c) {
-    if (range_begin(c + 1, total, groups) <= lo || range_begin(c, total, groups) >= hi) continue;
-    const float *part = p.part + (((long long)(c + b) * pairs + hp) * 2 + hh) * kKProjPartFloats;
-    const float4 v = *reinterpret_cast<const float4 *>(part + off);
-    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-    if (blockIdx.y == 0 && threadIdx.x < 128) {
-#pragma unroll
-      for (int w = 0; w < 4; ++w) ks += part[128 * 128 + w * 128 + threadIdx.x];
-    }
-  }
-  *reinterpret_cast<float4 *>(p.cov + (long long)m * 128 * 128 + off) = acc;
-  if (blockIdx.y == 0 && threadIdx.x < 128) p.ksum[(long long)m * 128 + threadIdx.x] = ks;
-}
-
 }  // namespace
-
-int kproj_steps_per_b(int seq, int vis_start, int vis_len) {
-  const int t0 = (vis_start + kRows - 1) / kRows, t1 = (vis_len + kRows - 1) / kRows,
-            t2 = (seq - vis_start - vis_len + kRows - 1) / kRows;
-  return (t0 + 1) / 2 + (t1 + 1) / 2 + (t2 + 1) / 2;
-}
 
 int kproj_max_clusters(int dtype_is_bf16) {
   const int smem = KpSmem::kBytes + 1024;
@@ -593,8 +478,6 @@ cudaError_t launch_kproj_tc(int dtype_is_bf16, const KProjMaps &maps, const KPro
   cfg.numAttrs = 1;
   err = cudaLaunchKernelEx(&cfg, kernel, maps, p);
   if (err != cudaSuccess) return err;
-  kproj_reduce_kernel<<<dim3(p.batch * p.heads, kReduceSplit), 256, 0, stream>>>(
-      p, kproj_steps_per_b(p.seq, p.vis_start, p.vis_len));
   return cudaGetLastError();
 }
 
