@@ -82,8 +82,7 @@ struct KpSmem {
   static constexpr int kNumBars = 2 * kStages + 4;
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemSlot + 4;                     // bounded-wait abort flag
-  static constexpr int kBias = (kAbort + 4 + 15) & ~15;           // fp32 [2][128]
-  static constexpr int kBytes = kBias + 256 * 4;
+  static constexpr int kBytes = kAbort + 4;
   static_assert(kStage % 1024 == 0 && kStageBytes % 1024 == 0, "swizzled boxes need 1024-byte alignment");
   // + 1024 alignment slack; no static shared memory in the kernel (it would
   // sit in front of the 1024-aligned dynamic array)
@@ -165,22 +164,37 @@ __device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
 // fetched once and serve both heads.
 
 // Drain one head's 64 accumulator columns of this thread's row:
-// k = round(acc + bias).  `cols` addresses channel 32 c of the head.
+// k = round(acc + bias).  `cols` addresses channel 32 c of the head, `bias`
+// the same channel of the head's bias in global memory (NULL: none).  The
+// bias is read with warp-uniform 16-byte loads (one L1 wavefront each; a
+// broadcast 16-byte shared-memory load takes four).
 template <typename T>
-__device__ __forceinline__ void drain_half(uint32_t cols, const float *bias, uint32_t (&k)[32]) {
-  uint32_t r[4][16];
-  tmem_ld16_nowait(cols, r[0]);
-  tmem_ld16_nowait(cols + 16, r[1]);
-  tmem_ld16_nowait(cols + 64, r[2]);
-  tmem_ld16_nowait(cols + 80, r[3]);
-  tmem_wait_ld();
+__device__ __forceinline__ void drain_half(uint32_t cols, const T *bias, uint32_t (&k)[32]) {
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const float *bc = bias + (c & 1) * 16 + (c >> 1) * 64;
+  for (int c2 = 0; c2 < 4; c2 += 2) {        // low channels, then their partners + 64
+    uint32_t r[2][16];
+    tmem_ld16_nowait(cols + 32 * c2, r[0]);
+    tmem_ld16_nowait(cols + 32 * c2 + 16, r[1]);
+    float bf[32];
+    if (bias != nullptr) {
 #pragma unroll
-    for (int e = 0; e < 16; e += 2)
-      k[8 * c + e / 2] = pack2<T>(__fadd_rn(__uint_as_float(r[c][e]), bc[e]),
-                                  __fadd_rn(__uint_as_float(r[c][e + 1]), bc[e + 1]));
+      for (int q = 0; q < 4; ++q) {
+        float f[8];
+        unpack8<T>(__ldg(reinterpret_cast<const uint4 *>(bias + 32 * c2 + 8 * q)), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) bf[8 * q + e] = f[e];
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) bf[e] = 0.f;
+    }
+    tmem_wait_ld();
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+      for (int e = 0; e < 16; e += 2)
+        k[8 * (c2 + c) + e / 2] = pack2<T>(__fadd_rn(__uint_as_float(r[c][e]), bf[16 * c + e]),
+                                           __fadd_rn(__uint_as_float(r[c][e + 1]), bf[16 * c + e + 1]));
   }
 }
 
@@ -209,21 +223,46 @@ __device__ __forceinline__ void ldg_16ch(const T *ptr, bool wide, uint4 &a, uint
 //   out_lo = round(round(k_lo cos_lo) - round(k_hi sin_lo))   channels d < 64
 //   out_hi = round(round(k_hi cos_hi) + round(k_lo sin_hi))   channels d + 64
 // which is torch's  k * cos + rotate_half(k) * sin  in the Keys' dtype.
-// cos / sin are unpacked two channels at a time, so few values are live.
+// Computed two channels at a time with the packed 16-bit instructions, each
+// one rounding (.rn) of the exact result.  That equals torch's fp32 compute
+// then round: the product of two 16-bit values is exact in fp32, and a sum
+// of two 16-bit values is either exact in fp32 or so lopsided that both
+// roundings return the larger operand.  .rn also keeps the compiler from
+// fusing a product into the sum.
+template <typename T>
+__device__ __forceinline__ uint32_t mul2_rn(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+template <typename T>
+__device__ __forceinline__ uint32_t add2_rn(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+template <typename T>
+__device__ __forceinline__ uint32_t sub2_rn(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 template <typename T>
 __device__ __forceinline__ void rope_pair(uint32_t cl, uint32_t ch, uint32_t sl, uint32_t sh, uint32_t &klo,
                                           uint32_t &khi) {
-  float c0, c1, d0, d1, s0, s1, t0, t1, l0, l1, h0, h1;
-  unpack2<T>(cl, c0, c1);
-  unpack2<T>(ch, d0, d1);
-  unpack2<T>(sl, s0, s1);
-  unpack2<T>(sh, t0, t1);
-  unpack2<T>(klo, l0, l1);
-  unpack2<T>(khi, h0, h1);
-  klo = pack2<T>(__fsub_rn(round_to<T>(__fmul_rn(l0, c0)), round_to<T>(__fmul_rn(h0, s0))),
-                 __fsub_rn(round_to<T>(__fmul_rn(l1, c1)), round_to<T>(__fmul_rn(h1, s1))));
-  khi = pack2<T>(__fadd_rn(round_to<T>(__fmul_rn(h0, d0)), round_to<T>(__fmul_rn(l0, t0))),
-                 __fadd_rn(round_to<T>(__fmul_rn(h1, d1)), round_to<T>(__fmul_rn(l1, t1))));
+  const uint32_t lo = klo, hi = khi;
+  klo = sub2_rn<T>(mul2_rn<T>(lo, cl), mul2_rn<T>(hi, sl));
+  khi = add2_rn<T>(mul2_rn<T>(hi, ch), mul2_rn<T>(lo, sh));
 }
 
 template <typename T>
@@ -249,7 +288,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *acc_full = empty_bar + kStages;   // [2] accumulator ready (both CTAs)
   uint64_t *acc_empty = acc_full + 2;         // [2] rank 0: drained, one arrival per epilogue warp of the pair
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + KpSmem::kTmemSlot);
-  float *bias_s = reinterpret_cast<float *>(smem + KpSmem::kBias);
   unsigned char *stage = smem + KpSmem::kStage;
   int &abort_flag = *reinterpret_cast<int *>(smem + KpSmem::kAbort);
 
@@ -355,27 +393,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t stage_u32 = smem_u32(stage);
     const T *bias_g = static_cast<const T *>(p.bias);
     const bool wide = p.cs_wide != 0;
-    int cur_unit = -1;
     bool stored = false;
     for (int i = 0; i < nt; ++i) {
       const int j = rg.begin + i;
       const int b = rg.unit(j), step = rg.step(j);
       const int a = i & 1;
       const StepTile mine = step_tile(sp, step, static_cast<int>(r));
-      if (b != cur_unit) {   // both heads' bias
-        named_barrier_sync(1, 256);
-        const int hb = tid >> 7;
-        bias_s[tid] = ((hb == 0 || has1) && bias_g != nullptr) ? to_f32<T>(bias_g[(2 * hp + hb) * 128 + (tid & 127)])
-                                                               : 0.f;
-        named_barrier_sync(1, 256);
-        cur_unit = b;
-      }
       mbar_wait_cluster_bounded(&acc_full[a], (i >> 1) & 1, &abort_flag, status);
       tc_fence_after();
       uint32_t kv[2][32];
       const uint32_t acc = tmem_lane + kAccCols * a;
-      drain_half<T>(acc + 32 * ch, bias_s + 32 * ch, kv[0]);
-      if (has1) drain_half<T>(acc + 128 + 32 * ch, bias_s + 128 + 32 * ch, kv[1]);
+      drain_half<T>(acc + 32 * ch, bias_g == nullptr ? nullptr : bias_g + 2 * hp * 128 + 32 * ch, kv[0]);
+      if (has1)
+        drain_half<T>(acc + 128 + 32 * ch, bias_g == nullptr ? nullptr : bias_g + (2 * hp + 1) * 128 + 32 * ch, kv[1]);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * a);   // this buffer may be overwritten
