@@ -1071,10 +1071,11 @@ KPROJ = dict(batch=8, prompt=64, vision=15360, text=576, hidden=3584)
 def run_kproj(args):
     """One layer's prefill Key path as the adapters run it -- k_proj, RoPE,
     then the rotation build of the visual span (llama_visionzip.py:144-165) --
-    from the layer's hidden states.  Ours: ``build_rotation_projected`` (fused
-    projection + RoPE + covariance sums, Jacobi, rotate).  Beside it on the same
-    GPU: cuBLAS k_proj + torch RoPE + ``build_rotation`` (the adapter path with
-    this build's builder)."""
+    from the layer's hidden states.  Ours: ``build_rotation_projected``
+    (projection + bias + RoPE in one tensor-core kernel, the visual span's sums
+    from the Keys it wrote, eigensolver, rotate).  Beside it on the same GPU:
+    cuBLAS k_proj + torch RoPE + ``build_rotation`` (the adapter path with this
+    build's builder)."""
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     from rotatek_b200 import rotation as rot
@@ -1148,7 +1149,7 @@ def run_kproj(args):
                    "l2": f"hidden states {x.numel() * 2 / 1e9:.2f} GB > 126 MB L2; no flush"},
         "phases_us": {"key_projection_fused": proj, "cublas_k_proj_alone": lin},
         "adapter_path_us": theirs, "speedup_vs_adapter_path": theirs / ours,
-        "roofline": {"bound": "tensor", "kernel": "kproj_pair_kernel + kproj_reduce_kernel",
+        "roofline": {"bound": "tensor", "kernel": "kproj_pair_kernel + cov_tc_kernel (visual-span sums)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "algorithmic_flops_per_launch": flops,
                      "traffic": ncu_traffic_per_launch("kproj_pair_small_case.txt", "dram_bytes_per_launch_config4"),

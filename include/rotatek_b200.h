@@ -263,8 +263,8 @@ int rtk_build_rotation(const rtk_tensor *keys_vision, const rtk_tensor *queries_
                        const rtk_tensor *eigvals_out, void *workspace, size_t workspace_bytes,
                        void *stream);
 
-/* The prefill Key path of the attention adapters, fused with the covariance
- * sums.  Replaces k_proj -> view / transpose -> apply_rotary_pos_emb
+/* The prefill Key path of the attention adapters, followed by the covariance
+ * sums of its visual span.  Replaces k_proj -> view / transpose -> apply_rotary_pos_emb
  * (integrations/lmms_eval/models/model_utils/llava_next/llama_visionzip.py:144-153;
  * qwen/qwen2_5vl_visionzip.py:932-942 once the multimodal cos / sin sections are
  * merged) and the covariance pass over its visual span (kv_pruning_utils.py:112-115):
@@ -272,8 +272,9 @@ int rtk_build_rotation(const rtk_tensor *keys_vision, const rtk_tensor *queries_
  *   k = hidden[b, s] . w_k[h*128 : h*128 + 128]^T + bias[h*128 : ...]
  * rounded as torch rounds those bf16 / fp16 ops, for every token s; cov_out and
  * ksum_out as rtk_key_covariance over the visual tokens
- * [vis_start, vis_start + vis_len) of keys_out.  One pass on the tcgen05
- * tensor cores.
+ * [vis_start, vis_start + vis_len) of keys_out.  The projection, bias and
+ * RoPE are one tcgen05 tensor-core kernel; the sums are then taken from the
+ * visual Keys it wrote.
  *   hidden     [B, S, hidden]      bf16 | f16, hidden % 64 == 0, 16-byte aligned rows
  *   w_k        [H_kv * 128, hidden]  same dtype (nn.Linear weight)
  *   bias       [H_kv * 128]        same dtype, contiguous, nullable
@@ -281,20 +282,19 @@ int rtk_build_rotation(const rtk_tensor *keys_vision, const rtk_tensor *queries_
  *   keys_out   [B, H_kv, S, 128]   same dtype, channel stride 1
  *   cov_out    [B, H_kv, 128, 128] f32 contiguous; ksum_out [B, H_kv, 128] f32 contiguous
  *   workspace  rtk_key_projection_workspace_size() bytes: the device-status word
- *              (first 256 bytes, as in the build workspace) and per-CTA partial
- *              sums (no zeroing needed)                                          */
+ *              (256 bytes, as in the build workspace)                            */
 int rtk_key_projection(const rtk_tensor *hidden, const rtk_tensor *w_k, const rtk_tensor *bias,
                        const rtk_tensor *cos, const rtk_tensor *sin, int64_t vis_start, int64_t vis_len,
                        const rtk_tensor *keys_out, const rtk_tensor *cov_out, const rtk_tensor *ksum_out,
                        void *workspace, size_t workspace_bytes, void *stream);
 
-/* Bytes of workspace rtk_key_projection needs on `device` (its SM count sets
- * the number of partial sums): 256 + about 132 KiB x (SMs + B * ceil(H_kv / 2)). */
+/* Bytes of workspace rtk_key_projection needs: the 256-byte status word (the
+ * arguments are kept for callers that size per shape and device).            */
 size_t rtk_key_projection_workspace_size(int64_t batch, int64_t kv_heads, int64_t seq, int64_t vis_start,
                                          int64_t vis_len, int32_t device);
 
 /* Bytes of workspace rtk_build_rotation_projected needs: the build workspace
- * followed by the projection's partial sums.                                */
+ * (rtk_build_rotation_workspace_size(batch, kv_heads, 128)).                 */
 size_t rtk_build_rotation_projected_workspace_size(int64_t batch, int64_t kv_heads, int64_t seq,
                                                    int64_t vis_start, int64_t vis_len, int32_t device);
 
