@@ -393,7 +393,11 @@ def run_ours(args):
                          "traffic": ncu_traffic_per_launch()},
             "e2e": {"value": e2e_ms * 1e3 / (e2e_steps * world), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": e2e_steps},
+                    "steps": e2e_steps,
+                    # every step copies its inputs from pinned host memory, so the
+                    # end-to-end time is set by the host link, not by the kernel
+                    "bound": "host link (pinned H2D copy of the step's inputs)",
+                    "host_link_gbs": (h2d + d2h) / (e2e_ms / e2e_steps / 1e3) / 1e9 if e2e_ms > 0 else None},
             "gpu_launches": args.steps,
             "clocks": clocks,
             "device_status": status,

@@ -137,3 +137,20 @@ def projector_distance(R_a, R_b) -> np.ndarray:
     Invariant to column signs and to any rotation inside the kept subspace."""
     diff = projector(R_a) - projector(R_b)
     return np.sqrt((diff ** 2).sum(axis=(-1, -2)))
+
+
+def subspace_iteration(cov: np.ndarray, v0: np.ndarray, num_iters: int) -> np.ndarray:
+    """The reference's optional solver, ``power_iteration_gpu``
+    (rotatek/rotation.py:68-91): from a start V0 [..., D, k], ``num_iters``
+    times V <- cov V, then V <- V L^-T with L the Cholesky factor of V^T V (so
+    V^T V = I).  float64 here; the reference runs it in cov's dtype from
+    torch.randn(generator=manual_seed(seed)) on the device."""
+    v = np.asarray(v0, dtype=np.float64)
+    c = np.asarray(cov, dtype=np.float64)
+    for _ in range(num_iters):
+        v = c @ v
+        gram = np.swapaxes(v, -1, -2) @ v
+        L = np.linalg.cholesky(gram)
+        # V L^-T: solve L X^T = V^T
+        v = np.swapaxes(np.linalg.solve(L, np.swapaxes(v, -1, -2)), -1, -2)
+    return v

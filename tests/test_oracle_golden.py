@@ -177,3 +177,19 @@ def test_spark_recovery_and_decode_oracle(golden, case):
     out = osp.spark_decode(g["q_decode"], k_full, v_full, None, g["k_compact"], idx, g["pruned_mean"], v_vis,
                            g["num_kv_groups"])
     assert_matches_reference(out, g["out_spark"], g["dtype"])
+
+
+def test_subspace_iteration_restatement():
+    """oracle.rotation.subspace_iteration (the reference's power_iteration_gpu,
+    rotatek/rotation.py:68-91): orthonormal after every step, and on a spectrum
+    with a clear gap after the k-th eigenvalue it reaches LAPACK's subspace."""
+    rng = np.random.default_rng(7)
+    q, _ = np.linalg.qr(rng.standard_normal((3, 128, 128)))
+    lam = np.concatenate([np.linspace(4.0, 2.0, 8), np.linspace(1.0, 0.1, 120)])
+    cov = (q * lam) @ np.swapaxes(q, -1, -2)
+    v0 = rng.standard_normal((3, 128, 8))
+    v1 = orot.subspace_iteration(cov, v0, 1)
+    assert np.abs(np.swapaxes(v1, -1, -2) @ v1 - np.eye(8)).max() < 1e-12
+    v = orot.subspace_iteration(cov, v0, 60)
+    w, vecs = np.linalg.eigh(cov)
+    assert orot.projector_distance(v, vecs[..., ::-1][..., :8]).max() < 1e-8
