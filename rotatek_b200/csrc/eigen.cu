@@ -126,12 +126,12 @@ __device__ __forceinline__ float round_to(float v, int dtype) {
 // 31 selects).  The bits come through inline asm, which the compiler cannot
 // see through: a select by comparing each register's index with i would be
 // turned back into dynamic indexing, which moves the array to local memory.
-__device__ __forceinline__ float pick32(const float (&a)[32], int i) {
+__device__ __forceinline__ float pick32(const float2 (&a)[16], int i) {
   uint32_t bits;
   asm volatile("mov.b32 %0, %1;" : "=r"(bits) : "r"(i));
   float t16[16], t8[8], t4[4], t2[2];
 #pragma unroll
-  for (int u = 0; u < 16; ++u) t16[u] = (bits & 1u) ? a[2 * u + 1] : a[2 * u];
+  for (int u = 0; u < 16; ++u) t16[u] = (bits & 1u) ? a[u].y : a[u].x;
 #pragma unroll
   for (int u = 0; u < 8; ++u) t8[u] = (bits & 2u) ? t16[2 * u + 1] : t16[2 * u];
 #pragma unroll
@@ -326,9 +326,12 @@ __global__ void __launch_bounds__(kThreads, KMAX <= 32 ? 2 : 1) eigh_kernel(cons
   // the next reads.  The Householder vectors go to the matrix's shared-memory
   // rows (row k = v_k), which the registers have freed.
   const int col = tid & (kN - 1), qtr = tid >> 7, r0 = 32 * qtr;
-  float a[32];
+  // rows r0 + 2u, r0 + 2u + 1 in a2[u]: register pairs for the packed fp32
+  // FMAs (fma.rn.f32x2, one rounding per lane as fmaf) of the two hot loops
+  float2 a2[16];
+#define AR(r) (((r) & 1) ? a2[(r) >> 1].y : a2[(r) >> 1].x)
 #pragma unroll
-  for (int r = 0; r < 32; ++r) a[r] = A[(r0 + r) * kAS + col];
+  for (int u = 0; u < 16; ++u) a2[u] = make_float2(A[(r0 + 2 * u) * kAS + col], A[(r0 + 2 * u + 1) * kAS + col]);
   __syncthreads();
   // column 0 and row 1 for step 0
   if (col == 0) {
@@ -336,13 +339,13 @@ __global__ void __launch_bounds__(kThreads, KMAX <= 32 ? 2 : 1) eigh_kernel(cons
 #pragma unroll
     for (int r = 0; r < 32; ++r) {
       const int j = r0 + r;
-      const float t = j >= 2 ? a[r] : 0.f;
+      const float t = j >= 2 ? AR(r) : 0.f;
       sm.xbuf[0][j] = t;
       ss = fmaf(t, t, ss);
     }
     sm.ssbuf[0][qtr] = ss;
   }
-  if (qtr == 0) sm.rowbuf[0][col] = a[1];
+  if (qtr == 0) sm.rowbuf[0][col] = a2[0].y;
   __syncthreads();
 #pragma unroll 1
   for (int k = 0; k < kN - 2; ++k) {
@@ -371,16 +374,15 @@ __global__ void __launch_bounds__(kThreads, KMAX <= 32 ? 2 : 1) eigh_kernel(cons
       // p = tau A22 v: this thread's rows; row k+1 (v = v0) is added from rowbuf below
       float acc = 0.f;
       if (live_rows && col > k) {
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        // four partial sums (rows = 0, 1, 2, 3 mod 4), combined as (0 + 1) + (2 + 3)
+        float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int r = 0; r < 32; r += 4) {
           const float4 xv = *reinterpret_cast<const float4 *>(&sm.xbuf[cur][r0 + r]);
-          a0 = fmaf(a[r], xv.x, a0);
-          a1 = fmaf(a[r + 1], xv.y, a1);
-          a2 = fmaf(a[r + 2], xv.z, a2);
-          a3 = fmaf(a[r + 3], xv.w, a3);
+          s01 = __ffma2_rn(a2[r >> 1], make_float2(xv.x, xv.y), s01);
+          s23 = __ffma2_rn(a2[(r >> 1) + 1], make_float2(xv.z, xv.w), s23);
         }
-        acc = (a0 + a1) + (a2 + a3);
+        acc = (s01.x + s01.y) + (s23.x + s23.y);
       }
       sm.part[qtr][col] = acc;
       __syncthreads();
@@ -407,14 +409,16 @@ __global__ void __launch_bounds__(kThreads, KMAX <= 32 ? 2 : 1) eigh_kernel(cons
         const float K = 0.5f * sm.tau[k] * (sm.red[0][0] + sm.red[0][1] + sm.red[0][2] + sm.red[0][3]);
         const float vc = sm.xbuf[cur][col];
         const float cc = fmaf(-2.f * K, vc, sm.pbuf[col]);
+        const float2 ncc = make_float2(-cc, -cc), nvc = make_float2(-vc, -vc);
 #pragma unroll
         for (int r = 0; r < 32; r += 4) {
           const float4 xv = *reinterpret_cast<const float4 *>(&sm.xbuf[cur][r0 + r]);
           const float4 pv4 = *reinterpret_cast<const float4 *>(&sm.pbuf[r0 + r]);
-          a[r] = fmaf(-xv.x, cc, fmaf(-pv4.x, vc, a[r]));
-          a[r + 1] = fmaf(-xv.y, cc, fmaf(-pv4.y, vc, a[r + 1]));
-          a[r + 2] = fmaf(-xv.z, cc, fmaf(-pv4.z, vc, a[r + 2]));
-          a[r + 3] = fmaf(-xv.w, cc, fmaf(-pv4.w, vc, a[r + 3]));
+          // a -= x cc + p vc, as fmaf(-x, cc, fmaf(-p, vc, a)) lane by lane
+          a2[r >> 1] = __ffma2_rn(make_float2(xv.x, xv.y), ncc,
+                                  __ffma2_rn(make_float2(pv4.x, pv4.y), nvc, a2[r >> 1]));
+          a2[(r >> 1) + 1] = __ffma2_rn(make_float2(xv.z, xv.w), ncc,
+                                        __ffma2_rn(make_float2(pv4.z, pv4.w), nvc, a2[(r >> 1) + 1]));
         }
       }
     } else if (tid == 0) {                          // column k is already reduced
@@ -428,22 +432,23 @@ __global__ void __launch_bounds__(kThreads, KMAX <= 32 ? 2 : 1) eigh_kernel(cons
 #pragma unroll
       for (int r = 0; r < 32; r += 4) {
         float4 t;
-        t.x = r0 + r > k2 ? a[r] : 0.f;
-        t.y = r0 + r + 1 > k2 ? a[r + 1] : 0.f;
-        t.z = r0 + r + 2 > k2 ? a[r + 2] : 0.f;
-        t.w = r0 + r + 3 > k2 ? a[r + 3] : 0.f;
+        t.x = r0 + r > k2 ? a2[r >> 1].x : 0.f;
+        t.y = r0 + r + 1 > k2 ? a2[r >> 1].y : 0.f;
+        t.z = r0 + r + 2 > k2 ? a2[(r >> 1) + 1].x : 0.f;
+        t.w = r0 + r + 3 > k2 ? a2[(r >> 1) + 1].y : 0.f;
         *reinterpret_cast<float4 *>(&sm.xbuf[nxt][r0 + r]) = t;
         ssn = fmaf(t.x, t.x, fmaf(t.y, t.y, fmaf(t.z, t.z, fmaf(t.w, t.w, ssn))));
       }
       sm.ssbuf[nxt][qtr] = ssn;
     }
-    if (qtr == (k2 >> 5)) sm.rowbuf[nxt][col] = pick32(a, k2 & 31);
+    if (qtr == (k2 >> 5)) sm.rowbuf[nxt][col] = pick32(a2, k2 & 31);
     __syncthreads();
   }
   // the diagonal (column c leaves the trailing block after step c - 1 and is
   // not touched again) and the last off-diagonal element
-  if (qtr == (col >> 5)) sm.d[col] = pick32(a, col & 31);
-  if (qtr == 3 && col == kN - 2) sm.e[kN - 2] = a[31];
+  if (qtr == (col >> 5)) sm.d[col] = pick32(a2, col & 31);
+  if (qtr == 3 && col == kN - 2) sm.e[kN - 2] = a2[15].y;
+#undef AR
   if (tid == 0) {
     sm.e[kN - 1] = 0.f;
     sm.tau[kN - 2] = sm.tau[kN - 1] = 0.f;
