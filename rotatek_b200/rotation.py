@@ -192,8 +192,9 @@ def _cos_sin_3d(cos: torch.Tensor, sin: torch.Tensor):
 
 def key_projection(hidden_states: torch.Tensor, w_k: torch.Tensor, bias: Optional[torch.Tensor],
                    cos: torch.Tensor, sin: torch.Tensor, vis_start: int, vis_len: int):
-    """Post-RoPE Keys straight from the hidden states, with the covariance sums
-    of their visual span, in one tensor-core pass.
+    """Post-RoPE Keys straight from the hidden states (projection, bias and
+    RoPE in one tensor-core kernel), then the covariance sums of their visual
+    span from the Keys just written.
 
     Equals ``apply_rotary_pos_emb(k_proj(hidden_states).view(B, S, H_kv, D)
     .transpose(1, 2), cos, sin)`` -- llama_visionzip.py:144-153 -- (rounded as

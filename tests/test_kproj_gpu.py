@@ -85,6 +85,30 @@ def test_key_projection_vs_oracle(dtype, B, S, hidden, H, vs, vl, bias, per_batc
     assert rot.read_build_status() == 0
 
 
+def test_key_projection_cos_sin_16_byte_rows():
+    """cos / sin rows that are 16- but not 32-byte aligned (a view into wider
+    tables) take the 128-bit load path; the result equals the one from
+    contiguous copies of the same tables bit for bit."""
+    B, S, hidden, H, vs, vl = 2, 600, 256, 2, 40, 500
+    gen = torch.Generator(device=DEV).manual_seed(3)
+    x = torch.randn(B, S, hidden, device=DEV, generator=gen).to(torch.bfloat16)
+    w = (torch.randn(H * 128, hidden, device=DEV, generator=gen) * hidden ** -0.5).to(torch.bfloat16)
+    b = (torch.randn(H * 128, device=DEV, generator=gen) * 0.1).to(torch.bfloat16)
+    cos, sin = rope_tables(B, S, torch.bfloat16)
+    # rows of 136 elements (272 bytes), the table starting 8 elements in: 16-byte aligned only
+    wide_c = torch.zeros(B, S, 136, device=DEV, dtype=torch.bfloat16)
+    wide_s = torch.zeros_like(wide_c)
+    wide_c[..., 8:] = cos
+    wide_s[..., 8:] = sin
+    cos_v, sin_v = wide_c[..., 8:], wide_s[..., 8:]
+    assert cos_v.data_ptr() % 32 == 16 and cos_v.stride(1) * 2 % 32 == 16
+    keys, cov, ksum = rot.key_projection(x, w, b, cos_v, sin_v, vs, vl)
+    keys2, cov2, ksum2 = rot.key_projection(x, w, b, cos, sin, vs, vl)
+    assert torch.equal(keys, keys2)
+    assert torch.equal(cov, cov2) and torch.equal(ksum, ksum2)
+    assert rot.read_build_status() == 0
+
+
 def test_key_projection_matches_torch_on_gpu():
     """Against the adapters' own ops run by torch on the GPU (cuBLAS k_proj,
     transformers-style RoPE in bf16), at a LLaVA-NeXT-7B-like width."""
