@@ -36,9 +36,7 @@ struct KProjParams {
   int batch, heads, seq, hidden;  // hidden % 64 == 0
   int vis_start, vis_len;
   const void *bias;                       // [heads * 128] or NULL
-  const void *cos, *sin;                  // [B | 1, S, 128] (element strides below, channel stride 1)
-  long long cs_sb, cs_ss;                 // batch stride (0 = broadcast), token stride
-  int cs_wide;                            // cos / sin rows 32-byte aligned: 256-bit loads
+  long long cs_sb;                        // cos / sin batch stride (0 = one table for every b)
   unsigned int *status;                   // device status word (bounded-wait timeouts)
   int grid;                               // CTAs: groups * ceil(H / 2) clusters of 2
 };
@@ -47,9 +45,10 @@ inline long long kproj_pairs(long long heads) { return (heads + 1) / 2; }
 
 // x: [B, S, hidden] 3-D map, box {64, 128, 1}; w: [H*128, hidden] 2-D map, box
 // {64, 128}; k_out[i]: the output [B, H, len_i, 128] of span i (prompt, visual,
-// text) as 4-D maps with box {64, 128, 1, 1}; all 128B-swizzled.
+// text) as 4-D maps with box {64, 128, 1, 1}; cs[0] / cs[1]: cos / sin
+// [B | 1, S, 128] as 3-D maps with box {64, 128, 1}; all 128B-swizzled.
 struct KProjMaps {
-  CUtensorMap x, w, k_out[3];
+  CUtensorMap x, w, k_out[3], cs[2];
 };
 
 // Two-CTA clusters of the projection kernel that fit the current device at once (0 if unknown).

@@ -946,6 +946,17 @@ int run_key_projection(const rtk_tensor *x, const rtk_tensor *w, const rtk_tenso
     if (!encode_map_rank(&maps.w, tdt, 2, w->data, dims, strides, box))
       return fail(RTK_ERR_UNSUPPORTED, "w_k layout is not describable by TMA (16-byte aligned rows needed)");
   }
+  {
+    // cos / sin rows: one 3-D map each; a table shared by every b has batch extent 1
+    const int64_t bc = cs_sb == 0 ? 1 : B;
+    const cuuint64_t dims[3] = {128, (cuuint64_t)S, (cuuint64_t)bc};
+    const cuuint64_t strides[2] = {(cuuint64_t)(cos->stride[1] * 2),
+                                   (cuuint64_t)(bc == 1 ? S * cos->stride[1] * 2 : cs_sb * 2)};
+    const cuuint32_t box[3] = {64, 128, 1};
+    if (!encode_map_rank(&maps.cs[0], tdt, 3, cos->data, dims, strides, box) ||
+        !encode_map_rank(&maps.cs[1], tdt, 3, sin->data, dims, strides, box))
+      return fail(RTK_ERR_UNSUPPORTED, "cos / sin layout is not describable by TMA (16-byte aligned rows needed)");
+  }
   const int64_t span_start[3] = {0, vis_start, vis_start + vis_len};
   const int64_t span_len[3] = {vis_start, vis_len, S - vis_start - vis_len};
   for (int i = 0; i < 3; ++i) {
@@ -962,10 +973,7 @@ int run_key_projection(const rtk_tensor *x, const rtk_tensor *w, const rtk_tenso
   kp.batch = (int)B; kp.heads = (int)H; kp.seq = (int)S; kp.hidden = (int)Hd;
   kp.vis_start = (int)vis_start; kp.vis_len = (int)vis_len;
   kp.bias = bias != nullptr ? bias->data : nullptr;
-  kp.cos = cos->data; kp.sin = sin->data;
-  kp.cs_sb = cs_sb; kp.cs_ss = cos->stride[1];
-  kp.cs_wide = (cos->stride[1] * 2) % 32 == 0 && (cs_sb * 2) % 32 == 0 &&
-               reinterpret_cast<uintptr_t>(cos->data) % 32 == 0 && reinterpret_cast<uintptr_t>(sin->data) % 32 == 0;
+  kp.cs_sb = cs_sb;
   kp.status = status;
   // persistent: groups x head pairs x 2 CTAs, one CTA per SM; contiguous shares of the B x steps items
   const int device = current_device();

@@ -1,12 +1,11 @@
-// Fused Key projection + RoPE + covariance sums on the 5th-generation tensor cores.
+// Key projection + bias + RoPE on the 5th-generation tensor cores.
 //
 // The attention adapters compute the prefill Keys as k_proj(X) -> RoPE
-// (llava_next/llama_visionzip.py:144-153, qwen/qwen2_5vl_visionzip.py:932-942),
-// and ChannelPruner.update_rotatek then reads the visual Keys again for their
-// mean and covariance (kv_pruning_utils.py:112-115).  This kernel produces the
-// post-RoPE Keys and, in the same pass, the raw sums sum_s k k^T and sum_s k of
-// the visual span -- the inputs of the eigensolver prologue -- so the covariance
-// pass over K disappears.
+// (llava_next/llama_visionzip.py:144-153, qwen/qwen2_5vl_visionzip.py:932-942).
+// This kernel writes the post-RoPE Keys of every token straight from the
+// hidden states, so neither the projection's output nor a RoPE pass goes
+// through HBM; the visual span's sums (kv_pruning_utils.py:112-115) are taken
+// afterwards from the Keys written, by the builder's covariance kernel.
 //
 // CTA pairs.  A cluster of two CTAs computes a {256 tokens x 256 channels}
 // tile -- a pair of KV heads -- with tcgen05.mma.cta_group::2 (M = 256, N = 256,
@@ -19,40 +18,33 @@
 //   warp 0     TMA producer: X box {64 hidden x 128 tokens} and W box {64 x 128
 //              channels} per 64-wide hidden chunk into a 5-stage ring; both
 //              CTAs' bytes complete on rank 0's full barrier
-//   warp 1     TMEM (512 columns, allocated for the pair); on rank 0 the MMA
-//              issuer: projection into columns 0-255, and per staged tile the
-//              covariance MMAs (M = N = 256, K = 256 tokens, both operands the
-//              staging tiles read MN-major) into columns 256-511 -- issued
-//              right after the next tile's projection, while its accumulator
-//              drains
+//   warp 1     TMEM (512 columns: two accumulators of 256); on rank 0 the MMA
+//              issuer, tile i into accumulator i mod 2, so the tensor pipe
+//              never waits for a drain
 //   warps 2-9  epilogue, one token row per thread; warp group c (warps 2-5,
 //              6-9) takes channel half c of BOTH heads: the channels
-//              [32 c, 32 c + 32) and their RoPE partners + 64.  Drain TMEM
-//              (+ bias, round) into registers, free the accumulator, fetch the
-//              row's cos / sin once for both heads, RoPE with torch's
-//              roundings, then write head h's part of the row into head h's
-//              staging tile -- which lives in CTA h, so one head goes through
-//              DSMEM.  CTA h's staging thus holds head h for all 256 tokens:
-//              the TMA-store source, the covariance operand (D's rows in CTA h
-//              are head h's channels, and its columns 128 h ... hold
-//              cov(head h); the other 128 columns get cross terms that are
-//              never read), and the source of head h's channel sums, which
-//              all eight warps of CTA h read.
+//              [32 c, 32 c + 32) and their RoPE partners + 64.  Per tile:
+//              thread 0 loads the tile's cos rows into head 0's staging boxes
+//              and its sin rows into head 1's (TMA); every thread drains its
+//              accumulator columns (+ bias, round) into registers and frees
+//              the accumulator, then applies RoPE with torch's roundings,
+//              reading cos / sin from the staging boxes and writing its Keys
+//              over exactly the values it read; thread 0 stores the boxes
+//              with TMA (per-span tensor maps clip rows past a span).
 //
 //              The epilogue shares the SM's L1 / shared-memory data path with
 //              the tensor core's operand reads and the TMA writes, so what it
-//              costs there is what it takes from the GEMM: cos / sin are read
-//              once per row (not once per head) and 32 bytes per lane.
+//              costs there is what it takes from the GEMM: cos / sin come in
+//              by TMA once per tile (not once per head, not per thread) and
+//              the Keys leave by TMA.
 //
 // Work split: each span (prompt, visual, text) is tiled from its own start in
 // 128-token tiles, and its tiles are taken two at a time (CTA 0, CTA 1) -- a
 // pair step never mixes spans.  The B x steps items are cut into contiguous
 // ranges over groups of ceil(H / 2) pairs; the pairs of a group (one per head
-// pair) walk the same range in step, so an X tile comes from HBM once.  When a
-// range leaves a b, its covariance and channel-sum partials go to the
-// workspace; a second kernel sums them in a fixed order (deterministic).
-// Rows past the end of their span are zeroed (no covariance contribution) and
-// clipped by the span's output tensor map.  No multicast loads.
+// pair) walk the same range in step, so an X tile comes from HBM once.  Rows
+// past the end of their span are zeroed and clipped by the span's output
+// tensor map.  No multicast loads.
 #include <type_traits>
 
 #include "builder.h"
@@ -78,8 +70,8 @@ struct KpSmem {
   // this CTA's 128 tokens of both heads: boxes [head][channels 0-63 | 64-127]
   static constexpr int kStage = kRing + kStages * kStageBytes;
   static constexpr int kBar = kStage + 4 * kBox;
-  // full[S], empty[S], acc_full[2], acc_empty[2]
-  static constexpr int kNumBars = 2 * kStages + 4;
+  // full[S], empty[S], acc_full[2], acc_empty[2], cos / sin landed
+  static constexpr int kNumBars = 2 * kStages + 5;
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemSlot + 4;                     // bounded-wait abort flag
   static constexpr int kBytes = kAbort + 4;
@@ -198,25 +190,6 @@ __device__ __forceinline__ void drain_half(uint32_t cols, const T *bias, uint32_
   }
 }
 
-__device__ __forceinline__ void ldg_v8(const void *ptr, uint4 &a, uint4 &b) {
-  asm("ld.global.nc.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-      : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w), "=r"(b.x), "=r"(b.y), "=r"(b.z), "=r"(b.w)
-      : "l"(ptr));
-}
-
-// 16 channels (two 8-channel groups) of a cos / sin row: one 256-bit load
-// when the row is 32-byte aligned (one L1 wavefront per 32 bytes, where
-// 16-byte loads of different rows take one per 16), else two 128-bit loads.
-template <typename T>
-__device__ __forceinline__ void ldg_16ch(const T *ptr, bool wide, uint4 &a, uint4 &b) {
-  if (wide) {
-    ldg_v8(ptr, a, b);
-  } else {
-    a = __ldg(reinterpret_cast<const uint4 *>(ptr));
-    b = __ldg(reinterpret_cast<const uint4 *>(ptr + 8));
-  }
-}
-
 // RoPE on 8 channel pairs of a half row (group u: low channels k[4u .. 4u+3],
 // their partners + 64 in k[16 + 4u ...]), in place, for both heads (the
 // second only when `both`):
@@ -287,6 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *empty_bar = full_bar + kStages;
   uint64_t *acc_full = empty_bar + kStages;   // [2] accumulator ready (both CTAs)
   uint64_t *acc_empty = acc_full + 2;         // [2] rank 0: drained, one arrival per epilogue warp of the pair
+  uint64_t *cs_bar = acc_empty + 2;           // this CTA's cos / sin rows in the staging boxes
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + KpSmem::kTmemSlot);
   unsigned char *stage = smem + KpSmem::kStage;
   int &abort_flag = *reinterpret_cast<int *>(smem + KpSmem::kAbort);
@@ -319,6 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 2 * kEpiWarps);
     }
+    mbar_init(cs_bar, 1);
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -392,13 +367,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t acc_empty0 = map_to_cta(smem_u32(acc_empty), 0);
     const uint32_t stage_u32 = smem_u32(stage);
     const T *bias_g = static_cast<const T *>(p.bias);
-    const bool wide = p.cs_wide != 0;
     bool stored = false;
+    int ncs = 0;   // cos / sin loads so far (phase of cs_bar)
     for (int i = 0; i < nt; ++i) {
       const int j = rg.begin + i;
       const int b = rg.unit(j), step = rg.step(j);
       const int a = i & 1;
       const StepTile mine = step_tile(sp, step, static_cast<int>(r));
+      // the staging boxes are free once the previous step's stores have read
+      // them; this step's cos rows then go into head 0's boxes and its sin rows
+      // into head 1's, where each thread's Keys will overwrite exactly the
+      // values it has read
+      if (tid == 0 && stored) bulk_wait_read_all();
+      named_barrier_sync(1, 256);
+      if (tid == 0 && mine.exists) {
+        mbar_arrive_expect_tx(cs_bar, 4 * kBox);
+        const int bc = p.cs_sb == 0 ? 0 : b;
+        for (int c = 0; c < 2; ++c) {
+          tma_load_3d(stage + c * kBox, &maps.cs[0], 64 * c, mine.row0, bc, cs_bar);
+          tma_load_3d(stage + (2 + c) * kBox, &maps.cs[1], 64 * c, mine.row0, bc, cs_bar);
+        }
+      }
       mbar_wait_cluster_bounded(&acc_full[a], (i >> 1) & 1, &abort_flag, status);
       tc_fence_after();
       uint32_t kv[2][32];
@@ -409,39 +398,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * a);   // this buffer may be overwritten
-      const int t = mine.row0 + row;
-      const bool valid = mine.exists && t < mine.end;   // rows past the span's end become zero
-      // the staging boxes are free once the previous step's stores have read them
-      if (tid == 0 && stored) bulk_wait_read_all();
-      named_barrier_sync(1, 256);
-      const long long cs = (long long)b * p.cs_sb + (long long)(valid ? t : 0) * p.cs_ss + 32 * ch;
-      const T *crow = static_cast<const T *>(p.cos) + cs, *srow = static_cast<const T *>(p.sin) + cs;
-      // two rounds of 16 channel pairs: the row's cos / sin serve both heads
+      if (mine.exists) {
+        mbar_wait_bounded(cs_bar, ncs & 1, &abort_flag, status);
+        ++ncs;
+        const bool valid = mine.row0 + row < mine.end;   // rows past the span's end become zero
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint4 clo[2], chi[2], slo[2], shi[2];
-        if (valid) {
-          ldg_16ch<T>(crow + 16 * half, wide, clo[0], clo[1]);
-          ldg_16ch<T>(crow + 64 + 16 * half, wide, chi[0], chi[1]);
-          ldg_16ch<T>(srow + 16 * half, wide, slo[0], slo[1]);
-          ldg_16ch<T>(srow + 64 + 16 * half, wide, shi[0], shi[1]);
-        }
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const int u = 2 * half + q;
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t off = stage_u32 + swizzled_offset<128>(row, (4 * ch + u) * 8);
+          const uint4 clo = ld_shared_u4(off), chi = ld_shared_u4(off + kBox);
+          const uint4 slo = ld_shared_u4(off + 2 * kBox), shi = ld_shared_u4(off + 3 * kBox);
           if (valid) {
-            rope_group<T>(clo[q], chi[q], slo[q], shi[q], u, has1, kv[0], kv[1]);
+            rope_group<T>(clo, chi, slo, shi, u, has1, kv[0], kv[1]);
           } else {
 #pragma unroll
             for (int k = 0; k < 4; ++k)
               kv[0][4 * u + k] = kv[0][16 + 4 * u + k] = kv[1][4 * u + k] = kv[1][16 + 4 * u + k] = 0u;
           }
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            if (h == 1 && !has1) continue;
-            const uint32_t cbase = stage_u32 + (2 * h) * kBox + swizzled_offset<128>(row, (4 * ch + u) * 8);
-            st_shared_v4(cbase, kv[h][4 * u], kv[h][4 * u + 1], kv[h][4 * u + 2], kv[h][4 * u + 3]);
-            st_shared_v4(cbase + kBox, kv[h][16 + 4 * u], kv[h][17 + 4 * u], kv[h][18 + 4 * u], kv[h][19 + 4 * u]);
+          st_shared_v4(off, kv[0][4 * u], kv[0][4 * u + 1], kv[0][4 * u + 2], kv[0][4 * u + 3]);
+          st_shared_v4(off + kBox, kv[0][16 + 4 * u], kv[0][17 + 4 * u], kv[0][18 + 4 * u], kv[0][19 + 4 * u]);
+          if (has1) {
+            st_shared_v4(off + 2 * kBox, kv[1][4 * u], kv[1][4 * u + 1], kv[1][4 * u + 2], kv[1][4 * u + 3]);
+            st_shared_v4(off + 3 * kBox, kv[1][16 + 4 * u], kv[1][17 + 4 * u], kv[1][18 + 4 * u], kv[1][19 + 4 * u]);
           }
         }
       }
