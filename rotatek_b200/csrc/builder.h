@@ -63,7 +63,8 @@ cudaError_t launch_kproj_tc(int dtype_is_bf16, const KProjMaps &maps, const KPro
 // reflections; the top `keep` eigenvectors (descending eigenvalue) go out as R,
 // plus delta_mu.  No global scratch.
 struct EighParams {
-  int nmat, heads;              // matrix m = b * heads + h
+  int nmat, heads;              // matrices m0 .. m0 + nmat - 1 of this launch; m = b * heads + h
+  int m0;
   const float *cov;             // [nmat][128][128]
   const float *ksum;            // [nmat][128] or NULL: `cov` is already the matrix to solve
   int count;                    // tokens behind cov / ksum
@@ -88,6 +89,7 @@ struct RotateParams {
   const void *R; long long R_s[4];                // [B, H, 128, keep]
   void *out; long long o_s[4];                    // [B, H, S, keep]
   unsigned int *status;                           // device status word (bounded-wait timeouts)
+  int max_ctas;                                   // TMA kernel: CTAs at most (0: one per SM)
 };
 
 // keep in {16, 32, 48, 64}; keys_map: [B, H, S, 128] bf16/f16, box 64 x 64, 128B swizzle

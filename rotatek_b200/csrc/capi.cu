@@ -736,7 +736,8 @@ cudaError_t launch_covariance(const View4 &kv, int dt, float *cov, float *ksum, 
 // kept = K . R on the tensor cores where the layouts allow (TMA kernel for
 // keep <= 64, cp.async kernel for keep in {96, 128}), else the CUDA-core kernel.
 cudaError_t launch_rotation(const View4 &kv, int dt, int64_t keep, const rtk_tensor *R_out,
-                            const rtk_tensor *kept_out, unsigned int *status, cudaStream_t st) {
+                            const rtk_tensor *kept_out, unsigned int *status, cudaStream_t st,
+                            int max_ctas = 0) {
   const int64_t B = kv.n[0], H = kv.n[1], S = kv.n[2];
   if (S == 0) return cudaSuccess;
   rtk::RotateParams rp;
@@ -752,6 +753,7 @@ cudaError_t launch_rotation(const View4 &kv, int dt, int64_t keep, const rtk_ten
   rp.R = R_out->data;
   rp.out = kept_out->data;
   rp.status = status;
+  rp.max_ctas = max_ctas;
   const bool rtc = is_half_type(dt) && keep % 16 == 0 && kv.s[3] == 1 && (kv.s[2] * 2) % 16 == 0 &&
                    (kv.s[1] * 2) % 16 == 0 && (kv.s[0] * 2) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(kv.data) % 16 == 0 && kept_out->stride[3] == 1 &&
@@ -811,6 +813,42 @@ int check_build_args(int64_t B, int64_t H, int64_t S, int64_t D, int dt, const r
 
 // The build after the sums are in w.cov / w.ksum: centring, query weighting,
 // eigensolver, top-k R and delta_mu, then kept = K_vis . R.
+// A private non-blocking stream and two events per device for the build's
+// overlap of the eigensolver's last wave with the rotation (created on first
+// use, kept for the process).
+struct SideStream {
+  cudaStream_t stream;
+  cudaEvent_t solved, rotated;
+};
+const SideStream *side_stream(int device, cudaStream_t caller) {
+  static std::mutex mu;
+  static SideStream cache[64];
+  static bool made[64] = {false};
+  if (device < 0 || device >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!made[device]) {
+    // not created while the caller's stream is being captured into a graph
+    // (that call takes the single-stream path; the next eager call creates it)
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(caller, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    SideStream s;
+    if (cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+    if (cudaEventCreateWithFlags(&s.solved, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&s.rotated, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    cache[device] = s;
+    made[device] = true;
+  }
+  return &cache[device];
+}
+
+int64_t dtype_size(int dt) { return dt == RTK_F32 ? 4 : 2; }
+
 int finish_build(const View4 &kv, int dt, const rtk_tensor *queries, int64_t num_kv_groups, int64_t keep,
                  const rtk_tensor *kept_out, const rtk_tensor *R_out, const rtk_tensor *delta_mu_out,
                  const rtk_tensor *eigvals_out, const BuildWs &w, cudaStream_t st) {
@@ -834,9 +872,57 @@ int finish_build(const View4 &kv, int dt, const rtk_tensor *queries, int64_t num
     for (int i = 0; i < 3; ++i) jp.dm_s[i] = delta_mu_out->stride[i];
   }
   jp.evals = eigvals_out ? static_cast<float *>(eigvals_out->data) : nullptr;
+  // One CTA per matrix.  When the matrices fill whole waves of the device's
+  // solver slots but a few, those few would run as a last wave on their own
+  // (a lone solve takes ~0.2 ms).  Split them off: the full waves first, then
+  // the tail, while the rotation of the solved batch rows streams on the SMs
+  // the tail leaves free (a side stream joined by events; capturable).
+  const int device = current_device();
+  const int64_t nmat = B * H;
+  const int64_t sms = sm_count(device);
+  const int64_t slots = (keep <= 32 ? 2 : 1) * sms;
+  const int64_t tail = nmat % slots;
+  const int64_t bt = (nmat > slots && tail > 0 && tail <= slots / 4 && S > 0) ? cdiv(tail, H) : 0;
+  const SideStream *side = bt > 0 && bt < B ? side_stream(device, st) : nullptr;
+  if (side == nullptr) {
+    cudaError_t e = rtk::launch_eigh(jp, st);
+    if (e != cudaSuccess) return cuda_fail(e, "rotation builder (eigensolver) launch");
+    e = launch_rotation(kv, dt, keep, R_out, kept_out, w.status, st);
+    if (e != cudaSuccess) return cuda_fail(e, "rotation builder (rotate) launch");
+    return RTK_OK;
+  }
+  const int64_t b1 = B - bt;
+  jp.m0 = 0;
+  jp.nmat = (int)(b1 * H);
   cudaError_t e = rtk::launch_eigh(jp, st);
+  if (e == cudaSuccess) e = cudaEventRecord(side->solved, st);
+  if (e == cudaSuccess) {
+    jp.m0 = (int)(b1 * H);
+    jp.nmat = (int)(bt * H);
+    e = rtk::launch_eigh(jp, st);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "rotation builder (eigensolver) launch");
-  e = launch_rotation(kv, dt, keep, R_out, kept_out, w.status, st);
+  // batch rows [0, b1) on the side stream, on the SMs the tail's CTAs leave free
+  View4 k1 = kv;
+  k1.n[0] = b1;
+  e = cudaStreamWaitEvent(side->stream, side->solved, 0);
+  if (e == cudaSuccess)
+    e = launch_rotation(k1, dt, keep, R_out, kept_out, w.status, side->stream,
+                        (int)std::max<int64_t>(1, sms - bt * H));   // a tail CTA may hold an SM alone
+  if (e == cudaSuccess) e = cudaEventRecord(side->rotated, side->stream);
+  // rows [b1, B) behind the tail on the caller's stream, then join
+  if (e == cudaSuccess) {
+    View4 k2 = kv;
+    k2.n[0] = bt;
+    k2.data = static_cast<const unsigned char *>(kv.data) + b1 * kv.s[0] * dtype_size(dt);
+    rtk_tensor R2 = *R_out, O2 = *kept_out;
+    R2.shape[0] = bt;
+    R2.data = static_cast<unsigned char *>(R_out->data) + b1 * R_out->stride[0] * dtype_size(R_out->dtype);
+    O2.shape[0] = bt;
+    O2.data = static_cast<unsigned char *>(kept_out->data) + b1 * kept_out->stride[0] * dtype_size(kept_out->dtype);
+    e = launch_rotation(k2, dt, keep, &R2, &O2, w.status, st);
+  }
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(st, side->rotated, 0);
   if (e != cudaSuccess) return cuda_fail(e, "rotation builder (rotate) launch");
   return RTK_OK;
 }

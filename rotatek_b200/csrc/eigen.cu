@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, KMAX <= 32 ? 2 : 1) eigh_kernel(cons
   ESmem<KMAX> &sm = *reinterpret_cast<ESmem<KMAX> *>(smem_raw);
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int m = blockIdx.x;
+  const int m = p.m0 + blockIdx.x;
   const int b = m / p.heads, h = m % p.heads;
   float *A = sm.A;
   const int keep = p.keep;

@@ -325,6 +325,7 @@ cudaError_t launch_rot_tma(const CUtensorMap &kmap, const RotateParams &p, cudaS
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (units >= (1ll << 31)) return cudaErrorInvalidValue;
+  if (p.max_ctas > 0 && p.max_ctas < sms) sms = p.max_ctas;
   const int grid = static_cast<int>(units < sms ? units : sms);
   if (grid == 0) return cudaSuccess;
   cudaError_t err = cudaFuncSetAttribute(rotate_tma_kernel<T, KEEP>,

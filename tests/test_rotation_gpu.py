@@ -281,6 +281,40 @@ def test_pruner_update_rotatek_contract():
     assert update_rotatek is ChannelPruner.update_rotatek
 
 
+def test_build_rotation_split_tail_matches_and_replays():
+    """Matrices filling whole waves of solver slots but a few: the few are
+    solved in a second launch while the rotation of the rest runs on a side
+    stream.  Every batch row's R matches a build of those rows alone (their
+    covariance pass may split tokens differently, so up to fp32 summation
+    order), every kept tile is that row's Keys rotated by the R returned, and
+    the split build captured in a CUDA graph replays bit for bit."""
+    slots = 2 * torch.cuda.get_device_properties(0).multi_processor_count
+    H = 4
+    B = slots // H + 1                      # slots + 4 matrices: a tail of one batch row
+    k = syn.lowrank_keys(B, H, 200, seed=41, device=DEV, dtype=torch.bfloat16)
+    q = syn.normal((B, H * 2, 32, 128), 42, DEV, torch.bfloat16)
+    split = rot.build_rotation(k, q, 32, 2)
+    kept, R, dm, mask = split
+    head = rot.build_rotation(k[:B - 1], q[:B - 1], 32, 2)
+    tail = rot.build_rotation(k[B - 1:], q[B - 1:], 32, 2)
+    R2 = torch.cat([head[1], tail[1]])
+    P, P2 = f64(R) @ f64(R).swapaxes(-1, -2), f64(R2) @ f64(R2).swapaxes(-1, -2)
+    assert np.sqrt(((P - P2) ** 2).sum(axis=(-1, -2))).max() < 2e-2
+    assert torch.equal(mask, torch.cat([head[3], tail[3]]))
+    want = f64(k) @ f64(R)
+    assert np.abs(f64(kept) - want).max() <= 2 ** -7 * np.abs(want).max()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = rot.build_rotation(k, q, 32, 2)
+    g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(split, out):
+        assert torch.equal(a, b)
+    assert rot.read_build_status() == 0
+    del g
+
+
 def test_build_rotation_cuda_graph_replay():
     """The build runs on the caller's stream with no host synchronisation, so it
     can be captured in a CUDA graph (after one eager call has sized the
