@@ -138,8 +138,8 @@ class RandomLlamaDecoder:
         hq, hk = c.heads * c.head_dim, c.kv_heads * c.head_dim
         for li, L in enumerate(self.layers):
             if c.fused_key_projection:
-                # K = RoPE(x W_k^T) for every token with the visual span's sums in
-                # one tensor-core pass, then the rest of the build on those Keys
+                # K = RoPE(x W_k^T) for every token from one tensor-core kernel,
+                # then the visual span's sums and the rest of the build on those Keys
                 xn = self._rms(x, L["ln1"])
                 q = F.linear(xn, L["wqkv"][:hq]).view(b, s_total, c.heads, c.head_dim).transpose(1, 2)
                 v = F.linear(xn, L["wqkv"][hq + hk:]).view(b, s_total, c.kv_heads, c.head_dim)
