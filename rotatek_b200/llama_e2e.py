@@ -13,8 +13,8 @@ synthetic embeddings.  Weights are random (there is no checkpoint); the shapes
 are the model's, so every byte and FLOP of the real model is moved and done.
 
 Prefill computes each layer's Keys with ``build_rotation_projected`` (K
-projection, RoPE and the visual span's covariance sums in one tensor-core pass,
-then the rest of the build), Queries and Values with cuBLAS; set
+projection and RoPE in one tensor-core kernel, then the visual span's
+covariance sums and the rest of the build), Queries and Values with cuBLAS; set
 ``fused_key_projection=False`` for the adapters' order (fused QKV GEMM, torch
 RoPE, ``build_rotation`` on the visual slice).
 
