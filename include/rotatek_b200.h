@@ -301,7 +301,7 @@ size_t rtk_build_rotation_projected_workspace_size(int64_t batch, int64_t kv_hea
 /* rtk_key_projection followed by the rest of rtk_build_rotation on the visual
  * span of keys_out: from a layer's hidden states to what the split cache stores
  * (K for every token; R, delta_mu and kept = K_vis . R for the visual span)
- * with one pass over the Keys fewer than projection + rtk_build_rotation.
+ * in one call; the covariance sums are taken once, by the projection step.
  * Arguments as in the two calls; kept_out is [B, H_kv, vis_len, keep];
  * workspace of rtk_build_rotation_projected_workspace_size() bytes.          */
 int rtk_build_rotation_projected(const rtk_tensor *hidden, const rtk_tensor *w_k, const rtk_tensor *bias,

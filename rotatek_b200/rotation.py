@@ -227,9 +227,10 @@ def build_rotation_projected(hidden_states: torch.Tensor, w_k: torch.Tensor, bia
                              cos: torch.Tensor, sin: torch.Tensor, vis_start: int, vis_len: int,
                              queries_recent: Optional[torch.Tensor], keep: int, num_kv_groups: int,
                              query_aware: Optional[bool] = None):
-    """``key_projection`` + ``build_rotation`` on the visual span, without the
-    covariance pass over the Keys: from one layer's hidden states to the Keys
-    of every token and the RotateK state of the visual span.
+    """``key_projection`` + ``build_rotation`` on the visual span in one call
+    (the covariance sums are taken once, by the projection step): from one
+    layer's hidden states to the Keys of every token and the RotateK state of
+    the visual span.
 
     Returns (keys [B, H_kv, S, 128], kept [B, H_kv, vis_len, keep], R_partial,
     delta_mu, keep_mask) -- ``build_rotation``'s outputs for
