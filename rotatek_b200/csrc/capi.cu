@@ -815,12 +815,15 @@ int check_build_args(int64_t B, int64_t H, int64_t S, int64_t D, int dt, const r
 // eigensolver, top-k R and delta_mu, then kept = K_vis . R.
 // A private non-blocking stream and two events per device for the build's
 // overlap of the eigensolver's last wave with the rotation (created on first
-// use, kept for the process).
+// use, kept for the process).  `mu` is held while a build enqueues its fork
+// and join, so that concurrent callers on one device never wait on each
+// other's event records.
 struct SideStream {
   cudaStream_t stream;
   cudaEvent_t solved, rotated;
+  std::mutex mu;
 };
-const SideStream *side_stream(int device, cudaStream_t caller) {
+SideStream *side_stream(int device, cudaStream_t caller) {
   static std::mutex mu;
   static SideStream cache[64];
   static bool made[64] = {false};
@@ -834,14 +837,13 @@ const SideStream *side_stream(int device, cudaStream_t caller) {
       cudaGetLastError();
       return nullptr;
     }
-    SideStream s;
+    SideStream &s = cache[device];
     if (cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
     if (cudaEventCreateWithFlags(&s.solved, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&s.rotated, cudaEventDisableTiming) != cudaSuccess) {
       cudaGetLastError();
       return nullptr;
     }
-    cache[device] = s;
     made[device] = true;
   }
   return &cache[device];
@@ -883,7 +885,7 @@ int finish_build(const View4 &kv, int dt, const rtk_tensor *queries, int64_t num
   const int64_t slots = (keep <= 32 ? 2 : 1) * sms;
   const int64_t tail = nmat % slots;
   const int64_t bt = (nmat > slots && tail > 0 && tail <= slots / 4 && S > 0) ? cdiv(tail, H) : 0;
-  const SideStream *side = bt > 0 && bt < B ? side_stream(device, st) : nullptr;
+  SideStream *side = bt > 0 && bt < B ? side_stream(device, st) : nullptr;
   if (side == nullptr) {
     cudaError_t e = rtk::launch_eigh(jp, st);
     if (e != cudaSuccess) return cuda_fail(e, "rotation builder (eigensolver) launch");
@@ -891,6 +893,7 @@ int finish_build(const View4 &kv, int dt, const rtk_tensor *queries, int64_t num
     if (e != cudaSuccess) return cuda_fail(e, "rotation builder (rotate) launch");
     return RTK_OK;
   }
+  std::lock_guard<std::mutex> fork_join(side->mu);
   const int64_t b1 = B - bt;
   jp.m0 = 0;
   jp.nmat = (int)(b1 * H);
