@@ -297,7 +297,7 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
       DK = R.n[3];
     }
   }
-  int64_t os[3];
+  int64_t os[3] = {0, 0, 0};
   out_view(a.out, B, Hq, D, os);
   const int dt = a.q->dtype;
   const int device = current_device();
@@ -504,7 +504,7 @@ int rtk_rotatek_decode(const rtk_tensor *q_full, const rtk_tensor *R_partial,
     if (t->dtype != q_full->dtype) return fail(RTK_ERR_INVALID, "all tensors but mask_full must share q_full's dtype");
   if (delta_mu != nullptr && delta_mu->dtype != q_full->dtype)
     return fail(RTK_ERR_INVALID, "all tensors but mask_full must share q_full's dtype");
-  int64_t os[3];
+  int64_t os[3] = {0, 0, 0};
   if (!out_view(out, B, Hq, D, os)) return fail(RTK_ERR_INVALID, "out must be [B, H_q, D] or [B, 1, H_q, D]");
   if (B * Hq == 0 || D == 0) return RTK_OK;
   DecodeArgs a{q_full, R_partial, delta_mu, k_full, v_full, mask_full, k_sparse, v_sparse, out, num_kv_groups, false};
@@ -548,7 +548,7 @@ int rtk_rotatek_decode_fp8(const rtk_tensor *q_full, const rtk_tensor *R_partial
     if (t->dtype != q_full->dtype) return fail(RTK_ERR_INVALID, "q, R, k_full, v_full and out must share a dtype");
   if (delta_mu != nullptr && delta_mu->dtype != q_full->dtype)
     return fail(RTK_ERR_INVALID, "q, R, k_full, v_full and out must share a dtype");
-  int64_t os[3];
+  int64_t os[3] = {0, 0, 0};
   if (!out_view(out, B, Hq, D, os)) return fail(RTK_ERR_INVALID, "out must be [B, H_q, D] or [B, 1, H_q, D]");
   if (B * Hq == 0 || D == 0) return RTK_OK;
   DecodeArgs a{q_full, R_partial, delta_mu, k_full, v_full, mask_full, k8, v8, out, num_kv_groups, false,
@@ -626,7 +626,7 @@ int rtk_full_channel_decode(const rtk_tensor *q, const rtk_tensor *k, const rtk_
                 (long long)Hkv, (long long)num_kv_groups);
   if (!dtype_ok(q->dtype) || k->dtype != q->dtype || v->dtype != q->dtype)
     return fail(RTK_ERR_INVALID, "q, k, v and out must share one dtype (float32, bfloat16 or float16)");
-  int64_t os[3];
+  int64_t os[3] = {0, 0, 0};
   if (!out_view(out, B, Hq, D, os) || out->dtype != q->dtype)
     return fail(RTK_ERR_INVALID, "out must be [B, H_q, D] or [B, 1, H_q, D] in q's dtype");
   if (B * Hq == 0 || D == 0) return RTK_OK;
@@ -663,7 +663,7 @@ int rtk_spark_decode(const rtk_tensor *q_full, const rtk_tensor *k_full, const r
   for (const rtk_tensor *t : {k_full, v_full, k_kept, pruned_mean, v_sparse, out})
     if (t->dtype != q_full->dtype)
       return fail(RTK_ERR_INVALID, "all tensors but mask_full and keep_idx must share q_full's dtype");
-  int64_t os[3];
+  int64_t os[3] = {0, 0, 0};
   if (!out_view(out, B, Hq, D, os)) return fail(RTK_ERR_INVALID, "out must be [B, H_q, D] or [B, 1, H_q, D]");
   if (B * Hq == 0 || D == 0) return RTK_OK;
   DecodeArgs a{q_full, nullptr, nullptr, k_full, v_full, mask_full, k_kept, v_sparse, out, num_kv_groups, false};
