@@ -69,6 +69,7 @@ def test_key_projection_matches_reference_path(golden, case):
     (torch.bfloat16, 2, 300, 64, 40, 20, 250, False, True),     # 40 units of 4 tiles
     (torch.bfloat16, 8, 300, 128, 15, 20, 250, True, True),     # odd H; CTA ranges cross units
     (torch.bfloat16, 1, 4000, 3584, 4, 32, 3900, True, False),  # Qwen2.5-VL-7B K projection width
+    (torch.bfloat16, 3, 259, 128, 2, 1, 257, True, True),       # one prompt and one text token
 ])
 def test_key_projection_vs_oracle(dtype, B, S, hidden, H, vs, vl, bias, per_batch):
     gen = torch.Generator(device=DEV).manual_seed(S + hidden)
