@@ -135,11 +135,12 @@ int rtk_rotatek_decode_static(const rtk_tensor *q_full, const rtk_tensor *R_part
 /* rtk_rotatek_decode with the visual span stored in fp8 (e4m3, one byte per
  * element; see rtk_quantize_visual_fp8): no counterpart in the reference.
  * Visual Keys and Values are read as
- *   k~[b,h,t,c] = k_scale[b,h,c] * e4m3(k8[b,h,t,c]),   v[b,h,t,d] = v_scale[b,h,t] * e4m3(v8[b,h,t,d])
+ *   k~[b,h,t,c] = k_scale[b,h,c] * e4m3(k8[b,h,t,c]),   v[b,h,t,d] = v_scale[b,h,t] * e4m3(v8[b,h,d,t])
  * and the result is rtk_rotatek_decode's on those values; the prompt/text span
  * stays in q's dtype (bf16 / fp16).  Half the visual bytes of the 16-bit path.
  *   k8 [B, H_kv, S_v, D_keep] u8 (D_keep 16, 32 or 64), k_scale [B, H_kv, D_keep] f32,
- *   v8 [B, H_kv, S_v, 128] u8, v_scale [B, H_kv, S_v] f32; the rest and the
+ *   v8 [B, H_kv, 128, S_v] u8 (the Values transposed: token stride 1, 16-byte
+ *   aligned channel rows), v_scale [B, H_kv, S_v] f32; the rest and the
  *   workspace (rtk_rotatek_decode_workspace_size) as rtk_rotatek_decode.       */
 int rtk_rotatek_decode_fp8(const rtk_tensor *q_full, const rtk_tensor *R_partial,
                            const rtk_tensor *delta_mu, const rtk_tensor *k_full,
@@ -153,8 +154,10 @@ int rtk_rotatek_decode_fp8(const rtk_tensor *q_full, const rtk_tensor *R_partial
  * Values; scale = amax / 448 (1 for an all-zero group), x8 = e4m3(x / scale)
  * rounded to nearest even, saturating.
  *   k_sparse [B, H_kv, S, D_keep], v_sparse [B, H_kv, S, 128]   bf16 | f16, channel stride 1
- *   k8_out, v8_out: contiguous u8 of the same shapes; k_scale_out [B, H_kv, D_keep],
- *   v_scale_out [B, H_kv, S]: contiguous f32.                                   */
+ *   k8_out [B, H_kv, S, D_keep]: contiguous u8; v8_out [B, H_kv, 128, S] u8, the
+ *   Values transposed: token stride 1, channel rows 16-byte aligned and at least
+ *   S rounded up to 16 bytes long (bytes past S up to there are written as 0);
+ *   k_scale_out [B, H_kv, D_keep], v_scale_out [B, H_kv, S]: contiguous f32.  */
 int rtk_quantize_visual_fp8(const rtk_tensor *k_sparse, const rtk_tensor *v_sparse, const rtk_tensor *k8_out,
                             const rtk_tensor *k_scale_out, const rtk_tensor *v8_out,
                             const rtk_tensor *v_scale_out, void *stream);

@@ -332,15 +332,15 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
     if (tc && Sv > 0 && !fp8 && !spark)
       tc = encode_map(&maps.ks, ks, et, (int)DK, kVisBlockTokens, swizzle_for_row_bytes((int)DK * 2)) &&
            encode_map(&maps.vs, vs, et, 64, kVisBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (tc && Sv > 0 && fp8)   // e4m3 rows of DK and 128 bytes
+    if (tc && Sv > 0 && fp8)   // e4m3 Key rows of DK bytes; V^T: 128 channel rows of 64 token bytes
       tc = encode_map(&maps.ks, ks, CU_TENSOR_MAP_DATA_TYPE_UINT8, (int)DK, kVisBlockTokens,
                       DK == 16 ? CU_TENSOR_MAP_SWIZZLE_NONE : swizzle_for_row_bytes((int)DK), 1) &&
-           encode_map(&maps.vs, vs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, kVisBlockTokens,
-                      CU_TENSOR_MAP_SWIZZLE_128B, 1);
+           encode_map(&maps.vs, vs, CU_TENSOR_MAP_DATA_TYPE_UINT8, kVisBlockTokens, 128,
+                      CU_TENSOR_MAP_SWIZZLE_64B, 1);
   }
   if (fp8 && !tc)
     return fail(RTK_ERR_UNSUPPORTED, "the fp8 visual span needs bf16 / fp16 queries, head_dim 128, D_keep 16, "
-                                     "32 or 64 and 16-byte aligned e4m3 rows");
+                                     "32 or 64 and 16-byte aligned e4m3 rows (Keys) and channel rows (V^T)");
   if (spark && !tc)
     return fail(RTK_ERR_UNSUPPORTED, "the SparK decode needs bf16 / fp16 tensors, head_dim 128, D_keep 16, 32 "
                                      "or 64, and channel-contiguous, 16-byte aligned rows");
@@ -538,8 +538,9 @@ int rtk_rotatek_decode_fp8(const rtk_tensor *q_full, const rtk_tensor *R_partial
   if (!same_dims(k8, 4, {B, Hkv, -1, DK}) || k8->dtype != RTK_U8)
     return fail(RTK_ERR_INVALID, "k_sparse_fp8 must be a uint8 (e4m3) [B, H_kv, S_sparse, D_keep]");
   const int64_t Sv = k8->shape[2];
-  if (!same_dims(v8, 4, {B, Hkv, Sv, D}) || v8->dtype != RTK_U8)
-    return fail(RTK_ERR_INVALID, "v_sparse_fp8 must be a uint8 (e4m3) [B, H_kv, S_sparse, D]");
+  if (!same_dims(v8, 4, {B, Hkv, D, Sv}) || v8->dtype != RTK_U8 || (Sv > 1 && v8->stride[3] != 1))
+    return fail(RTK_ERR_INVALID, "v_sparse_fp8 must be a uint8 (e4m3) [B, H_kv, D, S_sparse] with token stride 1 "
+                                 "(the Values transposed)");
   if (!same_dims(k_scale, 3, {B, Hkv, DK}) || k_scale->dtype != RTK_F32 || k_scale->stride[2] != 1)
     return fail(RTK_ERR_INVALID, "k_scale must be a float32 [B, H_kv, D_keep] with unit channel stride");
   if (!same_dims(v_scale, 3, {B, Hkv, Sv}) || v_scale->dtype != RTK_F32)
@@ -582,8 +583,19 @@ int rtk_quantize_visual_fp8(const rtk_tensor *k_sparse, const rtk_tensor *v_spar
   };
   if (!contiguous(k8_out, {B, H, S, DK}) || k8_out->dtype != RTK_U8)
     return fail(RTK_ERR_INVALID, "k8_out must be a contiguous uint8 [B, H_kv, S, D_keep]");
-  if (!contiguous(v8_out, {B, H, S, 128}) || v8_out->dtype != RTK_U8)
-    return fail(RTK_ERR_INVALID, "v8_out must be a contiguous uint8 [B, H_kv, S, 128]");
+  // V^T: [B, H, 128, S], token stride 1, channel rows of at least S rounded up
+  // to 16 bytes (the quantiser writes whole 16-byte chunks), strides in 16 bytes
+  const int64_t s16 = (S + 15) / 16 * 16;
+  const bool v8_ok = v8_out != nullptr && v8_out->ndim == 4 && v8_out->dtype == RTK_U8 &&
+                     v8_out->shape[0] == B && v8_out->shape[1] == H && v8_out->shape[2] == 128 &&
+                     v8_out->shape[3] == S && (S <= 1 || v8_out->stride[3] == 1) &&
+                     v8_out->stride[2] >= s16 && v8_out->stride[2] % 16 == 0 &&
+                     (H == 1 || (v8_out->stride[1] >= 128 * v8_out->stride[2] && v8_out->stride[1] % 16 == 0)) &&
+                     (B == 1 || (v8_out->stride[0] >= H * v8_out->stride[1] && v8_out->stride[0] % 16 == 0)) &&
+                     reinterpret_cast<uintptr_t>(v8_out->data) % 16 == 0;
+  if (!v8_ok)
+    return fail(RTK_ERR_INVALID, "v8_out must be a uint8 [B, H_kv, 128, S] (the Values transposed) with token "
+                                 "stride 1, 16-byte aligned rows of at least S rounded up to 16 bytes");
   if (!contiguous(k_scale_out, {B, H, DK}) || k_scale_out->dtype != RTK_F32)
     return fail(RTK_ERR_INVALID, "k_scale_out must be a contiguous float32 [B, H_kv, D_keep]");
   if (!contiguous(v_scale_out, {B, H, S}) || v_scale_out->dtype != RTK_F32)
@@ -602,7 +614,8 @@ int rtk_quantize_visual_fp8(const rtk_tensor *k_sparse, const rtk_tensor *v_spar
   for (int i = 0; i < 4; ++i) { qp.k_s[i] = ks.s[i]; qp.v_s[i] = vs.s[i]; }
   qp.keys8 = static_cast<uint8_t *>(k8_out->data);
   qp.k_scale = static_cast<float *>(k_scale_out->data);
-  qp.values8 = static_cast<uint8_t *>(v8_out->data);
+  qp.values8t = static_cast<uint8_t *>(v8_out->data);
+  for (int i = 0; i < 3; ++i) qp.v8_s[i] = v8_out->stride[i];
   qp.v_scale = static_cast<float *>(v_scale_out->data);
   const cudaError_t e = rtk::launch_quantize_fp8(k_sparse->dtype == RTK_BF16, qp, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "fp8 quantisation launch");

@@ -40,14 +40,16 @@ cudaError_t launch_decode_tc(int dtype_is_bf16, const DecodeTensorMaps &maps,
                              cudaStream_t stream);
 
 // fp8 visual span (decode_tc.cu with the fp8 flag): K~8 [B, H_kv, S_v, D_keep]
-// and V8 [B, H_kv, S_v, 128] e4m3, dequantised as k_scale[b, h, c] * K~8 and
-// v_scale[b, h, t] * V8 (quant_fp8.cu).
+// and the Values transposed, V8t [B, H_kv, 128, S_v] (token stride 1), e4m3,
+// dequantised as k_scale[b, h, c] * K~8[.., t, c] and v_scale[b, h, t] *
+// V8t[.., d, t] (quant_fp8.cu).
 struct DecodeFp8 {
   const float *k_scale; long long ksc_sb, ksc_sh;               // [B, H_kv, D_keep]
   const float *v_scale; long long vsc_sb, vsc_sh, vsc_ss;       // [B, H_kv, S_v]
 };
 
-// heads_tile 8 or 16, dk 16 / 32 / 64; maps.ks / maps.vs are uint8 maps.
+// heads_tile 8 or 16, dk 16 / 32 / 64; maps.ks / maps.vs are uint8 maps (maps.vs
+// over V8t: 64-token x 128-channel boxes, 64-byte swizzle).
 cudaError_t launch_decode_tc_fp8(int dtype_is_bf16, const DecodeTensorMaps &maps,
                                  const DecodeParams &p, const DecodeFp8 &f, int heads_tile, int dk,
                                  int grid, cudaStream_t stream);
@@ -84,7 +86,9 @@ struct QuantParams {
   const void *values; long long v_s[4];      // [B, H, S, 128], 16-bit, channel stride 1
   uint8_t *keys8;                            // [B, H, S, keep] contiguous
   float *k_scale;                            // [B, H, keep]
-  uint8_t *values8;                          // [B, H, S, 128] contiguous
+  uint8_t *values8t;                         // [B, H, 128, S] token stride 1; rows of
+  long long v8_s[3];                         //   >= S rounded up to 16 bytes, strides in
+                                             //   bytes, multiples of 16
   float *v_scale;                            // [B, H, S]
 };
 

@@ -59,7 +59,9 @@ constexpr float kNegBig = -1e30f;        // running-max floor (fused_decode.py:1
 
 // What the visual span holds:
 //   kModeRotK   rotated-truncated Keys k~ [S_v, D_keep] and Values, 16-bit
-//   kModeFp8    the same in e4m3 with per-channel Key / per-token Value scales
+//   kModeFp8    the same in e4m3 with per-channel Key / per-token Value scales;
+//               the Values stored transposed (V^T rows of tokens), so that the
+//               e4m3 bytes load straight into f16 A fragments (see fp8_afrag)
 //   kModeSpark  SparK's per-token channel pruning: the kept channels' values
 //               [S_v, D_keep] (channel order), their channel indices [S_v, D_keep]
 //               (uint8, ascending) and the pruned channels' mean per token; the
@@ -77,8 +79,13 @@ struct Cfg {
   // Values in two boxes | kept values [32][DK] | kept channel indices [32][DK]
   static constexpr int kSpValOff = 4 * kFullBoxBytes;
   static constexpr int kSpIdxOff = kSpValOff + kFullTokens * DK * 2;
-  static constexpr int kStageRaw =
-      MODE == kModeSpark ? kSpIdxOff + kFullTokens * DK : kKsBytes + 2 * kVisBoxBytes;
+  // fp8 visual block: e4m3 Keys [64 tokens][DK] | e4m3 V^T [128 channels][64 tokens]
+  static constexpr int kFp8VOff = kVisTokens * DK;
+  static constexpr int kFp8Raw = kFp8VOff + kVisBoxBytes > 4 * kFullBoxBytes ? kFp8VOff + kVisBoxBytes
+                                                                             : 4 * kFullBoxBytes;
+  static constexpr int kStageRaw = MODE == kModeSpark ? kSpIdxOff + kFullTokens * DK
+                                   : MODE == kModeFp8 ? kFp8Raw
+                                                      : kKsBytes + 2 * kVisBoxBytes;
   static constexpr int kStageBytes = (kStageRaw + 1023) / 1024 * 1024;
   static_assert(kStageBytes >= 4 * kFullBoxBytes, "a stage must hold a prompt/text block");
   // per-unit header: q rows [H][128], R [128][DK], delta_mu [128] (16-bit), mask bytes
@@ -128,14 +135,56 @@ struct Split {
   }
 };
 
+// ---- fp8 (e4m3) operands, converted in registers.
+// ldmatrix of e4m3 bytes as 16-bit elements gives lane (g, j) = (lane / 4,
+// lane % 4) bytes 4j .. 4j+3 of row g of each 8-row x 16-byte matrix.  An
+// m16n8k16 A fragment wants row g at k = 2j, 2j+1 (a0, a1 for row g+8) and at
+// k = 8+2j, 9+2j (a2, a3), so bytes 4j, 4j+1 serve as k = 2j, 2j+1 and bytes
+// 4j+2, 4j+3 as k = 8+2j, 9+2j: the MMA's k index runs over the 16 bytes of a
+// row in the order kperm(k) below, and its other operand follows that order.
+//   Keys [tokens][channels]: k = channel; the query's B fragments are permuted
+//     to channel order kperm once per unit (fp8_query_order).
+//   V^T [channels][tokens]: k = token; the probabilities' B fragments hold the
+//     logits tile's rows 2j, 2j+1 and 8+2j, 9+2j, so row rho of the logits tile
+//     is made token kperm(rho) of its 16 (the Keys' ldmatrix row addresses).
+__device__ __forceinline__ int kperm(int k) {   // 0..15 -> 0,1,4,5,8,9,12,13, 2,3,6,7,10,11,14,15
+  return ((k & 7) >> 1) * 4 + (k & 1) + ((k >> 3) << 1);
+}
+// two e4m3 (low byte first) -> two f16 (exact)
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(static_cast<uint16_t>(two)));
+  return r;
+}
+// the A fragment from the two ldmatrix registers of its rows 0-7 and 8-15
+__device__ __forceinline__ void fp8_afrag(uint32_t rows0, uint32_t rows8, uint32_t (&a)[4]) {
+  a[0] = e4m3x2_to_f16x2(rows0);
+  a[1] = e4m3x2_to_f16x2(rows8);
+  a[2] = e4m3x2_to_f16x2(rows0 >> 16);
+  a[3] = e4m3x2_to_f16x2(rows8 >> 16);
+}
+// B fragments (k = channel 2j, 2j+1 | 8+2j, 9+2j of head g) -> the same
+// channels in kperm order (channels 4j, 4j+1 | 4j+2, 4j+3): from lane
+// (g, 2j mod 4) and (g, 2j+1 mod 4), first or second register as 4j < 8
+__device__ __forceinline__ void fp8_query_order(uint32_t (&b)[2], int lane) {
+  const int s0 = (lane & ~3) | ((2 * lane) & 3);
+  const bool first = (lane & 3) < 2;
+  const uint32_t x0 = __shfl_sync(0xffffffffu, b[0], s0), y0 = __shfl_sync(0xffffffffu, b[1], s0);
+  const uint32_t x1 = __shfl_sync(0xffffffffu, b[0], s0 | 1), y1 = __shfl_sync(0xffffffffu, b[1], s0 | 1);
+  b[0] = first ? x0 : y0;
+  b[1] = first ? x1 : y1;
+}
+
 // Online softmax over MT 16-token tiles of scores already in log2 units,
 // then O^T += V^T . P^T with P split hi + lo.  `valid[mt][r]` masks row g8 + 8r
 // of tile mt.  V tile: rows = tokens, two 64-d boxes `vbox` bytes apart.
 // With `vscale` the probabilities of row g8 + 8r of tile mt are multiplied by
 // vscale[mt][r] after the normaliser has taken them (per-token Value scales of
 // an fp8 visual span: sum_t p_t (s_t v8_t)).  PLO = false drops the low half of
-// P's split (11 bits of P are plenty against e4m3 Values' 4).
-template <typename T, int NT, int MT, bool PLO = true>
+// P's split (11 bits of P are plenty against e4m3 Values' 4).  V8T: the Values
+// are e4m3 V^T rows (channel rows of 64 token bytes, 64-byte swizzle, at vbase)
+// and row rho of each score tile is token kperm(rho) of its 16.
+template <typename T, int NT, int MT, bool PLO = true, bool V8T = false>
 __device__ __forceinline__ void softmax_pv(float (&s)[MT][NT][4], const bool (&valid)[MT][2],
                                            float (&m_run)[NT][2], float (&l_run)[NT][2],
                                            float (&o)[8][NT][4], uint32_t vbase, uint32_t vbox,
@@ -211,6 +260,28 @@ __device__ __forceinline__ void softmax_pv(float (&s)[MT][NT][4], const bool (&v
         pl[mt][nt][1] = movmatrix_trans(pack2<T>(p2 - r2, p3 - r3));
       }
     }
+  }
+  if constexpr (V8T) {
+    // O^T[d, head] += V^T[d, tok] . P^T[tok, head]: e4m3 V^T rows d*16 + 0..15,
+    // tokens 16 kk + 0..15 and 16 (kk+1) + 0..15 per ldmatrix
+    static_assert(MT % 2 == 0 && !PLO, "token tiles in pairs, P without a low half");
+    const int vr = (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+    for (int d = 0; d < 8; ++d) {
+#pragma unroll
+      for (int kk = 0; kk < MT; kk += 2) {
+        uint32_t r[4], a0[4], a1[4];
+        ldmatrix_x4(vbase + swizzled_offset<64>(d * 16 + vr, (kk + (lane >> 4)) * 8), r[0], r[1], r[2], r[3]);
+        fp8_afrag(r[0], r[1], a0);
+        fp8_afrag(r[2], r[3], a1);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma_16816<T>(o[d][nt], a0, pb[kk][nt][0], pb[kk][nt][1]);
+          mma_16816<T>(o[d][nt], a1, pb[kk + 1][nt][0], pb[kk + 1][nt][1]);
+        }
+      }
+    }
+    return;
   }
   // O^T[d, head] += V^T[d, tok] . P^T[tok, head]   (ldmatrix.trans of V rows)
   const int vrow = (lane & 7) + ((lane >> 4) & 1) * 8;
@@ -409,72 +480,11 @@ __device__ __forceinline__ void merge_unit(const DecodeParams &p, int unit, int 
   }
 }
 
-// 16 e4m3 -> 16 f16 (exact), low bytes first
-__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two) {
-  uint32_t r;
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(static_cast<uint16_t>(two)));
-  return r;
-}
-__device__ __forceinline__ void e4m3x16_to_f16(const uint4 &in, uint4 &lo, uint4 &hi) {
-  lo = make_uint4(e4m3x2_to_f16x2(in.x), e4m3x2_to_f16x2(in.x >> 16), e4m3x2_to_f16x2(in.y),
-                  e4m3x2_to_f16x2(in.y >> 16));
-  hi = make_uint4(e4m3x2_to_f16x2(in.z), e4m3x2_to_f16x2(in.z >> 16), e4m3x2_to_f16x2(in.w),
-                  e4m3x2_to_f16x2(in.w >> 16));
-}
 // byte offset of 16-byte chunk c of row t in a TMA box of DK-byte rows
 template <int DK>
 __device__ __forceinline__ uint32_t k8_offset(int t, int c) {
   if constexpr (DK == 16) return static_cast<uint32_t>(t) * 16;
   else return swizzled_offset<DK>(t, c * 8);
-}
-
-// fp8 visual block: the stage holds K~8 (64 x DK bytes, at kKsBytes / 2) and
-// V8 (64 x 128 bytes, in the place of the second 16-bit V box); rewrite them in
-// place as the f16 tiles the 16-bit path reads (K~ rows of 2 DK bytes from 0,
-// V in two 64-channel boxes from kKsBytes).  32 rows per pass, one row per
-// lane; every lane reads the source bytes its pass overwrites before any lane
-// writes (K~ rows 32..63 land on K~8), and V box 1's row t is V8's row t.
-template <int DK>
-__device__ __forceinline__ void convert_fp8_stage(unsigned char *st, int lane) {
-  constexpr int kKs = kVisTokens * DK * 2;
-  unsigned char *k16 = st;
-  const unsigned char *k8 = st + kKs / 2;
-  unsigned char *v16 = st + kKs;
-  unsigned char *v8 = st + kKs + kVisBoxBytes;
-#pragma unroll
-  for (int pass = 0; pass < 2; ++pass) {
-    const int t = pass * 32 + lane;
-    uint4 kr[DK / 16], vr[4];
-#pragma unroll
-    for (int c = 0; c < DK / 16; ++c) kr[c] = *reinterpret_cast<const uint4 *>(k8 + k8_offset<DK>(t, c));
-#pragma unroll
-    for (int c = 0; c < 4; ++c) vr[c] = *reinterpret_cast<const uint4 *>(v8 + swizzled_offset<128>(t, c * 8));
-    __syncwarp();
-#pragma unroll
-    for (int c = 0; c < DK / 16; ++c) {
-      uint4 lo, hi;
-      e4m3x16_to_f16(kr[c], lo, hi);
-      *reinterpret_cast<uint4 *>(k16 + swizzled_offset<DK * 2>(t, 16 * c)) = lo;
-      *reinterpret_cast<uint4 *>(k16 + swizzled_offset<DK * 2>(t, 16 * c + 8)) = hi;
-    }
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {     // channels 0-63 -> box 0
-      uint4 lo, hi;
-      e4m3x16_to_f16(vr[c], lo, hi);
-      *reinterpret_cast<uint4 *>(v16 + swizzled_offset<128>(t, 16 * c)) = lo;
-      *reinterpret_cast<uint4 *>(v16 + swizzled_offset<128>(t, 16 * c + 8)) = hi;
-    }
-#pragma unroll
-    for (int c = 0; c < 4; ++c) vr[c] = *reinterpret_cast<const uint4 *>(v8 + swizzled_offset<128>(t, (c + 4) * 8));
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {     // channels 64-127 -> box 1 (over V8 row t)
-      uint4 lo, hi;
-      e4m3x16_to_f16(vr[c], lo, hi);
-      *reinterpret_cast<uint4 *>(v8 + swizzled_offset<128>(t, 16 * c)) = lo;
-      *reinterpret_cast<uint4 *>(v8 + swizzled_offset<128>(t, 16 * c + 8)) = hi;
-    }
-    __syncwarp();
-  }
 }
 
 // SparK visual block: rebuild the 32 tokens' full-width Keys as the two
@@ -628,10 +638,10 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
           } else {
             const int tok = (j - p.blocks_full) * kVisTokens;
             if constexpr (FP8) {
-              // e4m3 tiles at the places convert_fp8_stage reads them from
+              // e4m3 Key rows, then the 128 V^T rows of these 64 tokens
               mbar_arrive_expect_tx(&full_bar[stage], kVisTokens * DK + kVisBoxBytes);
-              tma_load_4d_hint(st + C::kKsBytes / 2, &tm_ks, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
-              tma_load_4d_hint(st + C::kKsBytes + kVisBoxBytes, &tm_vs, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
+              tma_load_4d_hint(st, &tm_ks, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
+              tma_load_4d_hint(st + C::kFp8VOff, &tm_vs, tok, 0, kvh, bk, &full_bar[stage], stream_pol);
             } else {
               mbar_arrive_expect_tx(&full_bar[stage], C::kKsBytes + 2 * kVisBoxBytes);
               tma_load_4d_hint(st, &tm_ks, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
@@ -737,6 +747,10 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
           qhi[mt][nt][half] = movmatrix_trans(h);
           qlo[mt][nt][half] = movmatrix_trans(pack2<TV>(v0 - h0, v1 - h1));
         }
+        if constexpr (FP8) {   // the e4m3 Key fragments' channel order
+          fp8_query_order(qhi[mt][nt], lane);
+          fp8_query_order(qlo[mt][nt], lane);
+        }
       }
     }
     // bias = q . delta_mu per head: lane sums 4 channels, butterfly over the warp
@@ -782,18 +796,19 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
     for (int i = first; i < seg_end; i += kWarps) {
       const int stage = i % kStages;
       const int j = j0 + (i - it);
-      // fp8 span: this block's per-token Value scales, requested before the
-      // stage wait so that their L2 latency hides behind it and the conversion
+      // fp8 span: this block's per-token Value scales (rows g8, g8 + 8 of each
+      // score tile: tokens kperm(g8), kperm(g8) + 2), requested before the
+      // stage wait so that their L2 latency hides behind it
       float vs[4][2];
       if constexpr (FP8) {
         if (j >= p.blocks_full) {
           const float *vsc = f8.v_scale + (long long)bk * f8.vsc_sb + (long long)kvh * f8.vsc_sh;
-          const int tv = (j - p.blocks_full) * kVisTokens + g8;
+          const int tv = (j - p.blocks_full) * kVisTokens + kperm(g8);
 #pragma unroll
           for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-              const int tok = tv + mt * 16 + 8 * r;
+              const int tok = tv + mt * 16 + 2 * r;
               vs[mt][r] = tok < p.seq_sparse ? __ldg(vsc + (long long)tok * f8.vsc_ss) : 0.f;
             }
         }
@@ -862,31 +877,66 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
         } else if constexpr (!SPARK) {
           // ---- visual block: 64 tokens, rotated-truncated Keys, (q~ . k~ + bias)
           const int tok0 = (j - p.blocks_full) * kVisTokens;
-          if constexpr (FP8) convert_fp8_stage<DK>(ring + stage * C::kStageBytes, lane);
           float s[4][NT][4];
 #pragma unroll
           for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) s[mt][nt][0] = s[mt][nt][1] = s[mt][nt][2] = s[mt][nt][3] = 0.f;
-#pragma unroll
-          for (int ks = 0; ks < DK / 16; ++ks) {
-#pragma unroll
-            for (int mt = 0; mt < 4; ++mt) {
-              uint32_t a[4];
-              ldmatrix_x4(sbase + swizzled_offset<kKsRowBytes>(mt * 16 + arow, ks * 16 + acol), a[0],
-                          a[1], a[2], a[3]);
+          if constexpr (FP8) {
+            // e4m3 Key rows straight into f16 A fragments; lane l addresses
+            // token kperm(l % 16) of the tile (and its next 16-byte chunk, or
+            // for D_keep 16 the next tile, in lanes 16-31)
+            const int krow = kperm(lane & 15);
+            auto kmma = [&](int mt, int ks, const uint32_t (&a)[4]) {
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt) {
                 mma_16816<TV>(s[mt][nt], a, qhi[ks][nt][0], qhi[ks][nt][1]);
                 mma_16816<TV>(s[mt][nt], a, qlo[ks][nt][0], qlo[ks][nt][1]);
               }
+            };
+#pragma unroll
+            for (int mt = 0; mt < 4; mt += (DK == 16 ? 2 : 1)) {
+#pragma unroll
+              for (int kc = 0; kc < (DK == 16 ? 1 : DK / 32); ++kc) {
+                uint32_t r[4], a0[4], a1[4];
+                const int t = DK == 16 ? (mt + (lane >> 4)) * 16 + krow : mt * 16 + krow;
+                const int c = DK == 16 ? 0 : 2 * kc + (lane >> 4);
+                ldmatrix_x4(sbase + k8_offset<DK>(t, c), r[0], r[1], r[2], r[3]);
+                fp8_afrag(r[0], r[1], a0);
+                fp8_afrag(r[2], r[3], a1);
+                if constexpr (DK == 16) {
+                  kmma(mt, 0, a0);
+                  kmma(mt + 1, 0, a1);
+                } else {
+                  kmma(mt, 2 * kc, a0);
+                  kmma(mt, 2 * kc + 1, a1);
+                }
+              }
+            }
+          } else {
+#pragma unroll
+            for (int ks = 0; ks < DK / 16; ++ks) {
+#pragma unroll
+              for (int mt = 0; mt < 4; ++mt) {
+                uint32_t a[4];
+                ldmatrix_x4(sbase + swizzled_offset<kKsRowBytes>(mt * 16 + arow, ks * 16 + acol), a[0],
+                            a[1], a[2], a[3]);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                  mma_16816<TV>(s[mt][nt], a, qhi[ks][nt][0], qhi[ks][nt][1]);
+                  mma_16816<TV>(s[mt][nt], a, qlo[ks][nt][0], qlo[ks][nt][1]);
+                }
+              }
             }
           }
+          // rows g8 and g8 + 8 of tile mt: tokens g8, g8 + 8, or for fp8
+          // kperm(g8), kperm(g8) + 2
+          const int row0 = FP8 ? kperm(g8) : g8, row1 = FP8 ? row0 + 2 : g8 + 8;
           bool valid[4][2];
 #pragma unroll
           for (int mt = 0; mt < 4; ++mt) {
-            valid[mt][0] = tok0 + mt * 16 + g8 < p.seq_sparse;
-            valid[mt][1] = tok0 + mt * 16 + g8 + 8 < p.seq_sparse;
+            valid[mt][0] = tok0 + mt * 16 + row0 < p.seq_sparse;
+            valid[mt][1] = tok0 + mt * 16 + row1 < p.seq_sparse;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
               s[mt][nt][0] = (s[mt][nt][0] + bias2[nt][0]) * p.scale_log2;
@@ -897,13 +947,13 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
           }
           if constexpr (FP8) {
             // per-token Value scales of the fp8 span fold into the probabilities
-            softmax_pv<TV, NT, 4, false>(s, valid, m_run, l_run, o, sbase + C::kKsBytes, kVisBoxBytes, lane, vs);
+            softmax_pv<TV, NT, 4, false, true>(s, valid, m_run, l_run, o, sbase + C::kFp8VOff, 0u, lane, vs);
           } else {
             softmax_pv<T, NT, 4>(s, valid, m_run, l_run, o, sbase + C::kKsBytes, kVisBoxBytes, lane);
           }
         }
       }
-      // this warp's reads (and, for fp8 / SparK, in-place writes) of the stage
+      // this warp's reads (and, for SparK, in-place writes) of the stage
       // are ordered before the TMA write that refills it (async proxy)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();

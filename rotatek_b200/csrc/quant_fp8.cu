@@ -5,7 +5,10 @@
 // first), so a per-channel scale keeps the small channels' resolution.  At
 // decode the scale folds into the rotated query: q~ . k~ = sum_c (q~_c s_c) k8_c.
 // Visual Values [B, H, S_v, 128]: one scale per (b, h, token); at decode it
-// folds into that token's softmax weight: sum_t p_t (s_t v8_t).
+// folds into that token's softmax weight: sum_t p_t (s_t v8_t).  The e4m3
+// Values are stored transposed, V8t [B, H, 128, S_v] (each channel a row of
+// token bytes, padded to 16 bytes), the operand layout of the decode's P.V
+// product.
 //
 //   amax  = max |x| over the group (channel over tokens, or token over channels)
 //   scale = amax / 448 (e4m3's largest finite value), 1 for an all-zero group
@@ -83,30 +86,55 @@ __global__ void __launch_bounds__(256) quant_keys_kernel(const QuantParams p) {
   }
 }
 
-// One warp per (b, h, token) row of 128 Values: lane holds channels 4 lane ... 4 lane + 3.
+// One CTA per (b, h, 64-token tile): warp w quantises tokens 8w .. 8w+7 of the
+// tile (lane: channels 4 lane .. 4 lane + 3) into a shared [128 channels][64
+// tokens] byte tile, then the CTA writes the tile's channel rows in 16-byte
+// chunks up to the span's end rounded up to 16 tokens (tokens past it are 0).
+constexpr int kVTile = 64;
+constexpr int kVTileRow = kVTile + 4;   // shared row bytes: word-aligned, rows spread over the banks
+
 template <typename T>
-__global__ void __launch_bounds__(256) quant_values_kernel(const QuantParams p) {
-  const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  const long long rows = (long long)p.batch * p.heads * p.seq;
-  if (row >= rows) return;
-  const int s = static_cast<int>(row % p.seq);
-  const long long bh = row / p.seq;
+__global__ void __launch_bounds__(256) quant_values_t_kernel(const QuantParams p) {
+  __shared__ __align__(16) uint8_t tile[128 * kVTileRow];
+  const int tiles = (p.seq + kVTile - 1) / kVTile;
+  const long long bh = blockIdx.x / tiles;
+  const int t0 = static_cast<int>(blockIdx.x % tiles) * kVTile;
   const int b = static_cast<int>(bh / p.heads), h = static_cast<int>(bh % p.heads);
-  const T *src = static_cast<const T *>(p.values) + (long long)b * p.v_s[0] + (long long)h * p.v_s[1] +
-                 (long long)s * p.v_s[2] + lane * 4;
-  const uint2 raw = *reinterpret_cast<const uint2 *>(src);
-  float f[4];
-  unpack2<T>(raw.x, f[0], f[1]);
-  unpack2<T>(raw.y, f[2], f[3]);
-  float mx = fmaxf(fmaxf(fabsf(f[0]), fabsf(f[1])), fmaxf(fabsf(f[2]), fabsf(f[3])));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const T *src = static_cast<const T *>(p.values) + (long long)b * p.v_s[0] + (long long)h * p.v_s[1] + lane * 4;
+  uint2 raw[8];
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-  const float sc = mx > 0.f ? __fdiv_rn(mx, kE4m3Max) : 1.f;
-  const uint32_t o = (uint32_t)e4m3x2(__fdiv_rn(f[0], sc), __fdiv_rn(f[1], sc)) |
-                     ((uint32_t)e4m3x2(__fdiv_rn(f[2], sc), __fdiv_rn(f[3], sc)) << 16);
-  *reinterpret_cast<uint32_t *>(p.values8 + row * 128 + lane * 4) = o;
-  if (lane == 0) p.v_scale[row] = sc;
+  for (int i = 0; i < 8; ++i) {
+    const int s = t0 + warp * 8 + i;
+    raw[i] = s < p.seq ? *reinterpret_cast<const uint2 *>(src + (long long)s * p.v_s[2]) : make_uint2(0u, 0u);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int tt = warp * 8 + i, s = t0 + tt;
+    float f[4];
+    unpack2<T>(raw[i].x, f[0], f[1]);
+    unpack2<T>(raw[i].y, f[2], f[3]);
+    float mx = fmaxf(fmaxf(fabsf(f[0]), fabsf(f[1])), fmaxf(fabsf(f[2]), fabsf(f[3])));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    const float sc = mx > 0.f ? __fdiv_rn(mx, kE4m3Max) : 1.f;
+    const uint32_t o = s < p.seq ? (uint32_t)e4m3x2(__fdiv_rn(f[0], sc), __fdiv_rn(f[1], sc)) |
+                                       ((uint32_t)e4m3x2(__fdiv_rn(f[2], sc), __fdiv_rn(f[3], sc)) << 16)
+                                 : 0u;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) tile[(4 * lane + c) * kVTileRow + tt] = static_cast<uint8_t>(o >> (8 * c));
+    if (lane == 0 && s < p.seq) p.v_scale[bh * p.seq + s] = sc;
+  }
+  __syncthreads();
+  const int s16 = (p.seq + 15) / 16 * 16;
+  uint8_t *dst = p.values8t + (long long)b * p.v8_s[0] + (long long)h * p.v8_s[1] + t0;
+#pragma unroll
+  for (int e = threadIdx.x; e < 128 * 4; e += 256) {
+    const int row = e >> 2, c = e & 3;
+    if (t0 + 16 * c >= s16) continue;
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(tile + row * kVTileRow + 16 * c);
+    *reinterpret_cast<uint4 *>(dst + (long long)row * p.v8_s[2] + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
 }
 
 template <typename T>
@@ -120,8 +148,8 @@ cudaError_t launch_quant(const QuantParams &p, cudaStream_t stream) {
   else return cudaErrorInvalidValue;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const long long rows = (long long)nmat * p.seq;
-  if (rows > 0) quant_values_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(p);
+  const long long tiles = (long long)nmat * ((p.seq + kVTile - 1) / kVTile);
+  if (tiles > 0) quant_values_t_kernel<T><<<(unsigned)tiles, 256, 0, stream>>>(p);
   return cudaGetLastError();
 }
 

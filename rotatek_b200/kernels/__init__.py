@@ -103,16 +103,20 @@ def quantize_visual_fp8(k_sparse: torch.Tensor, v_sparse: torch.Tensor):
 
     k_sparse [B, H_kv, S_v, D_keep] (D_keep 16 / 32 / 64) and v_sparse
     [B, H_kv, S_v, 128], bf16 or fp16.  Returns (k8, k_scale, v8, v_scale):
-    e4m3 bytes as uint8 [B, H_kv, S_v, D_keep] / [B, H_kv, S_v, 128] and fp32
-    scales [B, H_kv, D_keep] (per rotated channel) / [B, H_kv, S_v] (per
-    token), with x ~= scale * e4m3(x8), scale = amax / 448."""
+    e4m3 bytes as uint8, k8 [B, H_kv, S_v, D_keep] and v8 the Values
+    transposed, [B, H_kv, 128, S_v] (token stride 1; a view of rows padded to
+    16 bytes), and fp32 scales [B, H_kv, D_keep] (per rotated channel) /
+    [B, H_kv, S_v] (per token), with k ~= k_scale[c] * e4m3(k8[.., t, c]),
+    v ~= v_scale[t] * e4m3(v8[.., d, t]), scale = amax / 448."""
     if k_sparse.dim() != 4 or v_sparse.dim() != 4:
         raise ValueError("k_sparse must be [B, H_kv, S, D_keep] and v_sparse [B, H_kv, S, 128]")
     _lib.require_cuda(k_sparse, v_sparse)
     b, h, s, dk = k_sparse.shape
     dev = k_sparse.device
     k8 = torch.empty(b, h, s, dk, dtype=torch.uint8, device=dev)
-    v8 = torch.empty(b, h, s, v_sparse.shape[-1], dtype=torch.uint8, device=dev)
+    if v_sparse.shape[-1] != 128:
+        raise ValueError("k_sparse must be [B, H_kv, S, D_keep] and v_sparse [B, H_kv, S, 128]")
+    v8 = torch.empty(b, h, 128, (s + 15) // 16 * 16, dtype=torch.uint8, device=dev)[..., :s]
     ksc = torch.empty(b, h, dk, dtype=torch.float32, device=dev)
     vsc = torch.empty(b, h, s, dtype=torch.float32, device=dev)
     D = _lib.describe
@@ -124,7 +128,8 @@ def quantize_visual_fp8(k_sparse: torch.Tensor, v_sparse: torch.Tensor):
 def rotatek_decode_fp8(q_full, R_partial, delta_mu, k_full, v_full, mask_full, k8, k_scale, v8, v_scale,
                        num_kv_groups: int):
     """``rotatek_decode`` with the visual span in fp8: the visual Keys are
-    k_scale[c] * e4m3(k8) and the visual Values v_scale[t] * e4m3(v8) (from
+    k_scale[c] * e4m3(k8[.., t, c]) and the visual Values v_scale[t] *
+    e4m3(v8[.., d, t]) (v8 = V transposed, [B, H_kv, 128, S_v]; both from
     ``quantize_visual_fp8``; uint8 or float8_e4m3fn tensors); the prompt/text span
     and the output stay in q's dtype.  Returns (out [B, 1, H_q, D], None, None)."""
     if q_full.dim() != 3:

@@ -31,6 +31,11 @@ def e4m3_values(t8):
     return t8.view(torch.float8_e4m3fn).float().cpu().numpy().astype(np.float64)
 
 
+def values_natural(v8):
+    """The device's V^T bytes [B, H, 128, S] as e4m3 values [B, H, S, 128]."""
+    return e4m3_values(v8).swapaxes(-1, -2)
+
+
 def check(out, want, dtype):
     atol, rtol = TOL[dtype]
     err = np.abs(out.float().cpu().numpy() - want)
@@ -51,7 +56,12 @@ def test_quantize_bit_exact_and_decode(dtype, B, Hq, Hkv, Sv, Sf, keep):
     np.testing.assert_array_equal(ksc.cpu().numpy(), ksc_o)
     np.testing.assert_array_equal(vsc.cpu().numpy(), vsc_o)
     np.testing.assert_array_equal(e4m3_values(k8), kq)
-    np.testing.assert_array_equal(e4m3_values(v8), vq)
+    assert v8.shape == (B, Hkv, 128, Sv) and v8.stride(-1) == 1 and v8.stride(-2) % 16 == 0
+    np.testing.assert_array_equal(values_natural(v8), vq)
+    # the channel rows' padding to 16 tokens is written as zeros
+    s16 = (Sv + 15) // 16 * 16
+    padded = torch.as_strided(v8, (B, Hkv, 128, s16), v8.stride())
+    assert int(padded[..., Sv:].count_nonzero()) == 0
 
     out, _, _ = rotatek_decode_fp8(d.q_full, d.R_partial, d.delta_mu, d.k_full, d.v_full, d.mask_full,
                                    k8, ksc, v8, vsc, d.num_kv_groups)
@@ -78,6 +88,27 @@ def test_masks_no_bias_and_views():
     want = odec.rotatek_decode(d.q_full.cpu(), d.R_partial.cpu(), None, d.k_full.cpu(), d.v_full.cpu(),
                                mask.cpu(), kd, vd, 4)
     check(out, want, dtype)
+
+
+def test_values_in_wider_rows_and_one_token():
+    """V^T rows wider than the span (a view into a larger buffer) decode like the
+    quantiser's own rows; a one-token visual span."""
+    dtype = torch.bfloat16
+    for sv in (1, 150):
+        d = syn.make_decode(2, 14, 2, sv, 20, keep=32, seed=40 + sv, device=DEV, dtype=dtype)
+        k8, ksc, v8, vsc = quantize_visual_fp8(d.k_sparse, d.v_sparse)
+        wide = torch.full((2, 2, 128, 256 + 48), 0x7F, dtype=torch.uint8, device=DEV)  # e4m3 NaN outside the view
+        wide[..., 32:32 + sv] = v8
+        v8w = wide[..., 32:32 + sv]
+        args = (d.q_full, d.R_partial, d.delta_mu, d.k_full, d.v_full, d.mask_full, k8, ksc)
+        out, _, _ = rotatek_decode_fp8(*args, v8, vsc, d.num_kv_groups)
+        out_w, _, _ = rotatek_decode_fp8(*args, v8w, vsc, d.num_kv_groups)
+        assert torch.equal(out, out_w)
+        kq, ksc_o, vq, vsc_o = ofp8.quantize_visual(f64(d.k_sparse), f64(d.v_sparse))
+        kd, vd = ofp8.dequantize(kq, ksc_o, vq, vsc_o)
+        kw = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in d.as_kwargs().items()}
+        kw.update(k_sparse=kd, v_sparse=vd)
+        check(out, odec.rotatek_decode(**kw), dtype)
 
 
 def test_fp8_error_against_16bit_decode_at_config2_shape():
