@@ -71,9 +71,11 @@ enum : int { kModeRotK = 0, kModeFp8 = 1, kModeSpark = 2 };
 template <int NT, int DK, int MODE = kModeRotK>
 struct Cfg {
   static constexpr int kHeads = 8 * NT;
-  static constexpr int kWarps = (NT == 1 && DK <= 32) ? 5 : 4;   // consumer warps
+  // consumer warps: the fp8 span's 10 KB visual blocks leave room for a ring of
+  // 12 (16 KB) stages and a sixth warp
+  static constexpr int kWarps = (NT == 1 && DK <= 32) ? (MODE == kModeFp8 ? 6 : 5) : 4;
   static constexpr int kThreads = (kWarps + 1) * 32;             // + producer warp
-  static_assert(kWarps <= 5, "the host sizes the workspace for at most 5 partial slots per CTA");
+  static_assert(kWarps <= 6, "the host sizes the workspace for at most 6 partial slots per CTA");
   static constexpr int kKsBytes = kVisTokens * DK * 2;           // visual Keys of a block
   // SparK visual block (32 tokens): rebuilt dense Keys in two 64-channel boxes |
   // Values in two boxes | kept values [32][DK] | kept channel indices [32][DK]
