@@ -332,8 +332,8 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
     if (tc && Sv > 0 && !fp8 && !spark)
       tc = encode_map(&maps.ks, ks, et, (int)DK, kVisBlockTokens, swizzle_for_row_bytes((int)DK * 2)) &&
            encode_map(&maps.vs, vs, et, 64, kVisBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (tc && Sv > 0 && fp8)   // e4m3 Key rows of DK bytes; V^T: 128 channel rows of 64 token bytes
-      tc = encode_map(&maps.ks, ks, CU_TENSOR_MAP_DATA_TYPE_UINT8, (int)DK, kVisBlockTokens,
+    if (tc && Sv > 0 && fp8)   // 128 e4m3 Key rows of DK bytes; V^T: 128 channel rows of 64 token bytes
+      tc = encode_map(&maps.ks, ks, CU_TENSOR_MAP_DATA_TYPE_UINT8, (int)DK, 2 * kVisBlockTokens,
                       DK == 16 ? CU_TENSOR_MAP_SWIZZLE_NONE : swizzle_for_row_bytes((int)DK), 1) &&
            encode_map(&maps.vs, vs, CU_TENSOR_MAP_DATA_TYPE_UINT8, kVisBlockTokens, 128,
                       CU_TENSOR_MAP_SWIZZLE_64B, 1);
@@ -345,7 +345,9 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
     return fail(RTK_ERR_UNSUPPORTED, "the SparK decode needs bf16 / fp16 tensors, head_dim 128, D_keep 16, 32 "
                                      "or 64, and channel-contiguous, 16-byte aligned rows");
   if (tc) {
-    const TcShape t = tc_shape(B, Hkv, G, Sf, Sv, device, spark ? kFullBlockTokens : kVisBlockTokens);
+    // visual block tokens: 32 for SparK, 128 for fp8 (two halves of 64), else 64
+    const TcShape t = tc_shape(B, Hkv, G, Sf, Sv, device,
+                               spark ? kFullBlockTokens : fp8 ? 2 * kVisBlockTokens : kVisBlockTokens);
     const WorkspacePlan w = plan_workspace(B, Hq, t.slots, t.slot_floats);
     rtk::DecodeParams p;
     std::memset(&p, 0, sizeof(p));

@@ -10,8 +10,9 @@
 //   unit   = (batch, KV head, head chunk of <= 8*NT query heads); every query
 //            head of a GQA group shares each K/V tile, so K/V bytes are read
 //            once per group, not once per query head.
-//   block  = 32 prompt/text tokens or 64 visual tokens of one unit: first the
-//            ceil(S_f/32) full-width blocks, then the ceil(S_v/64) visual ones.
+//   block  = 32 prompt/text tokens or 64 visual tokens (128 in fp8, two halves
+//            of 64) of one unit: first the ceil(S_f/32) full-width blocks, then
+//            the visual ones.
 //   The U * blocks_per_unit blocks are cut into `grid` contiguous ranges, one
 //   per CTA (one CTA per SM), equal except that a range holding a unit start
 //   gives up a few blocks for the switch (`Split`).  Inside a CTA, block i goes
@@ -71,20 +72,25 @@ enum : int { kModeRotK = 0, kModeFp8 = 1, kModeSpark = 2 };
 template <int NT, int DK, int MODE = kModeRotK>
 struct Cfg {
   static constexpr int kHeads = 8 * NT;
-  // consumer warps: the fp8 span's 10 KB visual blocks leave room for a ring of
-  // 12 (16 KB) stages and a sixth warp
-  static constexpr int kWarps = (NT == 1 && DK <= 32) ? (MODE == kModeFp8 ? 6 : 5) : 4;
+  static constexpr int kWarps = (NT == 1 && DK <= 32) ? 5 : 4;   // consumer warps
   static constexpr int kThreads = (kWarps + 1) * 32;             // + producer warp
   static_assert(kWarps <= 6, "the host sizes the workspace for at most 6 partial slots per CTA");
+  // visual tokens per block: 64, or in fp8 128 (two halves of 64).  A ring
+  // stage's round trip (TMA issue, data in, consumer release, producer refill)
+  // takes a few microseconds whatever its size, so the bytes a stage carries
+  // set the stream's rate: 128 e4m3 tokens are 20 KB, as many as 64 16-bit ones
+  static constexpr int kVisBlk = MODE == kModeFp8 ? 2 * kVisTokens : kVisTokens;
+  static_assert(kVisBlk % kVisTokens == 0, "whole 64-token halves");
   static constexpr int kKsBytes = kVisTokens * DK * 2;           // visual Keys of a block
   // SparK visual block (32 tokens): rebuilt dense Keys in two 64-channel boxes |
   // Values in two boxes | kept values [32][DK] | kept channel indices [32][DK]
   static constexpr int kSpValOff = 4 * kFullBoxBytes;
   static constexpr int kSpIdxOff = kSpValOff + kFullTokens * DK * 2;
-  // fp8 visual block: e4m3 Keys [64 tokens][DK] | e4m3 V^T [128 channels][64 tokens]
-  static constexpr int kFp8VOff = kVisTokens * DK;
-  static constexpr int kFp8Raw = kFp8VOff + kVisBoxBytes > 4 * kFullBoxBytes ? kFp8VOff + kVisBoxBytes
-                                                                             : 4 * kFullBoxBytes;
+  // fp8 visual block: e4m3 Keys [128 tokens][DK] | e4m3 V^T [128 channels][64
+  // tokens] for each half
+  static constexpr int kFp8VOff = 2 * kVisTokens * DK;
+  static constexpr int kFp8Raw = kFp8VOff + 2 * kVisBoxBytes > 4 * kFullBoxBytes ? kFp8VOff + 2 * kVisBoxBytes
+                                                                                 : 4 * kFullBoxBytes;
   static constexpr int kStageRaw = MODE == kModeSpark ? kSpIdxOff + kFullTokens * DK
                                    : MODE == kModeFp8 ? kFp8Raw
                                                       : kKsBytes + 2 * kVisBoxBytes;
@@ -640,10 +646,13 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
           } else {
             const int tok = (j - p.blocks_full) * kVisTokens;
             if constexpr (FP8) {
-              // e4m3 Key rows, then the 128 V^T rows of these 64 tokens
-              mbar_arrive_expect_tx(&full_bar[stage], kVisTokens * DK + kVisBoxBytes);
-              tma_load_4d_hint(st, &tm_ks, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
-              tma_load_4d_hint(st + C::kFp8VOff, &tm_vs, tok, 0, kvh, bk, &full_bar[stage], stream_pol);
+              // 128 e4m3 Key rows, then the 128 V^T rows of each 64-token half
+              const int tok2 = (j - p.blocks_full) * C::kVisBlk;
+              mbar_arrive_expect_tx(&full_bar[stage], C::kVisBlk * DK + 2 * kVisBoxBytes);
+              tma_load_4d_hint(st, &tm_ks, 0, tok2, kvh, bk, &full_bar[stage], stream_pol);
+              tma_load_4d_hint(st + C::kFp8VOff, &tm_vs, tok2, 0, kvh, bk, &full_bar[stage], stream_pol);
+              tma_load_4d_hint(st + C::kFp8VOff + kVisBoxBytes, &tm_vs, tok2 + kVisTokens, 0, kvh, bk,
+                               &full_bar[stage], stream_pol);
             } else {
               mbar_arrive_expect_tx(&full_bar[stage], C::kKsBytes + 2 * kVisBoxBytes);
               tma_load_4d_hint(st, &tm_ks, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
@@ -801,18 +810,20 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
       // fp8 span: this block's per-token Value scales (rows g8, g8 + 8 of each
       // score tile: tokens kperm(g8), kperm(g8) + 2), requested before the
       // stage wait so that their L2 latency hides behind it
-      float vs[4][2];
+      float vs[2][4][2];
       if constexpr (FP8) {
         if (j >= p.blocks_full) {
           const float *vsc = f8.v_scale + (long long)bk * f8.vsc_sb + (long long)kvh * f8.vsc_sh;
-          const int tv = (j - p.blocks_full) * kVisTokens + kperm(g8);
+          const int tv = (j - p.blocks_full) * C::kVisBlk + kperm(g8);
 #pragma unroll
-          for (int mt = 0; mt < 4; ++mt)
+          for (int hf = 0; hf < 2; ++hf)
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-              const int tok = tv + mt * 16 + 2 * r;
-              vs[mt][r] = tok < p.seq_sparse ? __ldg(vsc + (long long)tok * f8.vsc_ss) : 0.f;
-            }
+            for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+              for (int r = 0; r < 2; ++r) {
+                const int tok = tv + hf * kVisTokens + mt * 16 + 2 * r;
+                vs[hf][mt][r] = tok < p.seq_sparse ? __ldg(vsc + (long long)tok * f8.vsc_ss) : 0.f;
+              }
         }
       }
       // SparK span: this lane's token's pruned-channel mean, likewise early
@@ -877,8 +888,13 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
           softmax_pv<T, NT, 2>(s, valid, m_run, l_run, o, sbase + 2 * kFullBoxBytes,
                                kFullBoxBytes, lane);
         } else if constexpr (!SPARK) {
-          // ---- visual block: 64 tokens, rotated-truncated Keys, (q~ . k~ + bias)
-          const int tok0 = (j - p.blocks_full) * kVisTokens;
+          // ---- visual block: 64 tokens (fp8: two halves of 64), rotated-truncated
+          //      Keys, (q~ . k~ + bias)
+#pragma unroll
+          for (int hf = 0; hf < C::kVisBlk / kVisTokens; ++hf) {
+          const int tok0 = (j - p.blocks_full) * C::kVisBlk + hf * kVisTokens;
+          if (tok0 >= p.seq_sparse) break;   // only an fp8 block's second half lies past the span
+          const uint32_t kbase = sbase + hf * kVisTokens * DK;   // this half's e4m3 Key rows
           float s[4][NT][4];
 #pragma unroll
           for (int mt = 0; mt < 4; ++mt)
@@ -903,7 +919,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
                 uint32_t r[4], a0[4], a1[4];
                 const int t = DK == 16 ? (mt + (lane >> 4)) * 16 + krow : mt * 16 + krow;
                 const int c = DK == 16 ? 0 : 2 * kc + (lane >> 4);
-                ldmatrix_x4(sbase + k8_offset<DK>(t, c), r[0], r[1], r[2], r[3]);
+                ldmatrix_x4(kbase + k8_offset<DK>(t, c), r[0], r[1], r[2], r[3]);
                 fp8_afrag(r[0], r[1], a0);
                 fp8_afrag(r[2], r[3], a1);
                 if constexpr (DK == 16) {
@@ -949,9 +965,11 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
           }
           if constexpr (FP8) {
             // per-token Value scales of the fp8 span fold into the probabilities
-            softmax_pv<TV, NT, 4, false, true>(s, valid, m_run, l_run, o, sbase + C::kFp8VOff, 0u, lane, vs);
+            softmax_pv<TV, NT, 4, false, true>(s, valid, m_run, l_run, o,
+                                               sbase + C::kFp8VOff + hf * kVisBoxBytes, 0u, lane, vs[hf]);
           } else {
             softmax_pv<T, NT, 4>(s, valid, m_run, l_run, o, sbase + C::kKsBytes, kVisBoxBytes, lane);
+          }
           }
         }
       }
