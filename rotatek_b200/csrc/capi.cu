@@ -324,10 +324,10 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
     if (Sf > 0)
       tc = encode_map(&maps.kf, kf, et, 64, kFullBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B) &&
            encode_map(&maps.vf, vf, et, 64, kFullBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (tc && Sv > 0 && spark)   // 32-token boxes; index rows of DK bytes
-      tc = encode_map(&maps.ks, ks, et, (int)DK, kFullBlockTokens, swizzle_for_row_bytes((int)DK * 2)) &&
+    if (tc && Sv > 0 && spark)   // 64-row kept values / index boxes (DK-byte index rows); 32-token Value boxes
+      tc = encode_map(&maps.ks, ks, et, (int)DK, 2 * kFullBlockTokens, swizzle_for_row_bytes((int)DK * 2)) &&
            encode_map(&maps.vs, vs, et, 64, kFullBlockTokens, CU_TENSOR_MAP_SWIZZLE_128B) &&
-           encode_map(&maps.ki, ki, CU_TENSOR_MAP_DATA_TYPE_UINT8, (int)DK, kFullBlockTokens,
+           encode_map(&maps.ki, ki, CU_TENSOR_MAP_DATA_TYPE_UINT8, (int)DK, 2 * kFullBlockTokens,
                       DK == 16 ? CU_TENSOR_MAP_SWIZZLE_NONE : swizzle_for_row_bytes((int)DK), 1);
     if (tc && Sv > 0 && !fp8 && !spark)
       tc = encode_map(&maps.ks, ks, et, (int)DK, kVisBlockTokens, swizzle_for_row_bytes((int)DK * 2)) &&
@@ -345,9 +345,10 @@ int run_decode(const DecodeArgs &a, void *workspace, size_t workspace_bytes, cud
     return fail(RTK_ERR_UNSUPPORTED, "the SparK decode needs bf16 / fp16 tensors, head_dim 128, D_keep 16, 32 "
                                      "or 64, and channel-contiguous, 16-byte aligned rows");
   if (tc) {
-    // visual block tokens: 32 for SparK, 128 for fp8 (two halves of 64), else 64
+    // visual block tokens: 64 for SparK (two halves of 32), 128 for fp8 (two
+    // halves of 64), else 64
     const TcShape t = tc_shape(B, Hkv, G, Sf, Sv, device,
-                               spark ? kFullBlockTokens : fp8 ? 2 * kVisBlockTokens : kVisBlockTokens);
+                               spark ? 2 * kFullBlockTokens : fp8 ? 2 * kVisBlockTokens : kVisBlockTokens);
     const WorkspacePlan w = plan_workspace(B, Hq, t.slots, t.slot_floats);
     rtk::DecodeParams p;
     std::memset(&p, 0, sizeof(p));

@@ -66,32 +66,36 @@ constexpr float kNegBig = -1e30f;        // running-max floor (fused_decode.py:1
 //   kModeSpark  SparK's per-token channel pruning: the kept channels' values
 //               [S_v, D_keep] (channel order), their channel indices [S_v, D_keep]
 //               (uint8, ascending) and the pruned channels' mean per token; the
-//               dense Keys are rebuilt in shared memory block by block
+//               dense Keys are rebuilt in shared memory, 32 tokens at a time, in
+//               an area of each consumer warp's own (64-token blocks, two halves)
 enum : int { kModeRotK = 0, kModeFp8 = 1, kModeSpark = 2 };
 
 template <int NT, int DK, int MODE = kModeRotK>
 struct Cfg {
   static constexpr int kHeads = 8 * NT;
-  static constexpr int kWarps = (NT == 1 && DK <= 32) ? 5 : 4;   // consumer warps
+  // consumer warps (SparK: fewer, so that its per-warp rebuild areas and a ring
+  // of 22 KB stages fit)
+  static constexpr int kWarps = MODE == kModeSpark ? (DK <= 32 ? 4 : 3) : (NT == 1 && DK <= 32) ? 5 : 4;
   static constexpr int kThreads = (kWarps + 1) * 32;             // + producer warp
   static_assert(kWarps <= 6, "the host sizes the workspace for at most 6 partial slots per CTA");
   // visual tokens per block: 64, or in fp8 128 (two halves of 64).  A ring
   // stage's round trip (TMA issue, data in, consumer release, producer refill)
   // takes a few microseconds whatever its size, so the bytes a stage carries
   // set the stream's rate: 128 e4m3 tokens are 20 KB, as many as 64 16-bit ones
-  static constexpr int kVisBlk = MODE == kModeFp8 ? 2 * kVisTokens : kVisTokens;
+  static constexpr int kVisBlk = MODE == kModeFp8 ? 2 * kVisTokens : MODE == kModeSpark ? 2 * kFullTokens
+                                                                                        : kVisTokens;
   static_assert(kVisBlk % kVisTokens == 0, "whole 64-token halves");
   static constexpr int kKsBytes = kVisTokens * DK * 2;           // visual Keys of a block
-  // SparK visual block (32 tokens): rebuilt dense Keys in two 64-channel boxes |
-  // Values in two boxes | kept values [32][DK] | kept channel indices [32][DK]
+  // SparK visual block (64 tokens): the Values of each 32-token half in two
+  // 64-channel boxes | kept values [64][DK] | kept channel indices [64][DK]
   static constexpr int kSpValOff = 4 * kFullBoxBytes;
-  static constexpr int kSpIdxOff = kSpValOff + kFullTokens * DK * 2;
+  static constexpr int kSpIdxOff = kSpValOff + 2 * kFullTokens * DK * 2;
   // fp8 visual block: e4m3 Keys [128 tokens][DK] | e4m3 V^T [128 channels][64
   // tokens] for each half
   static constexpr int kFp8VOff = 2 * kVisTokens * DK;
   static constexpr int kFp8Raw = kFp8VOff + 2 * kVisBoxBytes > 4 * kFullBoxBytes ? kFp8VOff + 2 * kVisBoxBytes
                                                                                  : 4 * kFullBoxBytes;
-  static constexpr int kStageRaw = MODE == kModeSpark ? kSpIdxOff + kFullTokens * DK
+  static constexpr int kStageRaw = MODE == kModeSpark ? kSpIdxOff + 2 * kFullTokens * DK
                                    : MODE == kModeFp8 ? kFp8Raw
                                                       : kKsBytes + 2 * kVisBoxBytes;
   static constexpr int kStageBytes = (kStageRaw + 1023) / 1024 * 1024;
@@ -99,7 +103,7 @@ struct Cfg {
   // per-unit header: q rows [H][128], R [128][DK], delta_mu [128] (16-bit), mask bytes
   static constexpr int kHdrQ = 0;
   static constexpr int kHdrR = kHdrQ + kHeads * kHeadDim * 2;
-  static constexpr int kHdrDm = kHdrR + kHeadDim * DK * 2;
+  static constexpr int kHdrDm = kHdrR + (MODE == kModeSpark ? 0 : kHeadDim * DK * 2);   // SparK: no R
   static constexpr int kHdrMask = kHdrDm + kHeadDim * 2;
   static constexpr int kHdrMaskBytes = 1024;  // prompt/text masks up to this length live here
   static constexpr int kHdrKsc = kHdrMask + kHdrMaskBytes;   // fp8 visual span: Key scales, fp32 [DK]
@@ -113,10 +117,13 @@ struct Cfg {
   static constexpr int kRingOff = (kHdrOff + kHdrBufs * kHdrBytes + 1023) / 1024 * 1024;
   // as many stages as fit, rounded down to a multiple of the consumer warps so
   // that every stage belongs to exactly one warp (its parity waits are exact)
-  static constexpr int kStages0 = (kSmemBudget - 1024 - kRingOff) / kStageBytes;
+  // SparK: each consumer warp's rebuilt Keys of a 32-token half, after the ring
+  static constexpr int kWarpKBytes = MODE == kModeSpark ? 2 * kFullBoxBytes : 0;
+  static constexpr int kStages0 = (kSmemBudget - 1024 - kRingOff - kWarps * kWarpKBytes) / kStageBytes;
   static constexpr int kStages = (kStages0 < kMaxStages ? kStages0 : kMaxStages) / kWarps * kWarps;
-  static_assert(kStages >= kWarps, "ring too small");
-  static constexpr int kBytes = kRingOff + kStages * kStageBytes;
+  static_assert(kStages >= 2 * kWarps, "ring too small: two stages per consumer warp");
+  static constexpr int kWarpKOff = kRingOff + kStages * kStageBytes;
+  static constexpr int kBytes = kWarpKOff + kWarps * kWarpKBytes;
 };
 
 // The split of the U * bpu blocks among the CTAs.  A CTA whose range crosses
@@ -317,11 +324,11 @@ __device__ __forceinline__ void softmax_pv(float (&s)[MT][NT][4], const bool (&v
 // the caller has each lane arrive on the header's barrier when its copies land,
 // so the producer goes back to issuing tiles at once.  The rest is staged
 // through registers (every load issued first) and stored before returning.
-template <typename T, int NT, int DK>
+template <typename T, int NT, int DK, int MODE>
 __device__ __forceinline__ void load_header(unsigned char *hdr, const DecodeParams &p, int b,
                                             int kvh, int head0, int nheads, int lane,
                                             const float *ksc = nullptr) {
-  using C = Cfg<NT, DK>;
+  using C = Cfg<NT, DK, MODE>;
   constexpr int kHeads = C::kHeads;
   constexpr int kRowChunks = kHeadDim / 8;  // 16-byte chunks of a 128-wide row
   unsigned char *hq = hdr + C::kHdrQ;
@@ -495,19 +502,22 @@ __device__ __forceinline__ uint32_t k8_offset(int t, int c) {
   else return swizzled_offset<DK>(t, c * 8);
 }
 
-// SparK visual block: rebuild the 32 tokens' full-width Keys as the two
-// 128B-swizzled {64 channels x 32 tokens} boxes a prompt/text block has, from
-// the kept values and channel indices the TMA put at kSpValOff / kSpIdxOff --
+// SparK visual block: rebuild one 32-token half's full-width Keys in `kdst` as
+// the two 128B-swizzled {64 channels x 32 tokens} boxes a prompt/text block
+// has, from the kept values and channel indices (rows 32 half + 0..31) the TMA
+// put at kSpValOff / kSpIdxOff of stage `st` --
 // the adapters' recovery (llama_visionzip.py:226-230): every channel first
 // takes the token's pruned-channel mean, then the kept channels their values.
 // Lane t owns token row t (its fill, its scatter), so only the caller's
 // __syncwarp before the MMAs orders lanes.  `mean2` is the token's mean (16-bit
 // bits) in both halves.  Indices are taken mod 128, so no write leaves the row.
 template <int DK>
-__device__ __forceinline__ void rebuild_spark_keys(unsigned char *st, int lane, uint32_t mean2) {
+__device__ __forceinline__ void rebuild_spark_keys(unsigned char *kdst, const unsigned char *st, int half,
+                                                   int lane, uint32_t mean2) {
   constexpr int kValOff = Cfg<1, DK, kModeSpark>::kSpValOff;
   constexpr int kIdxOff = Cfg<1, DK, kModeSpark>::kSpIdxOff;
-  const uint32_t row = smem_u32(st) + static_cast<uint32_t>(lane) * 128;
+  const int t = half * kFullTokens + lane;   // this lane's row of the kept values / indices
+  const uint32_t row = smem_u32(kdst) + static_cast<uint32_t>(lane) * 128;
   const uint32_t x = static_cast<uint32_t>(lane & 7) << 4;   // the row's 128B-swizzle pattern
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
@@ -517,12 +527,12 @@ __device__ __forceinline__ void rebuild_spark_keys(unsigned char *st, int lane, 
   uint32_t val[DK / 2], idx[DK / 4];
 #pragma unroll
   for (int c = 0; c < DK / 8; ++c) {
-    const uint4 v = *reinterpret_cast<const uint4 *>(st + kValOff + swizzled_offset<DK * 2>(lane, c * 8));
+    const uint4 v = *reinterpret_cast<const uint4 *>(st + kValOff + swizzled_offset<DK * 2>(t, c * 8));
     val[4 * c] = v.x; val[4 * c + 1] = v.y; val[4 * c + 2] = v.z; val[4 * c + 3] = v.w;
   }
 #pragma unroll
   for (int c = 0; c < DK / 16; ++c) {
-    const uint4 v = *reinterpret_cast<const uint4 *>(st + kIdxOff + k8_offset<DK>(lane, c));
+    const uint4 v = *reinterpret_cast<const uint4 *>(st + kIdxOff + k8_offset<DK>(t, c));
     idx[4 * c] = v.x; idx[4 * c + 1] = v.y; idx[4 * c + 2] = v.z; idx[4 * c + 3] = v.w;
   }
 #pragma unroll
@@ -613,7 +623,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
         if (lane == 0) ok = mbar_wait_bounded(&hdr_empty[buf], ((seg / kNB) & 1) ^ 1, abort_flag, p.status);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (ok)
-          load_header<T, NT, DK>(smem + C::kHdrOff + buf * C::kHdrBytes, p, bk, kvh,
+          load_header<T, NT, DK, MODE>(smem + C::kHdrOff + buf * C::kHdrBytes, p, bk, kvh,
                                  kvh * p.groups + hc * kHeads, min(kHeads, p.groups - hc * kHeads), lane,
                                  FP8 ? f8.k_scale + (long long)bk * f8.ksc_sb + (long long)kvh * f8.ksc_sh
                                      : nullptr);
@@ -635,12 +645,16 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
             tma_load_4d_hint(st + 2 * kFullBoxBytes, &tm_vf, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
             tma_load_4d_hint(st + 3 * kFullBoxBytes, &tm_vf, 64, tok, kvh, bk, &full_bar[stage], stream_pol);
           } else if constexpr (SPARK) {
-            // Values, kept values and kept channel indices; the Keys are rebuilt
-            // by the consumer in the first 2 * kFullBoxBytes
-            const int tok = (j - p.blocks_full) * kFullTokens;
-            mbar_arrive_expect_tx(&full_bar[stage], 2 * kFullBoxBytes + kFullTokens * DK * 3);
-            tma_load_4d_hint(st + 2 * kFullBoxBytes, &tm_vs, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
-            tma_load_4d_hint(st + 3 * kFullBoxBytes, &tm_vs, 64, tok, kvh, bk, &full_bar[stage], stream_pol);
+            // the Values of both 32-token halves, the kept values and the kept
+            // channel indices of all 64 tokens; the consumer rebuilds the Keys
+            const int tok = (j - p.blocks_full) * C::kVisBlk;
+            mbar_arrive_expect_tx(&full_bar[stage], 4 * kFullBoxBytes + C::kVisBlk * DK * 3);
+            tma_load_4d_hint(st, &tm_vs, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
+            tma_load_4d_hint(st + kFullBoxBytes, &tm_vs, 64, tok, kvh, bk, &full_bar[stage], stream_pol);
+            tma_load_4d_hint(st + 2 * kFullBoxBytes, &tm_vs, 0, tok + kFullTokens, kvh, bk, &full_bar[stage],
+                             stream_pol);
+            tma_load_4d_hint(st + 3 * kFullBoxBytes, &tm_vs, 64, tok + kFullTokens, kvh, bk, &full_bar[stage],
+                             stream_pol);
             tma_load_4d_hint(st + C::kSpValOff, &tm_ks, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
             tma_load_4d_hint(st + C::kSpIdxOff, &tm_ki, 0, tok, kvh, bk, &full_bar[stage], stream_pol);
           } else {
@@ -826,14 +840,18 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
               }
         }
       }
-      // SparK span: this lane's token's pruned-channel mean, likewise early
-      uint32_t mean2 = 0;
+      // SparK span: this lane's tokens' pruned-channel means (one per half),
+      // requested before the stage wait
+      uint32_t mean2[2] = {0u, 0u};
       if constexpr (SPARK) {
-        const int tok = (j - p.blocks_full) * kFullTokens + lane;
-        if (j >= p.blocks_full && tok < p.seq_sparse) {
-          const uint32_t m = __ldg(reinterpret_cast<const unsigned short *>(sp.mean) + (long long)bk * sp.mean_sb +
-                                   (long long)kvh * sp.mean_sh + (long long)tok * sp.mean_ss);
-          mean2 = m | (m << 16);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int tok = (j - p.blocks_full) * C::kVisBlk + hf * kFullTokens + lane;
+          if (j >= p.blocks_full && tok < p.seq_sparse) {
+            const uint32_t m = __ldg(reinterpret_cast<const unsigned short *>(sp.mean) + (long long)bk * sp.mean_sb +
+                                     (long long)kvh * sp.mean_sh + (long long)tok * sp.mean_ss);
+            mean2[hf] = m | (m << 16);
+          }
         }
       }
       const bool ready = mbar_wait_bounded(&full_bar[stage], (i / kStages) & 1, abort_flag, p.status);
@@ -841,13 +859,22 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
       const bool spark_vis = SPARK && j >= p.blocks_full;
       if (ready) {
         if (j < p.blocks_full || spark_vis) {
-          // ---- 32 tokens at full width, q . k: a prompt/text block, or a SparK
-          //      visual block once its Keys are rebuilt
-          const int tok0 = (spark_vis ? j - p.blocks_full : j) * kFullTokens;
+          // ---- 32 tokens at full width, q . k: a prompt/text block, or each
+          //      32-token half of a SparK visual block once its Keys are rebuilt
+          //      in this warp's area
+          unsigned char *wk = smem + C::kWarpKOff + cw * C::kWarpKBytes;
+#pragma unroll 1
+          for (int hf = 0; hf < (spark_vis ? 2 : 1); ++hf) {
+          const int tok0 = spark_vis ? (j - p.blocks_full) * C::kVisBlk + hf * kFullTokens : j * kFullTokens;
+          if (spark_vis && tok0 >= p.seq_sparse) break;   // a SparK block's second half past the span
+          uint32_t kb = sbase, vb = sbase + 2 * kFullBoxBytes;
           if constexpr (SPARK) {
             if (spark_vis) {
-              rebuild_spark_keys<DK>(ring + stage * C::kStageBytes, lane, mean2);
+              __syncwarp();   // every lane is done with the previous half's Keys
+              rebuild_spark_keys<DK>(wk, ring + stage * C::kStageBytes, hf, lane, hf == 0 ? mean2[0] : mean2[1]);
               __syncwarp();
+              kb = smem_u32(wk);
+              vb = sbase + hf * 2 * kFullBoxBytes;
             }
           }
           float s[2][NT][4];
@@ -857,7 +884,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
             for (int nt = 0; nt < NT; ++nt) s[mt][nt][0] = s[mt][nt][1] = s[mt][nt][2] = s[mt][nt][3] = 0.f;
 #pragma unroll
           for (int ks = 0; ks < kHeadDim / 16; ++ks) {
-            const uint32_t box = sbase + (ks >= 4 ? (uint32_t)kFullBoxBytes : 0u);
+            const uint32_t box = kb + (ks >= 4 ? (uint32_t)kFullBoxBytes : 0u);
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
               uint32_t a[4];
@@ -885,8 +912,8 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
 #pragma unroll
               for (int e = 0; e < 4; ++e) s[mt][nt][e] *= p.scale_log2;
           }
-          softmax_pv<T, NT, 2>(s, valid, m_run, l_run, o, sbase + 2 * kFullBoxBytes,
-                               kFullBoxBytes, lane);
+          softmax_pv<T, NT, 2>(s, valid, m_run, l_run, o, vb, kFullBoxBytes, lane);
+          }
         } else if constexpr (!SPARK) {
           // ---- visual block: 64 tokens (fp8: two halves of 64), rotated-truncated
           //      Keys, (q~ . k~ + bias)
