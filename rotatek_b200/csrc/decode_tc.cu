@@ -511,6 +511,11 @@ __device__ __forceinline__ uint32_t k8_offset(int t, int c) {
 // Lane t owns token row t (its fill, its scatter), so only the caller's
 // __syncwarp before the MMAs orders lanes.  `mean2` is the token's mean (16-bit
 // bits) in both halves.  Indices are taken mod 128, so no write leaves the row.
+// The area is this warp's own (no TMA writes it), so its 16-byte chunks are
+// swizzled by (row & 7) ^ ((row >> 3) & 3) rather than the TMA's row & 7: each
+// 8-row ldmatrix group still sees 8 distinct chunks, and rows t, t+8, t+16,
+// t+24 -- which under row & 7 put a channel that all four keep in one bank --
+// now differ.  spark_key_xor gives the reader the extra term.
 template <int DK>
 __device__ __forceinline__ void rebuild_spark_keys(unsigned char *kdst, const unsigned char *st, int half,
                                                    int lane, uint32_t mean2) {
@@ -518,7 +523,7 @@ __device__ __forceinline__ void rebuild_spark_keys(unsigned char *kdst, const un
   constexpr int kIdxOff = Cfg<1, DK, kModeSpark>::kSpIdxOff;
   const int t = half * kFullTokens + lane;   // this lane's row of the kept values / indices
   const uint32_t row = smem_u32(kdst) + static_cast<uint32_t>(lane) * 128;
-  const uint32_t x = static_cast<uint32_t>(lane & 7) << 4;   // the row's 128B-swizzle pattern
+  const uint32_t x = static_cast<uint32_t>((lane & 7) ^ ((lane >> 3) & 3)) << 4;   // the row's chunk pattern
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     st_shared_v4(row + ((c << 4) ^ x), mean2, mean2, mean2, mean2);
@@ -542,6 +547,10 @@ __device__ __forceinline__ void rebuild_spark_keys(unsigned char *kdst, const un
     st_shared_u16(addr, static_cast<uint16_t>(val[k >> 1] >> (16 * (k & 1))));
   }
 }
+
+// The rebuilt Keys' extra chunk XOR for row `row` (see rebuild_spark_keys), as
+// a byte mask to XOR into a 128B-swizzled offset.
+__device__ __forceinline__ uint32_t spark_key_xor(int row) { return static_cast<uint32_t>((row >> 3) & 3) << 4; }
 
 template <typename T, int NT, int DK, int MODE>
 __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
@@ -868,6 +877,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
           const int tok0 = spark_vis ? (j - p.blocks_full) * C::kVisBlk + hf * kFullTokens : j * kFullTokens;
           if (spark_vis && tok0 >= p.seq_sparse) break;   // a SparK block's second half past the span
           uint32_t kb = sbase, vb = sbase + 2 * kFullBoxBytes;
+          bool rebuilt = false;   // Keys in this warp's area (their own chunk pattern)
           if constexpr (SPARK) {
             if (spark_vis) {
               __syncwarp();   // every lane is done with the previous half's Keys
@@ -875,6 +885,7 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
               __syncwarp();
               kb = smem_u32(wk);
               vb = sbase + hf * 2 * kFullBoxBytes;
+              rebuilt = true;
             }
           }
           float s[2][NT][4];
@@ -888,7 +899,8 @@ __global__ void __launch_bounds__(Cfg<NT, DK, MODE>::kThreads, 1)
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
               uint32_t a[4];
-              ldmatrix_x4(box + swizzled_offset<128>(mt * 16 + arow, (ks & 3) * 16 + acol), a[0],
+              const uint32_t kx = rebuilt ? spark_key_xor(mt * 16 + arow) : 0u;
+              ldmatrix_x4(box + (swizzled_offset<128>(mt * 16 + arow, (ks & 3) * 16 + acol) ^ kx), a[0],
                           a[1], a[2], a[3]);
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt) mma_16816<T>(s[mt][nt], a, qf[ks][nt][0], qf[ks][nt][1]);
