@@ -429,6 +429,7 @@ def run_ours(args):
         extras = {}
         if world == 1:
             extras["build_config4"] = build_summary(dev, steps=10, warmup=3)
+            extras.update(fp8_spark_extras(dev))
         else:
             extras["strong_config2"] = strong_config2(dev, pg, rank, world, steps=200)
         # measured: at 2 GPUs the all_gather hides behind a 0.4 ms layer decode with no
@@ -936,6 +937,59 @@ def run_think(args):
 
 # ---------------------------------------------------------------- fp8 visual span (config 2 shape)
 FP8_METRIC = "fp8 visual-span decode us/step & HBM GB/s %peak, config 2 shape (bs32 16k ctx, 25% K channels kept)"
+
+
+def fp8_spark_extras(dev, steps=300):
+    """The two decode variants of this build at the config-2 shape, measured in
+    the default run: the visual span in e4m3 (``rotatek_decode_fp8``) and SparK
+    (``spark_decode``).  CUDA events over ``steps`` back-to-back calls after
+    warm-up; each against the measured HBM peak on its own algorithmic bytes
+    (every input read once, inputs larger than L2).  Their own workloads
+    (``--workload decode_fp8`` / ``spark``) add the comparisons."""
+    from rotatek_b200 import synthetic as syn
+    from rotatek_b200.kernels import pack_spark_indices, quantize_visual_fp8, rotatek_decode_fp8, spark_decode
+    e = lambda t: t.numel() * t.element_size()  # noqa: E731
+    peak, peak_kind = load_peak_hbm()
+
+    def timed(fn, n):
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / n
+
+    def summary(us, nbytes, what):
+        return {"value": us, "unit": "us/step", "algorithmic_bytes_per_launch": nbytes,
+                "hbm_frac": nbytes / us / 1e3 / peak, "peak_source": peak_kind, "steps": steps, "what": what}
+
+    out = {}
+    d = make_inputs(dev, seed=0)
+    k8, ksc, v8, vsc = quantize_visual_fp8(d.k_sparse, d.v_sparse)
+    args8 = (d.q_full, d.R_partial, d.delta_mu, d.k_full, d.v_full, d.mask_full, k8, ksc, v8, vsc, d.num_kv_groups)
+    nbytes = (e(k8) + e(ksc) + e(v8) + e(vsc) + e(d.k_full) + e(d.v_full) + e(d.R_partial) + e(d.delta_mu)
+              + 2 * e(d.q_full))
+    out["decode_fp8"] = summary(timed(lambda: rotatek_decode_fp8(*args8), steps), nbytes,
+                                "config 2 with the visual K~ and V in e4m3 (quantize_visual_fp8 once)")
+    del d, k8, ksc, v8, vsc, args8
+    torch.cuda.empty_cache()
+    b, hkv, sp, sv, st = CFG["batch"], CFG["kv_heads"], CFG["prompt"], CFG["vision"], CFG["text"]
+    g = CFG["q_heads"] // hkv
+    d = syn.make_spark(b, CFG["q_heads"], hkv, sv, sp + st, keep=CFG["keep"], seed=0, device=dev,
+                       dtype=torch.bfloat16)
+    idx = pack_spark_indices(d.keep_mask, CFG["keep"])
+    nbytes = (e(d.k_kept) + e(idx) + e(d.pruned_mean) + e(d.v_sparse) + e(d.k_full) + e(d.v_full)
+              + 2 * e(d.q_full))
+    out["spark"] = summary(timed(lambda: spark_decode(d.q_full, d.k_full, d.v_full, None, d.k_kept, idx,
+                                                      d.pruned_mean, d.v_sparse, g), steps), nbytes,
+                           "config 2 with SparK's per-token channel pruning (kept values + indices)")
+    del d, idx
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_decode_fp8(args):
