@@ -195,7 +195,7 @@ struct TcShape {
   int64_t units, blocks_full, blocks_sparse, blocks_per_unit, total;
   int grid;
   int slot_floats;
-  int64_t slots;  // one per (unit + cta, consumer warp); <= 6 consumer warps per CTA
+  int64_t slots;  // one per (unit + cta, consumer warp); <= 5 consumer warps per CTA
   int phantom;    // blocks each unit counts extra in the split among CTAs
 };
 
@@ -217,7 +217,7 @@ TcShape tc_shape(int64_t B, int64_t Hkv, int64_t G, int64_t Sf, int64_t Sv, int 
   t.total = t.units * t.blocks_per_unit;
   t.grid = (int)std::max<int64_t>(1, std::min<int64_t>(t.total, decode_ctas(device)));
   t.slot_floats = 32 + 16 * 128;
-  t.slots = (t.units + t.grid) * 6;
+  t.slots = (t.units + t.grid) * 5;
   t.phantom = t.total / t.grid >= 16 * kUnitSwitchBlocks ? kUnitSwitchBlocks : 0;
   return t;
 }

@@ -77,7 +77,7 @@ struct Cfg {
   // of 22 KB stages fit)
   static constexpr int kWarps = MODE == kModeSpark ? (DK <= 32 ? 4 : 3) : (NT == 1 && DK <= 32) ? 5 : 4;
   static constexpr int kThreads = (kWarps + 1) * 32;             // + producer warp
-  static_assert(kWarps <= 6, "the host sizes the workspace for at most 6 partial slots per CTA");
+  static_assert(kWarps <= 5, "the host sizes the workspace for at most 5 partial slots per CTA");
   // visual tokens per block: 64, or in fp8 128 (two halves of 64).  A ring
   // stage's round trip (TMA issue, data in, consumer release, producer refill)
   // takes a few microseconds whatever its size, so the bytes a stage carries
